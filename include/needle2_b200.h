@@ -1,0 +1,105 @@
+/*
+ * needle2_b200 — C ABI of the B200 build of OpenNeedle's quantized hot path.
+ *
+ * libneedle2_b200.so is a drop-in for the library that needle2/native.py
+ * loads (NEEDLE2_NATIVE_LIBRARY=<path>): the first block of entry points has
+ * the reference's names, argument meaning and ownership rules; everything
+ * after it is additive.  Plain C types only; host pointers unless a name ends
+ * in _device.
+ *
+ * Ownership: the GPU build copies packed weights, norms and the codebook to
+ * device memory at create time and owns those copies; host inputs are only
+ * read during the call (the reference borrows them for the handle's life).
+ * Errors: create functions return NULL; int functions return -1; in both cases,
+ * and after any failed void call, needle2_b200_error() holds the message
+ * (thread-local).  Calls on one handle must be serialised.
+ */
+#ifndef NEEDLE2_B200_H
+#define NEEDLE2_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- reference-compatible CQ matrix ABI --------------------------------- */
+
+/* Replaces needle2_native_features, needle2/csrc/cq.cpp:343-349. */
+const char *needle2_native_features(void);
+
+/* Replaces needle2_cq_create, needle2/csrc/cq.cpp:350-352.  bits in {2,3,4} or
+ * 5 (signed ternary crumbs, 3 centroids); group a power of two in [8, 16384]. */
+void *needle2_cq_create(const uint8_t *packed, const uint16_t *norms_fp16, int out, int in, int bits, int group,
+                        const float *codebook);
+/* Replaces needle2_cq_destroy, needle2/csrc/cq.cpp:353. */
+void needle2_cq_destroy(void *handle);
+/* Replaces needle2_cq_linear, needle2/csrc/cq.cpp:354-356: y[batch][out] =
+ * CQ(x[batch][in]) in FP32 mode.  `threads` is accepted and unused. */
+void needle2_cq_linear(void *handle, const float *x, float *y, int batch, int threads);
+/* Replaces needle2_cq_linear_lookup, needle2/csrc/cq.cpp:357-359.  The lookup
+ * table modes are CPU reassociations of the same FP32 sums; every mode runs
+ * the FP32 kernel here. */
+void needle2_cq_linear_lookup(void *handle, const float *x, float *y, int batch, int threads, int mode);
+/* Replaces needle2_cq_linear_many, needle2/csrc/cq.cpp:360-366: one input row
+ * against `count` matrices sharing its rotation. */
+void needle2_cq_linear_many(void *const *handles, int count, const float *x, float *const *ys, int threads,
+                            int mode);
+/* Replaces needle2_cq_rows, needle2/csrc/cq.cpp:367-370: dequantised rows. */
+void needle2_cq_rows(void *handle, const int64_t *ids, float *y, int count);
+
+/* ---- reference-compatible SDOT (int8) ABI ------------------------------- */
+
+/* Replaces needle2_sdot_supported, needle2/csrc/sdot.cpp:350: 1 on this build. */
+int needle2_sdot_supported(void);
+/* Replaces needle2_sdot_create, needle2/csrc/sdot.cpp:351-354: CQ2/CQ4,
+ * group in [64, 16384]; NULL otherwise. */
+void *needle2_sdot_create(const uint8_t *packed, const uint16_t *norms_fp16, int out, int in, int bits, int group,
+                          const float *codebook);
+/* Replaces needle2_sdot_destroy, needle2/csrc/sdot.cpp:355. */
+void needle2_sdot_destroy(void *handle);
+/* Replaces needle2_sdot_linear, needle2/csrc/sdot.cpp:356-359. */
+void needle2_sdot_linear(void *handle, const float *x, float *y, int batch, int threads);
+
+/* ---- additive: error channel, device pointers, debug exports ------------ */
+
+/* Message of the last failure on this thread ("" if none). */
+const char *needle2_b200_error(void);
+
+/* Int-returning forms of needle2_cq_linear / needle2_sdot_linear (0 or -1). */
+int needle2_cq_linear_checked(void *handle, const float *x, float *y, int batch);
+int needle2_sdot_linear_checked(void *handle, const float *x, float *y, int batch);
+
+/* Same computations on device pointers, enqueued on `stream` (a cudaStream_t,
+ * NULL for the legacy default stream); no host synchronisation.  The handle's
+ * device scratch is reused across calls, so calls on one handle must not run
+ * concurrently on different streams. */
+int needle2_cq_linear_device(void *handle, const float *x, float *y, int batch, void *stream);
+int needle2_sdot_linear_device(void *handle, const float *x, float *y, int batch, void *stream);
+
+/* Two-phase device form: prepare rotates (FP32 mode) or rotates and quantises
+ * (SDOT mode) x[batch][in] into the handle's device scratch; multiply then
+ * writes y[batch][out] from it.  Split as SdotCQ::prepare / SdotCQ::multiply,
+ * needle2/csrc/sdot.cpp:47-103,338-345.  multiply's batch must not exceed the
+ * last prepare's. */
+int needle2_cq_prepare_device(void *handle, const float *x, int batch, void *stream);
+int needle2_cq_multiply_device(void *handle, float *y, int batch, void *stream);
+int needle2_sdot_prepare_device(void *handle, const float *x, int batch, void *stream);
+int needle2_sdot_multiply_device(void *handle, float *y, int batch, void *stream);
+
+/* SDOT internals the reference never exports (its per-group int32 dots stay
+ * inside SdotCQ::row, needle2/csrc/sdot.cpp:142-149): partials[batch][out][groups]
+ * int32, q[batch][padded] int8 in natural element order, scales[batch][groups];
+ * any output pointer may be NULL.  Host pointers. */
+int needle2_sdot_debug(void *handle, const float *x, int batch, float *y, int32_t *partials, int8_t *q,
+                       float *scales);
+
+/* Geometry of a handle: out, in, bits, group, padded, groups. */
+int needle2_cq_geometry(void *handle, int *geometry6);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NEEDLE2_B200_H */
