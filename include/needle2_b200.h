@@ -98,6 +98,54 @@ int needle2_sdot_debug(void *handle, const float *x, int batch, float *y, int32_
 /* Geometry of a handle: out, in, bits, group, padded, groups. */
 int needle2_cq_geometry(void *handle, int *geometry6);
 
+/* ---- additive: batched INT8 KV cache with a shared prefix ---------------- */
+/*
+ * The reference keeps one sequence per Engine and an optional per-instance
+ * prefix snapshot (needle2/csrc/engine.cpp:192-199,376-499).  A KV pool holds
+ * `sessions` sequences of one layer that share ONE read-only prefix of
+ * `prefix_len` positions (the sinks of the reference's slot map) stored once on
+ * the device; each session owns window (or max_seq - prefix_len) further slots
+ * addressed as Engine::cache_slot does (engine.cpp:500).  Positions passed to
+ * the calls are absolute and must be >= prefix_len.  Quantisation is the
+ * reference's INT8 rule (engine.cpp:1005-1021); attention its
+ * compute_attention (engine.cpp:898-967).  Calls on one pool must be
+ * serialised; sessions within one call must be distinct.
+ */
+void *needle2_kv_create(int sessions, int heads, int kvheads, int head_dim, int max_seq, int window, int prefix_len);
+void needle2_kv_destroy(void *kv);
+size_t needle2_kv_storage_bytes(void *kv);
+/* Quantise and store the shared prefix: k, v [prefix_len][kvheads*head_dim]. */
+int needle2_kv_set_prefix(void *kv, const float *k, const float *v);
+int needle2_kv_set_prefix_device(void *kv, const float *k, const float *v, void *stream);
+/* Store one new token per listed session (k, v [count][kvheads*head_dim]). */
+int needle2_kv_store(void *kv, const int *session_ids, const int *positions, const float *k, const float *v,
+                     int count);
+int needle2_kv_store_device(void *kv, const int *session_ids, const int *positions, const float *k, const float *v,
+                            int count, void *stream);
+/* Attention of one query per listed session at `positions` over the current
+ * cache (q, out [count][heads*head_dim]); nothing is stored. */
+int needle2_attention_query(void *kv, const int *session_ids, const int *positions, const float *q, float *out,
+                            int count);
+int needle2_attention_query_device(void *kv, const int *session_ids, const int *positions, const float *q, float *out,
+                                   int count, void *stream);
+/* Decode step: store each session's new K/V at its position, then attend. */
+int needle2_attention_decode(void *kv, const int *session_ids, const int *positions, const float *q, const float *k,
+                             const float *v, float *out, int count);
+int needle2_attention_decode_device(void *kv, const int *session_ids, const int *positions, const float *q,
+                                    const float *k, const float *v, float *out, int count, void *stream);
+/* Prefill `tokens` new tokens per listed session starting at start_positions,
+ * causal, with the reference's store-then-attend order per token
+ * (engine.cpp:1170-1210).  q/out [count][tokens][heads*head_dim],
+ * k/v [count][tokens][kvheads*head_dim]. */
+int needle2_attention_prefill(void *kv, const int *session_ids, const int *start_positions, int tokens, const float *q,
+                              const float *k, const float *v, float *out, int count);
+int needle2_attention_prefill_device(void *kv, const int *session_ids, const int *start_positions, int tokens,
+                                     const float *q, const float *k, const float *v, float *out, int count,
+                                     void *stream);
+/* One session's cache in the reference layout: keys/values [capacity][kvheads*head_dim]
+ * int8, scales [capacity][kvheads], capacity = window ? window + prefix_len : max_seq. */
+int needle2_kv_export(void *kv, int session, int8_t *keys, int8_t *values, float *k_scales, float *v_scales);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,347 @@
+// INT8 KV-cache attention for B200 (sm_100a): quantise-store, split-K
+// flash-decode, and causal prefill over a shared, read-only cached prefix.
+//
+// Semantics follow OpenNeedle's Engine (needle2/csrc/engine.cpp):
+//  * store (1005-1021): per token and KV head, scale = max|k|/127 (1 if 0),
+//    k_i8 = clamp(round-half-even(k * (127/max)), -127, 127); same for v;
+//  * slots (500, 898-911): prefix sinks [0, P) are pinned; other positions
+//    cycle through `window` slots (or are linear without a window); a query at
+//    pos sees the sinks, then max(P, pos-window+1) .. pos;
+//  * scores (949-960): s = (q . float(k_i8)) * k_scale * (1/sqrt(HD)),
+//    softmax over the visible slots, out = sum p * v_scale * float(v_i8).
+//  * prefill (1170-1210): each token stores its K/V, then attends.  Here a
+//    prefill chunk attends over older slots plus the chunk's own freshly
+//    quantised K/V (a staging copy), and the ring is written afterwards, which
+//    is the same visible set and values as the token-by-token order.
+//
+// Device layout (head-major, so one (sequence, KV head) is one contiguous
+// stream):  prefix  k/v [KV][P][HD] int8, scales [KV][P];  per session
+// k/v [S][KV][Cs][HD], scales [S][KV][Cs], Cs = window ? window : max_seq - P.
+#include <math.h>
+
+#include <algorithm>
+
+#include "attention.cuh"
+#include "common.cuh"
+
+namespace nb200 {
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+// One warp per (token, KV head): quantise head_dim values of k and v.
+__global__ void kv_quantize_kernel(const float *__restrict__ k, const float *__restrict__ v, int tokens, int kvheads,
+                                   int hd, int8_t *__restrict__ ko, int8_t *__restrict__ vo, float *__restrict__ ks,
+                                   float *__restrict__ vs, KVDest dest) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= tokens * kvheads) return;
+    const int t = warp / kvheads, kh = warp % kvheads;
+    const float *kp = k + ((size_t)t * kvheads + kh) * hd, *vp = v + ((size_t)t * kvheads + kh) * hd;
+    float mk = 0.f, mv = 0.f;
+    for (int d = lane; d < hd; d += 32) {
+        mk = fmaxf(mk, fabsf(kp[d]));
+        mv = fmaxf(mv, fabsf(vp[d]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mk = fmaxf(mk, __shfl_xor_sync(kFull, mk, o));
+        mv = fmaxf(mv, __shfl_xor_sync(kFull, mv, o));
+    }
+    const float sk = mk > 0.f ? __fdiv_rn(mk, 127.f) : 1.f, sv = mv > 0.f ? __fdiv_rn(mv, 127.f) : 1.f;
+    const float ik = mk > 0.f ? __fdiv_rn(127.f, mk) : 0.f, iv = mv > 0.f ? __fdiv_rn(127.f, mv) : 0.f;
+    // destination row
+    size_t row;
+    if (dest.mode == KVDest::kLinear) {
+        row = (size_t)kh * dest.rows + t;                      // [KV][rows] (prefix or staging)
+    } else {
+        const int e = t / dest.tokens_per_entry, tt = t % dest.tokens_per_entry;
+        if (tt < dest.min_t) return;
+        const int s = dest.session[e], pos = dest.position[e] + tt;
+        const int slot = dest.window ? (pos - dest.prefix) % dest.window : pos - dest.prefix;
+        row = ((size_t)s * kvheads + kh) * dest.rows + slot;   // [S][KV][Cs]
+    }
+    for (int d = lane; d < hd; d += 32) {
+        ko[row * hd + d] = (int8_t)clamp127(rint_even(__fmul_rn(kp[d], ik)));
+        vo[row * hd + d] = (int8_t)clamp127(rint_even(__fmul_rn(vp[d], iv)));
+    }
+    if (lane == 0) {
+        ks[row] = sk;
+        vs[row] = sv;
+    }
+}
+
+// Exact int8 -> float for four packed bytes.
+__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float &a, float &b, float &c, float &d) {
+    a = (float)(int8_t)(w & 0xff);
+    b = (float)(int8_t)((w >> 8) & 0xff);
+    c = (float)(int8_t)((w >> 16) & 0xff);
+    d = (float)(int8_t)(w >> 24);
+}
+
+struct Row {
+    const int8_t *k, *v;
+    float ks, vs;
+};
+
+// Visible index i of query (session s, position pos) -> K/V row.
+__device__ __forceinline__ Row visible_row(const AttnParams &p, int s, int pos, int kh, int i, int prefix_count,
+                                           int start, int entry, int chunk_start) {
+    int position;
+    if (i < prefix_count) {
+        position = i;
+    } else {
+        position = start + (i - prefix_count);
+    }
+    Row r;
+    if (position < p.prefix) {
+        const size_t row = (size_t)kh * p.prefix + position;
+        r.k = p.pk + row * p.hd;
+        r.v = p.pv + row * p.hd;
+        r.ks = p.pks[row];
+        r.vs = p.pvs[row];
+    } else if (p.stage_k && position >= chunk_start) {
+        const size_t row = (size_t)kh * p.stage_rows + (size_t)entry * p.tokens + (position - chunk_start);
+        r.k = p.stage_k + row * p.hd;
+        r.v = p.stage_v + row * p.hd;
+        r.ks = p.stage_ks[row];
+        r.vs = p.stage_vs[row];
+    } else {
+        const int slot = p.window ? (position - p.prefix) % p.window : position - p.prefix;
+        const size_t row = ((size_t)s * p.kvheads + kh) * p.cs + slot;
+        r.k = p.sk + row * p.hd;
+        r.v = p.sv + row * p.hd;
+        r.ks = p.sks[row];
+        r.vs = p.svs[row];
+    }
+    return r;
+}
+
+// One CTA = (query, KV head, split): the R = heads/kvheads query heads of the
+// group over a contiguous range of the visible slots.  Lane-per-slot scores,
+// online softmax per warp, lane-per-dimension value accumulation.
+template <int HD, bool EXACT>
+__global__ void __launch_bounds__(128) attn_split_kernel(const AttnParams p) {
+    constexpr int NW = 4;
+    const int hd = EXACT ? HD : p.hd;
+    constexpr int DPL = (HD + 31) / 32;   // dims per lane in the PV phase
+    __shared__ float qs[kMaxGroup * HD];
+    __shared__ float wm[NW][kMaxGroup], wl[NW][kMaxGroup];
+    __shared__ float wacc[NW][kMaxGroup][HD];
+
+    const int split = blockIdx.x, kh = blockIdx.y, query = blockIdx.z;
+    const int entry = query / p.tokens, t = query % p.tokens;
+    const int s = p.session[entry];
+    const int chunk_start = p.position[entry];
+    const int pos = chunk_start + t;
+    const int R = p.heads / p.kvheads;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const int prefix_count = p.window ? min(p.prefix, pos + 1) : 0;
+    const int start = p.window ? max(p.prefix, pos - p.window + 1) : 0;
+    const int len = prefix_count + max(0, pos - start + 1);
+    const int per = (len + p.splits - 1) / p.splits;
+    const int i0 = split * per, i1 = min(len, i0 + per);
+
+    for (int idx = threadIdx.x; idx < R * hd; idx += blockDim.x) {
+        const int r = idx / hd, d = idx % hd;
+        qs[r * HD + d] = p.q[((size_t)query * p.heads + kh * R + r) * hd + d];
+    }
+    __syncthreads();
+
+    const float inv_sqrt = p.inv_sqrt_hd;
+    float m[kMaxGroup], l[kMaxGroup], acc[kMaxGroup][DPL];
+#pragma unroll
+    for (int r = 0; r < kMaxGroup; ++r) {
+        m[r] = -INFINITY;
+        l[r] = 0.f;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) acc[r][j] = 0.f;
+    }
+
+    for (int base = i0 + warp * 32; base < i1; base += NW * 32) {
+        const int i = base + lane;
+        const bool valid = i < i1;
+        Row row{};
+        float sc[kMaxGroup];
+#pragma unroll
+        for (int r = 0; r < kMaxGroup; ++r) sc[r] = -INFINITY;
+        if (valid) {
+            row = visible_row(p, s, pos, kh, i, prefix_count, start, entry, chunk_start);
+            float dot[kMaxGroup];
+#pragma unroll
+            for (int r = 0; r < kMaxGroup; ++r) dot[r] = 0.f;
+            if (hd % 4 == 0) {
+                const uint32_t *kw = reinterpret_cast<const uint32_t *>(row.k);
+#pragma unroll 4
+                for (int d4 = 0; d4 < hd / 4; ++d4) {
+                    float a, b, c, e;
+                    i8x4_to_f32(__ldg(kw + d4), a, b, c, e);
+#pragma unroll
+                    for (int r = 0; r < kMaxGroup; ++r) {
+                        if (r < R) {
+                            const float4 qv = *reinterpret_cast<const float4 *>(qs + r * HD + 4 * d4);
+                            dot[r] = fmaf(qv.x, a, dot[r]);
+                            dot[r] = fmaf(qv.y, b, dot[r]);
+                            dot[r] = fmaf(qv.z, c, dot[r]);
+                            dot[r] = fmaf(qv.w, e, dot[r]);
+                        }
+                    }
+                }
+            } else {
+                for (int d = 0; d < hd; ++d) {
+                    const float kf = (float)row.k[d];
+#pragma unroll
+                    for (int r = 0; r < kMaxGroup; ++r)
+                        if (r < R) dot[r] = fmaf(qs[r * HD + d], kf, dot[r]);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kMaxGroup; ++r) sc[r] = __fmul_rn(__fmul_rn(dot[r], row.ks), inv_sqrt);
+        }
+        // online softmax update per head
+        float pr[kMaxGroup];
+#pragma unroll
+        for (int r = 0; r < kMaxGroup; ++r) {
+            if (r >= R) { pr[r] = 0.f; continue; }
+            float bm = sc[r];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(kFull, bm, o));
+            const float mn = fmaxf(m[r], bm);
+            const float corr = m[r] == -INFINITY ? 0.f : expf(m[r] - mn);
+            pr[r] = valid ? expf(sc[r] - mn) : 0.f;
+            float ps = pr[r];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(kFull, ps, o);
+            l[r] = l[r] * corr + ps;
+            m[r] = mn;
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) acc[r][j] *= corr;
+            pr[r] *= valid ? row.vs : 0.f;     // fold the value scale into the weight
+        }
+        // values: lane owns dims lane + 32*j
+        const int nvalid = min(32, i1 - base);
+        for (int jt = 0; jt < nvalid; ++jt) {
+            const int8_t *vrow = reinterpret_cast<const int8_t *>(
+                __shfl_sync(kFull, reinterpret_cast<unsigned long long>(row.v), jt));
+            float w[kMaxGroup];
+#pragma unroll
+            for (int r = 0; r < kMaxGroup; ++r) w[r] = __shfl_sync(kFull, pr[r], jt);
+#pragma unroll
+            for (int j = 0; j < DPL; ++j) {
+                const int d = lane + 32 * j;
+                if (d < hd) {
+                    const float vf = (float)__ldg(vrow + d);
+#pragma unroll
+                    for (int r = 0; r < kMaxGroup; ++r)
+                        if (r < R) acc[r][j] = fmaf(w[r], vf, acc[r][j]);
+                }
+            }
+        }
+    }
+    // combine the warps of this CTA
+#pragma unroll
+    for (int r = 0; r < kMaxGroup; ++r) {
+        if (r >= R) continue;
+        if (lane == 0) {
+            wm[warp][r] = m[r];
+            wl[warp][r] = l[r];
+        }
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) {
+            const int d = lane + 32 * j;
+            if (d < hd) wacc[warp][r][d] = acc[r][j];
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < R * hd; idx += blockDim.x) {
+        const int r = idx / hd, d = idx % hd;
+        float mm = -INFINITY;
+        for (int w = 0; w < NW; ++w) mm = fmaxf(mm, wm[w][r]);
+        float ll = 0.f, aa = 0.f;
+        for (int w = 0; w < NW; ++w) {
+            if (wm[w][r] == -INFINITY) continue;
+            const float f = expf(wm[w][r] - mm);
+            ll += wl[w][r] * f;
+            aa += wacc[w][r][d] * f;
+        }
+        const int h = kh * R + r;
+        if (p.splits == 1) {
+            p.out[((size_t)query * p.heads + h) * hd + d] = ll > 0.f ? aa / ll : 0.f;
+        } else {
+            const size_t prow = ((size_t)query * p.heads + h) * p.splits + split;
+            p.part_acc[prow * hd + d] = aa;
+            if (d == 0) {
+                p.part_m[prow] = mm;
+                p.part_l[prow] = ll;
+            }
+        }
+    }
+}
+
+// Merge the split partials of each (query, head).
+__global__ void attn_combine_kernel(const AttnParams p, int hd) {
+    const int qh = blockIdx.x;   // query * heads + h
+    const float *pm = p.part_m + (size_t)qh * p.splits, *pl = p.part_l + (size_t)qh * p.splits;
+    float mm = -INFINITY;
+    for (int j = 0; j < p.splits; ++j) mm = fmaxf(mm, pm[j]);
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float ll = 0.f, aa = 0.f;
+        for (int j = 0; j < p.splits; ++j) {
+            if (pm[j] == -INFINITY) continue;
+            const float f = expf(pm[j] - mm);
+            ll += pl[j] * f;
+            aa += p.part_acc[((size_t)qh * p.splits + j) * hd + d] * f;
+        }
+        p.out[(size_t)qh * hd + d] = ll > 0.f ? aa / ll : 0.f;
+    }
+}
+
+}  // namespace
+
+bool launch_kv_quantize(const float *k, const float *v, int tokens, int kvheads, int hd, int8_t *ko, int8_t *vo,
+                        float *ks, float *vs, const KVDest &dest, cudaStream_t st) {
+    if (tokens <= 0) return true;
+    const long long warps = (long long)tokens * kvheads;
+    kv_quantize_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(k, v, tokens, kvheads, hd, ko, vo, ks, vs,
+                                                                             dest);
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+}
+
+int attention_splits(int max_len, int queries_x_kv, int sms) {
+    // enough CTAs to cover the machine about twice, at least 128 slots each
+    int splits = 1;
+    while (splits < 32 && (long long)queries_x_kv * splits < 2LL * sms * 4 && max_len / (splits * 2) >= 128) splits *= 2;
+    return splits;
+}
+
+bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
+    if (queries <= 0) return true;
+    if (p.heads % p.kvheads || p.heads / p.kvheads > kMaxGroup) {
+        set_error("attention supports up to 8 query heads per KV head");
+        return false;
+    }
+    dim3 grid(p.splits, p.kvheads, queries);
+    switch (p.hd) {
+        case 32: attn_split_kernel<32, true><<<grid, 128, 0, st>>>(p); break;
+        case 64: attn_split_kernel<64, true><<<grid, 128, 0, st>>>(p); break;
+        case 128: attn_split_kernel<128, true><<<grid, 128, 0, st>>>(p); break;
+        default:
+            if (p.hd <= 32) attn_split_kernel<32, false><<<grid, 128, 0, st>>>(p);
+            else if (p.hd <= 64) attn_split_kernel<64, false><<<grid, 128, 0, st>>>(p);
+            else if (p.hd <= 128) attn_split_kernel<128, false><<<grid, 128, 0, st>>>(p);
+            else {
+                set_error("head_dim above 128 is not supported by the GPU build");
+                return false;
+            }
+    }
+    NB_CUDA_TRY(cudaGetLastError());
+    if (p.splits > 1) {
+        attn_combine_kernel<<<queries * p.heads, 64, 0, st>>>(p, p.hd);
+        NB_CUDA_TRY(cudaGetLastError());
+    }
+    return true;
+}
+
+}  // namespace nb200

@@ -14,6 +14,7 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "cq_gemv.cuh"
 #include "cq_kernels.cuh"
 
 namespace nb200 {
@@ -514,6 +515,22 @@ bool launch_gemv_f32(const CQDevice &w, const float *rot, int M, float *y, int l
         NB_CUDA_TRY(cudaGetLastError());
         return true;
     }
+    if (w.bits != 5) {
+        const int cap = gemv_v2_max_rows(w.bits, w.group, w.groups, false);
+        if (cap > 0) {
+            for (int m0 = 0; m0 < M; m0 += cap) {
+                GemvV2Params p{};
+                p.packed = w.packed; p.norms = w.norms; p.out = w.out; p.groups = w.groups;
+                p.rowbytes = w.rowbytes; p.padded = w.padded; p.M = std::min(cap, M - m0);
+                p.rot = rot + (size_t)m0 * w.padded;
+                p.y = y + (size_t)m0 * ldy;
+                p.ldy = ldy;
+                for (int i = 0; i < 16; ++i) p.lut[i] = w.lut[i];
+                if (!launch_gemv_v2(p, w.bits, w.group, false, s)) return false;
+            }
+            return true;
+        }
+    }
     for (int m0 = 0; m0 < M; m0 += kGemvMaxRows) {
         GemvParams p{};
         p.packed = w.packed;
@@ -549,6 +566,25 @@ bool launch_gemv_i8(const CQDevice &w, const int8_t *q, const float *xs, int M, 
             ctab, w.centroid_scale);
         NB_CUDA_TRY(cudaGetLastError());
         return true;
+    }
+    {
+        const int cap = gemv_v2_max_rows(w.bits, w.group, w.groups, true);
+        if (cap > 0) {
+            for (int m0 = 0; m0 < M; m0 += cap) {
+                GemvV2Params p{};
+                p.packed = w.packed; p.norms = w.norms; p.out = w.out; p.groups = w.groups;
+                p.rowbytes = w.rowbytes; p.padded = w.padded; p.M = std::min(cap, M - m0);
+                p.q = q + (size_t)m0 * w.padded;
+                p.xs = xs + (size_t)m0 * w.groups;
+                p.y = y + (size_t)m0 * ldy;
+                p.ldy = ldy;
+                p.partials = partials ? partials + (size_t)m0 * w.out * w.groups : nullptr;
+                for (int i = 0; i < 4; ++i) p.ctab[i] = w.ctab[i];
+                p.cs = w.centroid_scale;
+                if (!launch_gemv_v2(p, w.bits, w.group, true, s)) return false;
+            }
+            return true;
+        }
     }
     for (int m0 = 0; m0 < M; m0 += kGemvMaxRows) {
         GemvParams p{};
