@@ -1,22 +1,26 @@
-"""Benchmark of the CQ decode GEMV on B200 (one JSON line on rank 0).
+"""Benchmark of the CQ4 decode GEMV on B200 (one JSON line on rank 0).
 
-Workload (the HBM-roofline GEMV of the benchmark plan): y = W x with W a CQ4
-matrix of 14336 x 4096 (group 128) packed from N(0, 0.02) seed-0 weights and x
-one 4096-wide N(0, 1) activation row (seed 1), SDOT int8 mode (per-group int8
-activations, int8 centroids, exact int32 per group).  One step = prepare
-(rotate + quantise x) + multiply on one of R distinct device copies of W,
-cycled so that the working set (R x 30.3 MB) is several times the 126 MB L2;
-every launch therefore streams its weights from HBM.
+Workload (the HBM-roofline decode GEMV of the benchmark plan): R = 17 distinct
+CQ4 matrices of 14336 x 4096 (group 128, the config-5 GEMM shape), each packed
+from N(0, 0.02) weights (seed 0), against one 4096-wide N(0, 1) activation row
+(seed 1), in the SDOT int8 mode (per-group int8 activations, int8 centroids,
+exact int32 per group).  One step = prepare (rotate + quantise x once) and one
+fused GEMV launch over the R matrices sharing that input, as the reference's
+fused projections do (needle2/csrc/engine.cpp:560-606): 516 MB of weights,
+more than 4x the 126 MB L2, so every step streams its weights from HBM.
 
-value    = algorithmic bytes of all steps on all ranks / max-over-ranks device time
-roofline = the GEMV kernel alone: algorithmic bytes per launch / its mean CUDA-event
-           duration, against the measured HBM copy bandwidth
-e2e      = the same metric through the reference-facing host call
-           (needle2_sdot_linear: host x -> device -> host y, synchronised)
-cpu_baseline / --impl reference = the reference's own CPU SDOT path
-           (oracle/_ref, compiled from its sources) on this host's cores.
+value     algorithmic bytes of all steps on all ranks / max-over-ranks device time
+          (K steps captured in one CUDA graph, replayed once between CUDA events)
+roofline  the fused GEMV kernel alone: its algorithmic bytes / its mean CUDA-event
+          duration, against the measured HBM copy bandwidth (MEASURED_PEAKS.json)
+e2e       the same metric through the reference-facing host call
+          (host x -> device, prepare, fused GEMV, R outputs -> host, synchronised)
+cpu_baseline / --impl reference
+          the reference's own CPU SDOT path (oracle/_ref, compiled from its
+          sources; SdotCQ prepare + multiply, OpenMP rows) on this host's cores,
+          one matrix per sample (a bounded sample of the R-matrix step).
 
-Multi-GPU: each rank runs the same workload on its own GPU (replicas; the
+Multi-GPU: each rank runs the same workload on its own GPU (replicas: the
 standalone GEMV does not shard), scaling "weak".
 """
 from __future__ import annotations
@@ -26,7 +30,6 @@ import ctypes as ct
 import json
 import os
 import re
-import subprocess
 import sys
 import threading
 import time
@@ -37,14 +40,19 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-N_OUT, K_IN, BITS, GROUP, M_ROWS = 14336, 4096, 4, 128, 1
+N_OUT, K_IN, BITS, GROUP, M_ROWS, COPIES = 14336, 4096, 4, 128, 1, 17
 L2_BYTES = 126 * 1024 * 1024
 
 
-def algorithmic_bytes(n=N_OUT, k=K_IN, bits=BITS, group=GROUP, m=M_ROWS) -> int:
-    """Packed weights + FP16 norms + FP32 input and output: N*(pad*b/8 + 2*pad/G) + 4*M*K + 4*M*N."""
+def matrix_bytes(n=N_OUT, k=K_IN, bits=BITS, group=GROUP) -> int:
+    """Packed weights + FP16 norms of one matrix: N*(pad*b/8 + 2*pad/G)."""
     pad = -(-k // group) * group
-    return n * (pad * bits // 8 + 2 * pad // group) + 4 * m * k + 4 * m * n
+    return n * (pad * bits // 8 + 2 * pad // group)
+
+
+def step_bytes(copies=COPIES, m=M_ROWS) -> int:
+    """Algorithmic bytes of one fused step: R matrices, the FP32 input once, R FP32 outputs."""
+    return copies * (matrix_bytes() + 4 * m * N_OUT) + 4 * m * K_IN
 
 
 def peaks():
@@ -57,57 +65,54 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples during the timed region."""
+    """SM clock and throttle-reason samples taken through NVML every ~1 ms
+    during the timed region (the fields of nvidia-smi's clocks query)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.lines: list[str] = []
+        self.samples: list[tuple[float, float, int]] = []
+        self._stop = threading.Event()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self._max = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._run, daemon=True)
             self.thread.start()
-        except OSError:
-            self.proc = None
+        except Exception:  # noqa: BLE001 - clocks are then reported as unavailable
+            self._nvml = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        n = self._nvml
+        while not self._stop.is_set():
+            try:
+                sm = n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((float(sm), float(self._max), int(reasons)))
+            except Exception:  # noqa: BLE001
+                break
+            time.sleep(0.001)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        if getattr(self, "thread", None):
+            self.thread.join(timeout=2)
 
     def summary(self):
-        sm, smax, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = max(smax, float(parts[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax or None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": "nvml"}
+        mask = 0
+        for s in self.samples:
+            mask |= s[2]
+        return {"sm_mhz": float(np.median([s[0] for s in self.samples])), "sm_max_mhz": self.samples[0][1],
+                "reasons": sorted(k for k, bit in self.REASONS.items() if mask & bit),
+                "samples": len(self.samples), "source": "nvml, ~1 ms period"}
 
 
 def cpu_threads() -> int:
@@ -126,25 +131,49 @@ def activations():
     return np.random.default_rng(1).normal(size=(M_ROWS, K_IN)).astype(np.float32)
 
 
+def profiled_traffic(tag):
+    """DRAM bytes per launch recorded from an ncu capture in profiles/ (or None)."""
+    for f in sorted((ROOT / "profiles").glob(f"{tag}*.md")):
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
+        if m:
+            return float(m.group(1))
+    return None
+
+
+def workload_config(copies, world):
+    return {"workload": f"cq4_sdot_gemv_fused{copies}x{N_OUT}x{K_IN}_m{M_ROWS}", "bits": BITS, "group": GROUP,
+            "M": M_ROWS, "N": N_OUT, "K": K_IN, "matrices_per_step": copies, "mode": "sdot-int8",
+            "weight_bytes_per_step": copies * matrix_bytes(),
+            "l2": f"inputs larger than L2: each step streams {copies} distinct 30 MB matrices",
+            "parallelism": f"replicas{world}", "bytes_per_step": step_bytes(copies)}
+
+
 # ----------------------------------------------------------- reference arm
 
-def reference_gemv(packed, norms, cb, x, seconds=None, steps=None, warmup=2, copies=4):
-    """Times the reference's SdotCQ (prepare + multiply, OpenMP rows) on all host threads.
-    Returns (GB/s, seconds per step, steps run, threads, kind)."""
+def reference_gemv(packed, norms, cb, x, seconds=None, steps=None, warmup=2, host_copies=4):
+    """Times the reference's SdotCQ (prepare + multiply, OpenMP rows) on all host
+    threads.  One sample = one GEMV of one 14336x4096 matrix (host copies cycled);
+    the rate in GB/s counts the same algorithmic bytes per matrix as the GPU arm.
+    Returns (GB/s, seconds per GEMV, GEMVs run, threads, kind)."""
     from oracle import oracle as O
     threads = cpu_threads()
     os.environ.setdefault("OMP_WAIT_POLICY", "PASSIVE")
     y = np.empty((M_ROWS, N_OUT), np.float32)
     if O.ref_available():
         L = O.ref_lib()
-        mats = [np.array(packed, copy=True) for _ in range(copies)]
+        mats = [np.array(packed, copy=True) for _ in range(host_copies)]
         handles = [L.ref_sdot_new(m.ctypes.data, norms.ctypes.data, N_OUT, K_IN, BITS, GROUP, cb.ctypes.data)
                    for m in mats]
-        run = lambda i: L.ref_sdot_run(handles[i % copies], x.ctypes.data, y.ctypes.data, M_ROWS, threads)  # noqa: E731
+
+        def run(i):
+            L.ref_sdot_run(handles[i % host_copies], x.ctypes.data, y.ctypes.data, M_ROWS, threads)
         kind, used = "reference", threads
     else:
-        run = lambda i: O.sdot_linear(packed, norms, (N_OUT, K_IN), BITS, GROUP, cb, x)  # noqa: E731
-        kind, used, handles = "port", 1, []
+        handles = []
+
+        def run(i):
+            O.sdot_linear(packed, norms, (N_OUT, K_IN), BITS, GROUP, cb, x)
+        kind, used = "port", 1
     for i in range(warmup):
         run(i)
     t0 = time.perf_counter()
@@ -156,30 +185,59 @@ def reference_gemv(packed, norms, cb, x, seconds=None, steps=None, warmup=2, cop
         if (steps is not None and n >= steps) or (seconds is not None and el >= seconds):
             break
     el = time.perf_counter() - t0
-    if handles:
-        for h in handles:
-            O.ref_lib().ref_sdot_free(h)
-    return algorithmic_bytes() * n / el / 1e9, el / n, n, used, kind
+    for h in handles:
+        O.ref_lib().ref_sdot_free(h)
+    per_matrix = matrix_bytes() + 4 * M_ROWS * (N_OUT + K_IN)
+    return per_matrix * n / el / 1e9, el / n, n, used, kind
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return None
+    packed, norms, cb = weights()
+    x = activations()
+    gbs, sec, n, threads, kind = reference_gemv(packed, norms, cb, x, steps=args.steps, warmup=args.warmup)
+    return {
+        "impl": "reference", "metric": "cq4_gemv_hbm_gbs", "value": gbs, "unit": "GB/s", "n_gpus": world,
+        "steps": n, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "i8", "data": "synthetic", "config": workload_config(COPIES, world),
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": f"each step one reference SdotCQ GEMV of one 14336x4096 CQ4 matrix (4 host "
+                                   f"copies cycled), {n} steps; a bounded sample of the {COPIES}-matrix step"},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
 
 
 # ------------------------------------------------------------- native arm
 
-class SdotHandle:
-    def __init__(self, lib, packed, norms, cb):
-        self.lib = lib
-        self.h = lib.needle2_sdot_create(packed.ctypes.data, norms.ctypes.data, N_OUT, K_IN, BITS, GROUP,
-                                         cb.ctypes.data)
-        if not self.h:
-            raise RuntimeError(lib.needle2_b200_error().decode())
-
-    def __del__(self):
-        if getattr(self, "h", None):
-            self.lib.needle2_sdot_destroy(self.h)
-
-
 def check(status, lib):
     if status:
         raise RuntimeError(lib.needle2_b200_error().decode())
+
+
+def create(lib, packed, norms, cb, sdot):
+    fn = lib.needle2_sdot_create if sdot else lib.needle2_cq_create
+    h = fn(packed.ctypes.data, norms.ctypes.data, N_OUT, K_IN, BITS, GROUP, cb.ctypes.data)
+    if not h:
+        raise RuntimeError(lib.needle2_b200_error().decode())
+    return h
+
+
+def kernel_ms(lib, handles, x, yp, stream, sdot, n):
+    """Mean CUDA-event duration of the fused GEMV launch alone (prepare outside)."""
+    import torch
+    sp = stream.cuda_stream
+    hp = (ct.c_void_p * len(handles))(*handles)
+    prep = lib.needle2_sdot_prepare_device if sdot else lib.needle2_cq_prepare_device
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    for i in range(n):
+        check(prep(handles[0], x.data_ptr(), M_ROWS, sp), lib)
+        starts[i].record(stream)
+        check(lib.needle2_cq_multiply_many_device(hp, len(handles), yp, M_ROWS, int(sdot), sp), lib)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    return float(np.mean([a.elapsed_time(b) for a, b in zip(starts, ends)]))
 
 
 def run_native(args, rank, world, dist):
@@ -196,22 +254,29 @@ def run_native(args, rank, world, dist):
     torch.cuda.set_device(dev)
     packed, norms, cb = weights()
     x_host = activations()
-    bytes_step = algorithmic_bytes()
-    per_copy = N_OUT * (packed.shape[1] + 2 * norms.shape[1])
-    copies = args.copies or max(4, -(-4 * L2_BYTES // per_copy))  # working set >= 4x L2
-    handles = [SdotHandle(lib, packed, norms, cb) for _ in range(copies)]
+    copies = args.copies or COPIES
+    handles = [create(lib, packed, norms, cb, True) for _ in range(copies)]
+    hp = (ct.c_void_p * copies)(*handles)
     x = torch.from_numpy(x_host).to(dev)
-    y = torch.empty(M_ROWS, N_OUT, device=dev)
+    ys = torch.empty(copies, M_ROWS, N_OUT, device=dev)
+    yp = (ct.c_void_p * copies)(*[ys[i].data_ptr() for i in range(copies)])
     stream = torch.cuda.current_stream(dev)
-    sp = stream.cuda_stream
+    bytes_step = step_bytes(copies)
 
-    def step(i):
-        h = handles[i % copies].h
-        check(lib.needle2_sdot_prepare_device(h, x.data_ptr(), M_ROWS, sp), lib)
-        check(lib.needle2_sdot_multiply_device(h, y.data_ptr(), M_ROWS, sp), lib)
+    def step(sp):
+        check(lib.needle2_cq_linear_many_device(hp, copies, x.data_ptr(), yp, M_ROWS, 1, sp), lib)
 
-    for i in range(args.warmup):
-        step(i)
+    for _ in range(args.warmup):
+        step(stream.cuda_stream)
+    torch.cuda.synchronize(dev)
+    # K timed steps captured once into a CUDA graph and replayed once; the
+    # kernels inside chain by programmatic dependent launch
+    graph_stream = torch.cuda.Stream(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(graph_stream):
+        with torch.cuda.graph(graph, stream=graph_stream):
+            for _ in range(args.steps):
+                step(graph_stream.cuda_stream)
     torch.cuda.synchronize(dev)
     if dist is not None:
         dist.barrier()
@@ -219,54 +284,57 @@ def run_native(args, rank, world, dist):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index) as clocks:
         start.record(stream)
-        for i in range(args.steps):
-            step(args.warmup + i)
+        graph.replay()
         end.record(stream)
         torch.cuda.synchronize(dev)
     elapsed_ms = start.elapsed_time(end)
+    del graph
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize(dev)
 
-    # kernel alone: events around each multiply launch
-    kstart = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    kend = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    for i in range(args.steps):
-        h = handles[i % copies].h
-        check(lib.needle2_sdot_prepare_device(h, x.data_ptr(), M_ROWS, sp), lib)
-        kstart[i].record(stream)
-        check(lib.needle2_sdot_multiply_device(h, y.data_ptr(), M_ROWS, sp), lib)
-        kend[i].record(stream)
-    torch.cuda.synchronize(dev)
-    kernel_ms = float(np.mean([a.elapsed_time(b_) for a, b_ in zip(kstart, kend)]))
+    n_kernel = max(5, min(args.steps, 40))
+    fused_ms = kernel_ms(lib, handles, x, yp, stream, True, n_kernel)
+    single_ms = kernel_ms(lib, handles[:1], x, yp, stream, True, n_kernel)
 
-    # end to end through the reference-facing host call
-    e2e_s = float("nan")
+    e2e = None
     if not args.skip_e2e:
-        lib_y = np.empty((M_ROWS, N_OUT), np.float32)
-        for i in range(3):
-            check(lib.needle2_sdot_linear_checked(handles[i % copies].h, x_host.ctypes.data, lib_y.ctypes.data,
-                                                  M_ROWS), lib)
-        e2e_steps = max(args.steps, 20)
+        ys_host = [np.empty((M_ROWS, N_OUT), np.float32) for _ in range(copies)]
+        yhp = (ct.c_void_p * copies)(*[a.ctypes.data for a in ys_host])
+        for _ in range(3):
+            check(lib.needle2_cq_linear_many_checked(hp, copies, x_host.ctypes.data, yhp, M_ROWS, 1), lib)
+        n_e2e = max(10, min(args.steps, 100))
         t0 = time.perf_counter()
-        for i in range(e2e_steps):
-            check(lib.needle2_sdot_linear_checked(handles[i % copies].h, x_host.ctypes.data, lib_y.ctypes.data,
-                                                  M_ROWS), lib)
-        e2e_s = (time.perf_counter() - t0) / e2e_steps
+        for _ in range(n_e2e):
+            check(lib.needle2_cq_linear_many_checked(hp, copies, x_host.ctypes.data, yhp, M_ROWS, 1), lib)
+        e2e_s = (time.perf_counter() - t0) / n_e2e
+        e2e = {"value": bytes_step / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 4 * M_ROWS * K_IN,
+               "d2h_bytes_per_step": 4 * M_ROWS * N_OUT * copies, "ms_per_step": e2e_s * 1e3,
+               "call": "needle2_cq_linear_many_checked (host buffers, synchronised)"}
 
-    # FP32 mode beside it (same weights, same copies)
-    fp32 = None if args.skip_fp32 else run_fp32_mode(lib, packed, norms, cb, x, y, copies, stream, args, dev)
+    fp32 = None
+    if not args.skip_fp32:
+        fh = [create(lib, packed, norms, cb, False) for _ in range(copies)]
+        fhp = (ct.c_void_p * copies)(*fh)
+        for _ in range(3):
+            check(lib.needle2_cq_linear_many_device(fhp, copies, x.data_ptr(), yp, M_ROWS, 0, stream.cuda_stream), lib)
+        fms = kernel_ms(lib, fh, x, yp, stream, False, n_kernel)
+        for h in fh:
+            lib.needle2_cq_destroy(h)
+        gbs = bytes_step / (fms * 1e-3) / 1e9
+        fp32 = {"kernel": f"cq_gemv_kernel<FP32,CQ4,G128,M1> fused over {copies} matrices", "kernel_ms": fms,
+                "achieved_gbs": gbs, "frac": gbs / peaks()[0]}
 
-    t = torch.tensor([elapsed_ms, kernel_ms, e2e_s], dtype=torch.float64, device=dev)
+    t = torch.tensor([elapsed_ms, fused_ms, single_ms], dtype=torch.float64, device=dev)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms, kernel_ms, e2e_s = t.tolist()
-    total_bytes = bytes_step * args.steps * world
+    elapsed_ms, fused_ms, single_ms = t.tolist()
     hbm, peak_kind = peaks()
-    achieved = bytes_step / (kernel_ms * 1e-3) / 1e9
+    achieved = bytes_step / (fused_ms * 1e-3) / 1e9
+    single_gbs = (matrix_bytes() + 4 * M_ROWS * (N_OUT + K_IN)) / (single_ms * 1e-3) / 1e9
     result = {
         "metric": "cq4_gemv_hbm_gbs",
-        "value": total_bytes / (elapsed_ms * 1e-3) / 1e9,
+        "value": bytes_step * args.steps * world / (elapsed_ms * 1e-3) / 1e9,
         "unit": "GB/s",
         "n_gpus": world,
         "steps": args.steps,
@@ -277,86 +345,28 @@ def run_native(args, rank, world, dist):
         "vs_baseline": None,
         "dtype": "i8",
         "data": "synthetic",
-        "config": {"workload": f"cq4_sdot_gemv_m{M_ROWS}_{N_OUT}x{K_IN}", "bits": BITS, "group": GROUP,
-                   "M": M_ROWS, "N": N_OUT, "K": K_IN, "mode": "sdot-int8", "weight_copies": copies,
-                   "working_set_bytes": per_copy * copies,
-                   "l2": "inputs larger than L2: distinct weight copies cycled, working set >= 4x L2",
-                   "parallelism": f"replicas{world}", "bytes_per_step": bytes_step},
+        "config": workload_config(copies, world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_source": peak_kind, "kernel": "cq_gemv_kernel<I8,4>", "kernel_ms": kernel_ms,
-                     "traffic": profiled_traffic("cq_gemv_i8")},
-        "e2e": None if args.skip_e2e else {
-            "value": bytes_step / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 4 * M_ROWS * K_IN,
-            "d2h_bytes_per_step": 4 * M_ROWS * N_OUT, "ms_per_step": e2e_s * 1e3},
+                     "peak_source": peak_kind,
+                     "kernel": f"cq_gemv_kernel<SDOT,CQ4,G128,M1> fused over {copies} matrices",
+                     "kernel_ms": fused_ms, "traffic": profiled_traffic("cq_gemv_sdot_fused")},
+        "single_matrix": {"kernel_ms": single_ms, "achieved_gbs": single_gbs, "frac": single_gbs / hbm,
+                          "note": "one 14336x4096 matrix per launch (launch and DRAM ramp overheads included)"},
+        "e2e": e2e,
         "gpu_launches": 2 * args.steps,
+        "timing": "K steps captured in one CUDA graph, replayed once between CUDA events on the launching stream",
         "clocks": clocks.summary(),
         "fp32_mode": fp32,
     }
+    for h in handles:
+        lib.needle2_sdot_destroy(h)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, sec, n, threads, kind = reference_gemv(packed, norms, cb, x_host, seconds=args.cpu_seconds)
         result["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind,
-                                  "sample": f"{n} SDOT GEMVs of the same 14336x4096 CQ4 matrix (4 host copies "
-                                            f"cycled), {sec * 1e3:.2f} ms each, ~{args.cpu_seconds:.0f} s bound; "
-                                            "x86 runs the reference's portable (non-NEON) branches"}
+                                  "sample": f"{n} reference SdotCQ GEMVs of one 14336x4096 CQ4 matrix (4 host copies "
+                                            f"cycled), {sec * 1e3:.1f} ms each, ~{args.cpu_seconds:.0f} s bound; x86 "
+                                            "runs the reference's portable (non-NEON) branches"}
     return result
-
-
-def run_fp32_mode(lib, packed, norms, cb, x, y, copies, stream, args, dev):
-    import torch
-    sp = stream.cuda_stream
-    hs = []
-    for _ in range(copies):
-        h = lib.needle2_cq_create(packed.ctypes.data, norms.ctypes.data, N_OUT, K_IN, BITS, GROUP, cb.ctypes.data)
-        if not h:
-            raise RuntimeError(lib.needle2_b200_error().decode())
-        hs.append(h)
-    try:
-        for i in range(args.warmup):
-            check(lib.needle2_cq_prepare_device(hs[i % copies], x.data_ptr(), M_ROWS, sp), lib)
-            check(lib.needle2_cq_multiply_device(hs[i % copies], y.data_ptr(), M_ROWS, sp), lib)
-        ks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ke = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        for i in range(args.steps):
-            h = hs[i % copies]
-            check(lib.needle2_cq_prepare_device(h, x.data_ptr(), M_ROWS, sp), lib)
-            ks[i].record(stream)
-            check(lib.needle2_cq_multiply_device(h, y.data_ptr(), M_ROWS, sp), lib)
-            ke[i].record(stream)
-        torch.cuda.synchronize(dev)
-        kms = float(np.mean([a.elapsed_time(b) for a, b in zip(ks, ke)]))
-    finally:
-        for h in hs:
-            lib.needle2_cq_destroy(h)
-    hbm, _ = peaks()
-    gbs = algorithmic_bytes() / (kms * 1e-3) / 1e9
-    return {"kernel": "cq_gemv_kernel<FP32,4>", "kernel_ms": kms, "achieved_gbs": gbs, "frac": gbs / hbm}
-
-
-def profiled_traffic(tag):
-    """DRAM bytes per launch recorded from an ncu capture in profiles/ (or None)."""
-    for f in sorted((ROOT / "profiles").glob(f"{tag}*.md")):
-        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
-        if m:
-            return float(m.group(1))
-    return None
-
-
-def run_reference_arm(args, rank, world):
-    if rank != 0:
-        return None
-    packed, norms, cb = weights()
-    x = activations()
-    gbs, sec, n, threads, kind = reference_gemv(packed, norms, cb, x, steps=args.steps, warmup=args.warmup)
-    return {
-        "impl": "reference", "metric": "cq4_gemv_hbm_gbs", "value": gbs, "unit": "GB/s", "n_gpus": world,
-        "steps": n, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "i8", "data": "synthetic",
-        "config": {"workload": f"cq4_sdot_gemv_m{M_ROWS}_{N_OUT}x{K_IN}", "bits": BITS, "group": GROUP, "M": M_ROWS,
-                   "N": N_OUT, "K": K_IN, "mode": "sdot-int8", "parallelism": "host cores (OpenMP rows)"},
-        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind,
-                         "sample": f"{n} steps of the reference SdotCQ GEMV over 4 host copies of the matrix"},
-        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
 
 
 def main():
@@ -367,7 +377,7 @@ def main():
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--copies", type=int, default=0, help="weight copies (default: working set >= 4x L2)")
+    ap.add_argument("--copies", type=int, default=0, help=f"matrices per step (default {COPIES})")
     ap.add_argument("--skip-fp32", action="store_true", help="omit the FP32-mode side measurement")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer end-to-end measurement")
     args = ap.parse_args()

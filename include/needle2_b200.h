@@ -78,6 +78,21 @@ int needle2_sdot_linear_checked(void *handle, const float *x, float *y, int batc
 int needle2_cq_linear_device(void *handle, const float *x, float *y, int batch, void *stream);
 int needle2_sdot_linear_device(void *handle, const float *x, float *y, int batch, void *stream);
 
+/* Several matrices against one activation batch: ys[i][batch][out_i].  Matrices
+ * with the same input geometry and codebook share one prepared activation and
+ * run as one fused launch (the fused projections of needle2/csrc/engine.cpp:560-606);
+ * others run one after another.  `sdot` selects the int8 mode (all handles
+ * must be of that kind).  Host pointers / device pointers respectively. */
+int needle2_cq_linear_many_checked(void *const *handles, int count, const float *x, float *const *ys, int batch,
+                                   int sdot);
+int needle2_cq_linear_many_device(void *const *handles, int count, const float *x, float *const *ys, int batch,
+                                  int sdot, void *stream);
+/* Fused multiply only, from the activations last prepared on handles[0]
+ * (needle2_cq_prepare_device / needle2_sdot_prepare_device); the matrices must
+ * be able to share a launch. */
+int needle2_cq_multiply_many_device(void *const *handles, int count, float *const *ys, int batch, int sdot,
+                                    void *stream);
+
 /* Two-phase device form: prepare rotates (FP32 mode) or rotates and quantises
  * (SDOT mode) x[batch][in] into the handle's device scratch; multiply then
  * writes y[batch][out] from it.  Split as SdotCQ::prepare / SdotCQ::multiply,
@@ -94,6 +109,11 @@ int needle2_sdot_multiply_device(void *handle, float *y, int batch, void *stream
  * any output pointer may be NULL.  Host pointers. */
 int needle2_sdot_debug(void *handle, const float *x, int batch, float *y, int32_t *partials, int8_t *q,
                        float *scales);
+
+/* 1 if a kernel's bounded wait on an asynchronous copy ran out since the last
+ * call (the kernel then abandons its work instead of spinning); 0 otherwise,
+ * -1 if the flag could not be read.  Reading clears it. */
+int needle2_b200_device_fault(void);
 
 /* Geometry of a handle: out, in, bits, group, padded, groups. */
 int needle2_cq_geometry(void *handle, int *geometry6);

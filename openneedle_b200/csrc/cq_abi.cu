@@ -11,6 +11,7 @@
 
 #include "../../include/needle2_b200.h"
 #include "common.cuh"
+#include "cq_gemv.cuh"
 #include "cq_kernels.cuh"
 
 namespace nb200 {
@@ -55,6 +56,7 @@ struct Matrix {
     cudaStream_t stream = nullptr;
     uint8_t *d_packed = nullptr;
     uint16_t *d_norms = nullptr;
+    uint16_t *d_norms8 = nullptr;   // padded copy when groups % 8 != 0 (int8 mode)
     Scratch<float> x, y, rot, xs;
     Scratch<int8_t> q;
     Scratch<int32_t> partials;
@@ -67,6 +69,7 @@ struct Matrix {
         x.release(); y.release(); rot.release(); xs.release(); q.release(); partials.release(); ids.release();
         if (d_packed) cudaFree(d_packed);
         if (d_norms) cudaFree(d_norms);
+        if (d_norms8) cudaFree(d_norms8);
         if (stream) cudaStreamDestroy(stream);
     }
 };
@@ -112,6 +115,25 @@ Matrix *create_matrix(const uint8_t *packed, const uint16_t *norms, int out, int
             cent[i] = (int8_t)std::min(127.f, std::max(-127.f, std::nearbyint(cb[i] / cs)));
     std::memcpy(w.ctab, cent, 16);
     w.centroid_scale = cs;
+    // Sign split of the CQ4 int8 table (any sorted codebook with eight
+    // non-positive and eight non-negative centroids): the decode then needs
+    // two byte permutes per four elements, one per sign.
+    w.split = 0;
+    w.ntab[0] = w.ntab[1] = w.ptab[0] = w.ptab[1] = 0;
+    if (bits == 4) {
+        bool ok = true;
+        uint8_t nb[8], pb[8];
+        for (int i = 0; i < 8; ++i) {
+            ok = ok && cent[i] <= 0 && cent[8 + i] >= 0;
+            nb[i] = (uint8_t)(-cent[i]);
+            pb[i] = (uint8_t)cent[8 + i];
+        }
+        if (ok) {
+            w.split = 1;
+            std::memcpy(w.ntab, nb, 8);
+            std::memcpy(w.ptab, pb, 8);
+        }
+    }
 
     cudaGetDevice(&m->device);
     const size_t pbytes = (size_t)out * w.rowbytes, nbytes = sizeof(uint16_t) * (size_t)out * w.groups;
@@ -128,6 +150,23 @@ Matrix *create_matrix(const uint8_t *packed, const uint16_t *norms, int out, int
     }
     w.packed = m->d_packed;
     w.norms = m->d_norms;
+    w.norms8 = m->d_norms;
+    if (sdot && w.groups % 8) {
+        // int8 kernels fetch the norms of eight groups at a time
+        const int g8 = (w.groups + 7) / 8 * 8;
+        std::vector<uint16_t> padded8((size_t)out * g8, 0);
+        for (int r = 0; r < out; ++r)
+            std::memcpy(&padded8[(size_t)r * g8], norms + (size_t)r * w.groups, sizeof(uint16_t) * w.groups);
+        e = cudaMalloc(&m->d_norms8, sizeof(uint16_t) * padded8.size());
+        if (e == cudaSuccess)
+            e = cudaMemcpy(m->d_norms8, padded8.data(), sizeof(uint16_t) * padded8.size(), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            set_error(std::string("CQ device upload failed: ") + cudaGetErrorString(e));
+            delete m;
+            return nullptr;
+        }
+        w.norms8 = m->d_norms8;
+    }
     return m;
 }
 
@@ -221,14 +260,159 @@ void needle2_cq_linear_lookup(void *handle, const float *x, float *y, int batch,
     needle2_cq_linear(handle, x, y, batch, threads);
 }
 
+namespace nb200 {
+namespace {
+
+// Matrices that can share one prepared activation and one fused launch.
+bool fusable(Matrix *const *ms, int count) {
+    if (count < 1) return false;
+    const CQDevice &a = ms[0]->w;
+    if (!gemv_max_rows(a.bits, a.group, a.groups, ms[0]->sdot)) return false;
+    for (int i = 0; i < count; ++i) {
+        if (!ms[i]) return false;
+        const CQDevice &w = ms[i]->w;
+        if (ms[i]->sdot != ms[0]->sdot || ms[i]->device != ms[0]->device || w.in != a.in ||
+            w.group != a.group || w.bits != a.bits || std::memcmp(w.lut, a.lut, sizeof(a.lut)) ||
+            std::memcmp(w.ctab, a.ctab, sizeof(a.ctab)) || w.centroid_scale != a.centroid_scale)
+            return false;
+    }
+    return true;
+}
+
+bool multiply_many(Matrix *const *ms, int count, float *const *ys, int batch, cudaStream_t st);
+
+// y_i[batch][out_i] = W_i x for device x / y_i: one prepare (on the first
+// matrix's scratch), then fused launches of up to kGemvMaxMats matrices.
+bool many_device(Matrix *const *ms, int count, const float *x, float *const *ys, int batch, cudaStream_t st) {
+    if (batch <= 0 || count <= 0) return true;
+    if (!fusable(ms, count)) {
+        for (int i = 0; i < count; ++i)
+            if (!run_linear_device(ms[i], x, ys[i], batch, st, nullptr)) return false;
+        return true;
+    }
+    Matrix *m0 = ms[0];
+    const CQDevice &w = m0->w;
+    const bool i8 = m0->sdot;
+    if (i8) {
+        if (!m0->q.reserve((size_t)batch * w.padded) || !m0->xs.reserve((size_t)batch * w.groups)) return false;
+        if (!launch_quantize(w, x, batch, m0->q.ptr, m0->xs.ptr, st)) return false;
+    } else {
+        if (!m0->rot.reserve((size_t)batch * w.padded)) return false;
+        if (!launch_rotate(w, x, batch, m0->rot.ptr, st)) return false;
+    }
+    m0->prepared = batch;
+    return multiply_many(ms, count, ys, batch, st);
+}
+
+// Fused launches from the activations prepared on ms[0].
+bool multiply_many(Matrix *const *ms, int count, float *const *ys, int batch, cudaStream_t st) {
+    Matrix *m0 = ms[0];
+    const CQDevice &w = m0->w;
+    const bool i8 = m0->sdot;
+    if (batch > m0->prepared) { set_error("multiply batch exceeds the prepared batch"); return false; }
+    const int cap = gemv_max_rows(w.bits, w.group, w.groups, i8);
+    for (int i0 = 0; i0 < count; i0 += kGemvMaxMats) {
+        const int n = std::min(kGemvMaxMats, count - i0);
+        for (int r0 = 0; r0 < batch; r0 += cap) {
+            GemvBatch b = single_batch(w);
+            b.nmat = n;
+            b.M = std::min(cap, batch - r0);
+            for (int j = 0; j < n; ++j) {
+                const CQDevice &wj = ms[i0 + j]->w;
+                b.mat[j].packed = wj.packed;
+                b.mat[j].norms = wj.norms;
+                b.mat[j].norms8 = wj.norms8;
+                b.mat[j].out = wj.out;
+                b.mat[j].y = ys[i0 + j] + (size_t)r0 * wj.out;
+            }
+            if (i8) {
+                b.q = m0->q.ptr + (size_t)r0 * w.padded;
+                b.xs = m0->xs.ptr + (size_t)r0 * w.groups;
+            } else {
+                b.rot = m0->rot.ptr + (size_t)r0 * w.padded;
+            }
+            if (!launch_gemv(b, i8, st)) return false;
+        }
+    }
+    return true;
+}
+
+// Host form: x[batch][in] -> ys[i][batch][out_i], synchronised.
+bool many_host(Matrix *const *ms, int count, const float *x, float *const *ys, int batch) {
+    clear_error();
+    if (count <= 0 || batch <= 0) return true;
+    for (int i = 0; i < count; ++i)
+        if (!ms[i]) { set_error("null handle"); return false; }
+    Matrix *m0 = ms[0];
+    NB_CUDA_TRY(cudaSetDevice(m0->device));
+    const cudaStream_t st = m0->stream;
+    size_t total = 0;
+    for (int i = 0; i < count; ++i) total += (size_t)batch * ms[i]->w.out;
+    if (!m0->x.reserve((size_t)batch * m0->w.in) || !m0->y.reserve(total)) return false;
+    NB_CUDA_TRY(cudaMemcpyAsync(m0->x.ptr, x, sizeof(float) * (size_t)batch * m0->w.in, cudaMemcpyHostToDevice, st));
+    std::vector<float *> dys(count);
+    size_t off = 0;
+    for (int i = 0; i < count; ++i) {
+        dys[i] = m0->y.ptr + off;
+        off += (size_t)batch * ms[i]->w.out;
+    }
+    if (!many_device(ms, count, m0->x.ptr, dys.data(), batch, st)) return false;
+    for (int i = 0; i < count; ++i)
+        NB_CUDA_TRY(cudaMemcpyAsync(ys[i], dys[i], sizeof(float) * (size_t)batch * ms[i]->w.out,
+                                    cudaMemcpyDeviceToHost, st));
+    NB_CUDA_TRY(cudaStreamSynchronize(st));
+    return true;
+}
+
+}  // namespace
+}  // namespace nb200
+
 void needle2_cq_linear_many(void *const *handles, int count, const float *x, float *const *ys, int threads,
                             int mode) {
     (void)mode;
-    nb200::clear_error();
-    for (int i = 0; i < count; ++i) {
-        if (needle2_cq_linear_checked(handles[i], x, ys[i], 1)) return;
-    }
     (void)threads;
+    std::vector<Matrix *> ms(count > 0 ? count : 0);
+    for (int i = 0; i < count; ++i) {
+        ms[i] = static_cast<Matrix *>(handles[i]);
+        if (ms[i] && ms[i]->sdot) { nb200::set_error("needle2_cq_linear_many takes FP32-mode handles"); return; }
+    }
+    nb200::many_host(ms.data(), count, x, ys, 1);
+}
+
+int needle2_cq_linear_many_checked(void *const *handles, int count, const float *x, float *const *ys, int batch,
+                                   int sdot) {
+    std::vector<Matrix *> ms(count > 0 ? count : 0);
+    for (int i = 0; i < count; ++i) {
+        ms[i] = static_cast<Matrix *>(handles[i]);
+        if (!ms[i] || ms[i]->sdot != (sdot != 0)) { nb200::set_error("null or wrong-kind handle"); return -1; }
+    }
+    return nb200::many_host(ms.data(), count, x, ys, batch) ? 0 : -1;
+}
+
+int needle2_cq_multiply_many_device(void *const *handles, int count, float *const *ys, int batch, int sdot,
+                                    void *stream) {
+    nb200::clear_error();
+    std::vector<Matrix *> ms(count > 0 ? count : 0);
+    for (int i = 0; i < count; ++i) {
+        ms[i] = static_cast<Matrix *>(handles[i]);
+        if (!ms[i] || ms[i]->sdot != (sdot != 0)) { nb200::set_error("null or wrong-kind handle"); return -1; }
+    }
+    if (count <= 0 || batch <= 0) return 0;
+    if (!nb200::fusable(ms.data(), count)) { nb200::set_error("matrices cannot share one launch"); return -1; }
+    if (cudaSetDevice(ms[0]->device) != cudaSuccess) { nb200::set_error("cudaSetDevice failed"); return -1; }
+    return nb200::multiply_many(ms.data(), count, ys, batch, static_cast<cudaStream_t>(stream)) ? 0 : -1;
+}
+
+int needle2_cq_linear_many_device(void *const *handles, int count, const float *x, float *const *ys, int batch,
+                                  int sdot, void *stream) {
+    nb200::clear_error();
+    std::vector<Matrix *> ms(count > 0 ? count : 0);
+    for (int i = 0; i < count; ++i) {
+        ms[i] = static_cast<Matrix *>(handles[i]);
+        if (!ms[i] || ms[i]->sdot != (sdot != 0)) { nb200::set_error("null or wrong-kind handle"); return -1; }
+    }
+    if (count > 0 && cudaSetDevice(ms[0]->device) != cudaSuccess) { nb200::set_error("cudaSetDevice failed"); return -1; }
+    return nb200::many_device(ms.data(), count, x, ys, batch, static_cast<cudaStream_t>(stream)) ? 0 : -1;
 }
 
 void needle2_cq_rows(void *handle, const int64_t *ids, float *y, int count) {
@@ -341,6 +525,8 @@ int needle2_sdot_prepare_device(void *h, const float *x, int batch, void *stream
 int needle2_sdot_multiply_device(void *h, float *y, int batch, void *stream) {
     return multiply_device(h, y, batch, stream, true);
 }
+
+int needle2_b200_device_fault() { return nb200::read_and_clear_gemv_fault(); }
 
 int needle2_cq_geometry(void *handle, int *g) {
     auto *m = static_cast<Matrix *>(handle);

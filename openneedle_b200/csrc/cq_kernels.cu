@@ -15,6 +15,7 @@
 
 #include "common.cuh"
 #include "cq_gemv.cuh"
+#include "sm100_async.cuh"
 #include "cq_kernels.cuh"
 
 namespace nb200 {
@@ -108,6 +109,8 @@ __global__ void __launch_bounds__(256) rotate_warp_kernel(const float *__restric
                                                           int8_t *__restrict__ q, float *__restrict__ xs,
                                                           int cq2_planes) {
     using S = WarpShape<G>;
+    pdl_launch_dependents();
+    pdl_wait();   // x may be produced by the preceding kernel in the stream
     const int groups = padded / G;
     const int lane = threadIdx.x & 31;
     const int lig = lane % S::LANES, sub = lane / S::LANES;
@@ -196,7 +199,17 @@ bool launch_rotate_impl(const CQDevice &w, const float *x, int M, float *rot, in
     auto warp_launch = [&](auto kernel, int per_warp) {
         long long warps = (items + per_warp - 1) / per_warp;
         int blocks = (int)std::min<long long>((warps + 7) / 8, 65535);
-        kernel<<<blocks, 256, 0, st>>>(x, M, w.in, w.padded, scale, rot, q, xs, cq2_planes);
+        // programmatic dependent launch: may start while the previous kernel drains
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(blocks);
+        cfg.blockDim = dim3(256);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaLaunchKernelEx(&cfg, kernel, x, M, w.in, w.padded, scale, rot, q, xs, cq2_planes);
     };
     switch (w.group) {
         case 8: warp_launch(rotate_warp_kernel<8, QUANT>, 4); break;
@@ -503,6 +516,29 @@ bool launch_quantize(const CQDevice &w, const float *x, int M, int8_t *q, float 
     return launch_rotate_impl<true>(w, x, M, nullptr, q, xs, w.bits == 2 ? 1 : 0, s);
 }
 
+GemvBatch single_batch(const CQDevice &w) {
+    GemvBatch b{};
+    b.nmat = 1;
+    b.mat[0].packed = w.packed;
+    b.mat[0].norms = w.norms;
+    b.mat[0].norms8 = w.norms8;
+    b.mat[0].out = w.out;
+    b.bits = w.bits;
+    b.group = w.group;
+    b.groups = w.groups;
+    b.rowbytes = w.rowbytes;
+    b.padded = w.padded;
+    for (int i = 0; i < 16; ++i) b.lut[i] = w.lut[i];
+    for (int i = 0; i < 4; ++i) b.ctab[i] = w.ctab[i];
+    for (int i = 0; i < 2; ++i) {
+        b.ntab[i] = w.ntab[i];
+        b.ptab[i] = w.ptab[i];
+    }
+    b.split = w.split;
+    b.cs = w.centroid_scale;
+    return b;
+}
+
 bool launch_gemv_f32(const CQDevice &w, const float *rot, int M, float *y, int ldy, cudaStream_t s) {
     if (M <= 0 || w.out <= 0) return true;
     if (!gemv_fast_path(w)) {
@@ -515,18 +551,15 @@ bool launch_gemv_f32(const CQDevice &w, const float *rot, int M, float *y, int l
         NB_CUDA_TRY(cudaGetLastError());
         return true;
     }
-    if (w.bits != 5) {
-        const int cap = gemv_v2_max_rows(w.bits, w.group, w.groups, false);
+    if (w.bits != 5 && ldy == w.out) {
+        const int cap = gemv_max_rows(w.bits, w.group, w.groups, false);
         if (cap > 0) {
             for (int m0 = 0; m0 < M; m0 += cap) {
-                GemvV2Params p{};
-                p.packed = w.packed; p.norms = w.norms; p.out = w.out; p.groups = w.groups;
-                p.rowbytes = w.rowbytes; p.padded = w.padded; p.M = std::min(cap, M - m0);
-                p.rot = rot + (size_t)m0 * w.padded;
-                p.y = y + (size_t)m0 * ldy;
-                p.ldy = ldy;
-                for (int i = 0; i < 16; ++i) p.lut[i] = w.lut[i];
-                if (!launch_gemv_v2(p, w.bits, w.group, false, s)) return false;
+                GemvBatch b = single_batch(w);
+                b.M = std::min(cap, M - m0);
+                b.rot = rot + (size_t)m0 * w.padded;
+                b.mat[0].y = y + (size_t)m0 * ldy;
+                if (!launch_gemv(b, false, s)) return false;
             }
             return true;
         }
@@ -557,6 +590,21 @@ bool launch_gemv_i8(const CQDevice &w, const int8_t *q, const float *xs, int M, 
         set_error("SDOT requires CQ2/CQ4 with group size between 64 and 131072");
         return false;
     }
+    if (ldy == w.out) {
+        const int cap = gemv_max_rows(w.bits, w.group, w.groups, true);
+        if (cap > 0) {
+            for (int m0 = 0; m0 < M; m0 += cap) {
+                GemvBatch b = single_batch(w);
+                b.M = std::min(cap, M - m0);
+                b.q = q + (size_t)m0 * w.padded;
+                b.xs = xs + (size_t)m0 * w.groups;
+                b.mat[0].y = y + (size_t)m0 * ldy;
+                b.partials = partials ? partials + (size_t)m0 * w.out * w.groups : nullptr;
+                if (!launch_gemv(b, true, s)) return false;
+            }
+            return true;
+        }
+    }
     if (!gemv_fast_path(w)) {
         uint4 ctab;
         memcpy(&ctab, w.ctab, 16);
@@ -566,25 +614,6 @@ bool launch_gemv_i8(const CQDevice &w, const int8_t *q, const float *xs, int M, 
             ctab, w.centroid_scale);
         NB_CUDA_TRY(cudaGetLastError());
         return true;
-    }
-    {
-        const int cap = gemv_v2_max_rows(w.bits, w.group, w.groups, true);
-        if (cap > 0) {
-            for (int m0 = 0; m0 < M; m0 += cap) {
-                GemvV2Params p{};
-                p.packed = w.packed; p.norms = w.norms; p.out = w.out; p.groups = w.groups;
-                p.rowbytes = w.rowbytes; p.padded = w.padded; p.M = std::min(cap, M - m0);
-                p.q = q + (size_t)m0 * w.padded;
-                p.xs = xs + (size_t)m0 * w.groups;
-                p.y = y + (size_t)m0 * ldy;
-                p.ldy = ldy;
-                p.partials = partials ? partials + (size_t)m0 * w.out * w.groups : nullptr;
-                for (int i = 0; i < 4; ++i) p.ctab[i] = w.ctab[i];
-                p.cs = w.centroid_scale;
-                if (!launch_gemv_v2(p, w.bits, w.group, true, s)) return false;
-            }
-            return true;
-        }
     }
     for (int m0 = 0; m0 < M; m0 += kGemvMaxRows) {
         GemvParams p{};

@@ -14,8 +14,11 @@ struct CQDevice {
     int out, in, bits, group, padded, groups, storage_bits, rowbytes;
     const uint8_t *packed;    // [out][rowbytes] device
     const uint16_t *norms;    // [out][groups] FP16 bits, device
+    const uint16_t *norms8;   // SDOT: norms with rows padded to a multiple of 8 groups (== norms when aligned)
     float lut[16];            // FP32 mode: value of each stored index
     uint32_t ctab[4];         // SDOT: int8 centroids, four per word
+    uint32_t ntab[2], ptab[2];   // SDOT CQ4 sign split: |c| of entries 0-7, c of entries 8-15
+    int split;                // SDOT CQ4: entries 0-7 <= 0 <= entries 8-15 (sign-split decode applies)
     float centroid_scale;     // SDOT: max|cb|/127
 };
 
@@ -33,5 +36,9 @@ bool launch_gemv_i8(const CQDevice &w, const int8_t *q, const float *xs, int M, 
 bool launch_rows(const CQDevice &w, const int64_t *ids, int count, float *y, cudaStream_t s);
 
 bool gemv_fast_path(const CQDevice &w);
+
+struct GemvBatch;
+// A one-matrix GEMV batch description of w (activations and outputs unset).
+GemvBatch single_batch(const CQDevice &w);
 
 }  // namespace nb200

@@ -55,6 +55,13 @@ def _library() -> ct.CDLL:
     for name in ("needle2_cq_multiply_device", "needle2_sdot_multiply_device"):
         getattr(lib, name).argtypes = [_p, _p, _i, _p]
         getattr(lib, name).restype = _i
+    lib.needle2_cq_linear_many_checked.argtypes = [ct.POINTER(_p), _i, _p, ct.POINTER(_p), _i, _i]
+    lib.needle2_cq_linear_many_checked.restype = _i
+    lib.needle2_cq_linear_many_device.argtypes = [ct.POINTER(_p), _i, _p, ct.POINTER(_p), _i, _i, _p]
+    lib.needle2_cq_linear_many_device.restype = _i
+    lib.needle2_cq_multiply_many_device.argtypes = [ct.POINTER(_p), _i, ct.POINTER(_p), _i, _i, _p]
+    lib.needle2_cq_multiply_many_device.restype = _i
+    lib.needle2_b200_device_fault.restype = _i
     lib.needle2_cq_linear_lookup.argtypes = [_p, _p, _p, _i, _i, _i]
     lib.needle2_cq_linear_lookup.restype = None
     lib.needle2_cq_linear_many.argtypes = [ct.POINTER(_p), _i, _p, ct.POINTER(_p), _i, _i]
@@ -283,3 +290,22 @@ def linear_many(matrices, x, threads: int = 1, lookup: int = 0):
     lib.needle2_cq_linear_many(handles, len(matrices), x.ctypes.data, ys, int(threads), int(lookup))
     _check_void("needle2_cq_linear_many")
     return outs
+
+
+def linear_many_batch(matrices, x, *, sdot: bool = False):
+    """x [batch, in] against several matrices sharing the input: returns a list of
+    [batch, out_i] arrays; one fused launch when the geometry allows it."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, matrices[0].shape[1])
+    batch = x.shape[0]
+    outs = [np.empty((batch, m.shape[0]), np.float32) for m in matrices]
+    hs = [m._sdot() if sdot else m._handle for m in matrices]
+    handles = (_p * len(hs))(*hs)
+    ys = (_p * len(outs))(*[o.ctypes.data for o in outs])
+    _check(_library().needle2_cq_linear_many_checked(handles, len(hs), x.ctypes.data, ys, batch, int(sdot)),
+           "linear_many")
+    return outs
+
+
+def device_fault() -> int:
+    """1 if a kernel's bounded wait ran out since the last call (clears the flag)."""
+    return int(_library().needle2_b200_device_fault())

@@ -141,3 +141,25 @@ def test_linear_many_matches_single(native):
     ya, yb = native.linear_many([a, b], g["x"][0])
     np.testing.assert_array_equal(ya, a.linear(g["x"][0]))
     np.testing.assert_array_equal(yb, b.linear(g["x"][0]))
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+@pytest.mark.parametrize("sdot", [False, True])
+def test_fused_many_matches_single(native, bits, sdot):
+    """Several matrices sharing one input in one fused launch give exactly the
+    single-matrix results (the per-row arithmetic does not depend on fusion)."""
+    from openneedle_b200.quantize import synthetic_matrix
+    mats = []
+    for i, (n, k) in enumerate([(1536, 512), (512, 512), (33, 512), (2048, 512)]):
+        p, nrm, cb = synthetic_matrix(n, k, bits, seed=50 + i)
+        mats.append(native.NativeCQ(p, nrm, (n, k), bits, 128, cb))
+    x = np.random.default_rng(3).normal(size=(5, 512)).astype(np.float32)
+    outs = native.linear_many_batch(mats, x, sdot=sdot)
+    for m, o in zip(mats, outs):
+        np.testing.assert_array_equal(o, m.linear_sdot(x) if sdot else m.linear(x))
+    # more matrices than one launch holds
+    many = [mats[i % 4] for i in range(37)]
+    outs = native.linear_many_batch(many, x[:1], sdot=sdot)
+    for m, o in zip(many, outs):
+        np.testing.assert_array_equal(o, m.linear_sdot(x[:1]) if sdot else m.linear(x[:1]))
+    assert native.device_fault() == 0
