@@ -78,6 +78,19 @@ int needle2_sdot_linear_checked(void *handle, const float *x, float *y, int batc
 int needle2_cq_linear_device(void *handle, const float *x, float *y, int batch, void *stream);
 int needle2_sdot_linear_device(void *handle, const float *x, float *y, int batch, void *stream);
 
+/* No counterpart in the reference.  needle2_sdot_linear_device without any
+ * device allocation, for callers that may not allocate while they run (a
+ * serving loop on memory reserved up front, code that must avoid the
+ * device-wide synchronisation of cudaMalloc/cudaFree).  Its activation scratch
+ * is one fixed array pair per device inside this library: batch * padded input
+ * width must be <= 1048576 and batch * groups <= 16384, larger batches fail
+ * with -1 and a message.  The scratch needs no initial contents.  All calls on
+ * a device share it, so two calls whose kernels may overlap (different streams,
+ * or different threads without ordering) race: serialise them.  The first call
+ * on a device looks up the scratch address; make one call outside any stream
+ * capture before capturing. */
+int needle2_sdot_linear_device_noalloc(void *handle, const float *x, float *y, int batch, void *stream);
+
 /* Several matrices against one activation batch: ys[i][batch][out_i].  Matrices
  * with the same input geometry and codebook share one prepared activation and
  * run as one fused launch (the fused projections of needle2/csrc/engine.cpp:560-606);

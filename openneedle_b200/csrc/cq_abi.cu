@@ -5,6 +5,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -536,3 +537,80 @@ int needle2_cq_geometry(void *handle, int *g) {
 }
 
 }  // extern "C"
+
+// ---- SDOT on device pointers without any device allocation -----------------
+//
+// needle2_sdot_linear_device keeps the quantised activations in scratch that
+// the handle allocates (cudaMalloc) on first use and grows with the batch.
+// Callers that may not allocate device memory while they run -- a serving
+// loop on a memory pool sized up front, code that must not trigger the
+// device-wide synchronisation cudaMalloc/cudaFree imply -- use
+// needle2_sdot_linear_device_noalloc instead: its scratch is the two
+// fixed-size arrays below, which exist once on every device that loads this
+// library.  Neither array needs initial contents: each call's quantiser
+// writes every activation byte and scale that the same call's GEMV reads.
+
+namespace nb200 {
+
+constexpr size_t kNoAllocActivationBytes = size_t(1) << 20;   // batch * padded int8 activations
+constexpr size_t kNoAllocScales = size_t(1) << 14;            // batch * groups float scales
+
+static __device__ __align__(256) int8_t g_noalloc_q[kNoAllocActivationBytes];
+static __device__ __align__(256) float g_noalloc_xs[kNoAllocScales];
+
+namespace {
+
+struct NoAllocScratch {
+    int8_t *q = nullptr;
+    float *xs = nullptr;
+};
+
+// Device addresses of the two arrays on `device`, looked up once per device.
+bool noalloc_scratch(int device, NoAllocScratch &out) {
+    static std::mutex mu;
+    static NoAllocScratch cache[64];
+    static bool ready[64] = {};
+    if (device < 0 || device >= 64) {
+        set_error("device ordinal outside the no-allocation scratch table");
+        return false;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ready[device]) {
+        void *q = nullptr, *xs = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&q, g_noalloc_q);
+        if (e == cudaSuccess) e = cudaGetSymbolAddress(&xs, g_noalloc_xs);
+        if (e != cudaSuccess || !q || !xs) {
+            set_error(std::string("no-allocation scratch lookup failed: ") + cudaGetErrorString(e));
+            return false;
+        }
+        cache[device].q = static_cast<int8_t *>(q);
+        cache[device].xs = static_cast<float *>(xs);
+        ready[device] = true;
+    }
+    out = cache[device];
+    return true;
+}
+
+}  // namespace
+}  // namespace nb200
+
+extern "C" int needle2_sdot_linear_device_noalloc(void *handle, const float *x, float *y, int batch, void *stream) {
+    nb200::clear_error();
+    auto *m = static_cast<Matrix *>(handle);
+    if (!m || !m->sdot) { nb200::set_error("null or wrong-kind handle"); return -1; }
+    if (batch < 0) { nb200::set_error("negative batch"); return -1; }
+    if (batch == 0) return 0;
+    const nb200::CQDevice &w = m->w;
+    if ((size_t)batch * w.padded > nb200::kNoAllocActivationBytes ||
+        (size_t)batch * w.groups > nb200::kNoAllocScales) {
+        nb200::set_error("batch too large for the no-allocation scratch: batch * padded input must be <= 1048576 "
+                         "and batch * groups <= 16384; use needle2_sdot_linear_device");
+        return -1;
+    }
+    if (cudaSetDevice(m->device) != cudaSuccess) { nb200::set_error("cudaSetDevice failed"); return -1; }
+    nb200::NoAllocScratch s;
+    if (!nb200::noalloc_scratch(m->device, s)) return -1;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (!nb200::launch_quantize(w, x, batch, s.q, s.xs, st)) return -1;
+    return nb200::launch_gemv_i8(w, s.q, s.xs, batch, y, w.out, nullptr, st) ? 0 : -1;
+}
