@@ -296,6 +296,14 @@ def run_native(args, rank, world, dist):
     n_kernel = max(5, min(args.steps, 40))
     fused_ms = kernel_ms(lib, handles, x, yp, stream, True, n_kernel)
     single_ms = kernel_ms(lib, handles[:1], x, yp, stream, True, n_kernel)
+    # the int8 GEMV kernels side by side (the automatic choice is the fragment-order one)
+    int8_kernels = {}
+    for kind, name in ((1, "diag_mma"), (2, "tcgen05"), (3, "frag_mma")):
+        prev = lib.needle2_b200_set_int8_gemv(kind)
+        kernel_ms(lib, handles, x, yp, stream, True, 3)
+        ms = kernel_ms(lib, handles, x, yp, stream, True, n_kernel)
+        lib.needle2_b200_set_int8_gemv(prev)
+        int8_kernels[name] = {"kernel_ms": ms, "achieved_gbs": bytes_step / (ms * 1e-3) / 1e9}
 
     e2e = None
     if not args.skip_e2e:
@@ -348,7 +356,7 @@ def run_native(args, rank, world, dist):
         "config": workload_config(copies, world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": peak_kind,
-                     "kernel": f"cq_gemv_kernel<SDOT,CQ4,G128,M1> fused over {copies} matrices",
+                     "kernel": f"cq_gemv_frag_kernel<CQ4,G128,M1,sign-split> (mma.sync s8, fragment-order weights) fused over {copies} matrices",
                      "kernel_ms": fused_ms, "traffic": profiled_traffic("cq_gemv_sdot_fused")},
         "single_matrix": {"kernel_ms": single_ms, "achieved_gbs": single_gbs, "frac": single_gbs / hbm,
                           "note": "one 14336x4096 matrix per launch (launch and DRAM ramp overheads included)"},
@@ -357,6 +365,7 @@ def run_native(args, rank, world, dist):
         "timing": "K steps captured in one CUDA graph, replayed once between CUDA events on the launching stream",
         "clocks": clocks.summary(),
         "fp32_mode": fp32,
+        "int8_kernels": int8_kernels,
     }
     for h in handles:
         lib.needle2_sdot_destroy(h)

@@ -131,6 +131,14 @@ int needle2_b200_device_fault(void);
 /* Geometry of a handle: out, in, bits, group, padded, groups. */
 int needle2_cq_geometry(void *handle, int *geometry6);
 
+/* Which kernel runs int8 (SDOT) GEMVs of up to 16 activation rows, process-wide:
+ * 0 automatic (fragment-order warp-MMA kernel where the matrix geometry allows
+ * it, the diagonal warp-MMA kernel otherwise), 1 diagonal warp MMA, 2 tcgen05
+ * tensor-core kernel, 3 fragment-order warp MMA.  All give bit-identical
+ * results; the switch exists for tests and measurements.  Returns the previous
+ * setting, or -1 for an unknown kind. */
+int needle2_b200_set_int8_gemv(int kind);
+
 /* ---- additive: batched INT8 KV cache with a shared prefix ---------------- */
 /*
  * The reference keeps one sequence per Engine and an optional per-instance

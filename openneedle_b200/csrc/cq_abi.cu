@@ -58,6 +58,10 @@ struct Matrix {
     uint8_t *d_packed = nullptr;
     uint16_t *d_norms = nullptr;
     uint16_t *d_norms8 = nullptr;   // padded copy when groups % 8 != 0 (int8 mode)
+    uint8_t *d_tiled = nullptr;     // int8 mode: tile-major weights for the tcgen05 kernel
+    uint16_t *d_normsT = nullptr;   // int8 mode: tile-major norms
+    uint8_t *d_frag = nullptr;      // int8 mode: fragment-order weights for the warp-MMA kernel
+    uint16_t *d_normsF = nullptr;   // int8 mode: fragment-order norms
     Scratch<float> x, y, rot, xs;
     Scratch<int8_t> q;
     Scratch<int32_t> partials;
@@ -71,6 +75,10 @@ struct Matrix {
         if (d_packed) cudaFree(d_packed);
         if (d_norms) cudaFree(d_norms);
         if (d_norms8) cudaFree(d_norms8);
+        if (d_tiled) cudaFree(d_tiled);
+        if (d_normsT) cudaFree(d_normsT);
+        if (d_frag) cudaFree(d_frag);
+        if (d_normsF) cudaFree(d_normsF);
         if (stream) cudaStreamDestroy(stream);
     }
 };
@@ -167,6 +175,45 @@ Matrix *create_matrix(const uint8_t *packed, const uint16_t *norms, int out, int
             return nullptr;
         }
         w.norms8 = m->d_norms8;
+    }
+    if (sdot && (bits == 2 || bits == 4) && (group == 64 || group == 128 || group == 256)) {
+        // tile-major copy for the tcgen05 kernel (zero rows pad the last tile)
+        const int gb = group * bits / 8, g8 = (w.groups + 7) / 8 * 8;
+        const size_t tiles = ((size_t)out + 127) / 128;
+        std::vector<uint8_t> tp(tiles * g8 * 128 * (size_t)gb, 0);
+        std::vector<uint16_t> tn(tiles * g8 * 128, 0);
+        for (int r = 0; r < out; ++r)
+            for (int j = 0; j < w.groups; ++j) {
+                const uint8_t *src = packed + (size_t)r * w.rowbytes + (size_t)j * gb;
+                for (int b = 0; b < gb; b += 16) std::memcpy(&tp[nb200::tiled_offset(r, j, b, gb, g8)], src + b, 16);
+                tn[((size_t)(r / 128) * g8 + j) * 128 + r % 128] = norms[(size_t)r * w.groups + j];
+            }
+        e = cudaMalloc(&m->d_tiled, tp.size());
+        if (e == cudaSuccess) e = cudaMalloc(&m->d_normsT, sizeof(uint16_t) * tn.size());
+        if (e == cudaSuccess) e = cudaMemcpy(m->d_tiled, tp.data(), tp.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(m->d_normsT, tn.data(), sizeof(uint16_t) * tn.size(), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            set_error(std::string("CQ device upload failed: ") + cudaGetErrorString(e));
+            delete m;
+            return nullptr;
+        }
+        w.tiled = m->d_tiled;
+        w.normsT = m->d_normsT;
+        // fragment-order copy, repacked on the device from the row-major upload
+        const size_t fb = nb200::frag_bytes(out, w.groups, group, bits), fnc = nb200::frag_norm_count(out, w.groups);
+        e = cudaMalloc(&m->d_frag, fb);
+        if (e == cudaSuccess) e = cudaMalloc(&m->d_normsF, sizeof(uint16_t) * fnc);
+        bool ok = e == cudaSuccess && nb200::build_frag_layout(m->d_packed, m->d_norms, out, w.groups, group, bits,
+                                                                w.rowbytes, m->d_frag, m->d_normsF, m->stream);
+        if (ok) ok = cudaStreamSynchronize(m->stream) == cudaSuccess;
+        if (!ok) {
+            if (e != cudaSuccess) set_error(std::string("CQ device upload failed: ") + cudaGetErrorString(e));
+            delete m;
+            return nullptr;
+        }
+        w.frag = m->d_frag;
+        w.normsF = m->d_normsF;
     }
     return m;
 }
@@ -323,6 +370,10 @@ bool multiply_many(Matrix *const *ms, int count, float *const *ys, int batch, cu
                 b.mat[j].packed = wj.packed;
                 b.mat[j].norms = wj.norms;
                 b.mat[j].norms8 = wj.norms8;
+                b.mat[j].tiled = wj.tiled;
+                b.mat[j].normsT = wj.normsT;
+                b.mat[j].frag = wj.frag;
+                b.mat[j].normsF = wj.normsF;
                 b.mat[j].out = wj.out;
                 b.mat[j].y = ys[i0 + j] + (size_t)r0 * wj.out;
             }
@@ -613,4 +664,15 @@ extern "C" int needle2_sdot_linear_device_noalloc(void *handle, const float *x, 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (!nb200::launch_quantize(w, x, batch, s.q, s.xs, st)) return -1;
     return nb200::launch_gemv_i8(w, s.q, s.xs, batch, y, w.out, nullptr, st) ? 0 : -1;
+}
+
+extern "C" int needle2_b200_set_int8_gemv(int kind) {
+    const int previous = nb200::int8_gemv_kernel();
+    if (kind < 0 || kind > 3) {
+        nb200::set_error("int8 GEMV kernel kind must be 0 (automatic), 1 (diagonal warp MMA), 2 (tcgen05) or "
+                         "3 (fragment-order warp MMA)");
+        return -1;
+    }
+    nb200::set_int8_gemv_kernel(kind);
+    return previous;
 }

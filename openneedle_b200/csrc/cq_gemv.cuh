@@ -13,6 +13,10 @@ struct GemvMatrix {
     const uint8_t *packed;   // [out][rowbytes]
     const uint16_t *norms;   // [out][groups] FP16 bits
     const uint16_t *norms8;  // [out][groups rounded up to 8] FP16 bits (int8 mode)
+    const uint8_t *tiled;    // int8 mode, tcgen05 layout (tiled_offset) or null
+    const uint16_t *normsT;  // int8 mode: [tile][groups rounded up to 8][128] FP16 bits, or null
+    const uint8_t *frag;     // int8 mode: fragment-order copy (build_frag_layout), or null
+    const uint16_t *normsF;  // int8 mode: norms [16-row tile][group][row g: (g, g + 8)], or null
     float *y;                // [M][out]
     int out;
 };
@@ -36,6 +40,18 @@ struct GemvBatch {
     float cs;                // SDOT: centroid scale
 };
 
+// Tile-major copy of a CQ matrix for the tcgen05 int8 GEMV: rows in tiles of
+// 128; within a tile, group by group, each row's packed bytes of the group
+// (gb = group * bits / 8) with its 16-byte chunks XOR-swizzled so that eight
+// consecutive rows reading the same chunk hit distinct shared-memory banks.
+// Byte b of row r (tile-local rl = r % 128), group j, lives at the returned offset.
+inline size_t tiled_offset(int r, int j, int b, int gb, int groups8) {
+    const int rl = r % 128, tile = r / 128;
+    const int chunks = gb / 16, rows_per_128 = gb < 128 ? 128 / gb : 1;
+    const int c = (b / 16) ^ ((rl / rows_per_128) & (chunks - 1));
+    return (((size_t)tile * groups8 + j) * 128 + rl) * gb + (size_t)c * 16 + b % 16;
+}
+
 // Activation rows one launch can take for this geometry (0: not supported).
 int gemv_max_rows(int bits, int group, int groups, bool i8);
 bool launch_gemv(const GemvBatch &b, bool i8, cudaStream_t st);
@@ -43,6 +59,26 @@ bool launch_gemv(const GemvBatch &b, bool i8, cudaStream_t st);
 // launch_gemv routes int8 batches here.
 int gemv_mma_max_rows(int bits, int group, int groups);
 bool launch_gemv_mma(const GemvBatch &b, cudaStream_t st);
+// int8 GEMV on tcgen05 (cq_gemv_tc.cu).
+int gemv_tc_max_rows(int bits, int group, int groups);
+bool launch_gemv_tc(const GemvBatch &b, cudaStream_t st);
+// int8 GEMV with weights as the mma.sync A operand (cq_gemv_frag.cu).  The
+// fragment-order copy: 16-row tiles; per tile and group one block of
+// 32 lanes x (gb / 2) bytes; lane (g, t) holds, for every 32-wide K step s,
+// the indices of rows g and g + 8 at k = 32s + 4t..4t+3 (nibbles / crumbs 0-3)
+// and 32s + 16 + 4t..4t+3 (4-7); CQ2 words carry two K steps.  normsF holds
+// per tile and group the pairs (row g, row g + 8), g = 0..7.
+size_t frag_bytes(int out, int groups, int group, int bits);
+size_t frag_norm_count(int out, int groups);
+bool build_frag_layout(const uint8_t *packed, const uint16_t *norms, int out, int groups, int group, int bits,
+                       int rowbytes, uint8_t *frag, uint16_t *normsF, cudaStream_t st);
+int gemv_frag_max_rows(int bits, int group, int groups);
+bool launch_gemv_frag(const GemvBatch &b, cudaStream_t st);
+// Which int8 GEMV kernel launch_gemv uses: 0 automatic (fragment-order warp
+// MMA where the matrices carry that copy, else tcgen05, else the diagonal warp
+// MMA), 1 diagonal warp MMA, 2 tcgen05, 3 fragment-order warp MMA.
+void set_int8_gemv_kernel(int kind);
+int int8_gemv_kernel();
 // Fault flag of kernels with bounded waits (0 when none ran out); clears it.
 int read_and_clear_gemv_fault();
 

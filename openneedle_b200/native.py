@@ -55,6 +55,8 @@ def _library() -> ct.CDLL:
     for name in ("needle2_cq_multiply_device", "needle2_sdot_multiply_device"):
         getattr(lib, name).argtypes = [_p, _p, _i, _p]
         getattr(lib, name).restype = _i
+    lib.needle2_b200_set_int8_gemv.argtypes = [_i]
+    lib.needle2_b200_set_int8_gemv.restype = _i
     lib.needle2_cq_linear_many_checked.argtypes = [ct.POINTER(_p), _i, _p, ct.POINTER(_p), _i, _i]
     lib.needle2_cq_linear_many_checked.restype = _i
     lib.needle2_cq_linear_many_device.argtypes = [ct.POINTER(_p), _i, _p, ct.POINTER(_p), _i, _i, _p]
@@ -309,3 +311,12 @@ def linear_many_batch(matrices, x, *, sdot: bool = False):
 def device_fault() -> int:
     """1 if a kernel's bounded wait ran out since the last call (clears the flag)."""
     return int(_library().needle2_b200_device_fault())
+
+
+def set_int8_gemv(kind: int) -> int:
+    """Select the int8 GEMV kernel process-wide (0 automatic, 1 diagonal warp
+    MMA, 2 tcgen05, 3 fragment-order warp MMA); returns the previous setting."""
+    prev = _library().needle2_b200_set_int8_gemv(int(kind))
+    if prev < 0:
+        raise ValueError(last_error())
+    return prev

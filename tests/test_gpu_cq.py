@@ -20,6 +20,14 @@ def native():
     return native
 
 
+@pytest.fixture(params=[1, 2, 3], ids=["diag_mma", "tcgen05", "frag_mma"])
+def int8_kernel(request, native):
+    """Run an SDOT test once per int8 GEMV kernel (both must be bit-exact)."""
+    prev = native.set_int8_gemv(request.param)
+    yield request.param
+    native.set_int8_gemv(prev)
+
+
 @pytest.mark.parametrize("bits", [2, 4])
 def test_config1_fp32_matches_golden(native, bits):
     g = golden(f"cq{bits}_2048x512.npz")
@@ -31,7 +39,7 @@ def test_config1_fp32_matches_golden(native, bits):
 
 
 @pytest.mark.parametrize("bits", [2, 4])
-def test_config2_sdot_bit_exact_against_golden(native, bits):
+def test_config2_sdot_bit_exact_against_golden(native, int8_kernel, bits):
     g = golden(f"cq{bits}_2048x512.npz")
     q = native.NativeCQ(g["packed"], g["norms"], (2048, 512), bits, 128, g["codebook"])
     for m in (1, 4, 16, 64):
@@ -74,7 +82,7 @@ def test_fp32_empty_and_shape_errors(native):
 
 @pytest.mark.parametrize("bits", [2, 4])
 @pytest.mark.parametrize("group", [64, 128, 256, 1024, 2048])
-def test_sdot_random_against_oracle(native, oracle_lib, bits, group):
+def test_sdot_random_against_oracle(native, oracle_lib, int8_kernel, bits, group):
     packed, norms, shape, cb, _ = example(bits, rows=129, dim=257, group=group)
     q = native.NativeCQ(packed, norms, shape, bits, group, cb)
     x = np.random.default_rng(315).normal(size=(5, 257)).astype(np.float32)
@@ -90,7 +98,7 @@ def test_sdot_random_against_oracle(native, oracle_lib, bits, group):
 
 
 @pytest.mark.parametrize("bits", [2, 4])
-def test_sdot_rows_independent_of_block(native, bits):
+def test_sdot_rows_independent_of_block(native, int8_kernel, bits):
     """A row's output does not depend on which other rows share the launch
     (the property of tests/test_sdot_row4.py in OpenNeedle)."""
     from openneedle_b200.quantize import codebook, quantize_matrix
@@ -108,7 +116,7 @@ def test_sdot_rows_independent_of_block(native, bits):
 
 @pytest.mark.parametrize("bits", [2, 4])
 @pytest.mark.parametrize("n,k", [(8192, 4096), (11008, 4096), (32768, 512)])
-def test_large_shapes_against_oracle(native, oracle_lib, bits, n, k):
+def test_large_shapes_against_oracle(native, oracle_lib, int8_kernel, bits, n, k):
     from openneedle_b200.quantize import synthetic_matrix
     packed, norms, cb = synthetic_matrix(n, k, bits, seed=1000 + n)
     q = native.NativeCQ(packed, norms, (n, k), bits, 128, cb)
@@ -120,7 +128,7 @@ def test_large_shapes_against_oracle(native, oracle_lib, bits, n, k):
     np.testing.assert_array_equal(y, ry)
 
 
-def test_device_entry_points_match_host(native):
+def test_device_entry_points_match_host(native, int8_kernel):
     import torch
     g = golden("cq4_2048x512.npz")
     q = native.NativeCQ(g["packed"], g["norms"], (2048, 512), 4, 128, g["codebook"])
@@ -145,7 +153,7 @@ def test_linear_many_matches_single(native):
 
 @pytest.mark.parametrize("bits", [2, 4])
 @pytest.mark.parametrize("sdot", [False, True])
-def test_fused_many_matches_single(native, bits, sdot):
+def test_fused_many_matches_single(native, int8_kernel, bits, sdot):
     """Several matrices sharing one input in one fused launch give exactly the
     single-matrix results (the per-row arithmetic does not depend on fusion)."""
     from openneedle_b200.quantize import synthetic_matrix
