@@ -29,9 +29,9 @@
 namespace nb200 {
 namespace {
 
-constexpr int kFragThreads = 384;
+constexpr int kFragThreads = 512;
 constexpr int kFragWarps = kFragThreads / 32;
-constexpr int kFragMaxSmem = 200 * 1024;
+constexpr int kFragMaxSmem = 225 * 1024;
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     uint32_t d;
@@ -76,6 +76,16 @@ __device__ __forceinline__ void dec2(uint32_t w, uint32_t t, uint32_t (&r)[4]) {
     r[3] = prmt(t, t, shr_mul<16>(o));
 }
 
+// First K step of a group: D = A x B (zero accumulator input).
+__device__ __forceinline__ void mma_s8_first(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
 __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                        uint32_t b1) {
     asm volatile(
@@ -85,32 +95,18 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, ui
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-template <int W>
-struct Words {
-    uint32_t v[W];
-};
-
-template <int W>
-__device__ __forceinline__ Words<W> load_words(const uint8_t *p) {
-    Words<W> r;
-    if constexpr (W == 2) {
-        const uint2 u = __ldg(reinterpret_cast<const uint2 *>(p));
-        r.v[0] = u.x; r.v[1] = u.y;
-    } else {
-#pragma unroll
-        for (int i = 0; i < W; i += 4) {
-            const uint4 u = __ldg(reinterpret_cast<const uint4 *>(p) + i / 4);
-            r.v[i] = u.x; r.v[i + 1] = u.y; r.v[i + 2] = u.z; r.v[i + 3] = u.w;
-        }
-    }
-    return r;
+template <int N>
+__device__ __forceinline__ void cp_async(void *dst, const void *src) {
+    const uint32_t d = smem_addr(dst);
+    if constexpr (N == 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(d), "l"(src), "n"(N) : "memory");
 }
-
-// Shared memory: activations [NB][padded + 32] (each 32-wide K step stored in
-// B-fragment order: lane t's k = 4t..4t+3, 16+4t..16+4t+3 adjacent), then the
-// scales [NB][groups].
-__host__ __device__ inline size_t frag_smem(int padded, int groups, int nb) {
-    return (size_t)nb * (padded + 32) + 4 * (size_t)nb * groups;
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 template <int BITS, int G>
@@ -118,18 +114,29 @@ struct FragGeo {
     static constexpr int KK = G / 32;                     // K steps per group
     static constexpr int LW = BITS == 4 ? 2 * KK : KK;    // 32-bit words per lane per group
     static constexpr int LB = 4 * LW;                     // bytes per lane per group
-    static constexpr int PF = (64 / (LW + 1)) < 2 ? 2 : ((64 / (LW + 1)) > 8 ? 8 : 64 / (LW + 1));
+    static constexpr int SLOT = 32 * (LB + 4);            // one ring slot: the lanes' words, then their norm pairs
+    // ring depth: about 6 KB of weights per warp (deeper rings measured no faster)
+    static constexpr int PF = 6144 / (32 * LB) < 4 ? 4 : (6144 / (32 * LB) > 16 ? 16 : 6144 / (32 * LB));
 };
 
+// Shared memory: activations [NB][padded + 32] (each 32-wide K step stored in
+// B-fragment order: lane t's k = 4t..4t+3, 16+4t..16+4t+3 adjacent), the
+// scales [NB][groups], then per warp a ring of pf slots.
+__host__ __device__ inline size_t frag_smem(int padded, int groups, int nb, int slot_bytes, int pf) {
+    const size_t head = ((size_t)nb * (padded + 32) + 4 * (size_t)nb * groups + 127) / 128 * 128;
+    return head + (size_t)kFragWarps * pf * slot_bytes;
+}
+
 // MT: exact activation rows for MT <= 4, an upper bound (rows in b.M) for 8 / 16.
-template <int BITS, int G, int MT, bool SPLIT>
+// PF: ring slots per warp.
+template <int BITS, int G, int MT, bool SPLIT, int PF>
 __global__ void __launch_bounds__(kFragThreads, 1)
     cq_gemv_frag_kernel(const __grid_constant__ GemvBatch b, const int total_tiles) {
     using Geo = FragGeo<BITS, G>;
-    constexpr int KK = Geo::KK, LW = Geo::LW, LB = Geo::LB, PF = Geo::PF;
+    constexpr int KK = Geo::KK, LW = Geo::LW, LB = Geo::LB, SLOT = Geo::SLOT;
     constexpr int NB = MT <= 8 ? 8 : 16;
     constexpr int NP = NB / 8;   // B passes per K step
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int tile_base[kGemvMaxMats + 1];
 
     const int gpr = b.groups, M = MT <= 4 ? MT : b.M;
@@ -138,6 +145,10 @@ __global__ void __launch_bounds__(kFragThreads, 1)
     const int astride = b.padded + 32;
     uint8_t *act = smem;
     float *xs_s = reinterpret_cast<float *>(smem + (size_t)NB * astride);
+    const size_t head = ((size_t)NB * astride + 4 * (size_t)NB * gpr + 127) / 128 * 128;
+    // slot s: lane l's LB bytes at s*SLOT + l*LB (each lane copies and reads its own bytes; measured faster
+    // than a bank-conflict-free chunk-major order), its norm pair at s*SLOT + 32*LB + 4*l
+    uint8_t *ring = smem + head + (size_t)warp * PF * SLOT;
 
     const int s0 = (int)((long long)total_tiles * blockIdx.x / gridDim.x);
     const int s1 = (int)((long long)total_tiles * (blockIdx.x + 1) / gridDim.x);
@@ -153,8 +164,8 @@ __global__ void __launch_bounds__(kFragThreads, 1)
     }
     __syncthreads();
 
-    // load cursor: tiles s0 + warp, s0 + warp + kFragWarps, ...; PF groups ahead
-    int ltile = s0 + warp, lj = 0, lmat = 0;
+    // load cursor: tiles s0 + warp, s0 + warp + kFragWarps, ...; one commit group per group block
+    int ltile = s0 + warp, lj = 0, lmat = 0, lslot = 0;
     const uint8_t *lw = nullptr;
     const uint32_t *ln = nullptr;
     auto lseek = [&]() {
@@ -165,13 +176,16 @@ __global__ void __launch_bounds__(kFragThreads, 1)
             ln = reinterpret_cast<const uint32_t *>(b.mat[lmat].normsF) + lt * gpr * 8 + g;
         }
     };
-    lseek();
-    Words<LW> ring[PF];
-    uint32_t nring[PF];
-    auto load_next = [&](int p) {
+    auto issue = [&]() {
         if (ltile < s1) {
-            ring[p] = load_words<LW>(lw);
-            nring[p] = __ldg(ln);
+            uint8_t *dst = ring + (size_t)lslot * SLOT;
+            if constexpr (LB >= 16) {
+#pragma unroll
+                for (int c = 0; c < LB / 16; ++c) cp_async<16>(dst + lane * LB + 16 * c, lw + 16 * c);
+            } else {
+                cp_async<LB>(dst + lane * LB, lw);
+            }
+            cp_async<4>(dst + 32 * LB + 4 * lane, ln);
             lw += 32 * LB;
             ln += 8;
             if (++lj == gpr) {
@@ -180,23 +194,37 @@ __global__ void __launch_bounds__(kFragThreads, 1)
                 lseek();
             }
         }
+        cp_async_commit();
+        lslot = lslot + 1 == PF ? 0 : lslot + 1;
     };
+    lseek();
     // the weights do not depend on the preceding kernel: start streaming them first
-#pragma unroll
-    for (int p = 0; p < PF; ++p) load_next(p);
+    for (int p = 0; p < PF - 1; ++p) issue();
 
     pdl_wait();
-    const bool cq2 = BITS == 2;
-    for (int i = tid; i < NB * b.padded; i += kFragThreads) {
-        const int n = i / b.padded, pos = i % b.padded;
-        const int c = pos >> 5, within = pos & 31, tt = within >> 3, q8 = within & 7;
-        const int e = c * 32 + (q8 < 4 ? tt * 4 + q8 : 16 + tt * 4 + (q8 - 4));   // element of this byte
-        int8_t v = 0;
+    // one thread per 32-wide K step of one activation row: the natural element
+    // words w0..w7 (w_i = elements 4i..4i+3) go out as w0 w4 w1 w5 w2 w6 w3 w7,
+    // so lane t finds k = 4t..4t+3 and 16+4t..16+4t+3 in one 8-byte load
+    for (int i = tid; i < NB * (b.padded / 32); i += kFragThreads) {
+        const int n = i / (b.padded / 32), c = i % (b.padded / 32);
+        uint32_t w[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
         if (n < M) {
-            const int src = cq2 ? ((e & ~15) | ((e & 1) ? 8 + ((e & 15) >> 1) : ((e & 15) >> 1))) : e;
-            v = b.q[(size_t)n * b.padded + src];
+            const uint4 *src = reinterpret_cast<const uint4 *>(b.q + (size_t)n * b.padded + (size_t)c * 32);
+            const uint4 u0 = src[0], u1 = src[1];
+            if (BITS == 4) {
+                w[0] = u0.x; w[1] = u0.y; w[2] = u0.z; w[3] = u0.w;
+                w[4] = u1.x; w[5] = u1.y; w[6] = u1.z; w[7] = u1.w;
+            } else {
+                // CQ2 activations are stored per 16 elements as evens then odds
+                w[0] = prmt(u0.x, u0.z, 0x5140u); w[1] = prmt(u0.x, u0.z, 0x7362u);
+                w[2] = prmt(u0.y, u0.w, 0x5140u); w[3] = prmt(u0.y, u0.w, 0x7362u);
+                w[4] = prmt(u1.x, u1.z, 0x5140u); w[5] = prmt(u1.x, u1.z, 0x7362u);
+                w[6] = prmt(u1.y, u1.w, 0x5140u); w[7] = prmt(u1.y, u1.w, 0x7362u);
+            }
         }
-        act[(size_t)n * astride + pos] = (uint8_t)v;
+        uint4 *dst = reinterpret_cast<uint4 *>(act + (size_t)n * astride + (size_t)c * 32);
+        dst[0] = make_uint4(w[0], w[4], w[1], w[5]);
+        dst[1] = make_uint4(w[2], w[6], w[3], w[7]);
     }
     for (int i = tid; i < NB * gpr; i += kFragThreads) xs_s[i] = i < M * gpr ? b.xs[i] : 0.f;
     __syncthreads();
@@ -206,106 +234,120 @@ __global__ void __launch_bounds__(kFragThreads, 1)
     const float cs = b.cs;
 
     // consume cursor
-    int ctile = s0 + warp, cj = 0, cmat = 0;
+    int ctile = s0 + warp, cj = 0, cmat = 0, cslot = 0;
     while (cmat + 1 < b.nmat && ctile >= tile_base[cmat + 1]) ++cmat;
+    int row0 = (ctile - tile_base[cmat]) * 16;
     float acc[NP][4];
 #pragma unroll
     for (int q = 0; q < NP; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
     const uint8_t *abase = act + (size_t)g * astride + t * 8;
 
     while (ctile < s1) {
+        issue();                        // the group PF - 1 ahead (its slot was consumed last iteration)
+        cp_async_wait<PF - 1>();        // this group's block has landed
+        const uint8_t *slot = ring + (size_t)cslot * SLOT;
+        cslot = cslot + 1 == PF ? 0 : cslot + 1;
+        uint32_t wv[LW];
+        if constexpr (LB >= 16) {
 #pragma unroll
-        for (int p = 0; p < PF; ++p) {
-            if (ctile >= s1) break;
-            const Words<LW> wv = ring[p];
-            const uint32_t nv = nring[p];
-            load_next(p);
-            int cp[NP][4], cn[SPLIT ? NP : 1][4];
-#pragma unroll
-            for (int q = 0; q < NP; ++q) {
-                cp[q][0] = cp[q][1] = cp[q][2] = cp[q][3] = 0;
-                if (SPLIT) cn[q][0] = cn[q][1] = cn[q][2] = cn[q][3] = 0;
+            for (int c = 0; c < LB / 16; ++c) {
+                const uint4 u = *reinterpret_cast<const uint4 *>(slot + lane * LB + 16 * c);
+                wv[4 * c] = u.x; wv[4 * c + 1] = u.y; wv[4 * c + 2] = u.z; wv[4 * c + 3] = u.w;
             }
-            const uint8_t *ab = abase + (size_t)cj * KK * 32;
-            if constexpr (BITS == 4) {
+        } else {
+            const uint2 u = *reinterpret_cast<const uint2 *>(slot + lane * LB);
+            wv[0] = u.x; wv[1] = u.y;
+        }
+        const uint32_t nv = *reinterpret_cast<const uint32_t *>(slot + 32 * LB + 4 * lane);
+        int cp[NP][4], cn[SPLIT ? NP : 1][4];
+        const uint8_t *ab = abase + (size_t)cj * KK * 32;
+        if constexpr (BITS == 4) {
 #pragma unroll
-                for (int s = 0; s < KK; ++s) {
-                    uint32_t a0, a1, a2, a3, n0 = 0, n1 = 0, n2 = 0, n3 = 0;
-                    if constexpr (SPLIT) {
-                        dec4_split(wv.v[2 * s], ntab, ptab, n0, n2, a0, a2);
-                        dec4_split(wv.v[2 * s + 1], ntab, ptab, n1, n3, a1, a3);
+            for (int s = 0; s < KK; ++s) {
+                uint32_t a0, a1, a2, a3, n0 = 0, n1 = 0, n2 = 0, n3 = 0;
+                if constexpr (SPLIT) {
+                    dec4_split(wv[2 * s], ntab, ptab, n0, n2, a0, a2);
+                    dec4_split(wv[2 * s + 1], ntab, ptab, n1, n3, a1, a3);
+                } else {
+                    dec4(wv[2 * s], ctab, a0, a2);
+                    dec4(wv[2 * s + 1], ctab, a1, a3);
+                }
+#pragma unroll
+                for (int q = 0; q < NP; ++q) {
+                    const uint2 bx = *reinterpret_cast<const uint2 *>(ab + (size_t)q * 8 * astride + s * 32);
+                    if (s == 0) {
+                        mma_s8_first(cp[q], a0, a1, a2, a3, bx.x, bx.y);
+                        if constexpr (SPLIT) mma_s8_first(cn[q], n0, n1, n2, n3, bx.x, bx.y);
                     } else {
-                        dec4(wv.v[2 * s], ctab, a0, a2);
-                        dec4(wv.v[2 * s + 1], ctab, a1, a3);
-                    }
-#pragma unroll
-                    for (int q = 0; q < NP; ++q) {
-                        const uint2 bx = *reinterpret_cast<const uint2 *>(ab + (size_t)q * 8 * astride + s * 32);
                         mma_s8(cp[q], a0, a1, a2, a3, bx.x, bx.y);
                         if constexpr (SPLIT) mma_s8(cn[q], n0, n1, n2, n3, bx.x, bx.y);
                     }
                 }
-            } else {
+            }
+        } else {
 #pragma unroll
-                for (int pp = 0; pp < KK / 2; ++pp) {
-                    uint32_t r0[4], r1[4];
-                    dec2(wv.v[2 * pp], ctab[0], r0);
-                    dec2(wv.v[2 * pp + 1], ctab[0], r1);
+            for (int pp = 0; pp < KK / 2; ++pp) {
+                uint32_t r0[4], r1[4];
+                dec2(wv[2 * pp], ctab[0], r0);
+                dec2(wv[2 * pp + 1], ctab[0], r1);
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int s = 2 * pp + h;
+                for (int h = 0; h < 2; ++h) {
+                    const int s = 2 * pp + h;
 #pragma unroll
-                        for (int q = 0; q < NP; ++q) {
-                            const uint2 bx = *reinterpret_cast<const uint2 *>(ab + (size_t)q * 8 * astride + s * 32);
+                    for (int q = 0; q < NP; ++q) {
+                        const uint2 bx = *reinterpret_cast<const uint2 *>(ab + (size_t)q * 8 * astride + s * 32);
+                        if (s == 0)
+                            mma_s8_first(cp[q], r0[2 * h], r1[2 * h], r0[2 * h + 1], r1[2 * h + 1], bx.x, bx.y);
+                        else
                             mma_s8(cp[q], r0[2 * h], r1[2 * h], r0[2 * h + 1], r1[2 * h + 1], bx.x, bx.y);
-                        }
                     }
                 }
             }
-            // epilogue of group cj: rows g (c0, c1) and g + 8 (c2, c3), activations 2t, 2t + 1 (+8 per pass)
+        }
+        // epilogue of group cj: rows g (c0, c1) and g + 8 (c2, c3), activations 2t, 2t + 1 (+8 per pass)
+        const float nsa = __fmul_rn(half_bits_to_float((uint16_t)(nv & 0xffffu)), cs);
+        const float nsb = __fmul_rn(half_bits_to_float((uint16_t)(nv >> 16)), cs);
+#pragma unroll
+        for (int q = 0; q < NP; ++q) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int a = 8 * q + 2 * t + (e & 1);
+                if (MT <= 4 ? a < MT : a < M) {
+                    int d = cp[q][e];
+                    if constexpr (SPLIT) d -= cn[q][e];
+                    const float ns = e < 2 ? nsa : nsb;
+                    acc[q][e] = __fadd_rn(acc[q][e], __fmul_rn(__fmul_rn(__int2float_rn(d), ns), xs_s[a * gpr + cj]));
+                    if (b.partials) {
+                        const int row = row0 + g + (e < 2 ? 0 : 8);
+                        if (row < b.mat[cmat].out) b.partials[((size_t)a * b.mat[cmat].out + row) * gpr + cj] = d;
+                    }
+                }
+            }
+        }
+        if (++cj == gpr) {
             const GemvMatrix &mat = b.mat[cmat];
-            const float nsa = __fmul_rn(half_bits_to_float((uint16_t)(nv & 0xffffu)), cs);
-            const float nsb = __fmul_rn(half_bits_to_float((uint16_t)(nv >> 16)), cs);
-            const int row0 = (ctile - tile_base[cmat]) * 16;
 #pragma unroll
             for (int q = 0; q < NP; ++q) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int a = 8 * q + 2 * t + (e & 1);
-                    if (MT <= 4 ? a < MT : a < M) {
-                        int d = cp[q][e];
-                        if constexpr (SPLIT) d -= cn[q][e];
-                        const float ns = e < 2 ? nsa : nsb;
-                        acc[q][e] = __fadd_rn(acc[q][e], __fmul_rn(__fmul_rn(__int2float_rn(d), ns), xs_s[a * gpr + cj]));
-                        if (b.partials) {
-                            const int row = row0 + g + (e < 2 ? 0 : 8);
-                            if (row < mat.out) b.partials[((size_t)a * mat.out + row) * gpr + cj] = d;
-                        }
-                    }
+                    const int row = row0 + g + (e < 2 ? 0 : 8);
+                    if ((MT <= 4 ? a < MT : a < M) && row < mat.out) mat.y[(size_t)a * mat.out + row] = acc[q][e];
+                    acc[q][e] = 0.f;
                 }
             }
-            if (++cj == gpr) {
-#pragma unroll
-                for (int q = 0; q < NP; ++q) {
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int a = 8 * q + 2 * t + (e & 1);
-                        const int row = row0 + g + (e < 2 ? 0 : 8);
-                        if ((MT <= 4 ? a < MT : a < M) && row < mat.out) mat.y[(size_t)a * mat.out + row] = acc[q][e];
-                        acc[q][e] = 0.f;
-                    }
-                }
-                cj = 0;
-                ctile += kFragWarps;
-                while (cmat + 1 < b.nmat && ctile >= tile_base[cmat + 1]) ++cmat;
-            }
+            cj = 0;
+            ctile += kFragWarps;
+            while (cmat + 1 < b.nmat && ctile >= tile_base[cmat + 1]) ++cmat;
+            row0 = (ctile - tile_base[cmat]) * 16;
         }
     }
+    cp_async_wait<0>();
 }
 
-template <int BITS, int G, int MT, bool SPLIT>
-bool launch_frag(const GemvBatch &b, size_t smem, cudaStream_t st) {
-    auto kernel = cq_gemv_frag_kernel<BITS, G, MT, SPLIT>;
+template <int BITS, int G, int MT, bool SPLIT, int PF>
+bool launch_frag_pf(const GemvBatch &b, size_t smem, cudaStream_t st) {
+    auto kernel = cq_gemv_frag_kernel<BITS, G, MT, SPLIT, PF>;
     static bool configured[64] = {};
     static int sms[64] = {};
     int dev = 0;
@@ -337,20 +379,37 @@ bool launch_frag(const GemvBatch &b, size_t smem, cudaStream_t st) {
     return true;
 }
 
+// Full ring depth when it fits the shared memory, else half.
+template <int BITS, int G, int MT, bool SPLIT>
+bool launch_frag(const GemvBatch &b, cudaStream_t st) {
+    using Geo = FragGeo<BITS, G>;
+    const int nb = MT <= 8 ? 8 : 16;
+    const size_t full = frag_smem(b.padded, b.groups, nb, Geo::SLOT, Geo::PF);
+    if (full <= (size_t)kFragMaxSmem) return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF>(b, full, st);
+    return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF / 2>(
+        b, frag_smem(b.padded, b.groups, nb, Geo::SLOT, Geo::PF / 2), st);
+}
+
 template <int BITS, int G, bool SPLIT>
-bool launch_frag_m(const GemvBatch &b, size_t smem, cudaStream_t st) {
+bool launch_frag_m(const GemvBatch &b, cudaStream_t st) {
     switch (b.M) {
-        case 1: return launch_frag<BITS, G, 1, SPLIT>(b, smem, st);
-        case 2: return launch_frag<BITS, G, 2, SPLIT>(b, smem, st);
-        case 3: return launch_frag<BITS, G, 3, SPLIT>(b, smem, st);
-        case 4: return launch_frag<BITS, G, 4, SPLIT>(b, smem, st);
-        default: return b.M <= 8 ? launch_frag<BITS, G, 8, SPLIT>(b, smem, st) : launch_frag<BITS, G, 16, SPLIT>(b, smem, st);
+        case 1: return launch_frag<BITS, G, 1, SPLIT>(b, st);
+        case 2: return launch_frag<BITS, G, 2, SPLIT>(b, st);
+        case 3: return launch_frag<BITS, G, 3, SPLIT>(b, st);
+        case 4: return launch_frag<BITS, G, 4, SPLIT>(b, st);
+        default: return b.M <= 8 ? launch_frag<BITS, G, 8, SPLIT>(b, st) : launch_frag<BITS, G, 16, SPLIT>(b, st);
     }
 }
 
 template <int G>
-bool launch_frag_cq4(const GemvBatch &b, size_t smem, cudaStream_t st) {
-    return b.split ? launch_frag_m<4, G, true>(b, smem, st) : launch_frag_m<4, G, false>(b, smem, st);
+bool launch_frag_cq4(const GemvBatch &b, cudaStream_t st) {
+    return b.split ? launch_frag_m<4, G, true>(b, st) : launch_frag_m<4, G, false>(b, st);
+}
+
+int slot_bytes_of(int bits, int group) { return 32 * (group * bits / 16 + 4); }
+int ring_depth_of(int bits, int group) {
+    const int lb = group * bits / 16, pf = 6144 / (32 * lb);
+    return pf < 4 ? 4 : (pf > 16 ? 16 : pf);
 }
 
 // One thread per 32-bit word of the fragment-order copy (see frag layout in
@@ -419,7 +478,9 @@ bool build_frag_layout(const uint8_t *packed, const uint16_t *norms, int out, in
 int gemv_frag_max_rows(int bits, int group, int groups) {
     if ((bits != 2 && bits != 4) || (group != 64 && group != 128 && group != 256) || groups < 1) return 0;
     for (int m : {16, 8})
-        if (frag_smem(group * groups, groups, m <= 8 ? 8 : 16) <= (size_t)kFragMaxSmem) return m;
+        if (frag_smem(group * groups, groups, m <= 8 ? 8 : 16, slot_bytes_of(bits, group), ring_depth_of(bits, group) / 2) <=
+            (size_t)kFragMaxSmem)
+            return m;
     return 0;
 }
 
@@ -434,15 +495,14 @@ bool launch_gemv_frag(const GemvBatch &b, cudaStream_t st) {
             set_error("int8 GEMV launch without the fragment-order weight layout");
             return false;
         }
-    const size_t smem = frag_smem(b.padded, b.groups, b.M <= 8 ? 8 : 16);
     if (b.bits == 4) {
-        if (b.group == 64) return launch_frag_cq4<64>(b, smem, st);
-        if (b.group == 128) return launch_frag_cq4<128>(b, smem, st);
-        return launch_frag_cq4<256>(b, smem, st);
+        if (b.group == 64) return launch_frag_cq4<64>(b, st);
+        if (b.group == 128) return launch_frag_cq4<128>(b, st);
+        return launch_frag_cq4<256>(b, st);
     }
-    if (b.group == 64) return launch_frag_m<2, 64, false>(b, smem, st);
-    if (b.group == 128) return launch_frag_m<2, 128, false>(b, smem, st);
-    return launch_frag_m<2, 256, false>(b, smem, st);
+    if (b.group == 64) return launch_frag_m<2, 64, false>(b, st);
+    if (b.group == 128) return launch_frag_m<2, 128, false>(b, st);
+    return launch_frag_m<2, 256, false>(b, st);
 }
 
 }  // namespace nb200
