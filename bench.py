@@ -300,8 +300,13 @@ def run_native(args, rank, world, dist):
     int8_kernels = {}
     for kind, name in ((1, "diag_mma"), (2, "tcgen05"), (3, "frag_mma")):
         prev = lib.needle2_b200_set_int8_gemv(kind)
-        kernel_ms(lib, handles, x, yp, stream, True, 3)
-        ms = kernel_ms(lib, handles, x, yp, stream, True, n_kernel)
+        # the tcgen05 kernel reads a tile-major copy that handles build only while it is selected
+        hs = [create(lib, packed, norms, cb, True) for _ in range(copies)] if kind == 2 else handles
+        kernel_ms(lib, hs, x, yp, stream, True, 3)
+        ms = kernel_ms(lib, hs, x, yp, stream, True, n_kernel)
+        if kind == 2:
+            for h in hs:
+                lib.needle2_sdot_destroy(h)
         lib.needle2_b200_set_int8_gemv(prev)
         int8_kernels[name] = {"kernel_ms": ms, "achieved_gbs": bytes_step / (ms * 1e-3) / 1e9}
 
@@ -357,7 +362,7 @@ def run_native(args, rank, world, dist):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": peak_kind,
                      "kernel": f"cq_gemv_frag_kernel<CQ4,G128,M1,sign-split> (mma.sync s8, fragment-order weights) fused over {copies} matrices",
-                     "kernel_ms": fused_ms, "traffic": profiled_traffic("cq_gemv_sdot_fused")},
+                     "kernel_ms": fused_ms, "traffic": profiled_traffic("cq_gemv_frag_sdot_fused")},
         "single_matrix": {"kernel_ms": single_ms, "achieved_gbs": single_gbs, "frac": single_gbs / hbm,
                           "note": "one 14336x4096 matrix per launch (launch and DRAM ramp overheads included)"},
         "e2e": e2e,

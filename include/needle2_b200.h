@@ -135,8 +135,10 @@ int needle2_cq_geometry(void *handle, int *geometry6);
  * 0 automatic (fragment-order warp-MMA kernel where the matrix geometry allows
  * it, the diagonal warp-MMA kernel otherwise), 1 diagonal warp MMA, 2 tcgen05
  * tensor-core kernel, 3 fragment-order warp MMA.  All give bit-identical
- * results; the switch exists for tests and measurements.  Returns the previous
- * setting, or -1 for an unknown kind. */
+ * results; the switch exists for tests and measurements.  The tcgen05 kernel
+ * reads a tile-major weight copy that SDOT handles only build while kind 2 is
+ * selected, so select it before creating the handles it should run on.
+ * Returns the previous setting, or -1 for an unknown kind. */
 int needle2_b200_set_int8_gemv(int kind);
 
 /* ---- additive: batched INT8 KV cache with a shared prefix ---------------- */

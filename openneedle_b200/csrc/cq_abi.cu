@@ -177,29 +177,32 @@ Matrix *create_matrix(const uint8_t *packed, const uint16_t *norms, int out, int
         w.norms8 = m->d_norms8;
     }
     if (sdot && (bits == 2 || bits == 4) && (group == 64 || group == 128 || group == 256)) {
-        // tile-major copy for the tcgen05 kernel (zero rows pad the last tile)
-        const int gb = group * bits / 8, g8 = (w.groups + 7) / 8 * 8;
-        const size_t tiles = ((size_t)out + 127) / 128;
-        std::vector<uint8_t> tp(tiles * g8 * 128 * (size_t)gb, 0);
-        std::vector<uint16_t> tn(tiles * g8 * 128, 0);
-        for (int r = 0; r < out; ++r)
-            for (int j = 0; j < w.groups; ++j) {
-                const uint8_t *src = packed + (size_t)r * w.rowbytes + (size_t)j * gb;
-                for (int b = 0; b < gb; b += 16) std::memcpy(&tp[nb200::tiled_offset(r, j, b, gb, g8)], src + b, 16);
-                tn[((size_t)(r / 128) * g8 + j) * 128 + r % 128] = norms[(size_t)r * w.groups + j];
+        if (nb200::int8_gemv_kernel() == 2) {
+            // tile-major copy for the tcgen05 kernel (zero rows pad the last tile); made
+            // only while that kernel is selected, since the default kernel does not read it
+            const int gb = group * bits / 8, g8 = (w.groups + 7) / 8 * 8;
+            const size_t tiles = ((size_t)out + 127) / 128;
+            std::vector<uint8_t> tp(tiles * g8 * 128 * (size_t)gb, 0);
+            std::vector<uint16_t> tn(tiles * g8 * 128, 0);
+            for (int r = 0; r < out; ++r)
+                for (int j = 0; j < w.groups; ++j) {
+                    const uint8_t *src = packed + (size_t)r * w.rowbytes + (size_t)j * gb;
+                    for (int b = 0; b < gb; b += 16) std::memcpy(&tp[nb200::tiled_offset(r, j, b, gb, g8)], src + b, 16);
+                    tn[((size_t)(r / 128) * g8 + j) * 128 + r % 128] = norms[(size_t)r * w.groups + j];
+                }
+            e = cudaMalloc(&m->d_tiled, tp.size());
+            if (e == cudaSuccess) e = cudaMalloc(&m->d_normsT, sizeof(uint16_t) * tn.size());
+            if (e == cudaSuccess) e = cudaMemcpy(m->d_tiled, tp.data(), tp.size(), cudaMemcpyHostToDevice);
+            if (e == cudaSuccess)
+                e = cudaMemcpy(m->d_normsT, tn.data(), sizeof(uint16_t) * tn.size(), cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) {
+                set_error(std::string("CQ device upload failed: ") + cudaGetErrorString(e));
+                delete m;
+                return nullptr;
             }
-        e = cudaMalloc(&m->d_tiled, tp.size());
-        if (e == cudaSuccess) e = cudaMalloc(&m->d_normsT, sizeof(uint16_t) * tn.size());
-        if (e == cudaSuccess) e = cudaMemcpy(m->d_tiled, tp.data(), tp.size(), cudaMemcpyHostToDevice);
-        if (e == cudaSuccess)
-            e = cudaMemcpy(m->d_normsT, tn.data(), sizeof(uint16_t) * tn.size(), cudaMemcpyHostToDevice);
-        if (e != cudaSuccess) {
-            set_error(std::string("CQ device upload failed: ") + cudaGetErrorString(e));
-            delete m;
-            return nullptr;
+            w.tiled = m->d_tiled;
+            w.normsT = m->d_normsT;
         }
-        w.tiled = m->d_tiled;
-        w.normsT = m->d_normsT;
         // fragment-order copy, repacked on the device from the row-major upload
         const size_t fb = nb200::frag_bytes(out, w.groups, group, bits), fnc = nb200::frag_norm_count(out, w.groups);
         e = cudaMalloc(&m->d_frag, fb);
