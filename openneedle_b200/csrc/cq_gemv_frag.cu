@@ -29,8 +29,6 @@
 namespace nb200 {
 namespace {
 
-constexpr int kFragThreads = 512;
-constexpr int kFragWarps = kFragThreads / 32;
 constexpr int kFragMaxSmem = 225 * 1024;
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -122,16 +120,18 @@ struct FragGeo {
 // Shared memory: activations [NB][padded + 32] (each 32-wide K step stored in
 // B-fragment order: lane t's k = 4t..4t+3, 16+4t..16+4t+3 adjacent), the
 // scales [NB][groups], then per warp a ring of pf slots.
-__host__ __device__ inline size_t frag_smem(int padded, int groups, int nb, int slot_bytes, int pf) {
+__host__ __device__ inline size_t frag_smem(int padded, int groups, int nb, int slot_bytes, int pf, int warps) {
     const size_t head = ((size_t)nb * (padded + 32) + 4 * (size_t)nb * groups + 127) / 128 * 128;
-    return head + (size_t)kFragWarps * pf * slot_bytes;
+    return head + (size_t)warps * pf * slot_bytes;
 }
 
 // MT: exact activation rows for MT <= 4, an upper bound (rows in b.M) for 8 / 16.
-// PF: ring slots per warp.
-template <int BITS, int G, int MT, bool SPLIT, int PF>
-__global__ void __launch_bounds__(kFragThreads, 1)
+// PF: ring slots per warp.  NT: threads per CTA.  DBG: also write the int32
+// group dots to b.partials.
+template <int BITS, int G, int MT, bool SPLIT, int PF, int NT, bool DBG>
+__global__ void __launch_bounds__(NT, 1)
     cq_gemv_frag_kernel(const __grid_constant__ GemvBatch b, const int total_tiles) {
+    constexpr int kFragThreads = NT, kFragWarps = NT / 32;
     using Geo = FragGeo<BITS, G>;
     constexpr int KK = Geo::KK, LW = Geo::LW, LB = Geo::LB, SLOT = Geo::SLOT;
     constexpr int NB = MT <= 8 ? 8 : 16;
@@ -233,121 +233,115 @@ __global__ void __launch_bounds__(kFragThreads, 1)
     const uint32_t ntab[2] = {b.ntab[0], b.ntab[1]}, ptab[2] = {b.ptab[0], b.ptab[1]};
     const float cs = b.cs;
 
-    // consume cursor
-    int ctile = s0 + warp, cj = 0, cmat = 0, cslot = 0;
-    while (cmat + 1 < b.nmat && ctile >= tile_base[cmat + 1]) ++cmat;
-    int row0 = (ctile - tile_base[cmat]) * 16;
-    float acc[NP][4];
-#pragma unroll
-    for (int q = 0; q < NP; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+    // consume side: the warp's tiles in order, each group by group
     const uint8_t *abase = act + (size_t)g * astride + t * 8;
-
-    while (ctile < s1) {
-        issue();                        // the group PF - 1 ahead (its slot was consumed last iteration)
-        cp_async_wait<PF - 1>();        // this group's block has landed
-        const uint8_t *slot = ring + (size_t)cslot * SLOT;
-        cslot = cslot + 1 == PF ? 0 : cslot + 1;
-        uint32_t wv[LW];
-        if constexpr (LB >= 16) {
+    int cslot = 0, cmat = 0;
+    for (int ctile = s0 + warp; ctile < s1; ctile += kFragWarps) {
+        while (cmat + 1 < b.nmat && ctile >= tile_base[cmat + 1]) ++cmat;
+        const int row0 = (ctile - tile_base[cmat]) * 16;
+        float acc[NP][4];
 #pragma unroll
-            for (int c = 0; c < LB / 16; ++c) {
-                const uint4 u = *reinterpret_cast<const uint4 *>(slot + lane * LB + 16 * c);
-                wv[4 * c] = u.x; wv[4 * c + 1] = u.y; wv[4 * c + 2] = u.z; wv[4 * c + 3] = u.w;
-            }
-        } else {
-            const uint2 u = *reinterpret_cast<const uint2 *>(slot + lane * LB);
-            wv[0] = u.x; wv[1] = u.y;
-        }
-        const uint32_t nv = *reinterpret_cast<const uint32_t *>(slot + 32 * LB + 4 * lane);
-        int cp[NP][4], cn[SPLIT ? NP : 1][4];
-        const uint8_t *ab = abase + (size_t)cj * KK * 32;
-        if constexpr (BITS == 4) {
-#pragma unroll
-            for (int s = 0; s < KK; ++s) {
-                uint32_t a0, a1, a2, a3, n0 = 0, n1 = 0, n2 = 0, n3 = 0;
-                if constexpr (SPLIT) {
-                    dec4_split(wv[2 * s], ntab, ptab, n0, n2, a0, a2);
-                    dec4_split(wv[2 * s + 1], ntab, ptab, n1, n3, a1, a3);
-                } else {
-                    dec4(wv[2 * s], ctab, a0, a2);
-                    dec4(wv[2 * s + 1], ctab, a1, a3);
+        for (int q = 0; q < NP; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+        const uint8_t *ab = abase;
+        for (int cj = 0; cj < gpr; ++cj, ab += KK * 32) {
+            issue();                        // the group PF - 1 ahead (its slot was consumed last iteration)
+            cp_async_wait<PF - 1>();        // this group's block has landed
+            const uint8_t *slot = ring + (size_t)cslot * SLOT;
+            cslot = cslot + 1 == PF ? 0 : cslot + 1;
+            uint32_t wv[LW];
+            if constexpr (LB >= 16) {
+    #pragma unroll
+                for (int c = 0; c < LB / 16; ++c) {
+                    const uint4 u = *reinterpret_cast<const uint4 *>(slot + lane * LB + 16 * c);
+                    wv[4 * c] = u.x; wv[4 * c + 1] = u.y; wv[4 * c + 2] = u.z; wv[4 * c + 3] = u.w;
                 }
-#pragma unroll
-                for (int q = 0; q < NP; ++q) {
-                    const uint2 bx = *reinterpret_cast<const uint2 *>(ab + (size_t)q * 8 * astride + s * 32);
-                    if (s == 0) {
-                        mma_s8_first(cp[q], a0, a1, a2, a3, bx.x, bx.y);
-                        if constexpr (SPLIT) mma_s8_first(cn[q], n0, n1, n2, n3, bx.x, bx.y);
+            } else {
+                const uint2 u = *reinterpret_cast<const uint2 *>(slot + lane * LB);
+                wv[0] = u.x; wv[1] = u.y;
+            }
+            const uint32_t nv = *reinterpret_cast<const uint32_t *>(slot + 32 * LB + 4 * lane);
+            int cp[NP][4], cn[SPLIT ? NP : 1][4];
+            if constexpr (BITS == 4) {
+    #pragma unroll
+                for (int s = 0; s < KK; ++s) {
+                    uint32_t a0, a1, a2, a3, n0 = 0, n1 = 0, n2 = 0, n3 = 0;
+                    if constexpr (SPLIT) {
+                        dec4_split(wv[2 * s], ntab, ptab, n0, n2, a0, a2);
+                        dec4_split(wv[2 * s + 1], ntab, ptab, n1, n3, a1, a3);
                     } else {
-                        mma_s8(cp[q], a0, a1, a2, a3, bx.x, bx.y);
-                        if constexpr (SPLIT) mma_s8(cn[q], n0, n1, n2, n3, bx.x, bx.y);
+                        dec4(wv[2 * s], ctab, a0, a2);
+                        dec4(wv[2 * s + 1], ctab, a1, a3);
                     }
-                }
-            }
-        } else {
-#pragma unroll
-            for (int pp = 0; pp < KK / 2; ++pp) {
-                uint32_t r0[4], r1[4];
-                dec2(wv[2 * pp], ctab[0], r0);
-                dec2(wv[2 * pp + 1], ctab[0], r1);
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int s = 2 * pp + h;
-#pragma unroll
+    #pragma unroll
                     for (int q = 0; q < NP; ++q) {
                         const uint2 bx = *reinterpret_cast<const uint2 *>(ab + (size_t)q * 8 * astride + s * 32);
-                        if (s == 0)
-                            mma_s8_first(cp[q], r0[2 * h], r1[2 * h], r0[2 * h + 1], r1[2 * h + 1], bx.x, bx.y);
-                        else
-                            mma_s8(cp[q], r0[2 * h], r1[2 * h], r0[2 * h + 1], r1[2 * h + 1], bx.x, bx.y);
+                        if (s == 0) {
+                            mma_s8_first(cp[q], a0, a1, a2, a3, bx.x, bx.y);
+                            if constexpr (SPLIT) mma_s8_first(cn[q], n0, n1, n2, n3, bx.x, bx.y);
+                        } else {
+                            mma_s8(cp[q], a0, a1, a2, a3, bx.x, bx.y);
+                            if constexpr (SPLIT) mma_s8(cn[q], n0, n1, n2, n3, bx.x, bx.y);
+                        }
+                    }
+                }
+            } else {
+    #pragma unroll
+                for (int pp = 0; pp < KK / 2; ++pp) {
+                    uint32_t r0[4], r1[4];
+                    dec2(wv[2 * pp], ctab[0], r0);
+                    dec2(wv[2 * pp + 1], ctab[0], r1);
+    #pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int s = 2 * pp + h;
+    #pragma unroll
+                        for (int q = 0; q < NP; ++q) {
+                            const uint2 bx = *reinterpret_cast<const uint2 *>(ab + (size_t)q * 8 * astride + s * 32);
+                            if (s == 0)
+                                mma_s8_first(cp[q], r0[2 * h], r1[2 * h], r0[2 * h + 1], r1[2 * h + 1], bx.x, bx.y);
+                            else
+                                mma_s8(cp[q], r0[2 * h], r1[2 * h], r0[2 * h + 1], r1[2 * h + 1], bx.x, bx.y);
+                        }
                     }
                 }
             }
-        }
-        // epilogue of group cj: rows g (c0, c1) and g + 8 (c2, c3), activations 2t, 2t + 1 (+8 per pass)
-        const float nsa = __fmul_rn(half_bits_to_float((uint16_t)(nv & 0xffffu)), cs);
-        const float nsb = __fmul_rn(half_bits_to_float((uint16_t)(nv >> 16)), cs);
-#pragma unroll
-        for (int q = 0; q < NP; ++q) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int a = 8 * q + 2 * t + (e & 1);
-                if (MT <= 4 ? a < MT : a < M) {
-                    int d = cp[q][e];
-                    if constexpr (SPLIT) d -= cn[q][e];
-                    const float ns = e < 2 ? nsa : nsb;
-                    acc[q][e] = __fadd_rn(acc[q][e], __fmul_rn(__fmul_rn(__int2float_rn(d), ns), xs_s[a * gpr + cj]));
-                    if (b.partials) {
-                        const int row = row0 + g + (e < 2 ? 0 : 8);
-                        if (row < b.mat[cmat].out) b.partials[((size_t)a * b.mat[cmat].out + row) * gpr + cj] = d;
-                    }
-                }
-            }
-        }
-        if (++cj == gpr) {
-            const GemvMatrix &mat = b.mat[cmat];
+            // epilogue of group cj: rows g (c0, c1) and g + 8 (c2, c3), activations 2t, 2t + 1 (+8 per pass)
+            const float nsa = __fmul_rn(half_bits_to_float((uint16_t)(nv & 0xffffu)), cs);
+            const float nsb = __fmul_rn(half_bits_to_float((uint16_t)(nv >> 16)), cs);
 #pragma unroll
             for (int q = 0; q < NP; ++q) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int a = 8 * q + 2 * t + (e & 1);
-                    const int row = row0 + g + (e < 2 ? 0 : 8);
-                    if ((MT <= 4 ? a < MT : a < M) && row < mat.out) mat.y[(size_t)a * mat.out + row] = acc[q][e];
-                    acc[q][e] = 0.f;
+                    if (MT <= 4 ? a < MT : a < M) {
+                        int d = cp[q][e];
+                        if constexpr (SPLIT) d -= cn[q][e];
+                        const float ns = e < 2 ? nsa : nsb;
+                        acc[q][e] = __fadd_rn(acc[q][e], __fmul_rn(__fmul_rn(__int2float_rn(d), ns), xs_s[a * gpr + cj]));
+                        if constexpr (DBG) {
+                            const int row = row0 + g + (e < 2 ? 0 : 8);
+                            if (row < b.mat[cmat].out) b.partials[((size_t)a * b.mat[cmat].out + row) * gpr + cj] = d;
+                        }
+                    }
                 }
             }
-            cj = 0;
-            ctile += kFragWarps;
-            while (cmat + 1 < b.nmat && ctile >= tile_base[cmat + 1]) ++cmat;
-            row0 = (ctile - tile_base[cmat]) * 16;
+        }
+        const GemvMatrix &mat = b.mat[cmat];
+#pragma unroll
+        for (int q = 0; q < NP; ++q) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int a = 8 * q + 2 * t + (e & 1);
+                const int row = row0 + g + (e < 2 ? 0 : 8);
+                if ((MT <= 4 ? a < MT : a < M) && row < mat.out) mat.y[(size_t)a * mat.out + row] = acc[q][e];
+            }
         }
     }
     cp_async_wait<0>();
 }
 
-template <int BITS, int G, int MT, bool SPLIT, int PF>
+template <int BITS, int G, int MT, bool SPLIT, int PF, int NT, bool DBG = false>
 bool launch_frag_pf(const GemvBatch &b, size_t smem, cudaStream_t st) {
-    auto kernel = cq_gemv_frag_kernel<BITS, G, MT, SPLIT, PF>;
+    auto kernel = cq_gemv_frag_kernel<BITS, G, MT, SPLIT, PF, NT, DBG>;
     static bool configured[64] = {};
     static int sms[64] = {};
     int dev = 0;
@@ -362,12 +356,13 @@ bool launch_frag_pf(const GemvBatch &b, size_t smem, cudaStream_t st) {
             sms[dev] = n;
         }
     }
+    constexpr int warps = NT / 32;
     int total = 0;
     for (int j = 0; j < b.nmat; ++j) total += (b.mat[j].out + 15) / 16;
-    const int grid = std::max(1, std::min((total + kFragWarps - 1) / kFragWarps, cached ? sms[dev] : 148));
+    const int grid = std::max(1, std::min((total + warps - 1) / warps, cached ? sms[dev] : 148));
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kFragThreads);
+    cfg.blockDim = dim3(NT);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -379,15 +374,36 @@ bool launch_frag_pf(const GemvBatch &b, size_t smem, cudaStream_t st) {
     return true;
 }
 
-// Full ring depth when it fits the shared memory, else half.
+// Warps per CTA from the work: every 16-row tile is one warp's, so a launch
+// with few tiles uses 8 warps per CTA (spreading them over all SMs, two CTAs per
+// SM), a large one 32 warps with a 4-slot ring (measured fastest for one to
+// four activation rows and groups up to 128; 64 registers per thread), else 16
+// warps with the full ring, or half of it when shared memory is short.
 template <int BITS, int G, int MT, bool SPLIT>
 bool launch_frag(const GemvBatch &b, cudaStream_t st) {
     using Geo = FragGeo<BITS, G>;
     const int nb = MT <= 8 ? 8 : 16;
-    const size_t full = frag_smem(b.padded, b.groups, nb, Geo::SLOT, Geo::PF);
-    if (full <= (size_t)kFragMaxSmem) return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF>(b, full, st);
-    return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF / 2>(
-        b, frag_smem(b.padded, b.groups, nb, Geo::SLOT, Geo::PF / 2), st);
+    if (b.partials) {   // debug export of the int32 group dots: 16 warps
+        const size_t full = frag_smem(b.padded, b.groups, nb, Geo::SLOT, Geo::PF, 16);
+        if (full <= (size_t)kFragMaxSmem) return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF, 512, true>(b, full, st);
+        return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF / 2, 512, true>(
+            b, frag_smem(b.padded, b.groups, nb, Geo::SLOT, Geo::PF / 2, 16), st);
+    }
+    int tiles = 0;
+    for (int j = 0; j < b.nmat; ++j) tiles += (b.mat[j].out + 15) / 16;
+    if (tiles <= 148 * 8) {
+        const size_t narrow = frag_smem(b.padded, b.groups, nb, Geo::SLOT, Geo::PF, 8);
+        if (narrow <= (size_t)kFragMaxSmem) return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF, 256>(b, narrow, st);
+    }
+    if constexpr (MT <= 4 && G <= 128) {
+        const size_t wide = frag_smem(b.padded, b.groups, nb, Geo::SLOT, 4, 32);
+        if (tiles > 148 * 16 && wide <= (size_t)kFragMaxSmem)
+            return launch_frag_pf<BITS, G, MT, SPLIT, 4, 1024>(b, wide, st);
+    }
+    const size_t full = frag_smem(b.padded, b.groups, nb, Geo::SLOT, Geo::PF, 16);
+    if (full <= (size_t)kFragMaxSmem) return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF, 512>(b, full, st);
+    return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF / 2, 512>(
+        b, frag_smem(b.padded, b.groups, nb, Geo::SLOT, Geo::PF / 2, 16), st);
 }
 
 template <int BITS, int G, bool SPLIT>
@@ -478,7 +494,8 @@ bool build_frag_layout(const uint8_t *packed, const uint16_t *norms, int out, in
 int gemv_frag_max_rows(int bits, int group, int groups) {
     if ((bits != 2 && bits != 4) || (group != 64 && group != 128 && group != 256) || groups < 1) return 0;
     for (int m : {16, 8})
-        if (frag_smem(group * groups, groups, m <= 8 ? 8 : 16, slot_bytes_of(bits, group), ring_depth_of(bits, group) / 2) <=
+        if (frag_smem(group * groups, groups, m <= 8 ? 8 : 16, slot_bytes_of(bits, group), ring_depth_of(bits, group) / 2,
+                      16) <=
             (size_t)kFragMaxSmem)
             return m;
     return 0;
