@@ -61,6 +61,8 @@ struct Matrix {
     uint8_t *d_tiled = nullptr;     // int8 mode: tile-major weights for the tcgen05 kernel
     uint16_t *d_normsT = nullptr;   // int8 mode: tile-major norms
     uint8_t *d_frag = nullptr;      // int8 mode: fragment-order weights for the warp-MMA kernel
+    int8_t *d_w8 = nullptr;         // int8 mode: decoded weights for the prefill GEMM (made at first use)
+    float *d_nsT = nullptr;         // int8 mode: group scales for the prefill GEMM
     uint16_t *d_normsF = nullptr;   // int8 mode: fragment-order norms
     Scratch<float> x, y, rot, xs;
     Scratch<int8_t> q;
@@ -78,6 +80,8 @@ struct Matrix {
         if (d_tiled) cudaFree(d_tiled);
         if (d_normsT) cudaFree(d_normsT);
         if (d_frag) cudaFree(d_frag);
+        if (d_w8) cudaFree(d_w8);
+        if (d_nsT) cudaFree(d_nsT);
         if (d_normsF) cudaFree(d_normsF);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -222,6 +226,30 @@ Matrix *create_matrix(const uint8_t *packed, const uint16_t *norms, int out, int
 }
 
 // Enqueue y = W x on `st` for device x[batch][in] -> y[batch][out].
+// int8 products of a prepared batch: the tensor-core GEMM from kGemmMinRows
+// activation rows on (decoding the matrix for it at the first such call), the
+// GEMV otherwise and whenever the int32 group dots are exported.
+bool sdot_multiply(Matrix *m, const int8_t *q, const float *xs, int batch, float *y, int32_t *partials,
+                   cudaStream_t st) {
+    const CQDevice &w = m->w;
+    if (partials || batch < kGemmMinRows || !gemm_supported(w.bits, w.group, w.padded))
+        return launch_gemv_i8(w, q, xs, batch, y, w.out, partials, st);
+    if (!m->d_w8) {
+        cudaError_t e = cudaMalloc(&m->d_w8, gemm_w8_bytes(w.out, w.padded));
+        if (e == cudaSuccess) e = cudaMalloc(&m->d_nsT, sizeof(float) * gemm_ns_count(w.out, w.groups));
+        if (e != cudaSuccess) {
+            if (m->d_w8) cudaFree(m->d_w8);
+            m->d_w8 = nullptr;
+            set_error(std::string("prefill weight allocation failed: ") + cudaGetErrorString(e));
+            return false;
+        }
+        if (!gemm_prepare(w.packed, w.norms, w.out, w.groups, w.group, w.bits, w.rowbytes, w.padded, w.ctab,
+                          w.centroid_scale, m->d_w8, m->d_nsT, st))
+            return false;
+    }
+    return launch_gemm_i8(q, xs, batch, m->d_w8, m->d_nsT, w.out, w.padded, w.groups, y, w.out, st);
+}
+
 bool run_linear_device(Matrix *m, const float *x, float *y, int batch, cudaStream_t st, int32_t *partials) {
     m->prepared = 0;
     if (batch <= 0) return true;
@@ -233,7 +261,7 @@ bool run_linear_device(Matrix *m, const float *x, float *y, int batch, cudaStrea
     }
     if (!m->q.reserve((size_t)batch * w.padded) || !m->xs.reserve((size_t)batch * w.groups)) return false;
     if (!launch_quantize(w, x, batch, m->q.ptr, m->xs.ptr, st)) return false;
-    return launch_gemv_i8(w, m->q.ptr, m->xs.ptr, batch, y, w.out, partials, st);
+    return sdot_multiply(m, m->q.ptr, m->xs.ptr, batch, y, partials, st);
 }
 
 bool run_linear_host(Matrix *m, const float *x, float *y, int batch, int32_t *partials_host, int8_t *q_host,
@@ -361,6 +389,12 @@ bool multiply_many(Matrix *const *ms, int count, float *const *ys, int batch, cu
     const CQDevice &w = m0->w;
     const bool i8 = m0->sdot;
     if (batch > m0->prepared) { set_error("multiply batch exceeds the prepared batch"); return false; }
+    if (i8 && batch >= kGemmMinRows && gemm_supported(w.bits, w.group, w.padded)) {
+        // prefill-sized batches: one tensor-core GEMM per matrix on the shared input
+        for (int i = 0; i < count; ++i)
+            if (!sdot_multiply(ms[i], m0->q.ptr, m0->xs.ptr, batch, ys[i], nullptr, st)) return false;
+        return true;
+    }
     const int cap = gemv_max_rows(w.bits, w.group, w.groups, i8);
     for (int i0 = 0; i0 < count; i0 += kGemvMaxMats) {
         const int n = std::min(kGemvMaxMats, count - i0);
@@ -563,7 +597,7 @@ static int multiply_device(void *handle, float *y, int batch, void *stream, bool
     if (cudaSetDevice(m->device) != cudaSuccess) { nb200::set_error("cudaSetDevice failed"); return -1; }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const nb200::CQDevice &w = m->w;
-    bool ok = sdot ? nb200::launch_gemv_i8(w, m->q.ptr, m->xs.ptr, batch, y, w.out, nullptr, st)
+    bool ok = sdot ? nb200::sdot_multiply(m, m->q.ptr, m->xs.ptr, batch, y, nullptr, st)
                    : nb200::launch_gemv_f32(w, m->rot.ptr, batch, y, w.out, st);
     return ok ? 0 : -1;
 }

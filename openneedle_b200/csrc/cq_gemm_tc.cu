@@ -1,0 +1,335 @@
+// SDOT (int8) CQ2/CQ4 prefill GEMM on the sm_100a tensor cores:
+// y[m][n] = sum_g ((float(d[m,n,g]) * ns[n,g]) * xs[m,g]) in group order, with
+// d[m,n,g] the exact int32 dot of group g (needle2/csrc/sdot.cpp:108-149).
+//
+// The weights are decoded once per matrix (lazily, at the first prefill) to an
+// int8 copy W8[N][padded] in the activations' element order, and the group
+// scales ns[n,g] = half(norm) * cs to nsT[g][N'] (N' = N rounded up to 256).
+// A CTA computes a 128 x 256 output tile:
+//   * warp 0 (one lane): TMA loads of the group's activation tile (128 x 128
+//     bytes) and weight tile (256 x 128 bytes), 128-byte swizzled, into a
+//     4-stage ring, and a bulk copy of the group's 256 scales into an 8-deep
+//     ring;
+//   * warp 1 (one lane): per group four tcgen05.mma kind::i8 (M = 128,
+//     N = 256, K = 32) into one of two TMEM accumulators, then commits;
+//   * warps 2-17: thread = accumulator lane (activation row) x 64 columns;
+//     per group it reads its int32 dots back (tcgen05.ld) and adds the group
+//     terms to its 64 running sums in registers, in group order.
+// All waits are bounded; on timeout the CTA raises the device fault flag.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "cq_gemv.cuh"
+#include "tcgen05.cuh"
+
+namespace nb200 {
+
+extern __device__ int g_gemv_fault;
+
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 128;   // tile rows, columns, K per group step
+constexpr int kStages = 4, kNsRing = 8;
+constexpr int kEpiWarps = 16;
+constexpr int kThreads = (2 + kEpiWarps) * 32;    // 576
+constexpr int kStageA = kBM * kBK, kStageB = kBN * kBK, kStageBytes = kStageA + kStageB;
+constexpr size_t kSmem = (size_t)kStages * kStageBytes + (size_t)kNsRing * kBN * 4 + 1024;
+constexpr uint32_t kWaitLimit = 1u << 24;
+
+__device__ __forceinline__ bool gwait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    const uint32_t a = smem_addr(bar);
+    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((i & 1023) == 1023 && *abort_flag) return false;
+    }
+    *abort_flag = 1;
+    atomicExch(&g_gemv_fault, 1);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// K-major, 128-byte swizzled operand: 8-row atoms of 1 KB (SBO = 1024).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+struct GemmArgs {
+    int M, N, groups, ldy;
+    const float *xs;    // [M][groups]
+    const float *nsT;   // [groups][N rounded up to 256]
+    int nstride;        // N rounded up to 256
+    float *y;           // [M][ldy]
+};
+
+// 18 warps: five share some SM sub-partitions, so 96 registers per thread at most.
+__global__ void __launch_bounds__(kThreads, 1)
+    cq_gemm_i8_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                      const __grid_constant__ GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float *ns_ring = reinterpret_cast<float *>(smem + (size_t)kStages * kStageBytes);
+    __shared__ __align__(8) uint64_t full[kStages], empty[kStages], dfull[2], dfree[2], nsfull[kNsRing],
+        nsfree[kNsRing];
+    __shared__ uint32_t tmem_s;
+    __shared__ volatile int abort_flag;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;
+    const int G = a.groups;
+
+    if (warp == 1) tc::alloc(&tmem_s, 512);
+    if (tid == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int d = 0; d < 2; ++d) {
+            mbar_init(&dfull[d], 1);
+            mbar_init(&dfree[d], kEpiWarps);
+        }
+        for (int r = 0; r < kNsRing; ++r) {
+            mbar_init(&nsfull[r], 1);
+            mbar_init(&nsfree[r], kEpiWarps);
+        }
+        fence_barrier_init();
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = tmem_s;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            pdl_wait();   // the activations come from the preceding kernel
+            for (int g = 0; g < G && !abort_flag; ++g) {
+                const int s = g % kStages;
+                if (g >= kStages && !gwait(&empty[s], (uint32_t)((g / kStages) - 1) & 1, &abort_flag)) break;
+                uint8_t *st = smem + (size_t)s * kStageBytes;
+                mbar_arrive_expect_tx(&full[s], kStageBytes);
+                tma_load_2d(st, &ta, g * kBK, m0, &full[s]);
+                tma_load_2d(st + kStageA, &tb, g * kBK, n0, &full[s]);
+                const int r = g % kNsRing;
+                if (g >= kNsRing && !gwait(&nsfree[r], (uint32_t)((g / kNsRing) - 1) & 1, &abort_flag)) break;
+                mbar_arrive_expect_tx(&nsfull[r], kBN * 4);
+                bulk_g2s(ns_ring + (size_t)r * kBN, a.nsT + (size_t)g * a.nstride + n0, kBN * 4, &nsfull[r]);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = tc::idesc_s8(kBM, kBN);
+            for (int g = 0; g < G && !abort_flag; ++g) {
+                const int s = g % kStages, d = g & 1;
+                if (!gwait(&full[s], (uint32_t)(g / kStages) & 1, &abort_flag)) break;
+                if (g >= 2 && !gwait(&dfree[d], (uint32_t)((g / 2) - 1) & 1, &abort_flag)) break;
+                tc::fence_after();
+                const uint32_t sa = smem_addr(smem + (size_t)s * kStageBytes), sb = sa + kStageA;
+#pragma unroll
+                for (int kk = 0; kk < kBK / 32; ++kk)
+                    tc::mma_i8_ss(tmem + (uint32_t)(d * kBN), sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc,
+                                  kk > 0);
+                tc::commit(&empty[s]);
+                tc::commit(&dfull[d]);
+            }
+        }
+        __syncwarp();
+    } else {
+        // epilogue: this thread's activation row (TMEM lane) and 64 columns
+        const int q = warp & 3, slice = (warp - 2) >> 2;
+        const int row = m0 + 32 * q + lane, col0 = slice * 64;
+        const uint32_t lane_bits = (uint32_t)(32 * q) << 16;
+        const float *xsr = a.xs + (size_t)min(row, a.M - 1) * G;
+        float acc[64];
+#pragma unroll
+        for (int c = 0; c < 64; ++c) acc[c] = 0.f;
+        pdl_wait();
+        bool ok = true;
+        for (int g = 0; g < G && ok; ++g) {
+            const int d = g & 1, r = g % kNsRing;
+            const float xsg = __ldg(xsr + g);
+            if (!gwait(&dfull[d], (uint32_t)(g / 2) & 1, &abort_flag) ||
+                !gwait(&nsfull[r], (uint32_t)(g / kNsRing) & 1, &abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc::fence_after();
+            const float *nsr = ns_ring + (size_t)r * kBN + col0;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t v[32];
+                uint32_t t0[16], t1[16];
+                tc::ld16(tmem + lane_bits + (uint32_t)(d * kBN + col0 + 32 * h), t0);
+                tc::ld16(tmem + lane_bits + (uint32_t)(d * kBN + col0 + 32 * h + 16), t1);
+                tc::wait_ld();
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    v[c] = t0[c];
+                    v[16 + c] = t1[c];
+                }
+#pragma unroll
+                for (int c = 0; c < 32; c += 4) {
+                    const float4 n4 = *reinterpret_cast<const float4 *>(nsr + 32 * h + c);
+                    const float nsv[4] = {n4.x, n4.y, n4.z, n4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        acc[32 * h + c + e] = __fadd_rn(
+                            acc[32 * h + c + e], __fmul_rn(__fmul_rn(__int2float_rn((int)v[c + e]), nsv[e]), xsg));
+                }
+            }
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&dfree[d]);
+                mbar_arrive(&nsfree[r]);
+            }
+        }
+        if (ok && row < a.M) {
+            float *yr = a.y + (size_t)row * a.ldy;
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+                if (n0 + col0 + c < a.N) yr[n0 + col0 + c] = acc[c];
+        }
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (warp == 1) tc::dealloc(tmem, 512);
+}
+
+// Decoded int8 weights in the activations' element order (CQ2 activations are
+// stored per 16 elements as evens then odds) and transposed group scales.
+__global__ void gemm_prepare_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ norms, int out,
+                                    int groups, int G, int bits, int rowbytes, int padded, uint4 ctab, float cs,
+                                    int nstride, int8_t *__restrict__ w8, float *__restrict__ nsT) {
+    const int8_t *tab = reinterpret_cast<const int8_t *>(&ctab);
+    const long long total = (long long)out * padded;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int n = (int)(i / padded), p = (int)(i % padded);
+        int e = p;   // element stored at position p
+        if (bits == 2) {
+            const int r = p & 15;
+            e = (p & ~15) | (r < 8 ? 2 * r : 2 * (r - 8) + 1);
+        }
+        const uint8_t *rp = packed + (size_t)n * rowbytes;
+        const int idx = bits == 4 ? ((rp[e >> 1] >> (4 * (e & 1))) & 15) : ((rp[e >> 2] >> (2 * (e & 3))) & 3);
+        w8[i] = tab[idx];
+    }
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < (long long)groups * nstride;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int g = (int)(i / nstride), n = (int)(i % nstride);
+        nsT[i] = n < out ? __fmul_rn(half_bits_to_float(norms[(size_t)n * groups + g]), cs) : 0.f;
+    }
+    (void)G;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+bool make_map(CUtensorMap *map, const void *base, int rows, int cols, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) {
+        set_error("cuTensorMapEncodeTiled is not available from the driver");
+        return false;
+    }
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed for the prefill GEMM operands");
+        return false;
+    }
+    return true;
+}
+
+}  // namespace
+
+size_t gemm_w8_bytes(int out, int padded) { return (size_t)out * padded; }
+size_t gemm_ns_count(int out, int groups) { return (size_t)groups * ((out + kBN - 1) / kBN * kBN); }
+
+bool gemm_prepare(const uint8_t *packed, const uint16_t *norms, int out, int groups, int group, int bits, int rowbytes,
+                  int padded, const uint32_t ctab[4], float cs, int8_t *w8, float *nsT, cudaStream_t st) {
+    uint4 t;
+    std::memcpy(&t, ctab, 16);
+    const int nstride = (out + kBN - 1) / kBN * kBN;
+    gemm_prepare_kernel<<<148 * 8, 256, 0, st>>>(packed, norms, out, groups, group, bits, rowbytes, padded, t, cs,
+                                                nstride, w8, nsT);
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+}
+
+bool gemm_supported(int bits, int group, int padded) {
+    return (bits == 2 || bits == 4) && group == kBK && padded % kBK == 0 && padded >= kBK;
+}
+
+bool launch_gemm_i8(const int8_t *q, const float *xs, int M, const int8_t *w8, const float *nsT, int N, int padded,
+                    int groups, float *y, int ldy, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return true;
+    if (padded % kBK || groups * kBK != padded) {
+        set_error("prefill GEMM requires group size 128");
+        return false;
+    }
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(w8)) & 15) {
+        set_error("prefill GEMM operands must be 16-byte aligned");
+        return false;
+    }
+    CUtensorMap ta, tb;
+    if (!make_map(&ta, q, M, padded, kBM) || !make_map(&tb, w8, N, padded, kBN)) return false;
+    GemmArgs args{M, N, groups, ldy, xs, nsT, (N + kBN - 1) / kBN * kBN, y};
+    static bool configured[64] = {};
+    int dev = 0;
+    NB_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+        NB_CUDA_TRY(cudaFuncSetAttribute(cq_gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem));
+        if (dev >= 0 && dev < 64) configured[dev] = true;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((M + kBM - 1) / kBM, (N + kBN - 1) / kBN);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, cq_gemm_i8_kernel, ta, tb, args));
+    return true;
+}
+
+}  // namespace nb200

@@ -74,6 +74,19 @@ bool build_frag_layout(const uint8_t *packed, const uint16_t *norms, int out, in
                        int rowbytes, uint8_t *frag, uint16_t *normsF, cudaStream_t st);
 int gemv_frag_max_rows(int bits, int group, int groups);
 bool launch_gemv_frag(const GemvBatch &b, cudaStream_t st);
+// int8 prefill GEMM on tcgen05 (cq_gemm_tc.cu) for group size 128: weights
+// decoded once to int8 W8[out][padded] (activation element order) and group
+// scales nsT[groups][out rounded up to 256].
+size_t gemm_w8_bytes(int out, int padded);
+size_t gemm_ns_count(int out, int groups);
+bool gemm_supported(int bits, int group, int padded);
+bool gemm_prepare(const uint8_t *packed, const uint16_t *norms, int out, int groups, int group, int bits, int rowbytes,
+                  int padded, const uint32_t ctab[4], float cs, int8_t *w8, float *nsT, cudaStream_t st);
+bool launch_gemm_i8(const int8_t *q, const float *xs, int M, const int8_t *w8, const float *nsT, int N, int padded,
+                    int groups, float *y, int ldy, cudaStream_t st);
+// Activation rows from which int8 products run as the tensor-core GEMM.
+constexpr int kGemmMinRows = 64;
+
 // Which int8 GEMV kernel launch_gemv uses: 0 automatic (fragment-order warp
 // MMA where the matrices carry that copy, else tcgen05, else the diagonal warp
 // MMA), 1 diagonal warp MMA, 2 tcgen05, 3 fragment-order warp MMA.
