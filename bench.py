@@ -240,6 +240,47 @@ def kernel_ms(lib, handles, x, yp, stream, sdot, n):
     return float(np.mean([a.elapsed_time(b) for a, b in zip(starts, ends)]))
 
 
+def prefill_gemm(lib, dev, stream, reps=20):
+    """Config 3's largest case on the int8 prefill GEMM: x[2048][4096] against a
+    CQ4 8192 x 4096 matrix (group 128); the GEMM kernel alone (quantised input
+    prepared outside the timed launches), against twice the measured bf16 dense
+    rate (B200 issues int8 MMAs at twice the bf16 rate)."""
+    import torch
+    from openneedle_b200.quantize import synthetic_matrix
+    m, n, k = 2048, 8192, 4096
+    packed, norms, cb = synthetic_matrix(n, k, 4, GROUP, seed=3)
+    h = lib.needle2_sdot_create(packed.ctypes.data, norms.ctypes.data, n, k, 4, GROUP, cb.ctypes.data)
+    if not h:
+        raise RuntimeError(lib.needle2_b200_error().decode())
+    x = torch.randn(m, k, device=dev)
+    y = torch.empty(m, n, device=dev)
+    sp = stream.cuda_stream
+    check(lib.needle2_sdot_linear_device(h, x.data_ptr(), y.data_ptr(), m, sp), lib)   # decodes the weights once
+    check(lib.needle2_sdot_prepare_device(h, x.data_ptr(), m, sp), lib)
+    for _ in range(3):
+        check(lib.needle2_sdot_multiply_device(h, y.data_ptr(), m, sp), lib)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(reps):
+        check(lib.needle2_sdot_multiply_device(h, y.data_ptr(), m, sp), lib)
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / reps
+    lib.needle2_sdot_destroy(h)
+    tops = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+    bf16 = None
+    try:
+        with open(ROOT / "MEASURED_PEAKS.json") as f:
+            bf16 = float(json.load(f)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        pass
+    peak = 2 * bf16 if bf16 else 2 * 1590.0
+    return {"config": "M=2048 x K=4096 x N=8192, CQ4 group 128, int8 (SDOT) mode, bit-exact epilogue",
+            "kernel": "cq_gemm_i8_kernel (tcgen05 kind::i8, 128x256 tiles, TMA 128B-swizzled)",
+            "kernel_ms": ms, "achieved": tops, "unit": "TOP/s", "bound": "tensor", "peak": peak,
+            "frac": tops / peak, "peak_source": "2 x measured bf16 dense" if bf16 else "2 x fallback bf16 dense"}
+
+
 def run_native(args, rank, world, dist):
     import torch
     from openneedle_b200 import build as b
@@ -374,6 +415,8 @@ def run_native(args, rank, world, dist):
     }
     for h in handles:
         lib.needle2_sdot_destroy(h)
+    if not args.skip_gemm:
+        result["prefill_gemm"] = prefill_gemm(lib, dev, stream)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, sec, n, threads, kind = reference_gemv(packed, norms, cb, x_host, seconds=args.cpu_seconds)
         result["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind,
@@ -394,6 +437,7 @@ def main():
     ap.add_argument("--copies", type=int, default=0, help=f"matrices per step (default {COPIES})")
     ap.add_argument("--skip-fp32", action="store_true", help="omit the FP32-mode side measurement")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer end-to-end measurement")
+    ap.add_argument("--skip-gemm", action="store_true", help="omit the prefill GEMM side measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))

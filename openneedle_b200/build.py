@@ -8,6 +8,7 @@ from __future__ import annotations
 
 import os
 import shutil
+from concurrent.futures import ThreadPoolExecutor
 import subprocess
 import sys
 from pathlib import Path
@@ -45,19 +46,26 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         return LIB
     objdir = PKG.parent / "_build" / "obj"
     objdir.mkdir(parents=True, exist_ok=True)
-    objs = []
+    headers = list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
+    newest_header = max((p.stat().st_mtime for p in headers), default=0.0)
+    jobs, objs = [], []
     for src in sources():
         obj = objdir / (src.stem + ".o")
-        cmd = [nvcc(), *ARCH, *FLAGS, "-dc", str(src), "-o", str(obj)]
+        objs.append(str(obj))
+        # an object is reused only when it is newer than its source and every header
+        if force or not obj.exists() or obj.stat().st_mtime < max(src.stat().st_mtime, newest_header):
+            jobs.append([nvcc(), *ARCH, *FLAGS, "-dc", str(src), "-o", str(obj)])
+
+    def run(cmd):
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
-        objs.append(str(obj))
+
+    with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as pool:
+        for f in [pool.submit(run, cmd) for cmd in jobs]:
+            f.result()
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *objs]
-    if verbose:
-        print(" ".join(cmd), file=sys.stderr)
-    subprocess.run(cmd, check=True)
+    run([nvcc(), *ARCH, "-shared", "-o", str(tmp), *objs])
     os.replace(tmp, LIB)
     return LIB
 

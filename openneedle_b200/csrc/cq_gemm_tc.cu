@@ -14,7 +14,9 @@
 //     N = 256, K = 32) into one of two TMEM accumulators, then commits;
 //   * warps 2-17: thread = accumulator lane (activation row) x 64 columns;
 //     per group it reads its int32 dots back (tcgen05.ld) and adds the group
-//     terms to its 64 running sums in registers, in group order.
+//     terms to its 64 running sums in registers, in group order (paired FP32
+//     instructions, exact per element); the finished tile leaves through
+//     shared memory in coalesced rows.
 // All waits are bounded; on timeout the CTA raises the device fault flag.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -67,6 +69,59 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+// Paired FP32 arithmetic (sm_100): two IEEE round-to-nearest results per
+// instruction, element by element identical to the scalar forms.
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    unsigned long long r, x, y;
+    memcpy(&x, &a, 8);
+    memcpy(&y, &b, 8);
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+    float2 o;
+    memcpy(&o, &r, 8);
+    return o;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    unsigned long long r, x, y;
+    memcpy(&x, &a, 8);
+    memcpy(&y, &b, 8);
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+    float2 o;
+    memcpy(&o, &r, 8);
+    return o;
+}
+
+// acc + t with one rounding, written as fma(t, one, acc) where one == 1.0f
+// arrives as a kernel argument. A paired multiply feeding a paired add may be
+// fused into a paired FMA by the assembler (measured: it changes the rounding
+// of about 4 in 10 terms), which the running sums must not see; the product
+// here is an FMA's multiplicand, which cannot be fused any further, and the
+// assembler cannot fold a multiplier it does not know.
+__device__ __forceinline__ float2 fma_one2(float2 t, float2 one, float2 acc) {
+    unsigned long long r, x, y, z;
+    memcpy(&x, &t, 8);
+    memcpy(&y, &one, 8);
+    memcpy(&z, &acc, 8);
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(x), "l"(y), "l"(z));
+    float2 o;
+    memcpy(&o, &r, 8);
+    return o;
+}
+
+// Two int32 dots (|d| <= 128 * 127 * 127 < 2^22) to float, exactly: the
+// integer added to the bit pattern of 1.5 * 2^23 lands in its binade, where
+// the float spacing is 1, so subtracting 1.5 * 2^23 leaves d itself. One
+// integer add per element and one paired subtract per two, instead of the
+// quarter-rate int-to-float conversion.
+__device__ __forceinline__ float2 int_pair(uint32_t a, uint32_t b) {
+    constexpr uint32_t kMagicBits = 0x4B400000u;   // 12582912.0f
+    const float2 f = make_float2(__uint_as_float(a + kMagicBits), __uint_as_float(b + kMagicBits));
+    return fadd2(f, make_float2(-12582912.0f, -12582912.0f));
+}
+
+__device__ __forceinline__ void named_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // K-major, 128-byte swizzled operand: 8-row atoms of 1 KB (SBO = 1024).
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
@@ -79,6 +134,7 @@ struct GemmArgs {
     const float *nsT;   // [groups][N rounded up to 256]
     int nstride;        // N rounded up to 256
     float *y;           // [M][ldy]
+    float one;          // 1.0f, passed at run time: see fma_one2
 };
 
 // 18 warps: five share some SM sub-partitions, so 96 registers per thread at most.
@@ -155,19 +211,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else {
-        // epilogue: this thread's activation row (TMEM lane) and 64 columns
+        // epilogue: this thread's activation row (TMEM lane) and 64 columns,
+        // kept as 32 pairs for the paired FP32 instructions
         const int q = warp & 3, slice = (warp - 2) >> 2;
-        const int row = m0 + 32 * q + lane, col0 = slice * 64;
+        const int rl = 32 * q + lane, row = m0 + rl, col0 = slice * 64;
         const uint32_t lane_bits = (uint32_t)(32 * q) << 16;
         const float *xsr = a.xs + (size_t)min(row, a.M - 1) * G;
-        float acc[64];
+        float2 acc[32];
 #pragma unroll
-        for (int c = 0; c < 64; ++c) acc[c] = 0.f;
+        for (int c = 0; c < 32; ++c) acc[c] = make_float2(0.f, 0.f);
         pdl_wait();
+        float xs_next = __ldg(xsr);
         bool ok = true;
         for (int g = 0; g < G && ok; ++g) {
             const int d = g & 1, r = g % kNsRing;
-            const float xsg = __ldg(xsr + g);
+            const float xsg = xs_next;
+            if (g + 1 < G) xs_next = __ldg(xsr + g + 1);
             if (!gwait(&dfull[d], (uint32_t)(g / 2) & 1, &abort_flag) ||
                 !gwait(&nsfull[r], (uint32_t)(g / kNsRing) & 1, &abort_flag)) {
                 ok = false;
@@ -175,26 +234,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tc::fence_after();
             const float *nsr = ns_ring + (size_t)r * kBN + col0;
+            const float2 xs2 = make_float2(xsg, xsg), one2 = make_float2(a.one, a.one);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t v[32];
-                uint32_t t0[16], t1[16];
-                tc::ld16(tmem + lane_bits + (uint32_t)(d * kBN + col0 + 32 * h), t0);
-                tc::ld16(tmem + lane_bits + (uint32_t)(d * kBN + col0 + 32 * h + 16), t1);
+            for (int h = 0; h < 8; ++h) {
+                uint32_t v[8];
+                tc::ld8(tmem + lane_bits + (uint32_t)(d * kBN + col0 + 8 * h), v);
                 tc::wait_ld();
 #pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    v[c] = t0[c];
-                    v[16 + c] = t1[c];
-                }
-#pragma unroll
-                for (int c = 0; c < 32; c += 4) {
-                    const float4 n4 = *reinterpret_cast<const float4 *>(nsr + 32 * h + c);
-                    const float nsv[4] = {n4.x, n4.y, n4.z, n4.w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        acc[32 * h + c + e] = __fadd_rn(
-                            acc[32 * h + c + e], __fmul_rn(__fmul_rn(__int2float_rn((int)v[c + e]), nsv[e]), xsg));
+                for (int c = 0; c < 8; c += 4) {
+                    const float4 n4 = *reinterpret_cast<const float4 *>(nsr + 8 * h + c);
+                    float2 &a0 = acc[4 * h + c / 2], &a1 = acc[4 * h + c / 2 + 1];
+                    a0 = fma_one2(fmul2(fmul2(int_pair(v[c], v[c + 1]), make_float2(n4.x, n4.y)), xs2), one2, a0);
+                    a1 = fma_one2(fmul2(fmul2(int_pair(v[c + 2], v[c + 3]), make_float2(n4.z, n4.w)), xs2), one2, a1);
                 }
             }
             tc::fence_before();
@@ -204,11 +255,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(&nsfree[r]);
             }
         }
-        if (ok && row < a.M) {
-            float *yr = a.y + (size_t)row * a.ldy;
+        // the output tile through shared memory (the operand ring is idle once the
+        // last group's dots are read), then written row by row
+        named_sync(2, kEpiWarps * 32);
+        float *out_s = reinterpret_cast<float *>(smem);
+        constexpr int kOutStride = kBN + 1;
 #pragma unroll
-            for (int c = 0; c < 64; ++c)
-                if (n0 + col0 + c < a.N) yr[n0 + col0 + c] = acc[c];
+        for (int c = 0; c < 32; ++c) {
+            out_s[rl * kOutStride + col0 + 2 * c] = acc[c].x;
+            out_s[rl * kOutStride + col0 + 2 * c + 1] = acc[c].y;
+        }
+        named_sync(2, kEpiWarps * 32);
+        if (ok) {
+            const int et = tid - 64;   // 0 .. 511
+            for (int i = et; i < kBM * kBN; i += kEpiWarps * 32) {
+                const int rr = i / kBN, cc = i % kBN;
+                if (m0 + rr < a.M && n0 + cc < a.N) a.y[(size_t)(m0 + rr) * a.ldy + n0 + cc] = out_s[rr * kOutStride + cc];
+            }
         }
     }
     tc::fence_before();
@@ -310,7 +373,7 @@ bool launch_gemm_i8(const int8_t *q, const float *xs, int M, const int8_t *w8, c
     }
     CUtensorMap ta, tb;
     if (!make_map(&ta, q, M, padded, kBM) || !make_map(&tb, w8, N, padded, kBN)) return false;
-    GemmArgs args{M, N, groups, ldy, xs, nsT, (N + kBN - 1) / kBN * kBN, y};
+    GemmArgs args{M, N, groups, ldy, xs, nsT, (N + kBN - 1) / kBN * kBN, y, 1.0f};
     static bool configured[64] = {};
     int dev = 0;
     NB_CUDA_TRY(cudaGetDevice(&dev));
