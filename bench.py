@@ -276,7 +276,7 @@ def prefill_gemm(lib, dev, stream, reps=20):
         pass
     peak = 2 * bf16 if bf16 else 2 * 1590.0
     return {"config": "M=2048 x K=4096 x N=8192, CQ4 group 128, int8 (SDOT) mode, bit-exact epilogue",
-            "kernel": "cq_gemm_i8_kernel (tcgen05 kind::i8, 128x256 tiles, TMA 128B-swizzled)",
+            "kernel": "cq_gemm_i8_kernel (tcgen05 kind::i8, 128x192 tiles, TMA 128B-swizzled)",
             "kernel_ms": ms, "achieved": tops, "unit": "TOP/s", "bound": "tensor", "peak": peak,
             "frac": tops / peak, "peak_source": "2 x measured bf16 dense" if bf16 else "2 x fallback bf16 dense"}
 

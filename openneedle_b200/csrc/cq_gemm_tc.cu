@@ -4,15 +4,17 @@
 //
 // The weights are decoded once per matrix (lazily, at the first prefill) to an
 // int8 copy W8[N][padded] in the activations' element order, and the group
-// scales ns[n,g] = half(norm) * cs to nsT[g][N'] (N' = N rounded up to 256).
-// A CTA computes a 128 x 256 output tile:
+// scales ns[n,g] = half(norm) * cs to nsT[g][N'] (N' = N rounded up to 192).
+// A CTA computes a 128 x 192 output tile (14 warps, so 128 registers a thread;
+// 192 columns also pack the SMs' waves better than 256 at the usual sizes):
 //   * warp 0 (one lane): TMA loads of the group's activation tile (128 x 128
-//     bytes) and weight tile (256 x 128 bytes), 128-byte swizzled, into a
-//     4-stage ring, and a bulk copy of the group's 256 scales into an 8-deep
+//     bytes) and weight tile (192 x 128 bytes), 128-byte swizzled, into a
+//     5-stage ring, and a bulk copy of the group's 192 scales into an 8-deep
 //     ring;
 //   * warp 1 (one lane): per group four tcgen05.mma kind::i8 (M = 128,
-//     N = 256, K = 32) into one of two TMEM accumulators, then commits;
-//   * warps 2-17: thread = accumulator lane (activation row) x 64 columns;
+//     N = 192, K = 32) into one of two TMEM accumulators, then commits; the
+//     accumulators hold a bias (see biased_pair) that the MMAs add onto;
+//   * warps 2-13: thread = accumulator lane (activation row) x 64 columns;
 //     per group it reads its int32 dots back (tcgen05.ld) and adds the group
 //     terms to its 64 running sums in registers, in group order (paired FP32
 //     instructions, exact per element); the finished tile leaves through
@@ -35,10 +37,11 @@ extern __device__ int g_gemv_fault;
 
 namespace {
 
-constexpr int kBM = 128, kBN = 256, kBK = 128;   // tile rows, columns, K per group step
-constexpr int kStages = 4, kNsRing = 8;
-constexpr int kEpiWarps = 16;
-constexpr int kThreads = (2 + kEpiWarps) * 32;    // 576
+constexpr int kBM = 128, kBN = 192, kBK = 128;   // tile rows, columns, K per group step
+constexpr int kDCols = 256;                       // TMEM columns between the two accumulators
+constexpr int kStages = 5, kNsRing = 8;
+constexpr int kEpiWarps = kBN / 64 * 4;           // 12: four lane quarters x 64-column slices
+constexpr int kThreads = (2 + kEpiWarps) * 32;    // 448
 constexpr int kStageA = kBM * kBK, kStageB = kBN * kBK, kStageBytes = kStageA + kStageB;
 constexpr size_t kSmem = (size_t)kStages * kStageBytes + (size_t)kNsRing * kBN * 4 + 1024;
 constexpr uint32_t kWaitLimit = 1u << 24;
@@ -107,15 +110,27 @@ __device__ __forceinline__ float2 fma_one2(float2 t, float2 one, float2 acc) {
     return o;
 }
 
-// Two int32 dots (|d| <= 128 * 127 * 127 < 2^22) to float, exactly: the
-// integer added to the bit pattern of 1.5 * 2^23 lands in its binade, where
-// the float spacing is 1, so subtracting 1.5 * 2^23 leaves d itself. One
-// integer add per element and one paired subtract per two, instead of the
-// quarter-rate int-to-float conversion.
-__device__ __forceinline__ float2 int_pair(uint32_t a, uint32_t b) {
-    constexpr uint32_t kMagicBits = 0x4B400000u;   // 12582912.0f
-    const float2 f = make_float2(__uint_as_float(a + kMagicBits), __uint_as_float(b + kMagicBits));
-    return fadd2(f, make_float2(-12582912.0f, -12582912.0f));
+// Two int32 dots to float, exactly. The accumulator starts every group at the
+// bit pattern of 1.5 * 2^23 (kBias), so the MMA leaves kBias + d there; with
+// |d| <= 128 * 127 * 127 < 2^22 that integer is the float 1.5 * 2^23 + d (same
+// binade, spacing 1), and subtracting 1.5 * 2^23 leaves d itself. This costs
+// one paired subtract per two elements instead of two quarter-rate
+// int-to-float conversions.
+constexpr uint32_t kBias = 0x4B400000u;   // 12582912.0f
+__device__ __forceinline__ float2 biased_pair(uint32_t a, uint32_t b) {
+    return fadd2(make_float2(__uint_as_float(a), __uint_as_float(b)), make_float2(-12582912.0f, -12582912.0f));
+}
+
+// Adds one group's terms for one 16x256b chunk (two column blocks of two rows):
+// acc += (d * ns) * xs per element, in that order, one rounding per operation.
+// v[0..1] / v[2..3] are rows 0 / 8 of block 0, v[4..7] the same of block 1.
+__device__ __forceinline__ void chunk_terms(const uint32_t (&v)[8], const float2 (&ns2)[2], float2 xs_a, float2 xs_b,
+                                            float2 one2, float2 *acc_a, float2 *acc_b) {
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        acc_a[b] = fma_one2(fmul2(fmul2(biased_pair(v[4 * b], v[4 * b + 1]), ns2[b]), xs_a), one2, acc_a[b]);
+        acc_b[b] = fma_one2(fmul2(fmul2(biased_pair(v[4 * b + 2], v[4 * b + 3]), ns2[b]), xs_b), one2, acc_b[b]);
+    }
 }
 
 __device__ __forceinline__ void named_sync(int id, int count) {
@@ -137,7 +152,7 @@ struct GemmArgs {
     float one;          // 1.0f, passed at run time: see fma_one2
 };
 
-// 18 warps: five share some SM sub-partitions, so 96 registers per thread at most.
+// 14 warps: at most four per SM sub-partition, so 128 registers per thread.
 __global__ void __launch_bounds__(kThreads, 1)
     cq_gemm_i8_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                       const __grid_constant__ GemmArgs a) {
@@ -198,79 +213,132 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int g = 0; g < G && !abort_flag; ++g) {
                 const int s = g % kStages, d = g & 1;
                 if (!gwait(&full[s], (uint32_t)(g / kStages) & 1, &abort_flag)) break;
-                if (g >= 2 && !gwait(&dfree[d], (uint32_t)((g / 2) - 1) & 1, &abort_flag)) break;
+                if (!gwait(&dfree[d], (uint32_t)(g / 2) & 1, &abort_flag)) break;
                 tc::fence_after();
                 const uint32_t sa = smem_addr(smem + (size_t)s * kStageBytes), sb = sa + kStageA;
 #pragma unroll
                 for (int kk = 0; kk < kBK / 32; ++kk)
-                    tc::mma_i8_ss(tmem + (uint32_t)(d * kBN), sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc,
-                                  kk > 0);
+                    tc::mma_i8_ss(tmem + (uint32_t)(d * kDCols), sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc,
+                                  1);
                 tc::commit(&empty[s]);
                 tc::commit(&dfull[d]);
             }
         }
         __syncwarp();
     } else {
-        // epilogue: this thread's activation row (TMEM lane) and 64 columns,
-        // kept as 32 pairs for the paired FP32 instructions
+        // epilogue: warp (q, slice) owns accumulator lanes 32q..32q+31 (activation
+        // rows) x 64 columns, read in the 16x256b shape: thread t holds rows
+        // 32q + t/4 + {0, 8, 16, 24} x columns 8b + 2(t%4) + {0, 1} (b = 0..7),
+        // so per group it needs 4 row scales and 16 column scales.
         const int q = warp & 3, slice = (warp - 2) >> 2;
-        const int rl = 32 * q + lane, row = m0 + rl, col0 = slice * 64;
-        const uint32_t lane_bits = (uint32_t)(32 * q) << 16;
-        const float *xsr = a.xs + (size_t)min(row, a.M - 1) * G;
-        float2 acc[32];
+        const int col0 = slice * 64, cpair = 2 * (lane & 3);
+        const int rbase = 32 * q + (lane >> 2);   // tile-local row of r = 0; r adds 8 r
+        int xoff[4];   // row r's scales start at a.xs + xoff[r] (rows past M read row M - 1)
 #pragma unroll
-        for (int c = 0; c < 32; ++c) acc[c] = make_float2(0.f, 0.f);
+        for (int r = 0; r < 4; ++r) xoff[r] = min(m0 + rbase + 8 * r, a.M - 1) * G;
+        float2 acc[4][8];   // [row][column block], a column pair each
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int b = 0; b < 8; ++b) acc[r][b] = make_float2(0.f, 0.f);
+        const uint32_t quarter = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)col0;
+        // both accumulators start at the bias; the MMA warp waits for this
+        for (int d = 0; d < 2; ++d)
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                tc::fill16x256_x2(quarter + ((uint32_t)(16 * (i & 1)) << 16) + (uint32_t)(d * kDCols + 16 * (i >> 1)),
+                                  kBias);
+        tc::wait_st();
+        tc::fence_before();
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(&dfree[0]);
+            mbar_arrive(&dfree[1]);
+        }
         pdl_wait();
-        float xs_next = __ldg(xsr);
+        float xs_next[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) xs_next[r] = __ldg(a.xs + xoff[r]);
         bool ok = true;
         for (int g = 0; g < G && ok; ++g) {
-            const int d = g & 1, r = g % kNsRing;
-            const float xsg = xs_next;
-            if (g + 1 < G) xs_next = __ldg(xsr + g + 1);
+            const int d = g & 1, ri = g % kNsRing;
+            float2 xs2[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                xs2[r] = make_float2(xs_next[r], xs_next[r]);
+                if (g + 1 < G) xs_next[r] = __ldg(a.xs + xoff[r] + g + 1);
+            }
             if (!gwait(&dfull[d], (uint32_t)(g / 2) & 1, &abort_flag) ||
-                !gwait(&nsfull[r], (uint32_t)(g / kNsRing) & 1, &abort_flag)) {
+                !gwait(&nsfull[ri], (uint32_t)(g / kNsRing) & 1, &abort_flag)) {
                 ok = false;
                 break;
             }
             tc::fence_after();
-            const float *nsr = ns_ring + (size_t)r * kBN + col0;
-            const float2 xs2 = make_float2(xsg, xsg), one2 = make_float2(a.one, a.one);
+            const float *nsr = ns_ring + (size_t)ri * kBN + col0 + cpair;
+            const float2 one2 = make_float2(a.one, a.one);
+            const uint32_t dq = quarter + (uint32_t)(d * kDCols);
+            // chunk i: lanes +16 (i & 1), columns 16 (i >> 1) .. +15 (blocks 2c, 2c + 1);
+            // read it, reset it to the bias for group g + 2, and keep the next
+            // chunk's read in flight while this one is summed
+            uint32_t va[8], vb[8];
+            float2 ns2[2];
+            tc::ld16x256_x2(dq, va);
 #pragma unroll
-            for (int h = 0; h < 8; ++h) {
-                uint32_t v[8];
-                tc::ld8(tmem + lane_bits + (uint32_t)(d * kBN + col0 + 8 * h), v);
+            for (int i = 0; i < 8; i += 2) {
+                const int c = i >> 1;
+                const uint32_t lo = dq + (uint32_t)(16 * c), hi = lo + (16u << 16);
+                ns2[0] = *reinterpret_cast<const float2 *>(nsr + 16 * c);
+                ns2[1] = *reinterpret_cast<const float2 *>(nsr + 16 * c + 8);
                 tc::wait_ld();
-#pragma unroll
-                for (int c = 0; c < 8; c += 4) {
-                    const float4 n4 = *reinterpret_cast<const float4 *>(nsr + 8 * h + c);
-                    float2 &a0 = acc[4 * h + c / 2], &a1 = acc[4 * h + c / 2 + 1];
-                    a0 = fma_one2(fmul2(fmul2(int_pair(v[c], v[c + 1]), make_float2(n4.x, n4.y)), xs2), one2, a0);
-                    a1 = fma_one2(fmul2(fmul2(int_pair(v[c + 2], v[c + 3]), make_float2(n4.z, n4.w)), xs2), one2, a1);
-                }
+                tc::hold8(va);
+                tc::fill16x256_x2(lo, kBias);
+                tc::ld16x256_x2(hi, vb);
+                chunk_terms(va, ns2, xs2[0], xs2[1], one2, acc[0] + 2 * c, acc[1] + 2 * c);
+                tc::wait_ld();
+                tc::hold8(vb);
+                tc::fill16x256_x2(hi, kBias);
+                if (i + 2 < 8) tc::ld16x256_x2(lo + 16, va);
+                chunk_terms(vb, ns2, xs2[2], xs2[3], one2, acc[2] + 2 * c, acc[3] + 2 * c);
             }
+            tc::wait_st();
             tc::fence_before();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&dfree[d]);
-                mbar_arrive(&nsfree[r]);
+                mbar_arrive(&nsfree[ri]);
             }
         }
         // the output tile through shared memory (the operand ring is idle once the
         // last group's dots are read), then written row by row
         named_sync(2, kEpiWarps * 32);
         float *out_s = reinterpret_cast<float *>(smem);
-        constexpr int kOutStride = kBN + 1;
+        // row stride = 8 mod 32 banks: the 8-byte writes of a half warp (4 rows
+        // x 4 column pairs) and the 16-byte row reads are conflict-free
+        constexpr int kOutStride = kBN + 8;
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-            out_s[rl * kOutStride + col0 + 2 * c] = acc[c].x;
-            out_s[rl * kOutStride + col0 + 2 * c + 1] = acc[c].y;
-        }
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int b = 0; b < 8; ++b)
+                *reinterpret_cast<float2 *>(out_s + (rbase + 8 * r) * kOutStride + col0 + 8 * b + cpair) = acc[r][b];
         named_sync(2, kEpiWarps * 32);
         if (ok) {
-            const int et = tid - 64;   // 0 .. 511
-            for (int i = et; i < kBM * kBN; i += kEpiWarps * 32) {
-                const int rr = i / kBN, cc = i % kBN;
-                if (m0 + rr < a.M && n0 + cc < a.N) a.y[(size_t)(m0 + rr) * a.ldy + n0 + cc] = out_s[rr * kOutStride + cc];
+            // warp e writes rows e, e + kEpiWarps, ...; each lane 4-column pieces of a row
+            const int ew = warp - 2;
+            const bool vec = (a.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+            for (int rr = ew; rr < kBM && m0 + rr < a.M; rr += kEpiWarps) {
+                float *yr = a.y + (size_t)(m0 + rr) * a.ldy + n0;
+#pragma unroll
+                for (int cc = 4 * lane; cc < kBN; cc += 128) {
+                    const float4 o = *reinterpret_cast<const float4 *>(out_s + rr * kOutStride + cc);
+                    if (vec && n0 + cc + 3 < a.N) {
+                        *reinterpret_cast<float4 *>(yr + cc) = o;
+                    } else {
+                        if (n0 + cc < a.N) yr[cc] = o.x;
+                        if (n0 + cc + 1 < a.N) yr[cc + 1] = o.y;
+                        if (n0 + cc + 2 < a.N) yr[cc + 2] = o.z;
+                        if (n0 + cc + 3 < a.N) yr[cc + 3] = o.w;
+                    }
+                }
             }
         }
     }

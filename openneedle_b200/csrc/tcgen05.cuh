@@ -51,6 +51,31 @@ __device__ __forceinline__ void st32(uint32_t addr, const uint32_t (&r)[32]) {
         "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
 }
+// Orders later uses of tcgen05.ld results after the tcgen05.wait::ld that
+// precedes this call (the compiler sees the registers redefined here).
+__device__ __forceinline__ void hold8(uint32_t (&r)[8]) {
+    asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]));
+}
+
+// 16 lanes x 16 columns (shape 16x256b, two repetitions). Thread t holds, in
+// register j, lane (base + t / 4 + 8 * ((j % 4) >= 2)) and column
+// (8 * (j / 4) + 2 * (t % 4) + (j & 1)) -- the mma.sync accumulator layout.
+__device__ __forceinline__ void ld16x256_x2(uint32_t addr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.16x256b.x2.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void fill16x256_x2(uint32_t addr, uint32_t v) {
+    asm volatile("tcgen05.st.sync.aligned.16x256b.x2.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(addr), "r"(v)
+                 : "memory");
+}
+
+// Warp-wide store of one value into 8 consecutive columns of each thread's lane.
+__device__ __forceinline__ void fill8(uint32_t addr, uint32_t v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(addr), "r"(v)
+                 : "memory");
+}
+
 __device__ __forceinline__ void st16(uint32_t addr, const uint32_t *r) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(

@@ -16,7 +16,7 @@ def native():
 
 
 @pytest.mark.parametrize("bits", [2, 4])
-@pytest.mark.parametrize("n,k,m", [(300, 512, 64), (300, 512, 130), (1000, 1024, 257), (2048, 512, 2048)])
+@pytest.mark.parametrize("n,k,m", [(300, 512, 64), (301, 512, 130), (1000, 1024, 257), (2048, 512, 2048)])
 def test_prefill_gemm_matches_oracle(native, oracle_lib, bits, n, k, m):
     from openneedle_b200.quantize import synthetic_matrix
     packed, norms, cb = synthetic_matrix(n, k, bits, seed=700 + n + bits)
