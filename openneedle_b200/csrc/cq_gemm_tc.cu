@@ -41,13 +41,26 @@ constexpr int kBM = 128, kBN = 192, kBK = 128;   // tile rows, columns, K per gr
 constexpr int kDCols = 256;                       // TMEM columns between the two accumulators
 constexpr int kStages = 5, kNsRing = 8;
 constexpr int kEpiWarps = kBN / 64 * 4;           // 12: four lane quarters x 64-column slices
-constexpr int kThreads = (2 + kEpiWarps) * 32;    // 448
+constexpr int kXsWarp = 2 + kEpiWarps;            // 14: loads the activation scales
+constexpr int kThreads = (3 + kEpiWarps) * 32;    // 480
 constexpr int kStageA = kBM * kBK, kStageB = kBN * kBK, kStageBytes = kStageA + kStageB;
-constexpr size_t kSmem = (size_t)kStages * kStageBytes + (size_t)kNsRing * kBN * 4 + 1024;
+constexpr size_t kSmem = (size_t)kStages * kStageBytes + (size_t)kNsRing * (kBN + kBM) * 4 + 1024;
 constexpr uint32_t kWaitLimit = 1u << 24;
 
 __device__ __forceinline__ bool gwait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
     const uint32_t a = smem_addr(bar);
+    {
+        // a phase that has already completed is the common case: the
+        // non-blocking test answers it without try_wait's suspend latency
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
     for (uint32_t i = 0; i < kWaitLimit; ++i) {
         uint32_t done;
         asm volatile(
@@ -117,7 +130,14 @@ __device__ __forceinline__ float2 fma_one2(float2 t, float2 one, float2 acc) {
 // one paired subtract per two elements instead of two quarter-rate
 // int-to-float conversions.
 constexpr uint32_t kBias = 0x4B400000u;   // 12582912.0f
+// true: the accumulators are reset to kBias in TMEM after each read (a TMEM
+// store per chunk); false: they start at zero and the bias is added here.
+constexpr bool kBiasInTmem = false;
 __device__ __forceinline__ float2 biased_pair(uint32_t a, uint32_t b) {
+    if (!kBiasInTmem) {
+        a += kBias;
+        b += kBias;
+    }
     return fadd2(make_float2(__uint_as_float(a), __uint_as_float(b)), make_float2(-12582912.0f, -12582912.0f));
 }
 
@@ -152,13 +172,14 @@ struct GemmArgs {
     float one;          // 1.0f, passed at run time: see fma_one2
 };
 
-// 14 warps: at most four per SM sub-partition, so 128 registers per thread.
+// 15 warps: at most four per SM sub-partition, so 128 registers per thread.
 __global__ void __launch_bounds__(kThreads, 1)
     cq_gemm_i8_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                       const __grid_constant__ GemmArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *ns_ring = reinterpret_cast<float *>(smem + (size_t)kStages * kStageBytes);
+    float *ns_ring = reinterpret_cast<float *>(smem + (size_t)kStages * kStageBytes);   // [kNsRing][kBN]
+    float *xs_ring = ns_ring + (size_t)kNsRing * kBN;                                  // [kNsRing][kBM]
     __shared__ __align__(8) uint64_t full[kStages], empty[kStages], dfull[2], dfree[2], nsfull[kNsRing],
         nsfree[kNsRing];
     __shared__ uint32_t tmem_s;
@@ -180,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&dfree[d], kEpiWarps);
         }
         for (int r = 0; r < kNsRing; ++r) {
-            mbar_init(&nsfull[r], 1);
+            mbar_init(&nsfull[r], 1 + 32);   // the scale copy, and each lane of the activation-scale warp
             mbar_init(&nsfree[r], kEpiWarps);
         }
         fence_barrier_init();
@@ -219,12 +240,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int kk = 0; kk < kBK / 32; ++kk)
                     tc::mma_i8_ss(tmem + (uint32_t)(d * kDCols), sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc,
-                                  1);
+                                  kBiasInTmem || kk > 0);
                 tc::commit(&empty[s]);
                 tc::commit(&dfull[d]);
             }
         }
         __syncwarp();
+    } else if (warp == kXsWarp) {
+        // the tile's 128 activation scales of each group into the ring slot that
+        // also takes the group's column scales; the epilogue then never waits on
+        // a global load (lanes: rows lane + 32 j)
+        pdl_wait();
+        for (int g = 0; g < G && !abort_flag; ++g) {
+            const int r = g % kNsRing;
+            if (g >= kNsRing && !gwait(&nsfree[r], (uint32_t)((g / kNsRing) - 1) & 1, &abort_flag)) break;
+#pragma unroll
+            for (int j = 0; j < kBM / 32; ++j) {
+                const int row = m0 + lane + 32 * j;
+                xs_ring[(size_t)r * kBM + lane + 32 * j] = row < a.M ? a.xs[(size_t)row * G + g] : 0.f;
+            }
+            mbar_arrive(&nsfull[r]);
+        }
     } else {
         // epilogue: warp (q, slice) owns accumulator lanes 32q..32q+31 (activation
         // rows) x 64 columns, read in the 16x256b shape: thread t holds rows
@@ -233,9 +269,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3, slice = (warp - 2) >> 2;
         const int col0 = slice * 64, cpair = 2 * (lane & 3);
         const int rbase = 32 * q + (lane >> 2);   // tile-local row of r = 0; r adds 8 r
-        int xoff[4];   // row r's scales start at a.xs + xoff[r] (rows past M read row M - 1)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) xoff[r] = min(m0 + rbase + 8 * r, a.M - 1) * G;
         float2 acc[4][8];   // [row][column block], a column pair each
 #pragma unroll
         for (int r = 0; r < 4; ++r)
@@ -243,37 +276,35 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int b = 0; b < 8; ++b) acc[r][b] = make_float2(0.f, 0.f);
         const uint32_t quarter = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)col0;
         // both accumulators start at the bias; the MMA warp waits for this
-        for (int d = 0; d < 2; ++d)
+        if (kBiasInTmem) {
+            for (int d = 0; d < 2; ++d)
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                tc::fill16x256_x2(quarter + ((uint32_t)(16 * (i & 1)) << 16) + (uint32_t)(d * kDCols + 16 * (i >> 1)),
-                                  kBias);
-        tc::wait_st();
+                for (int i = 0; i < 8; ++i)
+                    tc::fill16x256_x2(
+                        quarter + ((uint32_t)(16 * (i & 1)) << 16) + (uint32_t)(d * kDCols + 16 * (i >> 1)), kBias);
+            tc::wait_st();
+        }
         tc::fence_before();
         __syncwarp();
         if (lane == 0) {
             mbar_arrive(&dfree[0]);
             mbar_arrive(&dfree[1]);
         }
-        pdl_wait();
-        float xs_next[4];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) xs_next[r] = __ldg(a.xs + xoff[r]);
         bool ok = true;
         for (int g = 0; g < G && ok; ++g) {
             const int d = g & 1, ri = g % kNsRing;
-            float2 xs2[4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                xs2[r] = make_float2(xs_next[r], xs_next[r]);
-                if (g + 1 < G) xs_next[r] = __ldg(a.xs + xoff[r] + g + 1);
-            }
             if (!gwait(&dfull[d], (uint32_t)(g / 2) & 1, &abort_flag) ||
                 !gwait(&nsfull[ri], (uint32_t)(g / kNsRing) & 1, &abort_flag)) {
                 ok = false;
                 break;
             }
             tc::fence_after();
+            float2 xs2[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const float x = xs_ring[(size_t)ri * kBM + rbase + 8 * r];
+                xs2[r] = make_float2(x, x);
+            }
             const float *nsr = ns_ring + (size_t)ri * kBN + col0 + cpair;
             const float2 one2 = make_float2(a.one, a.one);
             const uint32_t dq = quarter + (uint32_t)(d * kDCols);
@@ -291,16 +322,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ns2[1] = *reinterpret_cast<const float2 *>(nsr + 16 * c + 8);
                 tc::wait_ld();
                 tc::hold8(va);
-                tc::fill16x256_x2(lo, kBias);
+                if (kBiasInTmem) tc::fill16x256_x2(lo, kBias);
                 tc::ld16x256_x2(hi, vb);
                 chunk_terms(va, ns2, xs2[0], xs2[1], one2, acc[0] + 2 * c, acc[1] + 2 * c);
                 tc::wait_ld();
                 tc::hold8(vb);
-                tc::fill16x256_x2(hi, kBias);
+                if (kBiasInTmem) tc::fill16x256_x2(hi, kBias);
                 if (i + 2 < 8) tc::ld16x256_x2(lo + 16, va);
                 chunk_terms(vb, ns2, xs2[2], xs2[3], one2, acc[2] + 2 * c, acc[3] + 2 * c);
             }
-            tc::wait_st();
+            if (kBiasInTmem) tc::wait_st();
             tc::fence_before();
             __syncwarp();
             if (lane == 0) {
