@@ -281,6 +281,54 @@ def prefill_gemm(lib, dev, stream, reps=20):
             "frac": tops / peak, "peak_source": "2 x measured bf16 dense" if bf16 else "2 x fallback bf16 dense"}
 
 
+def attention_decode(dev, stream, lengths=(512, 2048, 4096), reps=20):
+    """Config 4: INT8 KV decode attention for 256 sessions sharing a 384-token
+    prefix (H=8, KV=4, HD=64), one decode step (store the new token, attend)
+    per session at each context length L.  Bytes = unique KV read (prefix once,
+    each session's own L - 384 slots) x (2*KV*HD + 8*KV) + q, out, new k, v."""
+    import torch
+    from openneedle_b200.attention import KVCache
+    sessions, heads, kvh, hd, prefix, max_seq = 256, 8, 4, 64, 384, max(lengths)
+    kv = KVCache(sessions, heads, kvh, hd, max_seq, window=0, prefix_len=prefix)
+    g = torch.Generator(device=dev)
+    g.manual_seed(4)
+    kw = kvh * hd
+    kv.set_prefix_device(torch.randn(prefix, kw, device=dev, generator=g),
+                         torch.randn(prefix, kw, device=dev, generator=g), stream)
+    ids = np.arange(sessions, dtype=np.int32)
+    k_tok = torch.randn(sessions, kw, device=dev, generator=g)
+    v_tok = torch.randn(sessions, kw, device=dev, generator=g)
+    q = torch.randn(sessions, heads * hd, device=dev, generator=g)
+    out = torch.empty_like(q)
+    slot_bytes = 2 * kvh * hd + 8 * kvh
+    rows, filled = [], prefix
+    for length in lengths:
+        # fill every session's cache up to position length - 2 (fresh values per position)
+        while filled < length - 1:
+            k_tok.normal_(generator=g)
+            v_tok.normal_(generator=g)
+            kv.store_device(ids, np.full(sessions, filled, np.int32), k_tok, v_tok, stream)
+            filled += 1
+        pos = np.full(sessions, length - 1, np.int32)
+        for _ in range(3):
+            kv.decode_device(ids, pos, q, k_tok, v_tok, out, stream)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            kv.decode_device(ids, pos, q, k_tok, v_tok, out, stream)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = a.elapsed_time(b) / reps
+        unique = (prefix + sessions * (length - prefix)) * slot_bytes + sessions * 4 * (2 * heads * hd + 2 * kw)
+        gbs = unique / (ms * 1e-3) / 1e9
+        rows.append({"context": length, "ms_per_step": ms, "tokens_per_s": sessions / (ms * 1e-3),
+                     "algorithmic_bytes": unique, "achieved_gbs": gbs, "frac": gbs / peaks()[0]})
+    del kv
+    return {"config": "256 sessions, H=8, KV=4, HD=64, shared 384-token prefix, one decode step per session",
+            "kernels": "kv_quantize_kernel + attn_split_kernel + attn_combine_kernel (split-K flash decode)",
+            "bound": "hbm", "peak": peaks()[0], "unit": "GB/s", "by_context": rows}
+
+
 def run_native(args, rank, world, dist):
     import torch
     from openneedle_b200 import build as b
@@ -417,6 +465,8 @@ def run_native(args, rank, world, dist):
         lib.needle2_sdot_destroy(h)
     if not args.skip_gemm:
         result["prefill_gemm"] = prefill_gemm(lib, dev, stream)
+    if not args.skip_attention:
+        result["attention_decode"] = attention_decode(dev, stream)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, sec, n, threads, kind = reference_gemv(packed, norms, cb, x_host, seconds=args.cpu_seconds)
         result["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind,
@@ -438,6 +488,7 @@ def main():
     ap.add_argument("--skip-fp32", action="store_true", help="omit the FP32-mode side measurement")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer end-to-end measurement")
     ap.add_argument("--skip-gemm", action="store_true", help="omit the prefill GEMM side measurement")
+    ap.add_argument("--skip-attention", action="store_true", help="omit the INT8 KV attention side measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
