@@ -20,6 +20,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <cstring>
 
 #include "attention.cuh"
 #include "common.cuh"
@@ -279,6 +280,270 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const AttnParams p) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Streaming decode/prefill kernel for HD = 64 or 128 (the fast path).
+//
+// A warp walks a contiguous range of visible slots, 8 slots per step: lane
+// (j = lane / 4, c = lane % 4) owns slot base + j and dimensions
+// [c * HD/4, (c + 1) * HD/4), so a step's K rows (and V rows) arrive as 16-byte
+// coalesced loads.  int8 values become floats exactly through a byte permute
+// into the bit pattern of 2^23 + (b + 128) and one subtraction.  Scores are
+// reduced over the slot's four lanes; each chunk of CH steps updates the
+// running max once (per query head), and values accumulate per lane over its
+// slots, reduced across the warp at the end.  The R query heads of the KV group
+// share every K/V read.
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    unsigned long long r, x, y, z;
+    memcpy(&x, &a, 8);
+    memcpy(&y, &b, 8);
+    memcpy(&z, &c, 8);
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(x), "l"(y), "l"(z));
+    float2 o;
+    memcpy(&o, &r, 8);
+    return o;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    unsigned long long r, x, y;
+    memcpy(&x, &a, 8);
+    memcpy(&y, &b, 8);
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+    float2 o;
+    memcpy(&o, &r, 8);
+    return o;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    unsigned long long r, x, y;
+    memcpy(&x, &a, 8);
+    memcpy(&y, &b, 8);
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+    float2 o;
+    memcpy(&o, &r, 8);
+    return o;
+}
+
+// Four int8 (one word) -> exact floats, as pairs (bytes 0,1) and (2,3).
+__device__ __forceinline__ void i8x4_pairs(uint32_t w, float2 &lo, float2 &hi) {
+    const uint32_t u = w ^ 0x80808080u;   // b + 128, as unsigned bytes
+    const uint32_t top = 0x4B000000u;     // 2^23
+    const float2 off = make_float2(-8388736.f, -8388736.f);   // -(2^23 + 128)
+    lo = fadd2(make_float2(__uint_as_float(prmt(u, top, 0x7540)), __uint_as_float(prmt(u, top, 0x7541))), off);
+    hi = fadd2(make_float2(__uint_as_float(prmt(u, top, 0x7542)), __uint_as_float(prmt(u, top, 0x7543))), off);
+}
+
+template <int HD, int R, int CH>
+__global__ void __launch_bounds__(128) attn_stream_kernel(const AttnParams p) {
+    constexpr int NW = 4, DL = HD / 4, WL = DL / 4;   // dims and int8 words per lane
+    constexpr bool QREG = R * DL <= 32;                // query slice in registers
+    __shared__ __align__(16) float qs[R * HD];
+    __shared__ float wm[NW][R], wl[NW][R];
+    __shared__ float wacc[NW][R][HD];
+
+    const int split = blockIdx.x, kh = blockIdx.y, query = blockIdx.z;
+    const int entry = query / p.tokens, t = query % p.tokens;
+    const int s = p.session[entry];
+    const int chunk_start = p.position[entry];
+    const int pos = chunk_start + t;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane >> 2, c = lane & 3;
+
+    const int prefix_count = p.window ? min(p.prefix, pos + 1) : 0;
+    const int start = p.window ? max(p.prefix, pos - p.window + 1) : 0;
+    const int len = prefix_count + max(0, pos - start + 1);
+    const int per = (len + p.splits - 1) / p.splits;
+    const int i0 = split * per, i1 = min(len, i0 + per);
+    // this warp's share of the split, in whole steps of 8 slots
+    const int steps = (max(0, i1 - i0) + 7) / 8, wsteps = (steps + NW - 1) / NW;
+    const int w0 = i0 + warp * wsteps * 8, w1 = min(i1, w0 + wsteps * 8);
+
+    for (int idx = threadIdx.x; idx < R * HD; idx += blockDim.x)
+        qs[idx] = p.q[((size_t)query * p.heads + kh * R) * HD + idx];
+    __syncthreads();
+    float2 qr[QREG ? R : 1][QREG ? DL / 2 : 1];
+    if (QREG) {
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int e = 0; e < DL / 2; ++e) qr[r][e] = *reinterpret_cast<const float2 *>(qs + r * HD + c * DL + 2 * e);
+    }
+
+    const float inv_sqrt = p.inv_sqrt_hd;
+    float m[R], l[R];
+    float2 acc[R][DL / 2];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        m[r] = -INFINITY;
+        l[r] = 0.f;
+#pragma unroll
+        for (int e = 0; e < DL / 2; ++e) acc[r][e] = make_float2(0.f, 0.f);
+    }
+
+    for (int base = w0; base < w1; base += 8 * CH) {
+        uint4 kw[CH][WL / 4], vw[CH][WL / 4];
+        float ks[CH], vs[CH];
+        bool valid[CH];
+#pragma unroll
+        for (int st = 0; st < CH; ++st) {
+            const int i = base + 8 * st + j;
+            valid[st] = i < w1;
+            ks[st] = 0.f;
+            vs[st] = 0.f;
+            if (valid[st]) {
+                const Row row = visible_row(p, s, pos, kh, i, prefix_count, start, entry, chunk_start);
+#pragma unroll
+                for (int u = 0; u < WL / 4; ++u) {
+                    kw[st][u] = __ldg(reinterpret_cast<const uint4 *>(row.k + c * DL) + u);
+                    vw[st][u] = __ldg(reinterpret_cast<const uint4 *>(row.v + c * DL) + u);
+                }
+                ks[st] = row.ks;
+                vs[st] = row.vs;
+            } else {
+#pragma unroll
+                for (int u = 0; u < WL / 4; ++u) kw[st][u] = vw[st][u] = make_uint4(0, 0, 0, 0);
+            }
+        }
+        // scores of this chunk
+        float sc[CH][R];
+#pragma unroll
+        for (int st = 0; st < CH; ++st) {
+            float2 dot[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) dot[r] = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < WL; ++u) {
+                const uint32_t w = (&kw[st][u / 4].x)[u % 4];
+                float2 lo, hi;
+                i8x4_pairs(w, lo, hi);
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    float2 q0, q1;
+                    if (QREG) {
+                        q0 = qr[r][2 * u];
+                        q1 = qr[r][2 * u + 1];
+                    } else {
+                        const float4 qv = *reinterpret_cast<const float4 *>(qs + r * HD + c * DL + 4 * u);
+                        q0 = make_float2(qv.x, qv.y);
+                        q1 = make_float2(qv.z, qv.w);
+                    }
+                    dot[r] = ffma2(lo, q0, dot[r]);
+                    dot[r] = ffma2(hi, q1, dot[r]);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float d = dot[r].x + dot[r].y;
+                d += __shfl_xor_sync(kFull, d, 1);
+                d += __shfl_xor_sync(kFull, d, 2);
+                sc[st][r] = valid[st] ? __fmul_rn(__fmul_rn(d, ks[st]), inv_sqrt) : -INFINITY;
+            }
+        }
+        // running max, weights
+        float wgt[CH][R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            float mx = sc[0][r];
+#pragma unroll
+            for (int st = 1; st < CH; ++st) mx = fmaxf(mx, sc[st][r]);
+            mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 16));
+            const float mn = fmaxf(m[r], mx);
+            const float corr = m[r] == -INFINITY ? 0.f : expf(m[r] - mn);
+            m[r] = mn;
+            float ps = 0.f;
+#pragma unroll
+            for (int st = 0; st < CH; ++st) {
+                const float pr = valid[st] ? expf(sc[st][r] - mn) : 0.f;
+                ps += pr;
+                wgt[st][r] = pr * vs[st];   // the value scale folded into the weight
+            }
+            l[r] = l[r] * corr + (c == 0 ? ps : 0.f);   // one lane of each slot counts it
+            const float2 c2 = make_float2(corr, corr);
+#pragma unroll
+            for (int e = 0; e < DL / 2; ++e) acc[r][e] = fmul2(acc[r][e], c2);
+        }
+        // values
+#pragma unroll
+        for (int st = 0; st < CH; ++st) {
+#pragma unroll
+            for (int u = 0; u < WL; ++u) {
+                const uint32_t w = (&vw[st][u / 4].x)[u % 4];
+                float2 lo, hi;
+                i8x4_pairs(w, lo, hi);
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const float2 w2 = make_float2(wgt[st][r], wgt[st][r]);
+                    acc[r][2 * u] = ffma2(lo, w2, acc[r][2 * u]);
+                    acc[r][2 * u + 1] = ffma2(hi, w2, acc[r][2 * u + 1]);
+                }
+            }
+        }
+    }
+    // reduce over the warp's 8 slot lanes (same c), then over the CTA's warps
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            l[r] += __shfl_xor_sync(kFull, l[r], o);
+#pragma unroll
+            for (int e = 0; e < DL / 2; ++e) {
+                acc[r][e].x += __shfl_xor_sync(kFull, acc[r][e].x, o);
+                acc[r][e].y += __shfl_xor_sync(kFull, acc[r][e].y, o);
+            }
+        }
+        if (lane == 0) {
+            wm[warp][r] = m[r];
+            wl[warp][r] = l[r];
+        }
+        if (j == 0)
+#pragma unroll
+            for (int e = 0; e < DL / 2; ++e) *reinterpret_cast<float2 *>(&wacc[warp][r][c * DL + 2 * e]) = acc[r][e];
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < R * HD; idx += blockDim.x) {
+        const int r = idx / HD, d = idx % HD;
+        float mm = -INFINITY;
+        for (int w = 0; w < NW; ++w) mm = fmaxf(mm, wm[w][r]);
+        float ll = 0.f, aa = 0.f;
+        for (int w = 0; w < NW; ++w) {
+            if (wm[w][r] == -INFINITY) continue;
+            const float f = expf(wm[w][r] - mm);
+            ll += wl[w][r] * f;
+            aa += wacc[w][r][d] * f;
+        }
+        const int h = kh * R + r;
+        if (p.splits == 1) {
+            p.out[((size_t)query * p.heads + h) * HD + d] = ll > 0.f ? aa / ll : 0.f;
+        } else {
+            const size_t prow = ((size_t)query * p.heads + h) * p.splits + split;
+            p.part_acc[prow * HD + d] = aa;
+            if (d == 0) {
+                p.part_m[prow] = mm;
+                p.part_l[prow] = ll;
+            }
+        }
+    }
+}
+
+template <int HD, int CH>
+bool launch_stream(const AttnParams &p, dim3 grid, int R, cudaStream_t st) {
+    switch (R) {
+        case 1: attn_stream_kernel<HD, 1, CH><<<grid, 128, 0, st>>>(p); return true;
+        case 2: attn_stream_kernel<HD, 2, CH><<<grid, 128, 0, st>>>(p); return true;
+        case 4:
+            if constexpr (HD <= 64) {
+                attn_stream_kernel<HD, 4, CH><<<grid, 128, 0, st>>>(p);
+                return true;
+            }
+            return false;
+        default: return false;
+    }
+}
+
 // Merge the split partials of each (query, head).
 __global__ void attn_combine_kernel(const AttnParams p, int hd) {
     const int qh = blockIdx.x;   // query * heads + h
@@ -323,7 +588,12 @@ bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
         return false;
     }
     dim3 grid(p.splits, p.kvheads, queries);
-    switch (p.hd) {
+    const int R = p.heads / p.kvheads;
+    bool streamed = false;
+    // the streaming kernel where its per-lane state fits in registers
+    if (p.hd == 64 && R <= 4) streamed = launch_stream<64, 2>(p, grid, R, st);
+    else if (p.hd == 128 && R <= 2) streamed = launch_stream<128, 2>(p, grid, R, st);
+    if (!streamed) switch (p.hd) {
         case 32: attn_split_kernel<32, true><<<grid, 128, 0, st>>>(p); break;
         case 64: attn_split_kernel<64, true><<<grid, 128, 0, st>>>(p); break;
         case 128: attn_split_kernel<128, true><<<grid, 128, 0, st>>>(p); break;

@@ -54,7 +54,8 @@ def test_golden_cache_and_attention(attention, tag):
 
 
 @pytest.mark.parametrize("heads,kvheads,hd,window,prefix", [
-    (8, 4, 64, 0, 24), (8, 4, 64, 16, 7), (8, 8, 64, 0, 5), (6, 2, 38, 17, 7), (6, 2, 32, 0, 0), (4, 1, 128, 9, 3)])
+    (8, 4, 64, 0, 24), (8, 4, 64, 16, 7), (8, 8, 64, 0, 5), (6, 2, 38, 17, 7), (6, 2, 32, 0, 0), (4, 1, 128, 9, 3),
+    (4, 2, 128, 0, 5), (8, 2, 64, 12, 5), (16, 2, 64, 0, 3)])
 def test_decode_sessions_against_oracle(attention, oracle_lib, heads, kvheads, hd, window, prefix):
     O = oracle_lib
     rng = np.random.default_rng(11)
