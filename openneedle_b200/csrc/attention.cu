@@ -24,6 +24,7 @@
 
 #include "attention.cuh"
 #include "common.cuh"
+#include "sm100_async.cuh"
 
 namespace nb200 {
 
@@ -336,10 +337,52 @@ __device__ __forceinline__ void i8x4_pairs(uint32_t w, float2 &lo, float2 &hi) {
     hi = fadd2(make_float2(__uint_as_float(prmt(u, top, 0x7542)), __uint_as_float(prmt(u, top, 0x7543))), off);
 }
 
-template <int HD, int R, int CH>
-__global__ void __launch_bounds__(128) attn_stream_kernel(const AttnParams p) {
-    constexpr int NW = 4, DL = HD / 4, WL = DL / 4;   // dims and int8 words per lane
-    constexpr bool QREG = R * DL <= 32;                // query slice in registers
+// Global addresses of visible index i's K/V rows and scales.
+struct RowPtr {
+    const int8_t *k, *v;
+    const float *ks, *vs;
+};
+__device__ __forceinline__ RowPtr visible_ptr(const AttnParams &p, int s, int kh, int i, int prefix_count, int start,
+                                              int entry, int chunk_start) {
+    const int position = i < prefix_count ? i : start + (i - prefix_count);
+    size_t row;
+    RowPtr r;
+    if (position < p.prefix) {
+        row = (size_t)kh * p.prefix + position;
+        r.k = p.pk; r.v = p.pv; r.ks = p.pks; r.vs = p.pvs;
+    } else if (p.stage_k && position >= chunk_start) {
+        row = (size_t)kh * p.stage_rows + (size_t)entry * p.tokens + (position - chunk_start);
+        r.k = p.stage_k; r.v = p.stage_v; r.ks = p.stage_ks; r.vs = p.stage_vs;
+    } else {
+        const int slot = p.window ? (position - p.prefix) % p.window : position - p.prefix;
+        row = ((size_t)s * p.kvheads + kh) * p.cs + slot;
+        r.k = p.sk; r.v = p.sv; r.ks = p.sks; r.vs = p.svs;
+    }
+    r.k += row * p.hd;
+    r.v += row * p.hd;
+    r.ks += row;
+    r.vs += row;
+    return r;
+}
+
+template <int HD>
+struct StreamGeo {
+    static constexpr int NW = 4;                    // warps per CTA
+    static constexpr int DL = HD / 4;               // dimensions per lane
+    static constexpr int U = DL / 16;               // 16-byte pieces per lane and row
+    static constexpr int CH = HD <= 64 ? 4 : 2;     // steps (of 8 slots) per chunk
+    static constexpr int NCH = 2;                   // chunks in a warp's ring
+    static constexpr int STEP = 2 * 32 * 16 * U + 64;   // K pieces, V pieces, 8 x (k scale, v scale)
+    static constexpr int CHUNK = CH * STEP;
+    static constexpr int RING = NCH * CHUNK;        // bytes per warp
+};
+
+template <int HD, int R>
+__global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p) {
+    using Geo = StreamGeo<HD>;
+    constexpr int NW = Geo::NW, DL = Geo::DL, U = Geo::U, WL = DL / 4, CH = Geo::CH, NCH = Geo::NCH;
+    constexpr bool QREG = R * DL <= 32;   // query slice in registers
+    __shared__ __align__(16) uint8_t ring_all[NW * Geo::RING];
     __shared__ __align__(16) float qs[R * HD];
     __shared__ float wm[NW][R], wl[NW][R];
     __shared__ float wacc[NW][R][HD];
@@ -350,6 +393,7 @@ __global__ void __launch_bounds__(128) attn_stream_kernel(const AttnParams p) {
     const int chunk_start = p.position[entry];
     const int pos = chunk_start + t;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane >> 2, c = lane & 3;
+    uint8_t *ring = ring_all + warp * Geo::RING;
 
     const int prefix_count = p.window ? min(p.prefix, pos + 1) : 0;
     const int start = p.window ? max(p.prefix, pos - p.window + 1) : 0;
@@ -359,9 +403,36 @@ __global__ void __launch_bounds__(128) attn_stream_kernel(const AttnParams p) {
     // this warp's share of the split, in whole steps of 8 slots
     const int steps = (max(0, i1 - i0) + 7) / 8, wsteps = (steps + NW - 1) / NW;
     const int w0 = i0 + warp * wsteps * 8, w1 = min(i1, w0 + wsteps * 8);
+    const int nchunks = w1 > w0 ? (w1 - w0 + 8 * CH - 1) / (8 * CH) : 0;
+
+    // copies of chunk ch into its ring slot: lane (j, c) brings its own K and V
+    // pieces of slot j of each step; lane c = 0 of each slot brings the scales
+    auto issue = [&](int ch) {
+        if (ch < nchunks) {
+            uint8_t *dst = ring + (ch % NCH) * Geo::CHUNK;
+#pragma unroll
+            for (int st = 0; st < CH; ++st) {
+                const int i = w0 + (ch * CH + st) * 8 + j;
+                if (i < w1) {
+                    const RowPtr r = visible_ptr(p, s, kh, i, prefix_count, start, entry, chunk_start);
+                    uint8_t *sd = dst + st * Geo::STEP;
+#pragma unroll
+                    for (int u = 0; u < U; ++u) {
+                        cp_async<16>(sd + (lane * U + u) * 16, r.k + c * DL + 16 * u);
+                        cp_async<16>(sd + 32 * 16 * U + (lane * U + u) * 16, r.v + c * DL + 16 * u);
+                    }
+                    if (c == 0) cp_async<4>(sd + 2 * 32 * 16 * U + 8 * j, r.ks);
+                    if (c == 1) cp_async<4>(sd + 2 * 32 * 16 * U + 8 * j + 4, r.vs);
+                }
+            }
+        }
+        cp_async_commit();   // one group per chunk, empty ones included
+    };
 
     for (int idx = threadIdx.x; idx < R * HD; idx += blockDim.x)
         qs[idx] = p.q[((size_t)query * p.heads + kh * R) * HD + idx];
+#pragma unroll
+    for (int ch = 0; ch < NCH - 1; ++ch) issue(ch);
     __syncthreads();
     float2 qr[QREG ? R : 1][QREG ? DL / 2 : 1];
     if (QREG) {
@@ -382,55 +453,44 @@ __global__ void __launch_bounds__(128) attn_stream_kernel(const AttnParams p) {
         for (int e = 0; e < DL / 2; ++e) acc[r][e] = make_float2(0.f, 0.f);
     }
 
-    for (int base = w0; base < w1; base += 8 * CH) {
-        uint4 kw[CH][WL / 4], vw[CH][WL / 4];
-        float ks[CH], vs[CH];
+    for (int ch = 0; ch < nchunks; ++ch) {
+        issue(ch + NCH - 1);
+        cp_async_wait<NCH - 1>();   // chunk ch has landed (for this lane) ...
+        __syncwarp();               // ... and for every lane of the warp
+        const uint8_t *src = ring + (ch % NCH) * Geo::CHUNK;
         bool valid[CH];
-#pragma unroll
-        for (int st = 0; st < CH; ++st) {
-            const int i = base + 8 * st + j;
-            valid[st] = i < w1;
-            ks[st] = 0.f;
-            vs[st] = 0.f;
-            if (valid[st]) {
-                const Row row = visible_row(p, s, pos, kh, i, prefix_count, start, entry, chunk_start);
-#pragma unroll
-                for (int u = 0; u < WL / 4; ++u) {
-                    kw[st][u] = __ldg(reinterpret_cast<const uint4 *>(row.k + c * DL) + u);
-                    vw[st][u] = __ldg(reinterpret_cast<const uint4 *>(row.v + c * DL) + u);
-                }
-                ks[st] = row.ks;
-                vs[st] = row.vs;
-            } else {
-#pragma unroll
-                for (int u = 0; u < WL / 4; ++u) kw[st][u] = vw[st][u] = make_uint4(0, 0, 0, 0);
-            }
-        }
-        // scores of this chunk
         float sc[CH][R];
 #pragma unroll
         for (int st = 0; st < CH; ++st) {
+            valid[st] = w0 + (ch * CH + st) * 8 + j < w1;
+            const uint8_t *sd = src + st * Geo::STEP;
+            const float ks = *reinterpret_cast<const float *>(sd + 2 * 32 * 16 * U + 8 * j);
             float2 dot[R];
 #pragma unroll
             for (int r = 0; r < R; ++r) dot[r] = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int u = 0; u < WL; ++u) {
-                const uint32_t w = (&kw[st][u / 4].x)[u % 4];
-                float2 lo, hi;
-                i8x4_pairs(w, lo, hi);
+            for (int u = 0; u < U; ++u) {
+                const uint4 kw = *reinterpret_cast<const uint4 *>(sd + (lane * U + u) * 16);
+                const uint32_t words[4] = {kw.x, kw.y, kw.z, kw.w};
 #pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    float2 q0, q1;
-                    if (QREG) {
-                        q0 = qr[r][2 * u];
-                        q1 = qr[r][2 * u + 1];
-                    } else {
-                        const float4 qv = *reinterpret_cast<const float4 *>(qs + r * HD + c * DL + 4 * u);
-                        q0 = make_float2(qv.x, qv.y);
-                        q1 = make_float2(qv.z, qv.w);
+                for (int wi = 0; wi < 4; ++wi) {
+                    float2 lo, hi;
+                    i8x4_pairs(words[wi], lo, hi);
+                    const int e = (u * 4 + wi) * 2;   // pair index within the lane's DL dims
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        float2 q0, q1;
+                        if (QREG) {
+                            q0 = qr[r][e];
+                            q1 = qr[r][e + 1];
+                        } else {
+                            const float4 qv = *reinterpret_cast<const float4 *>(qs + r * HD + c * DL + 2 * e);
+                            q0 = make_float2(qv.x, qv.y);
+                            q1 = make_float2(qv.z, qv.w);
+                        }
+                        dot[r] = ffma2(lo, q0, dot[r]);
+                        dot[r] = ffma2(hi, q1, dot[r]);
                     }
-                    dot[r] = ffma2(lo, q0, dot[r]);
-                    dot[r] = ffma2(hi, q1, dot[r]);
                 }
             }
 #pragma unroll
@@ -438,7 +498,7 @@ __global__ void __launch_bounds__(128) attn_stream_kernel(const AttnParams p) {
                 float d = dot[r].x + dot[r].y;
                 d += __shfl_xor_sync(kFull, d, 1);
                 d += __shfl_xor_sync(kFull, d, 2);
-                sc[st][r] = valid[st] ? __fmul_rn(__fmul_rn(d, ks[st]), inv_sqrt) : -INFINITY;
+                sc[st][r] = valid[st] ? __fmul_rn(__fmul_rn(d, ks), inv_sqrt) : -INFINITY;
             }
         }
         // running max, weights
@@ -457,9 +517,10 @@ __global__ void __launch_bounds__(128) attn_stream_kernel(const AttnParams p) {
             float ps = 0.f;
 #pragma unroll
             for (int st = 0; st < CH; ++st) {
+                const float vs = *reinterpret_cast<const float *>(src + st * Geo::STEP + 2 * 32 * 16 * U + 8 * j + 4);
                 const float pr = valid[st] ? expf(sc[st][r] - mn) : 0.f;
                 ps += pr;
-                wgt[st][r] = pr * vs[st];   // the value scale folded into the weight
+                wgt[st][r] = valid[st] ? pr * vs : 0.f;   // the value scale folded into the weight
             }
             l[r] = l[r] * corr + (c == 0 ? ps : 0.f);   // one lane of each slot counts it
             const float2 c2 = make_float2(corr, corr);
@@ -469,20 +530,28 @@ __global__ void __launch_bounds__(128) attn_stream_kernel(const AttnParams p) {
         // values
 #pragma unroll
         for (int st = 0; st < CH; ++st) {
+            const uint8_t *sd = src + st * Geo::STEP + 32 * 16 * U;
 #pragma unroll
-            for (int u = 0; u < WL; ++u) {
-                const uint32_t w = (&vw[st][u / 4].x)[u % 4];
-                float2 lo, hi;
-                i8x4_pairs(w, lo, hi);
+            for (int u = 0; u < U; ++u) {
+                const uint4 vw = *reinterpret_cast<const uint4 *>(sd + (lane * U + u) * 16);
+                const uint32_t words[4] = {vw.x, vw.y, vw.z, vw.w};
 #pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const float2 w2 = make_float2(wgt[st][r], wgt[st][r]);
-                    acc[r][2 * u] = ffma2(lo, w2, acc[r][2 * u]);
-                    acc[r][2 * u + 1] = ffma2(hi, w2, acc[r][2 * u + 1]);
+                for (int wi = 0; wi < 4; ++wi) {
+                    float2 lo, hi;
+                    i8x4_pairs(words[wi], lo, hi);
+                    const int e = (u * 4 + wi) * 2;
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        const float2 w2 = make_float2(wgt[st][r], wgt[st][r]);
+                        acc[r][e] = ffma2(lo, w2, acc[r][e]);
+                        acc[r][e + 1] = ffma2(hi, w2, acc[r][e + 1]);
+                    }
                 }
             }
         }
+        __syncwarp();   // every lane is done with this ring slot before it is refilled
     }
+    cp_async_wait<0>();
     // reduce over the warp's 8 slot lanes (same c), then over the CTA's warps
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -529,14 +598,14 @@ __global__ void __launch_bounds__(128) attn_stream_kernel(const AttnParams p) {
     }
 }
 
-template <int HD, int CH>
+template <int HD>
 bool launch_stream(const AttnParams &p, dim3 grid, int R, cudaStream_t st) {
     switch (R) {
-        case 1: attn_stream_kernel<HD, 1, CH><<<grid, 128, 0, st>>>(p); return true;
-        case 2: attn_stream_kernel<HD, 2, CH><<<grid, 128, 0, st>>>(p); return true;
+        case 1: attn_stream_kernel<HD, 1><<<grid, 128, 0, st>>>(p); return true;
+        case 2: attn_stream_kernel<HD, 2><<<grid, 128, 0, st>>>(p); return true;
         case 4:
             if constexpr (HD <= 64) {
-                attn_stream_kernel<HD, 4, CH><<<grid, 128, 0, st>>>(p);
+                attn_stream_kernel<HD, 4><<<grid, 128, 0, st>>>(p);
                 return true;
             }
             return false;
@@ -591,8 +660,8 @@ bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
     const int R = p.heads / p.kvheads;
     bool streamed = false;
     // the streaming kernel where its per-lane state fits in registers
-    if (p.hd == 64 && R <= 4) streamed = launch_stream<64, 2>(p, grid, R, st);
-    else if (p.hd == 128 && R <= 2) streamed = launch_stream<128, 2>(p, grid, R, st);
+    if (p.hd == 64 && R <= 4) streamed = launch_stream<64>(p, grid, R, st);
+    else if (p.hd == 128 && R <= 2) streamed = launch_stream<128>(p, grid, R, st);
     if (!streamed) switch (p.hd) {
         case 32: attn_split_kernel<32, true><<<grid, 128, 0, st>>>(p); break;
         case 64: attn_split_kernel<64, true><<<grid, 128, 0, st>>>(p); break;
