@@ -337,26 +337,34 @@ __device__ __forceinline__ void i8x4_pairs(uint32_t w, float2 &lo, float2 &hi) {
     hi = fadd2(make_float2(__uint_as_float(prmt(u, top, 0x7542)), __uint_as_float(prmt(u, top, 0x7543))), off);
 }
 
-// Global addresses of visible index i's K/V rows and scales.
+// Global addresses of visible index i's K/V rows and scales, and how many
+// visible indices from i on map to consecutive rows of the same array (up to the
+// end of the prefix, of the staged chunk, or of the ring before it wraps).
 struct RowPtr {
     const int8_t *k, *v;
     const float *ks, *vs;
+    int run;
 };
 __device__ __forceinline__ RowPtr visible_ptr(const AttnParams &p, int s, int kh, int i, int prefix_count, int start,
                                               int entry, int chunk_start) {
+    constexpr int kLong = 1 << 30;
     const int position = i < prefix_count ? i : start + (i - prefix_count);
     size_t row;
     RowPtr r;
     if (position < p.prefix) {
         row = (size_t)kh * p.prefix + position;
         r.k = p.pk; r.v = p.pv; r.ks = p.pks; r.vs = p.pvs;
+        r.run = i < prefix_count ? prefix_count - i : p.prefix - position;
     } else if (p.stage_k && position >= chunk_start) {
         row = (size_t)kh * p.stage_rows + (size_t)entry * p.tokens + (position - chunk_start);
         r.k = p.stage_k; r.v = p.stage_v; r.ks = p.stage_ks; r.vs = p.stage_vs;
+        r.run = chunk_start + p.tokens - position;
     } else {
         const int slot = p.window ? (position - p.prefix) % p.window : position - p.prefix;
         row = ((size_t)s * p.kvheads + kh) * p.cs + slot;
         r.k = p.sk; r.v = p.sv; r.ks = p.sks; r.vs = p.svs;
+        r.run = p.window ? p.window - slot : kLong;
+        if (p.stage_k) r.run = min(r.run, chunk_start - position);
     }
     r.k += row * p.hd;
     r.v += row * p.hd;
@@ -410,11 +418,21 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
     auto issue = [&](int ch) {
         if (ch < nchunks) {
             uint8_t *dst = ring + (ch % NCH) * Geo::CHUNK;
+            const int ib = w0 + ch * CH * 8 + j;   // this lane's slot of the chunk's first step
+            const RowPtr r0 = ib < w1 ? visible_ptr(p, s, kh, ib, prefix_count, start, entry, chunk_start) : RowPtr{};
 #pragma unroll
             for (int st = 0; st < CH; ++st) {
-                const int i = w0 + (ch * CH + st) * 8 + j;
+                const int i = ib + 8 * st;
                 if (i < w1) {
-                    const RowPtr r = visible_ptr(p, s, kh, i, prefix_count, start, entry, chunk_start);
+                    RowPtr r = r0;
+                    if (8 * st < r0.run) {   // same array, 8 rows further on
+                        r.k += (size_t)8 * st * HD;
+                        r.v += (size_t)8 * st * HD;
+                        r.ks += 8 * st;
+                        r.vs += 8 * st;
+                    } else {
+                        r = visible_ptr(p, s, kh, i, prefix_count, start, entry, chunk_start);
+                    }
                     uint8_t *sd = dst + st * Geo::STEP;
 #pragma unroll
                     for (int u = 0; u < U; ++u) {
