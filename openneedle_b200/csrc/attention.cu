@@ -332,9 +332,11 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
 __device__ __forceinline__ void i8x4_pairs(uint32_t w, float2 &lo, float2 &hi) {
     const uint32_t u = w ^ 0x80808080u;   // b + 128, as unsigned bytes
     const uint32_t top = 0x4B000000u;     // 2^23
-    const float2 off = make_float2(-8388736.f, -8388736.f);   // -(2^23 + 128)
-    lo = fadd2(make_float2(__uint_as_float(prmt(u, top, 0x7540)), __uint_as_float(prmt(u, top, 0x7541))), off);
-    hi = fadd2(make_float2(__uint_as_float(prmt(u, top, 0x7542)), __uint_as_float(prmt(u, top, 0x7543))), off);
+    constexpr float off = -8388736.f;     // -(2^23 + 128)
+    lo.x = __fadd_rn(__uint_as_float(prmt(u, top, 0x7540)), off);
+    lo.y = __fadd_rn(__uint_as_float(prmt(u, top, 0x7541)), off);
+    hi.x = __fadd_rn(__uint_as_float(prmt(u, top, 0x7542)), off);
+    hi.y = __fadd_rn(__uint_as_float(prmt(u, top, 0x7543)), off);
 }
 
 // Global addresses of visible index i's K/V rows and scales, and how many
@@ -530,13 +532,13 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
             mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 8));
             mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 16));
             const float mn = fmaxf(m[r], mx);
-            const float corr = m[r] == -INFINITY ? 0.f : expf(m[r] - mn);
+            const float corr = m[r] == -INFINITY ? 0.f : __expf(m[r] - mn);
             m[r] = mn;
             float ps = 0.f;
 #pragma unroll
             for (int st = 0; st < CH; ++st) {
                 const float vs = *reinterpret_cast<const float *>(src + st * Geo::STEP + 2 * 32 * 16 * U + 8 * j + 4);
-                const float pr = valid[st] ? expf(sc[st][r] - mn) : 0.f;
+                const float pr = valid[st] ? __expf(sc[st][r] - mn) : 0.f;
                 ps += pr;
                 wgt[st][r] = valid[st] ? pr * vs : 0.f;   // the value scale folded into the weight
             }
@@ -598,7 +600,7 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
         float ll = 0.f, aa = 0.f;
         for (int w = 0; w < NW; ++w) {
             if (wm[w][r] == -INFINITY) continue;
-            const float f = expf(wm[w][r] - mm);
+            const float f = __expf(wm[w][r] - mm);
             ll += wl[w][r] * f;
             aa += wacc[w][r][d] * f;
         }
