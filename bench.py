@@ -325,7 +325,7 @@ def attention_decode(dev, stream, lengths=(512, 2048, 4096), reps=20):
                      "algorithmic_bytes": unique, "achieved_gbs": gbs, "frac": gbs / peaks()[0]})
     del kv
     return {"config": "256 sessions, H=8, KV=4, HD=64, shared 384-token prefix, one decode step per session",
-            "kernels": "kv_quantize_kernel + attn_split_kernel + attn_combine_kernel (split-K flash decode)",
+            "kernels": "kv_quantize_kernel + attn_stream_kernel + attn_combine_kernel (split-K flash decode)",
             "bound": "hbm", "peak": peaks()[0], "unit": "GB/s", "by_context": rows}
 
 
