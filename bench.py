@@ -329,6 +329,50 @@ def attention_decode(dev, stream, lengths=(512, 2048, 4096), reps=20):
             "bound": "hbm", "peak": peaks()[0], "unit": "GB/s", "by_context": rows}
 
 
+def sharded_gemm(dev, stream, world, dist, packed, norms, cb, m=2048, reps=10):
+    """Config 5b: the 14336 x 4096 CQ4 matrix N-sharded over the ranks (int8
+    mode, M = 2048 activation rows), its outputs all-gathered into every rank's
+    [M][N].  Times (max over ranks, CUDA events): the all-gather fused into the
+    GEMM epilogue (peer stores over NVLink, then a tiny all-reduce as the
+    barrier), a local GEMM followed by NCCL's all_gather_into_tensor, and the
+    local GEMM alone.  Each rank sends M * N/world * 4 bytes to every other rank."""
+    import torch
+    from openneedle_b200.sharded import ShardedSdot
+    sh = ShardedSdot(packed, norms, (N_OUT, K_IN), BITS, GROUP, cb, max_batch=m, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    x = torch.randn(m, K_IN, device=dev, generator=g)
+
+    def timed(fn):
+        for _ in range(3):
+            fn(x, stream)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            fn(x, stream)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) / reps
+
+    fused = timed(sh.forward)
+    nccl = timed(sh.forward_nccl)
+    local = timed(sh.forward_local)
+    t = torch.tensor([fused, nccl, local], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    fused, nccl, local = t.tolist()
+    sent = m * sh.ns * 4 * (world - 1)
+    flops = 2.0 * m * N_OUT * K_IN
+    res = {"config": f"{N_OUT}x{K_IN} CQ4 int8 mode, M={m}, {sh.ns} rows per GPU, outputs all-gathered to every GPU",
+           "fused_ms": fused, "nccl_ms": nccl, "local_gemm_ms": local,
+           "fused_top_s": flops / (fused * 1e-3) / 1e12, "nccl_top_s": flops / (nccl * 1e-3) / 1e12,
+           "nvlink_bytes_sent_per_rank": sent, "fused_send_gbs_per_rank": sent / (fused * 1e-3) / 1e9,
+           "timing": "max over ranks; each call = prepare + GEMM (+ exchange); fused includes the barrier all-reduce"}
+    sh.close()
+    return res
+
+
 def run_native(args, rank, world, dist):
     import torch
     from openneedle_b200 import build as b
@@ -467,6 +511,8 @@ def run_native(args, rank, world, dist):
         result["prefill_gemm"] = prefill_gemm(lib, dev, stream)
     if not args.skip_attention:
         result["attention_decode"] = attention_decode(dev, stream)
+    if world > 1 and not args.skip_sharded:
+        result["sharded_gemm"] = sharded_gemm(dev, stream, world, dist, packed, norms, cb)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         gbs, sec, n, threads, kind = reference_gemv(packed, norms, cb, x_host, seconds=args.cpu_seconds)
         result["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind,
@@ -489,6 +535,8 @@ def main():
     ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer end-to-end measurement")
     ap.add_argument("--skip-gemm", action="store_true", help="omit the prefill GEMM side measurement")
     ap.add_argument("--skip-attention", action="store_true", help="omit the INT8 KV attention side measurement")
+    ap.add_argument("--skip-sharded", action="store_true",
+                    help="omit the N-sharded GEMM + all-gather side measurement (multi-GPU runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -502,8 +550,10 @@ def main():
 
             import torch
             import torch.distributed as dist
-            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+            local = int(os.environ.get("LOCAL_RANK", 0))
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
         try:
             result = run_native(args, rank, world, dist)
         finally:

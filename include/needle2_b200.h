@@ -116,6 +116,24 @@ int needle2_cq_multiply_device(void *handle, float *y, int batch, void *stream);
 int needle2_sdot_prepare_device(void *handle, const float *x, int batch, void *stream);
 int needle2_sdot_multiply_device(void *handle, float *y, int batch, void *stream);
 
+/* N-sharded matrices (no counterpart in the reference, which runs on one host):
+ * multiply from the last prepare into ndst (1..8) device buffers at once, y[b][o]
+ * going to dsts[i][b * ldy + o] (ldy >= out).  With dsts[i] = this shard's
+ * column range of every rank's full [batch][N] output, the all-gather of an
+ * N-sharded GEMM happens in the GEMM's epilogue (peer stores over NVLink;
+ * batches of 64 rows and more with group 128), or as one copy per buffer
+ * otherwise.  The caller orders the ranks' calls before reading (a barrier). */
+int needle2_sdot_multiply_gather_device(void *handle, float *const *dsts, int ndst, int ldy, int batch,
+                                        void *stream);
+
+/* CUDA IPC between the processes of one node: export a device pointer as a
+ * 64-byte handle plus its offset inside its allocation; import gives this
+ * process a pointer to the same bytes (peer access enabled); close releases
+ * an imported pointer. */
+int needle2_b200_ipc_export(const void *ptr, void *handle64, unsigned long long *offset);
+int needle2_b200_ipc_import(const void *handle64, unsigned long long offset, void **ptr);
+int needle2_b200_ipc_close(void *ptr);
+
 /* SDOT internals the reference never exports (its per-group int32 dots stay
  * inside SdotCQ::row, needle2/csrc/sdot.cpp:142-149): partials[batch][out][groups]
  * int32, q[batch][padded] int8 in natural element order, scales[batch][groups];

@@ -229,11 +229,9 @@ Matrix *create_matrix(const uint8_t *packed, const uint16_t *norms, int out, int
 // int8 products of a prepared batch: the tensor-core GEMM from kGemmMinRows
 // activation rows on (decoding the matrix for it at the first such call), the
 // GEMV otherwise and whenever the int32 group dots are exported.
-bool sdot_multiply(Matrix *m, const int8_t *q, const float *xs, int batch, float *y, int32_t *partials,
-                   cudaStream_t st) {
+// Decoded int8 weights and group scales for the prefill GEMM, made at the first use.
+bool ensure_gemm_copy(Matrix *m, cudaStream_t st) {
     const CQDevice &w = m->w;
-    if (partials || batch < kGemmMinRows || !gemm_supported(w.bits, w.group, w.padded))
-        return launch_gemv_i8(w, q, xs, batch, y, w.out, partials, st);
     if (!m->d_w8) {
         cudaError_t e = cudaMalloc(&m->d_w8, gemm_w8_bytes(w.out, w.padded));
         if (e == cudaSuccess) e = cudaMalloc(&m->d_nsT, sizeof(float) * gemm_ns_count(w.out, w.groups));
@@ -247,7 +245,35 @@ bool sdot_multiply(Matrix *m, const int8_t *q, const float *xs, int batch, float
                           w.centroid_scale, m->d_w8, m->d_nsT, st))
             return false;
     }
+    return true;
+}
+
+bool sdot_multiply(Matrix *m, const int8_t *q, const float *xs, int batch, float *y, int32_t *partials,
+                   cudaStream_t st) {
+    const CQDevice &w = m->w;
+    if (partials || batch < kGemmMinRows || !gemm_supported(w.bits, w.group, w.padded))
+        return launch_gemv_i8(w, q, xs, batch, y, w.out, partials, st);
+    if (!ensure_gemm_copy(m, st)) return false;
     return launch_gemm_i8(q, xs, batch, m->d_w8, m->d_nsT, w.out, w.padded, w.groups, y, w.out, st);
+}
+
+// y[batch][out] written into each of dsts[0..ndst) with row stride ldy (for
+// instance this matrix's column range of every rank's [batch][N] output): the
+// GEMM writes all destinations from its epilogue; smaller batches run the GEMV
+// into scratch and copy it to each destination.
+bool sdot_multiply_to(Matrix *m, const int8_t *q, const float *xs, int batch, float *const *dsts, int ndst, int ldy,
+                      cudaStream_t st) {
+    const CQDevice &w = m->w;
+    if (batch >= kGemmMinRows && gemm_supported(w.bits, w.group, w.padded)) {
+        if (!ensure_gemm_copy(m, st)) return false;
+        return launch_gemm_i8_multi(q, xs, batch, m->d_w8, m->d_nsT, w.out, w.padded, w.groups, dsts, ndst, ldy, st);
+    }
+    if (!m->y.reserve((size_t)batch * w.out)) return false;
+    if (!launch_gemv_i8(w, q, xs, batch, m->y.ptr, w.out, nullptr, st)) return false;
+    for (int i = 0; i < ndst; ++i)
+        NB_CUDA_TRY(cudaMemcpy2DAsync(dsts[i], sizeof(float) * ldy, m->y.ptr, sizeof(float) * w.out,
+                                      sizeof(float) * w.out, batch, cudaMemcpyDeviceToDevice, st));
+    return true;
 }
 
 bool run_linear_device(Matrix *m, const float *x, float *y, int batch, cudaStream_t st, int32_t *partials) {
@@ -613,6 +639,22 @@ int needle2_sdot_prepare_device(void *h, const float *x, int batch, void *stream
 }
 int needle2_sdot_multiply_device(void *h, float *y, int batch, void *stream) {
     return multiply_device(h, y, batch, stream, true);
+}
+
+int needle2_sdot_multiply_gather_device(void *h, float *const *dsts, int ndst, int ldy, int batch, void *stream) {
+    nb200::clear_error();
+    auto *m = static_cast<Matrix *>(h);
+    if (!m || !m->sdot) { nb200::set_error("null or wrong-kind handle"); return -1; }
+    if (!dsts || ndst < 1 || ndst > nb200::kMaxGemmOutputs) { nb200::set_error("1 to 8 output buffers"); return -1; }
+    if (ldy < m->w.out) { nb200::set_error("ldy is smaller than the matrix's out"); return -1; }
+    if (batch < 0 || batch > m->prepared) { nb200::set_error("multiply batch exceeds the prepared batch"); return -1; }
+    for (int i = 0; i < ndst; ++i)
+        if (!dsts[i]) { nb200::set_error("null output buffer"); return -1; }
+    if (batch == 0) return 0;
+    if (cudaSetDevice(m->device) != cudaSuccess) { nb200::set_error("cudaSetDevice failed"); return -1; }
+    return nb200::sdot_multiply_to(m, m->q.ptr, m->xs.ptr, batch, dsts, ndst, ldy, static_cast<cudaStream_t>(stream))
+               ? 0
+               : -1;
 }
 
 int needle2_b200_device_fault() { return nb200::read_and_clear_gemv_fault(); }

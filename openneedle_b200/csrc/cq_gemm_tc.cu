@@ -170,6 +170,11 @@ struct GemmArgs {
     int nstride;        // N rounded up to 256
     float *y;           // [M][ldy]
     float one;          // 1.0f, passed at run time: see fma_one2
+    // outputs: y[m][n] is written to dst[i] + m * ldy + n for every i < ndst (the
+    // caller's own buffer, or the same columns of every rank's full output
+    // buffer when an all-gather is fused into the epilogue)
+    float *dst[kMaxGemmOutputs];
+    int ndst;
 };
 
 // 15 warps: at most four per SM sub-partition, so 128 registers per thread.
@@ -355,19 +360,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) {
             // warp e writes rows e, e + kEpiWarps, ...; each lane 4-column pieces of a row
             const int ew = warp - 2;
-            const bool vec = (a.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
-            for (int rr = ew; rr < kBM && m0 + rr < a.M; rr += kEpiWarps) {
-                float *yr = a.y + (size_t)(m0 + rr) * a.ldy + n0;
+            for (int di = 0; di < a.ndst; ++di) {
+                float *const y = a.dst[di];
+                const bool vec = (a.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+                for (int rr = ew; rr < kBM && m0 + rr < a.M; rr += kEpiWarps) {
+                    float *yr = y + (size_t)(m0 + rr) * a.ldy + n0;
 #pragma unroll
-                for (int cc = 4 * lane; cc < kBN; cc += 128) {
-                    const float4 o = *reinterpret_cast<const float4 *>(out_s + rr * kOutStride + cc);
-                    if (vec && n0 + cc + 3 < a.N) {
-                        *reinterpret_cast<float4 *>(yr + cc) = o;
-                    } else {
-                        if (n0 + cc < a.N) yr[cc] = o.x;
-                        if (n0 + cc + 1 < a.N) yr[cc + 1] = o.y;
-                        if (n0 + cc + 2 < a.N) yr[cc + 2] = o.z;
-                        if (n0 + cc + 3 < a.N) yr[cc + 3] = o.w;
+                    for (int cc = 4 * lane; cc < kBN; cc += 128) {
+                        const float4 o = *reinterpret_cast<const float4 *>(out_s + rr * kOutStride + cc);
+                        if (vec && n0 + cc + 3 < a.N) {
+                            *reinterpret_cast<float4 *>(yr + cc) = o;
+                        } else {
+                            if (n0 + cc < a.N) yr[cc] = o.x;
+                            if (n0 + cc + 1 < a.N) yr[cc + 1] = o.y;
+                            if (n0 + cc + 2 < a.N) yr[cc + 2] = o.z;
+                            if (n0 + cc + 3 < a.N) yr[cc + 3] = o.w;
+                        }
                     }
                 }
             }
@@ -461,7 +469,16 @@ bool gemm_supported(int bits, int group, int padded) {
 
 bool launch_gemm_i8(const int8_t *q, const float *xs, int M, const int8_t *w8, const float *nsT, int N, int padded,
                     int groups, float *y, int ldy, cudaStream_t st) {
+    return launch_gemm_i8_multi(q, xs, M, w8, nsT, N, padded, groups, &y, 1, ldy, st);
+}
+
+bool launch_gemm_i8_multi(const int8_t *q, const float *xs, int M, const int8_t *w8, const float *nsT, int N,
+                          int padded, int groups, float *const *dsts, int ndst, int ldy, cudaStream_t st) {
     if (M <= 0 || N <= 0) return true;
+    if (ndst < 1 || ndst > kMaxGemmOutputs) {
+        set_error("prefill GEMM: 1 to 8 output buffers");
+        return false;
+    }
     if (padded % kBK || groups * kBK != padded) {
         set_error("prefill GEMM requires group size 128");
         return false;
@@ -472,7 +489,18 @@ bool launch_gemm_i8(const int8_t *q, const float *xs, int M, const int8_t *w8, c
     }
     CUtensorMap ta, tb;
     if (!make_map(&ta, q, M, padded, kBM) || !make_map(&tb, w8, N, padded, kBN)) return false;
-    GemmArgs args{M, N, groups, ldy, xs, nsT, (N + kBN - 1) / kBN * kBN, y, 1.0f};
+    GemmArgs args{};
+    args.M = M;
+    args.N = N;
+    args.groups = groups;
+    args.ldy = ldy;
+    args.xs = xs;
+    args.nsT = nsT;
+    args.nstride = (N + kBN - 1) / kBN * kBN;
+    args.y = nullptr;
+    args.one = 1.0f;
+    for (int i = 0; i < ndst; ++i) args.dst[i] = dsts[i];
+    args.ndst = ndst;
     static bool configured[64] = {};
     int dev = 0;
     NB_CUDA_TRY(cudaGetDevice(&dev));

@@ -76,7 +76,7 @@ int gemv_frag_max_rows(int bits, int group, int groups);
 bool launch_gemv_frag(const GemvBatch &b, cudaStream_t st);
 // int8 prefill GEMM on tcgen05 (cq_gemm_tc.cu) for group size 128: weights
 // decoded once to int8 W8[out][padded] (activation element order) and group
-// scales nsT[groups][out rounded up to 256].
+// scales nsT[groups][out rounded up to the tile width].
 size_t gemm_w8_bytes(int out, int padded);
 size_t gemm_ns_count(int out, int groups);
 bool gemm_supported(int bits, int group, int padded);
@@ -84,6 +84,12 @@ bool gemm_prepare(const uint8_t *packed, const uint16_t *norms, int out, int gro
                   int padded, const uint32_t ctab[4], float cs, int8_t *w8, float *nsT, cudaStream_t st);
 bool launch_gemm_i8(const int8_t *q, const float *xs, int M, const int8_t *w8, const float *nsT, int N, int padded,
                     int groups, float *y, int ldy, cudaStream_t st);
+// The same GEMM writing every output element to each of dsts[0..ndst) (the
+// columns this matrix covers in several [M][ldy] buffers, e.g. every rank's
+// output of an N-sharded matrix: the all-gather fused into the epilogue).
+constexpr int kMaxGemmOutputs = 8;
+bool launch_gemm_i8_multi(const int8_t *q, const float *xs, int M, const int8_t *w8, const float *nsT, int N,
+                          int padded, int groups, float *const *dsts, int ndst, int ldy, cudaStream_t st);
 // Activation rows from which int8 products run as the tensor-core GEMM.
 constexpr int kGemmMinRows = 64;
 
