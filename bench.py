@@ -267,6 +267,21 @@ def prefill_gemm(lib, dev, stream, reps=20):
     torch.cuda.synchronize(dev)
     ms = a.elapsed_time(b) / reps
     lib.needle2_sdot_destroy(h)
+    # the same product in the FP32 mode (bf16 hi/lo split, three MMAs per K step)
+    hf = lib.needle2_cq_create(packed.ctypes.data, norms.ctypes.data, n, k, 4, GROUP, cb.ctypes.data)
+    if not hf:
+        raise RuntimeError(lib.needle2_b200_error().decode())
+    check(lib.needle2_cq_linear_device(hf, x.data_ptr(), y.data_ptr(), m, sp), lib)   # makes the bf16 copy
+    check(lib.needle2_cq_prepare_device(hf, x.data_ptr(), m, sp), lib)
+    for _ in range(3):
+        check(lib.needle2_cq_multiply_device(hf, y.data_ptr(), m, sp), lib)
+    a.record(stream)
+    for _ in range(reps):
+        check(lib.needle2_cq_multiply_device(hf, y.data_ptr(), m, sp), lib)
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    fms = a.elapsed_time(b) / reps
+    lib.needle2_cq_destroy(hf)
     tops = 2.0 * m * n * k / (ms * 1e-3) / 1e12
     bf16 = None
     try:
@@ -275,10 +290,18 @@ def prefill_gemm(lib, dev, stream, reps=20):
     except (OSError, KeyError, ValueError):
         pass
     peak = 2 * bf16 if bf16 else 2 * 1590.0
+    ftf = 2.0 * m * n * k / (fms * 1e-3) / 1e12
+    fp32 = {"kernel": "cq_gemm_f32x3_kernel (tcgen05 kind::f16, bf16 hi/lo split, 3 MMAs per K step, 128x256 tiles)",
+            "kernel_ms": fms, "achieved": ftf, "unit": "TFLOP/s", "peak": bf16 or 1590.0,
+            "frac": ftf / (bf16 or 1590.0), "tensor_pipe_frac": 3 * ftf / (bf16 or 1590.0),
+            "note": "FP32-equivalent flops against the measured bf16 dense rate; three bf16 products per FP32 "
+                    "product, so 1/3 is this kernel's ceiling (tensor_pipe_frac counts all three)",
+            "call": "needle2_cq_multiply_device (split activations + GEMM)"}
     return {"config": "M=2048 x K=4096 x N=8192, CQ4 group 128, int8 (SDOT) mode, bit-exact epilogue",
             "kernel": "cq_gemm_i8_kernel (tcgen05 kind::i8, 128x192 tiles, TMA 128B-swizzled)",
             "kernel_ms": ms, "achieved": tops, "unit": "TOP/s", "bound": "tensor", "peak": peak,
-            "frac": tops / peak, "peak_source": "2 x measured bf16 dense" if bf16 else "2 x fallback bf16 dense"}
+            "frac": tops / peak, "peak_source": "2 x measured bf16 dense" if bf16 else "2 x fallback bf16 dense",
+            "fp32_mode": fp32}
 
 
 def attention_decode(dev, stream, lengths=(512, 2048, 4096), reps=20):

@@ -63,9 +63,11 @@ struct Matrix {
     uint8_t *d_frag = nullptr;      // int8 mode: fragment-order weights for the warp-MMA kernel
     int8_t *d_w8 = nullptr;         // int8 mode: decoded weights for the prefill GEMM (made at first use)
     float *d_nsT = nullptr;         // int8 mode: group scales for the prefill GEMM
+    uint16_t *d_whl = nullptr;      // FP32 mode: bf16 hi/lo weights for the prefill GEMM (made at first use)
     uint16_t *d_normsF = nullptr;   // int8 mode: fragment-order norms
     Scratch<float> x, y, rot, xs;
     Scratch<int8_t> q;
+    Scratch<uint16_t> ahl;   // FP32 mode: bf16 hi/lo activations for the prefill GEMM
     Scratch<int32_t> partials;
     Scratch<int64_t> ids;
     int prepared = 0;  // activation rows held in rot / q+xs by the last prepare
@@ -74,6 +76,7 @@ struct Matrix {
         cudaSetDevice(device);
         if (stream) cudaStreamSynchronize(stream);
         x.release(); y.release(); rot.release(); xs.release(); q.release(); partials.release(); ids.release();
+        ahl.release();
         if (d_packed) cudaFree(d_packed);
         if (d_norms) cudaFree(d_norms);
         if (d_norms8) cudaFree(d_norms8);
@@ -82,6 +85,7 @@ struct Matrix {
         if (d_frag) cudaFree(d_frag);
         if (d_w8) cudaFree(d_w8);
         if (d_nsT) cudaFree(d_nsT);
+        if (d_whl) cudaFree(d_whl);
         if (d_normsF) cudaFree(d_normsF);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -276,6 +280,33 @@ bool sdot_multiply_to(Matrix *m, const int8_t *q, const float *xs, int batch, fl
     return true;
 }
 
+// FP32 mode, y[batch][out] from rotated activations: the tensor-core GEMM from
+// kGemmMinRows rows on (bf16 hi/lo weights made at the first such call; the
+// activations split here unless a_hilo already holds them), the GEMV otherwise.
+bool f32_multiply(Matrix *m, const float *rot, int batch, float *y, cudaStream_t st,
+                  const uint16_t *a_hilo = nullptr) {
+    const CQDevice &w = m->w;
+    if (batch < kGemmMinRows || !gemm_f32_supported(w.storage_bits, w.padded))
+        return launch_gemv_f32(w, rot, batch, y, w.out, st);
+    if (!m->d_whl) {
+        const cudaError_t e = cudaMalloc(&m->d_whl, sizeof(uint16_t) * gemm_f32_weight_elems(w.out, w.padded));
+        if (e != cudaSuccess) {
+            m->d_whl = nullptr;
+            set_error(std::string("prefill weight allocation failed: ") + cudaGetErrorString(e));
+            return false;
+        }
+        if (!gemm_f32_prepare(w.packed, w.norms, w.out, w.groups, w.group, w.storage_bits, w.rowbytes, w.padded,
+                              w.lut, m->d_whl, st))
+            return false;
+    }
+    if (!a_hilo) {
+        if (!m->ahl.reserve(2 * (size_t)batch * w.padded)) return false;
+        if (!launch_split_bf16(rot, (long long)batch * w.padded, m->ahl.ptr, st)) return false;
+        a_hilo = m->ahl.ptr;
+    }
+    return launch_gemm_f32x3(a_hilo, batch, m->d_whl, w.out, w.padded, y, w.out, st);
+}
+
 bool run_linear_device(Matrix *m, const float *x, float *y, int batch, cudaStream_t st, int32_t *partials) {
     m->prepared = 0;
     if (batch <= 0) return true;
@@ -283,7 +314,7 @@ bool run_linear_device(Matrix *m, const float *x, float *y, int batch, cudaStrea
     if (!m->sdot) {
         if (!m->rot.reserve((size_t)batch * w.padded)) return false;
         if (!launch_rotate(w, x, batch, m->rot.ptr, st)) return false;
-        return launch_gemv_f32(w, m->rot.ptr, batch, y, w.out, st);
+        return f32_multiply(m, m->rot.ptr, batch, y, st);
     }
     if (!m->q.reserve((size_t)batch * w.padded) || !m->xs.reserve((size_t)batch * w.groups)) return false;
     if (!launch_quantize(w, x, batch, m->q.ptr, m->xs.ptr, st)) return false;
@@ -419,6 +450,14 @@ bool multiply_many(Matrix *const *ms, int count, float *const *ys, int batch, cu
         // prefill-sized batches: one tensor-core GEMM per matrix on the shared input
         for (int i = 0; i < count; ++i)
             if (!sdot_multiply(ms[i], m0->q.ptr, m0->xs.ptr, batch, ys[i], nullptr, st)) return false;
+        return true;
+    }
+    if (!i8 && batch >= kGemmMinRows && gemm_f32_supported(w.storage_bits, w.padded)) {
+        // FP32 prefill-sized batches: the activations split once, one GEMM per matrix
+        if (!m0->ahl.reserve(2 * (size_t)batch * w.padded)) return false;
+        if (!launch_split_bf16(m0->rot.ptr, (long long)batch * w.padded, m0->ahl.ptr, st)) return false;
+        for (int i = 0; i < count; ++i)
+            if (!f32_multiply(ms[i], m0->rot.ptr, batch, ys[i], st, m0->ahl.ptr)) return false;
         return true;
     }
     const int cap = gemv_max_rows(w.bits, w.group, w.groups, i8);
@@ -624,7 +663,7 @@ static int multiply_device(void *handle, float *y, int batch, void *stream, bool
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const nb200::CQDevice &w = m->w;
     bool ok = sdot ? nb200::sdot_multiply(m, m->q.ptr, m->xs.ptr, batch, y, nullptr, st)
-                   : nb200::launch_gemv_f32(w, m->rot.ptr, batch, y, w.out, st);
+                   : nb200::f32_multiply(m, m->rot.ptr, batch, y, st);
     return ok ? 0 : -1;
 }
 

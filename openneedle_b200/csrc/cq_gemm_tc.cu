@@ -22,6 +22,7 @@
 // All waits are bounded; on timeout the CTA raises the device fault flag.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_bf16.h>
 
 #include <algorithm>
 #include <cstring>
@@ -447,6 +448,163 @@ bool make_map(CUtensorMap *map, const void *base, int rows, int cols, int box_ro
     return true;
 }
 
+// ---------------------------------------------------------------------------
+// FP32-mode prefill GEMM: y[m][r] = sum_k W'[r][k] * rot[m][k] with
+// W'[r][k] = half(norm[r, k / G]) * lut[idx[r][k]] (needle2/csrc/cq.cpp:75-109;
+// the per-group norm folded into the weights, a reassociation well inside the
+// FP32 tolerance).  Operands are split into bf16 pairs, v = hi + lo with
+// hi = bf16(v) and lo = bf16(v - hi), and each K step issues three
+// kind::f16 MMAs, A_hi B_hi + A_lo B_hi + A_hi B_lo, into one f32 accumulator
+// (about 2^-16 relative error per product; bf16 keeps FP32's exponent range).
+// 128 x 256 tiles, K = 64 (one 128-byte row of bf16) per stage, two stages of
+// 96 KB; warp 0 issues the TMA loads, warp 1 the MMAs, warps 2-5 read the
+// accumulator (32 rows each) and store y.
+constexpr int kFBM = 128, kFBN = 256, kFBK = 64;
+constexpr int kFStages = 2;
+constexpr int kFPartA = kFBM * kFBK * 2, kFPartB = kFBN * kFBK * 2;   // bytes of one bf16 part
+constexpr int kFStageBytes = 2 * kFPartA + 2 * kFPartB;               // 96 KB
+constexpr size_t kFSmem = (size_t)kFStages * kFStageBytes + 1024;
+constexpr int kFThreads = 6 * 32;
+
+struct GemmF32Args {
+    int M, N, ksteps, ldy;
+    float *y;
+};
+
+__global__ void __launch_bounds__(kFThreads, 1)
+    cq_gemm_f32x3_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
+                         const __grid_constant__ CUtensorMap tbh, const __grid_constant__ CUtensorMap tbl,
+                         const __grid_constant__ GemmF32Args a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t full[kFStages], empty[kFStages], dfull;
+    __shared__ uint32_t tmem_s;
+    __shared__ volatile int abort_flag;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int m0 = blockIdx.x * kFBM, n0 = blockIdx.y * kFBN;
+    const int S = a.ksteps;
+
+    if (warp == 1) tc::alloc(&tmem_s, 256);
+    if (tid == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < kFStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&dfull, 1);
+        fence_barrier_init();
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = tmem_s;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            pdl_wait();
+            for (int k = 0; k < S && !abort_flag; ++k) {
+                const int s = k % kFStages;
+                if (k >= kFStages && !gwait(&empty[s], (uint32_t)((k / kFStages) - 1) & 1, &abort_flag)) break;
+                uint8_t *st = smem + (size_t)s * kFStageBytes;
+                mbar_arrive_expect_tx(&full[s], kFStageBytes);
+                const int x = k * kFBK * 2;   // byte column of this K step
+                tma_load_2d(st, &tah, x, m0, &full[s]);
+                tma_load_2d(st + kFPartA, &tal, x, m0, &full[s]);
+                tma_load_2d(st + 2 * kFPartA, &tbh, x, n0, &full[s]);
+                tma_load_2d(st + 2 * kFPartA + kFPartB, &tbl, x, n0, &full[s]);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = tc::idesc_bf16(kFBM, kFBN);
+            for (int k = 0; k < S && !abort_flag; ++k) {
+                const int s = k % kFStages;
+                if (!gwait(&full[s], (uint32_t)(k / kFStages) & 1, &abort_flag)) break;
+                tc::fence_after();
+                const uint32_t ah = smem_addr(smem + (size_t)s * kFStageBytes), al = ah + kFPartA;
+                const uint32_t bh = ah + 2 * kFPartA, bl = bh + kFPartB;
+#pragma unroll
+                for (int kk = 0; kk < kFBK / 16; ++kk) {   // 16 bf16 = 32 bytes per MMA
+                    const uint32_t o = kk * 32;
+                    tc::mma_bf16_ss(tmem, sw128_desc(ah + o), sw128_desc(bh + o), idesc, (k | kk) != 0);
+                    tc::mma_bf16_ss(tmem, sw128_desc(al + o), sw128_desc(bh + o), idesc, 1);
+                    tc::mma_bf16_ss(tmem, sw128_desc(ah + o), sw128_desc(bl + o), idesc, 1);
+                }
+                tc::commit(&empty[s]);
+            }
+            tc::commit(&dfull);
+        }
+        __syncwarp();
+    } else {
+        // warps 2-5: TMEM lanes 32 (warp % 4) .. +31 = tile rows
+        const int q = warp & 3;
+        const int row = m0 + 32 * q + lane;
+        const bool ok = gwait(&dfull, 0, &abort_flag);
+        tc::fence_after();
+        if (ok) {
+            const bool vec = (a.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+            float *yr = a.y + (size_t)min(row, a.M - 1) * a.ldy + n0;
+            for (int c = 0; c < kFBN / 32; ++c) {
+                uint32_t v[32];
+                tc::ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(32 * c), v);
+                tc::wait_ld();
+                if (row < a.M) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        const int col = 32 * c + j;
+                        if (vec && n0 + col + 3 < a.N) {
+                            *reinterpret_cast<float4 *>(yr + col) = make_float4(
+                                __uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                __uint_as_float(v[j + 3]));
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                if (n0 + col + e < a.N) yr[col + e] = __uint_as_float(v[j + e]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (warp == 1) tc::dealloc(tmem, 256);
+}
+
+struct Lut16 {
+    float v[16];
+};
+
+// W'[r][k] split to bf16 hi [out][padded] and lo (the next out * padded values).
+__global__ void gemm_f32_prepare_kernel(const uint8_t *__restrict__ packed, const uint16_t *__restrict__ norms,
+                                        int out, int groups, int group, int sbits, int rowbytes, int padded, Lut16 lut,
+                                        uint16_t *__restrict__ hi, uint16_t *__restrict__ lo) {
+    const long long total = (long long)out * padded;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / padded), e = (int)(i % padded);
+        const uint8_t *rp = packed + (size_t)r * rowbytes;
+        const int idx = sbits == 4 ? ((rp[e >> 1] >> (4 * (e & 1))) & 15) : ((rp[e >> 2] >> (2 * (e & 3))) & 3);
+        const float w = __fmul_rn(half_bits_to_float(norms[(size_t)r * groups + e / group]), lut.v[idx]);
+        const __nv_bfloat16 h = __float2bfloat16_rn(w);
+        hi[i] = __bfloat16_as_ushort(h);
+        lo[i] = __bfloat16_as_ushort(__float2bfloat16_rn(__fsub_rn(w, __bfloat162float(h))));
+    }
+}
+
+// rot[n] -> bf16 hi[n], lo[n]
+__global__ void split_bf16_kernel(const float *__restrict__ x, long long n, uint16_t *__restrict__ hi,
+                                  uint16_t *__restrict__ lo) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        const __nv_bfloat16 h = __float2bfloat16_rn(v);
+        hi[i] = __bfloat16_as_ushort(h);
+        lo[i] = __bfloat16_as_ushort(__float2bfloat16_rn(__fsub_rn(v, __bfloat162float(h))));
+    }
+}
+
 }  // namespace
 
 size_t gemm_w8_bytes(int out, int padded) { return (size_t)out * padded; }
@@ -519,6 +677,64 @@ bool launch_gemm_i8_multi(const int8_t *q, const float *xs, int M, const int8_t 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, cq_gemm_i8_kernel, ta, tb, args));
+    return true;
+}
+
+bool gemm_f32_supported(int storage_bits, int padded) {
+    return (storage_bits == 2 || storage_bits == 4) && padded % kFBK == 0 && padded >= kFBK;
+}
+
+size_t gemm_f32_weight_elems(int out, int padded) { return 2 * (size_t)out * padded; }
+
+bool gemm_f32_prepare(const uint8_t *packed, const uint16_t *norms, int out, int groups, int group, int storage_bits,
+                      int rowbytes, int padded, const float lut[16], uint16_t *w_hilo, cudaStream_t st) {
+    Lut16 l;
+    std::memcpy(l.v, lut, sizeof(l.v));
+    gemm_f32_prepare_kernel<<<148 * 8, 256, 0, st>>>(packed, norms, out, groups, group, storage_bits, rowbytes, padded,
+                                                    l, w_hilo, w_hilo + (size_t)out * padded);
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+}
+
+bool launch_split_bf16(const float *x, long long n, uint16_t *hilo, cudaStream_t st) {
+    if (n <= 0) return true;
+    split_bf16_kernel<<<148 * 4, 256, 0, st>>>(x, n, hilo, hilo + n);
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+}
+
+bool launch_gemm_f32x3(const uint16_t *a_hilo, int M, const uint16_t *w_hilo, int N, int padded, float *y, int ldy,
+                       cudaStream_t st) {
+    if (M <= 0 || N <= 0) return true;
+    if (padded % kFBK) {
+        set_error("FP32 prefill GEMM requires the padded width to be a multiple of 64");
+        return false;
+    }
+    const size_t an = (size_t)M * padded, wn = (size_t)N * padded;
+    CUtensorMap tah, tal, tbh, tbl;
+    // bf16 rows seen as bytes: 2 * padded bytes per row, 128-byte (64-element) boxes
+    if (!make_map(&tah, a_hilo, M, 2 * padded, kFBM) || !make_map(&tal, a_hilo + an, M, 2 * padded, kFBM) ||
+        !make_map(&tbh, w_hilo, N, 2 * padded, kFBN) || !make_map(&tbl, w_hilo + wn, N, 2 * padded, kFBN))
+        return false;
+    GemmF32Args args{M, N, padded / kFBK, ldy, y};
+    static bool configured[64] = {};
+    int dev = 0;
+    NB_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+        NB_CUDA_TRY(cudaFuncSetAttribute(cq_gemm_f32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFSmem));
+        if (dev >= 0 && dev < 64) configured[dev] = true;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((M + kFBM - 1) / kFBM, (N + kFBN - 1) / kFBN);
+    cfg.blockDim = dim3(kFThreads);
+    cfg.dynamicSmemBytes = kFSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, cq_gemm_f32x3_kernel, tah, tal, tbh, tbl, args));
     return true;
 }
 

@@ -90,6 +90,16 @@ bool launch_gemm_i8(const int8_t *q, const float *xs, int M, const int8_t *w8, c
 constexpr int kMaxGemmOutputs = 8;
 bool launch_gemm_i8_multi(const int8_t *q, const float *xs, int M, const int8_t *w8, const float *nsT, int N,
                           int padded, int groups, float *const *dsts, int ndst, int ldy, cudaStream_t st);
+// FP32-mode prefill GEMM on tcgen05 (cq_gemm_tc.cu): weights W' = half(norm) *
+// lut[idx] split once to bf16 hi/lo [2][out][padded], activations split per
+// call, three bf16 MMAs per K step into an f32 accumulator.
+bool gemm_f32_supported(int storage_bits, int padded);
+size_t gemm_f32_weight_elems(int out, int padded);
+bool gemm_f32_prepare(const uint8_t *packed, const uint16_t *norms, int out, int groups, int group, int storage_bits,
+                      int rowbytes, int padded, const float lut[16], uint16_t *w_hilo, cudaStream_t st);
+bool launch_split_bf16(const float *x, long long n, uint16_t *hilo, cudaStream_t st);
+bool launch_gemm_f32x3(const uint16_t *a_hilo, int M, const uint16_t *w_hilo, int N, int padded, float *y, int ldy,
+                       cudaStream_t st);
 // Activation rows from which int8 products run as the tensor-core GEMM.
 constexpr int kGemmMinRows = 64;
 

@@ -51,3 +51,24 @@ def test_prefill_gemm_matches_gemv_at_config3_width(native, bits):
     torch.cuda.synchronize()
     np.testing.assert_array_equal(y_gemm.cpu().numpy(), y_gemv.cpu().numpy())
     assert native.device_fault() == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits", [2, 4])
+@pytest.mark.parametrize("n,k,m,group", [(300, 512, 64, 128), (301, 512, 130, 128), (1000, 1024, 257, 128),
+                                         (2048, 512, 2048, 128), (520, 640, 96, 64)])
+def test_fp32_prefill_gemm_matches_oracle(native, oracle_lib, bits, n, k, m, group):
+    """FP32 mode from 64 rows on runs the bf16 hi/lo tensor-core GEMM; it must stay
+    within the FP32 tolerance of the reference's per-group FP32 sums."""
+    from openneedle_b200.quantize import synthetic_matrix
+    from util import FP32_REL_TOL, rel_err
+    packed, norms, cb = synthetic_matrix(n, k, bits, group, seed=900 + n + bits)
+    q = native.NativeCQ(packed, norms, (n, k), bits, group, cb)
+    x = np.random.default_rng(m + k + 1).normal(size=(m, k)).astype(np.float32)
+    x[5] = 0
+    y = q.linear(x)
+    ref = oracle_lib.cq_linear(packed, norms, (n, k), bits, group, cb, x)
+    assert rel_err(y, ref) <= FP32_REL_TOL
+    # rows are independent of the batch they run in: the GEMV's result for the
+    # first 16 rows agrees within the same tolerance
+    assert rel_err(y[:16], q.linear(x[:16])) <= FP32_REL_TOL
