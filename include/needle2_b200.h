@@ -134,6 +134,16 @@ int needle2_b200_ipc_export(const void *ptr, void *handle64, unsigned long long 
 int needle2_b200_ipc_import(const void *handle64, unsigned long long offset, void **ptr);
 int needle2_b200_ipc_close(void *ptr);
 
+/* The engine's fake activation quantiser for activation_bits = bits, in place
+ * on x[rows][dim], each row separately: a = max|x|, unchanged when a is 0,
+ * otherwise x = clamp(round_half_even(x / (a / m)), -m - 1, m) * (a / m) with
+ * m = 2^(bits-1) - 1.  Replaces activation_quant, needle2/csrc/engine.cpp:185-191
+ * (applied before the QKVG, out_proj, engram and LM-head matmuls,
+ * engine.cpp:769,992,1024,1041).  bits 0 leaves x unchanged.  Device pointer on
+ * a stream / host pointer (synchronous). */
+int needle2_b200_activation_quant_device(float *x, int rows, int dim, int bits, void *stream);
+int needle2_b200_activation_quant(float *x, int rows, int dim, int bits);
+
 /* SDOT internals the reference never exports (its per-group int32 dots stay
  * inside SdotCQ::row, needle2/csrc/sdot.cpp:142-149): partials[batch][out][groups]
  * int32, q[batch][padded] int8 in natural element order, scales[batch][groups];

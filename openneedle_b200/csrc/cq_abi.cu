@@ -696,6 +696,36 @@ int needle2_sdot_multiply_gather_device(void *h, float *const *dsts, int ndst, i
                : -1;
 }
 
+int needle2_b200_activation_quant_device(float *x, int rows, int dim, int bits, void *stream) {
+    nb200::clear_error();
+    if (rows < 0 || dim < 0 || bits < 0 || bits > 16 || (rows && dim && !x)) {
+        nb200::set_error("activation_quant: bad arguments");
+        return -1;
+    }
+    return nb200::launch_activation_quant(x, rows, dim, bits, static_cast<cudaStream_t>(stream)) ? 0 : -1;
+}
+
+int needle2_b200_activation_quant(float *x, int rows, int dim, int bits) {
+    nb200::clear_error();
+    if (rows < 0 || dim < 0 || bits < 0 || bits > 16 || (rows && dim && !x)) {
+        nb200::set_error("activation_quant: bad arguments");
+        return -1;
+    }
+    if (!rows || !dim || !bits) return 0;
+    const size_t bytes = sizeof(float) * (size_t)rows * dim;
+    float *d = nullptr;
+    if (cudaMalloc(&d, bytes) != cudaSuccess) { nb200::set_error("cudaMalloc failed"); return -1; }
+    bool ok = cudaMemcpy(d, x, bytes, cudaMemcpyHostToDevice) == cudaSuccess;
+    if (!ok) nb200::set_error("activation_quant: host-to-device copy failed");
+    ok = ok && nb200::launch_activation_quant(d, rows, dim, bits, nullptr);
+    if (ok && cudaMemcpy(x, d, bytes, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        nb200::set_error("activation_quant: device-to-host copy failed");
+        ok = false;
+    }
+    cudaFree(d);
+    return ok ? 0 : -1;
+}
+
 int needle2_b200_device_fault() { return nb200::read_and_clear_gemv_fault(); }
 
 int needle2_cq_geometry(void *handle, int *g) {

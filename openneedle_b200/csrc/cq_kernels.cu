@@ -764,4 +764,37 @@ bool launch_rows(const CQDevice &w, const int64_t *ids, int count, float *y, cud
     return true;
 }
 
+namespace {
+
+// One warp per row: a = max|x|; unchanged when a == 0; otherwise
+// x = clamp(round_half_even(x / scale), -maxq - 1, maxq) * scale with
+// scale = a / maxq, maxq = 2^(bits-1) - 1 (needle2/csrc/engine.cpp:185-191;
+// IEEE divide and multiply, so the result is the reference's bit for bit).
+__global__ void activation_quant_kernel(float *__restrict__ x, int rows, int dim, int bits) {
+    const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    float *xr = x + (size_t)warp * dim;
+    float a = 0.f;
+    for (int i = lane; i < dim; i += 32) a = fmaxf(a, fabsf(xr[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if (!(a > 0.f)) return;
+    const int maxq = (1 << (bits - 1)) - 1;
+    const float scale = __fdiv_rn(a, (float)maxq), hi = (float)maxq, lo = (float)(-maxq - 1);
+    for (int i = lane; i < dim; i += 32) {
+        const float r = rintf(__fdiv_rn(xr[i], scale));
+        xr[i] = __fmul_rn(fmaxf(lo, fminf(hi, r)), scale);
+    }
+}
+
+}  // namespace
+
+bool launch_activation_quant(float *x, int rows, int dim, int bits, cudaStream_t st) {
+    if (rows <= 0 || dim <= 0 || bits == 0) return true;
+    const long long threads = (long long)rows * 32;
+    activation_quant_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(x, rows, dim, bits);
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+}
+
 }  // namespace nb200

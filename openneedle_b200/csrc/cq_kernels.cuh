@@ -40,6 +40,8 @@ bool launch_gemv_i8(const CQDevice &w, const int8_t *q, const float *xs, int M, 
 bool launch_rows(const CQDevice &w, const int64_t *ids, int count, float *y, cudaStream_t s);
 
 bool gemv_fast_path(const CQDevice &w);
+// The engine's fake activation quantiser, in place on x[rows][dim] (per row).
+bool launch_activation_quant(float *x, int rows, int dim, int bits, cudaStream_t st);
 
 struct GemvBatch;
 // A one-matrix GEMV batch description of w (activations and outputs unset).

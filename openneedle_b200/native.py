@@ -313,6 +313,19 @@ def device_fault() -> int:
     return int(_library().needle2_b200_device_fault())
 
 
+def activation_quant(x, bits: int = 8):
+    """The engine's fake activation quantiser (needle2/csrc/engine.cpp:185-191),
+    row by row on a copy of x[rows][dim] (a 1-D x is one row), on the GPU."""
+    lib = _library()
+    fn = lib.needle2_b200_activation_quant
+    fn.argtypes = [ct.c_void_p, ct.c_int, ct.c_int, ct.c_int]
+    fn.restype = ct.c_int
+    a = np.array(x, dtype=np.float32, copy=True, order="C")
+    rows, dim = (1, a.size) if a.ndim == 1 else a.shape
+    _check(fn(a.ctypes.data, int(rows), int(dim), int(bits)), "activation_quant")
+    return a
+
+
 def set_int8_gemv(kind: int) -> int:
     """Select the int8 GEMV kernel process-wide (0 automatic, 1 diagonal warp
     MMA, 2 tcgen05, 3 fragment-order warp MMA); returns the previous setting."""
