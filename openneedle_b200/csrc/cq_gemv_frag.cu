@@ -114,9 +114,10 @@ __host__ __device__ inline size_t frag_smem(int padded, int groups, int nb, int 
 // MT: exact activation rows for MT <= 4, an upper bound (rows in b.M) for 8 / 16.
 // PF: ring slots per warp.  NT: threads per CTA.  DBG: also write the int32
 // group dots to b.partials.
-template <int BITS, int G, int MT, bool SPLIT, int PF, int NT, bool DBG>
+template <int BITS, int G, int MT, bool SPLIT, int PF, int NT, bool DBG, bool PAIR>
 __global__ void __launch_bounds__(NT, 1)
     cq_gemv_frag_kernel(const __grid_constant__ GemvBatch b, const int total_tiles) {
+    static_assert(!PAIR || PF % 2 == 0, "paired groups need an even ring");
     constexpr int kFragThreads = NT, kFragWarps = NT / 32;
     using Geo = FragGeo<BITS, G>;
     constexpr int KK = Geo::KK, LW = Geo::LW, LB = Geo::LB, SLOT = Geo::SLOT;
@@ -162,30 +163,39 @@ __global__ void __launch_bounds__(NT, 1)
             ln = reinterpret_cast<const uint32_t *>(b.mat[lmat].normsF) + lt * gpr * 8 + g;
         }
     };
+    // one commit group per group block, or per two consecutive blocks of a tile
+    // (PAIR: the row's group count is even) in two consecutive slots
+    constexpr int GB = PAIR ? 2 : 1;        // group blocks per commit group
+    constexpr int AHEAD = PF / GB - 1;      // commit groups in flight ahead of the consumer
     auto issue = [&]() {
         if (ltile < s1) {
-            uint8_t *dst = ring + (size_t)lslot * SLOT;
-            if constexpr (LB >= 16) {
 #pragma unroll
-                for (int c = 0; c < LB / 16; ++c) cp_async<16>(dst + lane * LB + 16 * c, lw + 16 * c);
-            } else {
-                cp_async<LB>(dst + lane * LB, lw);
+            for (int h = 0; h < GB; ++h) {
+                uint8_t *dst = ring + (size_t)(lslot + h) * SLOT;
+                if constexpr (LB >= 16) {
+#pragma unroll
+                    for (int c = 0; c < LB / 16; ++c)
+                        cp_async<16>(dst + lane * LB + 16 * c, lw + h * 32 * LB + 16 * c);
+                } else {
+                    cp_async<LB>(dst + lane * LB, lw + h * 32 * LB);
+                }
+                cp_async<4>(dst + 32 * LB + 4 * lane, ln + 8 * h);
             }
-            cp_async<4>(dst + 32 * LB + 4 * lane, ln);
-            lw += 32 * LB;
-            ln += 8;
-            if (++lj == gpr) {
+            lw += GB * 32 * LB;
+            ln += 8 * GB;
+            lj += GB;
+            if (lj == gpr) {
                 lj = 0;
                 ltile += kFragWarps;
                 lseek();
             }
         }
         cp_async_commit();
-        lslot = lslot + 1 == PF ? 0 : lslot + 1;
+        lslot = lslot + GB == PF ? 0 : lslot + GB;
     };
     lseek();
     // the weights do not depend on the preceding kernel: start streaming them first
-    for (int p = 0; p < PF - 1; ++p) issue();
+    for (int p = 0; p < AHEAD; ++p) issue();
 
     pdl_wait();
     // one thread per 32-wide K step of one activation row: the natural element
@@ -229,11 +239,8 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
         for (int q = 0; q < NP; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
         const uint8_t *ab = abase;
-        for (int cj = 0; cj < gpr; ++cj, ab += KK * 32) {
-            issue();                        // the group PF - 1 ahead (its slot was consumed last iteration)
-            cp_async_wait<PF - 1>();        // this group's block has landed
-            const uint8_t *slot = ring + (size_t)cslot * SLOT;
-            cslot = cslot + 1 == PF ? 0 : cslot + 1;
+        // one group: its block from ring slot `slot`, activations at `ab`
+        auto group = [&](const uint8_t *slot, int cj, const uint8_t *ab) {
             uint32_t wv[LW];
             if constexpr (LB >= 16) {
     #pragma unroll
@@ -310,6 +317,13 @@ __global__ void __launch_bounds__(NT, 1)
                     }
                 }
             }
+                };
+        for (int cj = 0; cj < gpr; cj += GB, ab += GB * KK * 32) {
+            issue();                        // AHEAD commit groups ahead (their slots were consumed last iteration)
+            cp_async_wait<AHEAD>();         // this commit group's blocks have landed
+#pragma unroll
+            for (int h = 0; h < GB; ++h) group(ring + (size_t)(cslot + h) * SLOT, cj + h, ab + h * KK * 32);
+            cslot = cslot + GB == PF ? 0 : cslot + GB;
         }
         const GemvMatrix &mat = b.mat[cmat];
 #pragma unroll
@@ -325,9 +339,9 @@ __global__ void __launch_bounds__(NT, 1)
     cp_async_wait<0>();
 }
 
-template <int BITS, int G, int MT, bool SPLIT, int PF, int NT, bool DBG = false>
+template <int BITS, int G, int MT, bool SPLIT, int PF, int NT, bool DBG = false, bool PAIR = false>
 bool launch_frag_pf(const GemvBatch &b, size_t smem, cudaStream_t st) {
-    auto kernel = cq_gemv_frag_kernel<BITS, G, MT, SPLIT, PF, NT, DBG>;
+    auto kernel = cq_gemv_frag_kernel<BITS, G, MT, SPLIT, PF, NT, DBG, PAIR>;
     static bool configured[64] = {};
     static int sms[64] = {};
     int dev = 0;
@@ -383,8 +397,11 @@ bool launch_frag(const GemvBatch &b, cudaStream_t st) {
     }
     if constexpr (MT <= 4 && G <= 128) {
         const size_t wide = frag_smem(b.padded, b.groups, nb, Geo::SLOT, 4, 32);
-        if (tiles > 148 * 16 && wide <= (size_t)kFragMaxSmem)
+        if (tiles > 148 * 16 && wide <= (size_t)kFragMaxSmem) {
+            // an even group count: two group blocks per copy batch
+            if (b.groups % 2 == 0) return launch_frag_pf<BITS, G, MT, SPLIT, 4, 1024, false, true>(b, wide, st);
             return launch_frag_pf<BITS, G, MT, SPLIT, 4, 1024>(b, wide, st);
+        }
     }
     const size_t full = frag_smem(b.padded, b.groups, nb, Geo::SLOT, Geo::PF, 16);
     if (full <= (size_t)kFragMaxSmem) return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF, 512>(b, full, st);
