@@ -378,7 +378,8 @@ bool launch_frag_pf(const GemvBatch &b, size_t smem, cudaStream_t st) {
 // with few tiles uses 8 warps per CTA (spreading them over all SMs, two CTAs per
 // SM), a large one 32 warps with a 4-slot ring (measured fastest for one to
 // four activation rows and groups up to 128; 64 registers per thread), else 16
-// warps with the full ring, or half of it when shared memory is short.
+// warps with the full ring, or half of it when shared memory is short.  With an
+// even group count (and ring), copies go out two group blocks at a time.
 template <int BITS, int G, int MT, bool SPLIT>
 bool launch_frag(const GemvBatch &b, cudaStream_t st) {
     using Geo = FragGeo<BITS, G>;
@@ -391,20 +392,29 @@ bool launch_frag(const GemvBatch &b, cudaStream_t st) {
     }
     int tiles = 0;
     for (int j = 0; j < b.nmat; ++j) tiles += (b.mat[j].out + 15) / 16;
+    const bool pair = b.groups % 2 == 0;   // two group blocks per copy batch
     if (tiles <= 148 * 8) {
         const size_t narrow = frag_smem(b.padded, b.groups, nb, Geo::SLOT, Geo::PF, 8);
-        if (narrow <= (size_t)kFragMaxSmem) return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF, 256>(b, narrow, st);
+        if (narrow <= (size_t)kFragMaxSmem) {
+            if constexpr (Geo::PF % 2 == 0)
+                if (pair) return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF, 256, false, true>(b, narrow, st);
+            return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF, 256>(b, narrow, st);
+        }
     }
     if constexpr (MT <= 4 && G <= 128) {
         const size_t wide = frag_smem(b.padded, b.groups, nb, Geo::SLOT, 4, 32);
         if (tiles > 148 * 16 && wide <= (size_t)kFragMaxSmem) {
             // an even group count: two group blocks per copy batch
-            if (b.groups % 2 == 0) return launch_frag_pf<BITS, G, MT, SPLIT, 4, 1024, false, true>(b, wide, st);
+            if (pair) return launch_frag_pf<BITS, G, MT, SPLIT, 4, 1024, false, true>(b, wide, st);
             return launch_frag_pf<BITS, G, MT, SPLIT, 4, 1024>(b, wide, st);
         }
     }
     const size_t full = frag_smem(b.padded, b.groups, nb, Geo::SLOT, Geo::PF, 16);
-    if (full <= (size_t)kFragMaxSmem) return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF, 512>(b, full, st);
+    if (full <= (size_t)kFragMaxSmem) {
+        if constexpr (Geo::PF % 2 == 0)
+            if (pair) return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF, 512, false, true>(b, full, st);
+        return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF, 512>(b, full, st);
+    }
     return launch_frag_pf<BITS, G, MT, SPLIT, Geo::PF / 2, 512>(
         b, frag_smem(b.padded, b.groups, nb, Geo::SLOT, Geo::PF / 2, 16), st);
 }
