@@ -50,6 +50,53 @@ struct Scratch {
     }
 };
 
+// Page-locked host staging for copies to or from pageable user buffers: one
+// transfer of the whole batch instead of one staged transfer per matrix.
+struct PinnedStage {
+    float *ptr = nullptr;
+    size_t cap = 0;
+    bool reserve(size_t n) {
+        if (n <= cap) return true;
+        if (ptr) cudaFreeHost(ptr);
+        ptr = nullptr;
+        cap = 0;
+        cudaError_t e = cudaMallocHost(&ptr, sizeof(float) * (n ? n : 1));
+        if (e != cudaSuccess) {
+            set_error(std::string("pinned staging allocation failed: ") + cudaGetErrorString(e));
+            ptr = nullptr;
+            return false;
+        }
+        cap = n;
+        return true;
+    }
+    void release() {
+        if (ptr) cudaFreeHost(ptr);
+        ptr = nullptr;
+        cap = 0;
+    }
+};
+
+// True when p is page-locked (or device/managed) memory that async copies use directly.
+inline bool is_pinned(const void *p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();   // an unregistered pointer may report an error on older drivers
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost || a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// The device's address of page-locked host memory (kernels may store to it
+// directly), or null when p is not page-locked host memory.
+inline float *mapped_host(float *p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? static_cast<float *>(a.devicePointer) : nullptr;
+}
+
 struct Matrix {
     CQDevice w{};
     bool sdot = false;
@@ -68,6 +115,7 @@ struct Matrix {
     Scratch<float> x, y, rot, xs;
     Scratch<int8_t> q;
     Scratch<uint16_t> ahl;   // FP32 mode: bf16 hi/lo activations for the prefill GEMM
+    PinnedStage hin, hout;   // host staging for pageable inputs / outputs of the host-pointer calls
     Scratch<int32_t> partials;
     Scratch<int64_t> ids;
     int prepared = 0;  // activation rows held in rot / q+xs by the last prepare
@@ -76,7 +124,7 @@ struct Matrix {
         cudaSetDevice(device);
         if (stream) cudaStreamSynchronize(stream);
         x.release(); y.release(); rot.release(); xs.release(); q.release(); partials.release(); ids.release();
-        ahl.release();
+        ahl.release(); hin.release(); hout.release();
         if (d_packed) cudaFree(d_packed);
         if (d_norms) cudaFree(d_norms);
         if (d_norms8) cudaFree(d_norms8);
@@ -503,18 +551,40 @@ bool many_host(Matrix *const *ms, int count, const float *x, float *const *ys, i
     size_t total = 0;
     for (int i = 0; i < count; ++i) total += (size_t)batch * ms[i]->w.out;
     if (!m0->x.reserve((size_t)batch * m0->w.in) || !m0->y.reserve(total)) return false;
-    NB_CUDA_TRY(cudaMemcpyAsync(m0->x.ptr, x, sizeof(float) * (size_t)batch * m0->w.in, cudaMemcpyHostToDevice, st));
+    const size_t xn = (size_t)batch * m0->w.in;
+    if (is_pinned(x)) {
+        NB_CUDA_TRY(cudaMemcpyAsync(m0->x.ptr, x, sizeof(float) * xn, cudaMemcpyHostToDevice, st));
+    } else {
+        if (!m0->hin.reserve(xn)) return false;
+        NB_CUDA_TRY(cudaStreamSynchronize(st));   // the staging buffer may still feed an earlier copy
+        std::memcpy(m0->hin.ptr, x, sizeof(float) * xn);
+        NB_CUDA_TRY(cudaMemcpyAsync(m0->x.ptr, m0->hin.ptr, sizeof(float) * xn, cudaMemcpyHostToDevice, st));
+    }
+    // page-locked outputs: the kernels store the results straight into them
     std::vector<float *> dys(count);
+    bool mapped = true;
+    for (int i = 0; i < count && mapped; ++i) mapped = (dys[i] = mapped_host(ys[i])) != nullptr;
+    if (mapped) {
+        if (!many_device(ms, count, m0->x.ptr, dys.data(), batch, st)) return false;
+        NB_CUDA_TRY(cudaStreamSynchronize(st));
+        return true;
+    }
     size_t off = 0;
     for (int i = 0; i < count; ++i) {
         dys[i] = m0->y.ptr + off;
         off += (size_t)batch * ms[i]->w.out;
     }
     if (!many_device(ms, count, m0->x.ptr, dys.data(), batch, st)) return false;
-    for (int i = 0; i < count; ++i)
-        NB_CUDA_TRY(cudaMemcpyAsync(ys[i], dys[i], sizeof(float) * (size_t)batch * ms[i]->w.out,
-                                    cudaMemcpyDeviceToHost, st));
+    // pageable outputs: one transfer of all of them into pinned staging, then host copies
+    if (!m0->hout.reserve(total)) return false;
+    NB_CUDA_TRY(cudaMemcpyAsync(m0->hout.ptr, m0->y.ptr, sizeof(float) * total, cudaMemcpyDeviceToHost, st));
     NB_CUDA_TRY(cudaStreamSynchronize(st));
+    off = 0;
+    for (int i = 0; i < count; ++i) {
+        const size_t n = (size_t)batch * ms[i]->w.out;
+        std::memcpy(ys[i], m0->hout.ptr + off, sizeof(float) * n);
+        off += n;
+    }
     return true;
 }
 
