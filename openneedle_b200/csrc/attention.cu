@@ -618,6 +618,185 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Prefill with query tiles: one CTA per (entry, KV head, tile of TQ = 128 / R
+// queries), one thread per (query, head) row holding its query in registers.
+// Blocks of 32 positions -- the union of the tile's visible sets -- are read
+// once into shared memory as floats (with their scales) and used by every query
+// of the tile; per block each row computes its 32 scores (causally masked),
+// updates its running max once, and accumulates (p * v_scale) * v.
+constexpr int kPBK = 32;
+
+// Memory row of absolute position `position` of (session s, KV head kh) for a
+// query of entry `entry` whose chunk starts at chunk_start.
+__device__ __forceinline__ RowPtr position_ptr(const AttnParams &p, int s, int kh, int position, int entry,
+                                               int chunk_start) {
+    size_t row;
+    RowPtr r;
+    if (position < p.prefix) {
+        row = (size_t)kh * p.prefix + position;
+        r.k = p.pk; r.v = p.pv; r.ks = p.pks; r.vs = p.pvs;
+    } else if (p.stage_k && position >= chunk_start) {
+        row = (size_t)kh * p.stage_rows + (size_t)entry * p.tokens + (position - chunk_start);
+        r.k = p.stage_k; r.v = p.stage_v; r.ks = p.stage_ks; r.vs = p.stage_vs;
+    } else {
+        const int slot = p.window ? (position - p.prefix) % p.window : position - p.prefix;
+        row = ((size_t)s * p.kvheads + kh) * p.cs + slot;
+        r.k = p.sk; r.v = p.sv; r.ks = p.sks; r.vs = p.svs;
+    }
+    r.k += row * p.hd;
+    r.v += row * p.hd;
+    r.ks += row;
+    r.vs += row;
+    r.run = 0;
+    return r;
+}
+
+template <int HD, int R>
+__global__ void __launch_bounds__(128) attn_prefill_tile_kernel(const AttnParams p) {
+    constexpr int TQ = 128 / R;
+    __shared__ __align__(16) float ks_f[kPBK][HD], vs_f[kPBK][HD];
+    __shared__ float kscale[kPBK], vscale[kPBK];
+    __shared__ int kpos[kPBK];
+
+    const int tile = blockIdx.x, kh = blockIdx.y, entry = blockIdx.z;
+    const int s = p.session[entry], chunk_start = p.position[entry];
+    const int tid = threadIdx.x, r = tid % R, i = tid / R;
+    const int t = tile * TQ + i;
+    const bool active = t < p.tokens;
+    const int pos = chunk_start + min(t, p.tokens - 1);
+    const int h = kh * R + r;
+    // visible set of this row: sinks [0, prefix_count) and [start, pos]
+    const int prefix_count = p.window ? min(p.prefix, pos + 1) : 0;
+    const int start = p.window ? max(p.prefix, pos - p.window + 1) : 0;
+    // the tile's union: its last query has the largest position and the latest
+    // start; its first query the earliest start
+    const int t_last = min(p.tokens - 1, tile * TQ + TQ - 1), t_first = tile * TQ;
+    const int pos_hi = chunk_start + t_last, pos_lo = chunk_start + t_first;
+    const int sinks = p.window ? min(p.prefix, pos_hi + 1) : 0;
+    const int ustart = p.window ? max(p.prefix, pos_lo - p.window + 1) : 0;
+    const int nsink = sinks, nrange = max(0, pos_hi - max(ustart, nsink) + 1);
+    const int range0 = max(ustart, nsink);
+    const int total = nsink + nrange;   // union positions: [0, nsink) then range0 ...
+
+    float q[HD];
+    const float *qp = p.q + ((size_t)(entry * p.tokens + min(t, p.tokens - 1)) * p.heads + h) * HD;
+#pragma unroll
+    for (int d = 0; d < HD; d += 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(qp + d);
+        q[d] = v.x; q[d + 1] = v.y; q[d + 2] = v.z; q[d + 3] = v.w;
+    }
+    float acc[HD];
+#pragma unroll
+    for (int d = 0; d < HD; ++d) acc[d] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    const float inv_sqrt = p.inv_sqrt_hd;
+
+    for (int b0 = 0; b0 < total; b0 += kPBK) {
+        const int nb = min(kPBK, total - b0);
+        __syncthreads();   // the previous block is no longer read
+        // 128 threads: row j = tid / 4 of the block, 16 dims (HD = 64) or 32 (HD = 128) each
+        {
+            const int j = tid >> 2, part = tid & 3;
+            if (j < nb) {
+                const int u = b0 + j;
+                const int position = u < nsink ? u : range0 + (u - nsink);
+                const RowPtr rp = position_ptr(p, s, kh, position, entry, chunk_start);
+                constexpr int PER = HD / 4;
+#pragma unroll
+                for (int c = 0; c < PER; c += 16) {
+                    const uint4 kw = *reinterpret_cast<const uint4 *>(rp.k + part * PER + c);
+                    const uint4 vw = *reinterpret_cast<const uint4 *>(rp.v + part * PER + c);
+                    const uint32_t kwords[4] = {kw.x, kw.y, kw.z, kw.w}, vwords[4] = {vw.x, vw.y, vw.z, vw.w};
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) {
+                        float2 lo, hi;
+                        i8x4_pairs(kwords[w], lo, hi);
+                        float *kd = &ks_f[j][part * PER + c + 4 * w];
+                        kd[0] = lo.x; kd[1] = lo.y; kd[2] = hi.x; kd[3] = hi.y;
+                        i8x4_pairs(vwords[w], lo, hi);
+                        float *vd = &vs_f[j][part * PER + c + 4 * w];
+                        vd[0] = lo.x; vd[1] = lo.y; vd[2] = hi.x; vd[3] = hi.y;
+                    }
+                }
+                if (part == 0) {
+                    kscale[j] = *rp.ks;
+                    vscale[j] = *rp.vs;
+                    kpos[j] = position;
+                }
+            }
+        }
+        __syncthreads();
+        if (!active) continue;
+        float sc[kPBK];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kPBK; ++j) {
+            float v = -INFINITY;
+            if (j < nb) {
+                const int position = kpos[j];
+                const bool vis = position <= pos && (position < prefix_count || position >= start);
+                if (vis) {
+                    float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+                    for (int d = 0; d < HD; d += 4) {
+                        const float4 kv = *reinterpret_cast<const float4 *>(&ks_f[j][d]);
+                        d0 = fmaf(q[d], kv.x, d0);
+                        d1 = fmaf(q[d + 1], kv.y, d1);
+                        d0 = fmaf(q[d + 2], kv.z, d0);
+                        d1 = fmaf(q[d + 3], kv.w, d1);
+                    }
+                    v = __fmul_rn(__fmul_rn(d0 + d1, kscale[j]), inv_sqrt);
+                }
+            }
+            sc[j] = v;
+            mx = fmaxf(mx, v);
+        }
+        if (mx == -INFINITY) continue;   // nothing of this block is visible to this row
+        const float mn = fmaxf(m, mx);
+        const float corr = m == -INFINITY ? 0.f : __expf(m - mn);
+        m = mn;
+        l *= corr;
+#pragma unroll
+        for (int d = 0; d < HD; ++d) acc[d] *= corr;
+#pragma unroll
+        for (int j = 0; j < kPBK; ++j) {
+            if (sc[j] == -INFINITY) continue;
+            const float pr = __expf(sc[j] - mn);
+            l += pr;
+            const float w = pr * vscale[j];
+#pragma unroll
+            for (int d = 0; d < HD; d += 4) {
+                const float4 vv = *reinterpret_cast<const float4 *>(&vs_f[j][d]);
+                acc[d] = fmaf(w, vv.x, acc[d]);
+                acc[d + 1] = fmaf(w, vv.y, acc[d + 1]);
+                acc[d + 2] = fmaf(w, vv.z, acc[d + 2]);
+                acc[d + 3] = fmaf(w, vv.w, acc[d + 3]);
+            }
+        }
+    }
+    if (active) {
+        float *op = p.out + ((size_t)(entry * p.tokens + t) * p.heads + h) * HD;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+        for (int d = 0; d < HD; d += 4)
+            *reinterpret_cast<float4 *>(op + d) =
+                make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv, acc[d + 3] * inv);
+    }
+}
+
+template <int HD>
+bool launch_prefill_tile(const AttnParams &p, int entries, int R, cudaStream_t st) {
+    const int tq = 128 / R;
+    const dim3 grid((p.tokens + tq - 1) / tq, p.kvheads, entries);
+    switch (R) {
+        case 1: attn_prefill_tile_kernel<HD, 1><<<grid, 128, 0, st>>>(p); return true;
+        case 2: attn_prefill_tile_kernel<HD, 2><<<grid, 128, 0, st>>>(p); return true;
+        case 4: attn_prefill_tile_kernel<HD, 4><<<grid, 128, 0, st>>>(p); return true;
+        default: return false;
+    }
+}
+
 template <int HD>
 bool launch_stream(const AttnParams &p, dim3 grid, int R, cudaStream_t st) {
     switch (R) {
@@ -678,6 +857,12 @@ bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
     }
     dim3 grid(p.splits, p.kvheads, queries);
     const int R = p.heads / p.kvheads;
+    // prefill chunks of 16+ tokens: query tiles share every K/V read
+    if (p.tokens >= 16 && p.hd == 64 && R <= 4 && queries % p.tokens == 0) {
+        if (!launch_prefill_tile<64>(p, queries / p.tokens, R, st)) return false;
+        NB_CUDA_TRY(cudaGetLastError());
+        return true;
+    }
     bool streamed = false;
     // the streaming kernel where its per-lane state fits in registers
     if (p.hd == 64 && R <= 4) streamed = launch_stream<64>(p, grid, R, st);
