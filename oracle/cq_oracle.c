@@ -240,6 +240,23 @@ void oracle_sdot_linear(const uint8_t *packed, const uint16_t *norms, int out, i
     if (!partials_out) free(d);
 }
 
+/* Greedy token of one logits row: best = 0, then every later index whose
+ * logit is strictly greater than the best so far (the first maximum wins; a NaN
+ * is never greater, so NaNs after index 0 are skipped and a NaN at index 0
+ * keeps 0).  Follows Engine::decode_loop, needle2/csrc/engine.cpp:1434-1442
+ * (and the candidate scan, 1472-1479). */
+int oracle_argmax(const float *x, int n) {
+    int best = 0;
+    float max_v = x[0];
+    for (int i = 1; i < n; ++i) {
+        if (x[i] > max_v) {
+            max_v = x[i];
+            best = i;
+        }
+    }
+    return best;
+}
+
 /* A8 fake activation quantiser on one vector: a = max|x|; unchanged if 0;
  * x = clamp(round-half-even(x/(a/127)), -128, 127) * (a/127).
  * Follows activation_quant, needle2/csrc/engine.cpp:185-191. */

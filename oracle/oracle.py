@@ -53,6 +53,8 @@ def lib() -> ct.CDLL:
     L.oracle_sdot_partials.argtypes = [_p, _i, _i, _i, _i, _p, _p, _i, _p]
     L.oracle_sdot_linear.argtypes = [_p, _p, _i, _i, _i, _i, _p, _p, _p, _i, _p, _p, _p]
     L.oracle_activation_quant.argtypes = [_p, _i, _i]
+    L.oracle_argmax.argtypes = [_p, _i]
+    L.oracle_argmax.restype = _i
     L.oracle_kv_quantize.argtypes = [_p, _p, _i, _i, _p, _p, _p, _p]
     L.oracle_cache_slot.argtypes = [_i, _i, _i]
     L.oracle_cache_slot.restype = _i
@@ -168,6 +170,13 @@ def activation_quant(x, bits=8):
     x = _c(x, np.float32).copy()
     lib().oracle_activation_quant(x.ctypes.data, x.size, bits)
     return x
+
+
+def argmax(x):
+    """Greedy token of each row of x (first maximum wins, NaNs never win)."""
+    x = _c(x, np.float32)
+    rows = x.reshape(-1, x.shape[-1])
+    return np.array([lib().oracle_argmax(r.ctypes.data, r.size) for r in rows], np.int32)
 
 
 def kv_quantize(k, v, kvheads, head_dim):

@@ -150,3 +150,22 @@ def test_packer_round_trip():
     p, n = Q.quantize_matrix(w, 4, 128)
     d = Q.dequantize_matrix(p, n, w.shape, 4, 128)
     assert np.corrcoef(d.ravel(), w.ravel())[0, 1] > 0.99
+
+
+def test_argmax_first_max_and_nans(oracle_lib):
+    """The oracle's greedy scan against the reference loop written out in Python
+    (engine.cpp:1434-1442): ties, NaNs, infinities and signed zeros."""
+    def loop(row):
+        best, max_v = 0, row[0]
+        for i in range(1, len(row)):
+            if row[i] > max_v:
+                max_v, best = row[i], i
+        return best
+    rng = np.random.default_rng(8)
+    rows = [rng.normal(size=1000).astype(np.float32) for _ in range(4)]
+    rows[0][[10, 500]] = 9.0                        # a tie: the first wins
+    rows[1][0] = np.nan                             # NaN first: stays 0
+    rows[2][[3, 7]] = np.nan; rows[2][900] = np.inf # later NaNs skipped
+    rows[3][:] = -np.inf; rows[3][5] = -0.0; rows[3][6] = 0.0   # +0 is not > -0
+    for r in rows:
+        assert oracle_lib.argmax(r)[0] == loop(r.tolist())
