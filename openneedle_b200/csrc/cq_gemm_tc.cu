@@ -5,8 +5,9 @@
 // The weights are decoded once per matrix (lazily, at the first prefill) to an
 // int8 copy W8[N][padded] in the activations' element order, and the group
 // scales ns[n,g] = half(norm) * cs to nsT[g][N'] (N' = N rounded up to 192).
-// A CTA computes a 128 x 192 output tile (14 warps, so 128 registers a thread;
-// 192 columns also pack the SMs' waves better than 256 at the usual sizes):
+// One persistent CTA per SM walks 128 x 192 output tiles (15 warps, 128
+// registers a thread; 192 columns also pack the SMs' waves better than 256 at
+// the usual sizes), its pipelines running on across tile boundaries:
 //   * warp 0 (one lane): TMA loads of the group's activation tile (128 x 128
 //     bytes) and weight tile (192 x 128 bytes), 128-byte swizzled, into a
 //     5-stage ring, and a bulk copy of the group's 192 scales into an 8-deep
@@ -154,10 +155,6 @@ __device__ __forceinline__ void chunk_terms(const uint32_t (&v)[8], const float2
     }
 }
 
-__device__ __forceinline__ void named_sync(int id, int count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 // K-major, 128-byte swizzled operand: 8-row atoms of 1 KB (SBO = 1024).
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
@@ -176,6 +173,7 @@ struct GemmArgs {
     // buffer when an all-gather is fused into the epilogue)
     float *dst[kMaxGemmOutputs];
     int ndst;
+    int mtiles, tiles;   // tile t covers rows (t % mtiles) * 128 and columns (t / mtiles) * 192
 };
 
 // 15 warps: at most four per SM sub-partition, so 128 registers per thread.
@@ -192,7 +190,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ volatile int abort_flag;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;
     const int G = a.groups;
 
     if (warp == 1) tc::alloc(&tmem_s, 512);
@@ -217,55 +214,87 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::fence_after();
     const uint32_t tmem = tmem_s;
 
+    // persistent: CTA b takes tiles b, b + gridDim.x, ...; every ring, TMEM
+    // accumulator and barrier phase runs on the CTA's group counter gg, which
+    // continues across tiles, so the next tile's loads and MMAs overlap the
+    // previous tile's last groups and its output
     if (warp == 0) {
         if (lane == 0) {
             pdl_wait();   // the activations come from the preceding kernel
-            for (int g = 0; g < G && !abort_flag; ++g) {
-                const int s = g % kStages;
-                if (g >= kStages && !gwait(&empty[s], (uint32_t)((g / kStages) - 1) & 1, &abort_flag)) break;
-                uint8_t *st = smem + (size_t)s * kStageBytes;
-                mbar_arrive_expect_tx(&full[s], kStageBytes);
-                tma_load_2d(st, &ta, g * kBK, m0, &full[s]);
-                tma_load_2d(st + kStageA, &tb, g * kBK, n0, &full[s]);
-                const int r = g % kNsRing;
-                if (g >= kNsRing && !gwait(&nsfree[r], (uint32_t)((g / kNsRing) - 1) & 1, &abort_flag)) break;
-                mbar_arrive_expect_tx(&nsfull[r], kBN * 4);
-                bulk_g2s(ns_ring + (size_t)r * kBN, a.nsT + (size_t)g * a.nstride + n0, kBN * 4, &nsfull[r]);
+            int gg = 0;
+            bool stop = false;
+            for (int tile = blockIdx.x; tile < a.tiles && !stop; tile += gridDim.x) {
+                const int m0 = (tile % a.mtiles) * kBM, n0 = (tile / a.mtiles) * kBN;
+                for (int g = 0; g < G; ++g, ++gg) {
+                    const int s = gg % kStages;
+                    if (abort_flag ||
+                        (gg >= kStages && !gwait(&empty[s], (uint32_t)((gg / kStages) - 1) & 1, &abort_flag))) {
+                        stop = true;
+                        break;
+                    }
+                    uint8_t *st = smem + (size_t)s * kStageBytes;
+                    mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    tma_load_2d(st, &ta, g * kBK, m0, &full[s]);
+                    tma_load_2d(st + kStageA, &tb, g * kBK, n0, &full[s]);
+                    const int r = gg % kNsRing;
+                    if (gg >= kNsRing && !gwait(&nsfree[r], (uint32_t)((gg / kNsRing) - 1) & 1, &abort_flag)) {
+                        stop = true;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&nsfull[r], kBN * 4);
+                    bulk_g2s(ns_ring + (size_t)r * kBN, a.nsT + (size_t)g * a.nstride + n0, kBN * 4, &nsfull[r]);
+                }
             }
         }
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t idesc = tc::idesc_s8(kBM, kBN);
-            for (int g = 0; g < G && !abort_flag; ++g) {
-                const int s = g % kStages, d = g & 1;
-                if (!gwait(&full[s], (uint32_t)(g / kStages) & 1, &abort_flag)) break;
-                if (!gwait(&dfree[d], (uint32_t)(g / 2) & 1, &abort_flag)) break;
-                tc::fence_after();
-                const uint32_t sa = smem_addr(smem + (size_t)s * kStageBytes), sb = sa + kStageA;
+            int gg = 0;
+            bool stop = false;
+            for (int tile = blockIdx.x; tile < a.tiles && !stop; tile += gridDim.x) {
+                for (int g = 0; g < G; ++g, ++gg) {
+                    const int s = gg % kStages, d = gg & 1;
+                    if (abort_flag || !gwait(&full[s], (uint32_t)(gg / kStages) & 1, &abort_flag) ||
+                        !gwait(&dfree[d], (uint32_t)(gg / 2) & 1, &abort_flag)) {
+                        stop = true;
+                        break;
+                    }
+                    tc::fence_after();
+                    const uint32_t sa = smem_addr(smem + (size_t)s * kStageBytes), sb = sa + kStageA;
 #pragma unroll
-                for (int kk = 0; kk < kBK / 32; ++kk)
-                    tc::mma_i8_ss(tmem + (uint32_t)(d * kDCols), sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc,
-                                  kBiasInTmem || kk > 0);
-                tc::commit(&empty[s]);
-                tc::commit(&dfull[d]);
+                    for (int kk = 0; kk < kBK / 32; ++kk)
+                        tc::mma_i8_ss(tmem + (uint32_t)(d * kDCols), sw128_desc(sa + kk * 32),
+                                      sw128_desc(sb + kk * 32), idesc, kBiasInTmem || kk > 0);
+                    tc::commit(&empty[s]);
+                    tc::commit(&dfull[d]);
+                }
             }
         }
         __syncwarp();
     } else if (warp == kXsWarp) {
-        // the tile's 128 activation scales of each group into the ring slot that
+        // each group's 128 activation scales of the tile into the ring slot that
         // also takes the group's column scales; the epilogue then never waits on
         // a global load (lanes: rows lane + 32 j)
         pdl_wait();
-        for (int g = 0; g < G && !abort_flag; ++g) {
-            const int r = g % kNsRing;
-            if (g >= kNsRing && !gwait(&nsfree[r], (uint32_t)((g / kNsRing) - 1) & 1, &abort_flag)) break;
+        int gg = 0;
+        bool stop = false;
+        for (int tile = blockIdx.x; tile < a.tiles && !stop; tile += gridDim.x) {
+            const int m0 = (tile % a.mtiles) * kBM;
+            for (int g = 0; g < G; ++g, ++gg) {
+                const int r = gg % kNsRing;
+                if (abort_flag ||
+                    (gg >= kNsRing && !gwait(&nsfree[r], (uint32_t)((gg / kNsRing) - 1) & 1, &abort_flag))) {
+                    stop = true;
+                    break;
+                }
 #pragma unroll
-            for (int j = 0; j < kBM / 32; ++j) {
-                const int row = m0 + lane + 32 * j;
-                xs_ring[(size_t)r * kBM + lane + 32 * j] = row < a.M ? a.xs[(size_t)row * G + g] : 0.f;
+                for (int j = 0; j < kBM / 32; ++j) {
+                    const int row = m0 + lane + 32 * j;
+                    xs_ring[(size_t)r * kBM + lane + 32 * j] = row < a.M ? a.xs[(size_t)row * G + g] : 0.f;
+                }
+                mbar_arrive(&nsfull[r]);
             }
-            mbar_arrive(&nsfull[r]);
         }
     } else {
         // epilogue: warp (q, slice) owns accumulator lanes 32q..32q+31 (activation
@@ -275,11 +304,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3, slice = (warp - 2) >> 2;
         const int col0 = slice * 64, cpair = 2 * (lane & 3);
         const int rbase = 32 * q + (lane >> 2);   // tile-local row of r = 0; r adds 8 r
-        float2 acc[4][8];   // [row][column block], a column pair each
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int b = 0; b < 8; ++b) acc[r][b] = make_float2(0.f, 0.f);
         const uint32_t quarter = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)col0;
         // both accumulators start at the bias; the MMA warp waits for this
         if (kBiasInTmem) {
@@ -296,86 +320,82 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive(&dfree[0]);
             mbar_arrive(&dfree[1]);
         }
+        int gg = 0;
         bool ok = true;
-        for (int g = 0; g < G && ok; ++g) {
-            const int d = g & 1, ri = g % kNsRing;
-            if (!gwait(&dfull[d], (uint32_t)(g / 2) & 1, &abort_flag) ||
-                !gwait(&nsfull[ri], (uint32_t)(g / kNsRing) & 1, &abort_flag)) {
-                ok = false;
-                break;
-            }
-            tc::fence_after();
-            float2 xs2[4];
+        for (int tile = blockIdx.x; tile < a.tiles && ok; tile += gridDim.x) {
+            const int m0 = (tile % a.mtiles) * kBM, n0 = (tile / a.mtiles) * kBN;
+            float2 acc[4][8];   // [row][column block], a column pair each
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const float x = xs_ring[(size_t)ri * kBM + rbase + 8 * r];
-                xs2[r] = make_float2(x, x);
-            }
-            const float *nsr = ns_ring + (size_t)ri * kBN + col0 + cpair;
-            const float2 one2 = make_float2(a.one, a.one);
-            const uint32_t dq = quarter + (uint32_t)(d * kDCols);
-            // chunk i: lanes +16 (i & 1), columns 16 (i >> 1) .. +15 (blocks 2c, 2c + 1);
-            // read it, reset it to the bias for group g + 2, and keep the next
-            // chunk's read in flight while this one is summed
-            uint32_t va[8], vb[8];
-            float2 ns2[2];
-            tc::ld16x256_x2(dq, va);
+            for (int r = 0; r < 4; ++r)
 #pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-                const int c = i >> 1;
-                const uint32_t lo = dq + (uint32_t)(16 * c), hi = lo + (16u << 16);
-                ns2[0] = *reinterpret_cast<const float2 *>(nsr + 16 * c);
-                ns2[1] = *reinterpret_cast<const float2 *>(nsr + 16 * c + 8);
-                tc::wait_ld();
-                tc::hold8(va);
-                if (kBiasInTmem) tc::fill16x256_x2(lo, kBias);
-                tc::ld16x256_x2(hi, vb);
-                chunk_terms(va, ns2, xs2[0], xs2[1], one2, acc[0] + 2 * c, acc[1] + 2 * c);
-                tc::wait_ld();
-                tc::hold8(vb);
-                if (kBiasInTmem) tc::fill16x256_x2(hi, kBias);
-                if (i + 2 < 8) tc::ld16x256_x2(lo + 16, va);
-                chunk_terms(vb, ns2, xs2[2], xs2[3], one2, acc[2] + 2 * c, acc[3] + 2 * c);
+                for (int b = 0; b < 8; ++b) acc[r][b] = make_float2(0.f, 0.f);
+            for (int g = 0; g < G; ++g, ++gg) {
+                const int d = gg & 1, ri = gg % kNsRing;
+                if (!gwait(&dfull[d], (uint32_t)(gg / 2) & 1, &abort_flag) ||
+                    !gwait(&nsfull[ri], (uint32_t)(gg / kNsRing) & 1, &abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after();
+                float2 xs2[4];
+    #pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const float x = xs_ring[(size_t)ri * kBM + rbase + 8 * r];
+                    xs2[r] = make_float2(x, x);
+                }
+                const float *nsr = ns_ring + (size_t)ri * kBN + col0 + cpair;
+                const float2 one2 = make_float2(a.one, a.one);
+                const uint32_t dq = quarter + (uint32_t)(d * kDCols);
+                // chunk i: lanes +16 (i & 1), columns 16 (i >> 1) .. +15 (blocks 2c, 2c + 1);
+                // read it, reset it to the bias for group g + 2, and keep the next
+                // chunk's read in flight while this one is summed
+                uint32_t va[8], vb[8];
+                float2 ns2[2];
+                tc::ld16x256_x2(dq, va);
+    #pragma unroll
+                for (int i = 0; i < 8; i += 2) {
+                    const int c = i >> 1;
+                    const uint32_t lo = dq + (uint32_t)(16 * c), hi = lo + (16u << 16);
+                    ns2[0] = *reinterpret_cast<const float2 *>(nsr + 16 * c);
+                    ns2[1] = *reinterpret_cast<const float2 *>(nsr + 16 * c + 8);
+                    tc::wait_ld();
+                    tc::hold8(va);
+                    if (kBiasInTmem) tc::fill16x256_x2(lo, kBias);
+                    tc::ld16x256_x2(hi, vb);
+                    chunk_terms(va, ns2, xs2[0], xs2[1], one2, acc[0] + 2 * c, acc[1] + 2 * c);
+                    tc::wait_ld();
+                    tc::hold8(vb);
+                    if (kBiasInTmem) tc::fill16x256_x2(hi, kBias);
+                    if (i + 2 < 8) tc::ld16x256_x2(lo + 16, va);
+                    chunk_terms(vb, ns2, xs2[2], xs2[3], one2, acc[2] + 2 * c, acc[3] + 2 * c);
+                }
+                if (kBiasInTmem) tc::wait_st();
+                tc::fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&dfree[d]);
+                    mbar_arrive(&nsfree[ri]);
+                }
             }
-            if (kBiasInTmem) tc::wait_st();
-            tc::fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&dfree[d]);
-                mbar_arrive(&nsfree[ri]);
-            }
-        }
-        // the output tile through shared memory (the operand ring is idle once the
-        // last group's dots are read), then written row by row
-        named_sync(2, kEpiWarps * 32);
-        float *out_s = reinterpret_cast<float *>(smem);
-        // row stride = 8 mod 32 banks: the 8-byte writes of a half warp (4 rows
-        // x 4 column pairs) and the 16-byte row reads are conflict-free
-        constexpr int kOutStride = kBN + 8;
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-            for (int b = 0; b < 8; ++b)
-                *reinterpret_cast<float2 *>(out_s + (rbase + 8 * r) * kOutStride + col0 + 8 * b + cpair) = acc[r][b];
-        named_sync(2, kEpiWarps * 32);
-        if (ok) {
-            // warp e writes rows e, e + kEpiWarps, ...; each lane 4-column pieces of a row
-            const int ew = warp - 2;
+            if (!ok) break;
+            // the tile's rows straight from registers: for each (row, block) the four
+            // lanes of a row write one 32-byte sector
             for (int di = 0; di < a.ndst; ++di) {
                 float *const y = a.dst[di];
-                const bool vec = (a.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
-                for (int rr = ew; rr < kBM && m0 + rr < a.M; rr += kEpiWarps) {
-                    float *yr = y + (size_t)(m0 + rr) * a.ldy + n0;
+                const bool vec = (a.ldy & 1) == 0 && (reinterpret_cast<uintptr_t>(y) & 7) == 0;
 #pragma unroll
-                    for (int cc = 4 * lane; cc < kBN; cc += 128) {
-                        const float4 o = *reinterpret_cast<const float4 *>(out_s + rr * kOutStride + cc);
-                        if (vec && n0 + cc + 3 < a.N) {
-                            *reinterpret_cast<float4 *>(yr + cc) = o;
+                for (int r = 0; r < 4; ++r) {
+                    const int row = m0 + rbase + 8 * r;
+                    if (row >= a.M) continue;
+                    float *yr = y + (size_t)row * a.ldy + n0 + col0 + cpair;
+#pragma unroll
+                    for (int b = 0; b < 8; ++b) {
+                        const int col = n0 + col0 + 8 * b + cpair;
+                        if (vec && col + 1 < a.N) {
+                            *reinterpret_cast<float2 *>(yr + 8 * b) = acc[r][b];
                         } else {
-                            if (n0 + cc < a.N) yr[cc] = o.x;
-                            if (n0 + cc + 1 < a.N) yr[cc + 1] = o.y;
-                            if (n0 + cc + 2 < a.N) yr[cc + 2] = o.z;
-                            if (n0 + cc + 3 < a.N) yr[cc + 3] = o.w;
+                            if (col < a.N) yr[8 * b] = acc[r][b].x;
+                            if (col + 1 < a.N) yr[8 * b + 1] = acc[r][b].y;
                         }
                     }
                 }
@@ -667,7 +687,12 @@ bool launch_gemm_i8_multi(const int8_t *q, const float *xs, int M, const int8_t 
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((M + kBM - 1) / kBM, (N + kBN - 1) / kBN);
+    static int sms[64] = {};
+    if (dev >= 0 && dev < 64 && !sms[dev]) NB_CUDA_TRY(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+    const int nsm = dev >= 0 && dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
+    args.mtiles = (M + kBM - 1) / kBM;
+    args.tiles = args.mtiles * ((N + kBN - 1) / kBN);
+    cfg.gridDim = dim3(std::min(args.tiles, nsm));   // one persistent CTA per SM
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = kSmem;
     cfg.stream = st;
