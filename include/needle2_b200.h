@@ -134,6 +134,14 @@ int needle2_b200_ipc_export(const void *ptr, void *handle64, unsigned long long 
 int needle2_b200_ipc_import(const void *handle64, unsigned long long offset, void **ptr);
 int needle2_b200_ipc_close(void *ptr);
 
+/* The decode loop's greedy token of each row of logits[rows][ld] (vocab <= ld
+ * entries used): out[r] = the first index of the row's maximum, NaNs never
+ * chosen, 0 when the row's first logit is NaN -- the reference's scan
+ * (best = 0, then any strictly greater logit), Engine::decode_loop,
+ * needle2/csrc/engine.cpp:1434-1442 and the candidate scan 1472-1479.
+ * Device pointers on a stream. */
+int needle2_b200_argmax_device(const float *logits, int rows, int vocab, int ld, int *out, void *stream);
+
 /* The engine's fake activation quantiser for activation_bits = bits, in place
  * on x[rows][dim], each row separately: a = max|x|, unchanged when a is 0,
  * otherwise x = clamp(round_half_even(x / (a / m)), -m - 1, m) * (a / m) with

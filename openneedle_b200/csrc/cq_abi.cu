@@ -766,6 +766,15 @@ int needle2_sdot_multiply_gather_device(void *h, float *const *dsts, int ndst, i
                : -1;
 }
 
+int needle2_b200_argmax_device(const float *logits, int rows, int vocab, int ld, int *out, void *stream) {
+    nb200::clear_error();
+    if (rows < 0 || vocab <= 0 || ld < vocab || (rows && (!logits || !out))) {
+        nb200::set_error("argmax: bad arguments");
+        return -1;
+    }
+    return nb200::launch_argmax(logits, rows, vocab, ld, out, static_cast<cudaStream_t>(stream)) ? 0 : -1;
+}
+
 int needle2_b200_activation_quant_device(float *x, int rows, int dim, int bits, void *stream) {
     nb200::clear_error();
     if (rows < 0 || dim < 0 || bits < 0 || bits > 16 || (rows && dim && !x)) {

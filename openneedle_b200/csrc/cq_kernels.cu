@@ -789,6 +789,74 @@ __global__ void activation_quant_kernel(float *__restrict__ x, int rows, int dim
 
 }  // namespace
 
+namespace {
+
+// (value, index) candidates of the greedy scan: the larger value wins, an equal
+// one the smaller index; NaN never wins (index INT_MAX marks "none yet").
+__device__ __forceinline__ void better(float &v, int &i, float ov, int oi) {
+    if (ov > v || (ov == v && oi < i)) {
+        v = ov;
+        i = oi;
+    }
+}
+
+// One CTA per row: the reference's sequential scan (best = 0, then every index
+// strictly greater than the best so far, needle2/csrc/engine.cpp:1434-1442)
+// gives the first index of the maximum over the non-NaN logits, or 0 when
+// logits[0] is NaN.  Each thread scans its indices in increasing order, then
+// the candidates are reduced with the same order.
+__global__ void argmax_kernel(const float *__restrict__ x, int vocab, int ld, int *__restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const float *row = x + (size_t)blockIdx.x * ld;
+    const float x0 = row[0];
+    if (x0 != x0) {   // NaN first: nothing is ever greater
+        if (threadIdx.x == 0) out[blockIdx.x] = 0;
+        return;
+    }
+    float v = -INFINITY;
+    int idx = 0x7fffffff;
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+        const float y = row[i];
+        if (y > v || (y == v && idx == 0x7fffffff)) {   // first candidate of this thread, or a strictly larger one
+            v = y;
+            idx = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        better(v, idx, ov, oi);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    if (lane == 0) {
+        sv[warp] = v;
+        si[warp] = idx;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        v = lane < nw ? sv[lane] : -INFINITY;
+        idx = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+            better(v, idx, ov, oi);
+        }
+        if (lane == 0) out[blockIdx.x] = idx;   // x0 is a candidate, so idx is set
+    }
+}
+
+}  // namespace
+
+bool launch_argmax(const float *x, int rows, int vocab, int ld, int *out, cudaStream_t st) {
+    if (rows <= 0) return true;
+    argmax_kernel<<<rows, 1024, 0, st>>>(x, vocab, ld, out);
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+}
+
 bool launch_activation_quant(float *x, int rows, int dim, int bits, cudaStream_t st) {
     if (rows <= 0 || dim <= 0 || bits == 0) return true;
     const long long threads = (long long)rows * 32;

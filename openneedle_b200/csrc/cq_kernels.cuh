@@ -42,6 +42,9 @@ bool launch_rows(const CQDevice &w, const int64_t *ids, int count, float *y, cud
 bool gemv_fast_path(const CQDevice &w);
 // The engine's fake activation quantiser, in place on x[rows][dim] (per row).
 bool launch_activation_quant(float *x, int rows, int dim, int bits, cudaStream_t st);
+// The decode loop's greedy token of each logits row: out[r] = first index of
+// the row's maximum (NaNs never win; 0 when the first logit is NaN).
+bool launch_argmax(const float *x, int rows, int vocab, int ld, int *out, cudaStream_t st);
 
 struct GemvBatch;
 // A one-matrix GEMV batch description of w (activations and outputs unset).

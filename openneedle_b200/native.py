@@ -326,6 +326,24 @@ def activation_quant(x, bits: int = 8):
     return a
 
 
+def argmax_device(logits, out=None, stream=None):
+    """Greedy token of each row of a CUDA float32 tensor logits[rows, vocab]
+    (the decode loop's scan: first maximum wins, NaNs never chosen); returns an
+    int32 CUDA tensor (or fills `out`)."""
+    import torch
+    lib = _library()
+    fn = lib.needle2_b200_argmax_device
+    fn.argtypes = [ct.c_void_p, ct.c_int, ct.c_int, ct.c_int, ct.c_void_p, ct.c_void_p]
+    fn.restype = ct.c_int
+    if logits.dtype != torch.float32 or logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be a float32 [rows, vocab] tensor with unit column stride")
+    rows, vocab = logits.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    _check(fn(logits.data_ptr(), rows, vocab, logits.stride(0), out.data_ptr(), _stream_ptr(stream)), "argmax")
+    return out
+
+
 def set_int8_gemv(kind: int) -> int:
     """Select the int8 GEMV kernel process-wide (0 automatic, 1 diagonal warp
     MMA, 2 tcgen05, 3 fragment-order warp MMA); returns the previous setting."""
