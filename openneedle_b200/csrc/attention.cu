@@ -332,11 +332,9 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
 __device__ __forceinline__ void i8x4_pairs(uint32_t w, float2 &lo, float2 &hi) {
     const uint32_t u = w ^ 0x80808080u;   // b + 128, as unsigned bytes
     const uint32_t top = 0x4B000000u;     // 2^23
-    constexpr float off = -8388736.f;     // -(2^23 + 128)
-    lo.x = __fadd_rn(__uint_as_float(prmt(u, top, 0x7540)), off);
-    lo.y = __fadd_rn(__uint_as_float(prmt(u, top, 0x7541)), off);
-    hi.x = __fadd_rn(__uint_as_float(prmt(u, top, 0x7542)), off);
-    hi.y = __fadd_rn(__uint_as_float(prmt(u, top, 0x7543)), off);
+    const float2 off = make_float2(-8388736.f, -8388736.f);   // -(2^23 + 128)
+    lo = fadd2(make_float2(__uint_as_float(prmt(u, top, 0x7540)), __uint_as_float(prmt(u, top, 0x7541))), off);
+    hi = fadd2(make_float2(__uint_as_float(prmt(u, top, 0x7542)), __uint_as_float(prmt(u, top, 0x7543))), off);
 }
 
 // Global addresses of visible index i's K/V rows and scales, and how many
