@@ -726,50 +726,57 @@ __global__ void __launch_bounds__(128) attn_prefill_tile_kernel(const AttnParams
         }
         __syncthreads();
         if (!active) continue;
-        float sc[kPBK];
-        float mx = -INFINITY;
+        // sub-chunks of 8 keys (a rolled loop: the unrolled body stays small
+        // enough for the instruction cache); one max update and rescale each
+#pragma unroll 1
+        for (int j0 = 0; j0 < nb; j0 += 8) {
+            float sc[8];
+            float mx = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < kPBK; ++j) {
-            float v = -INFINITY;
-            if (j < nb) {
-                const int position = kpos[j];
-                const bool vis = position <= pos && (position < prefix_count || position >= start);
-                if (vis) {
-                    float d0 = 0.f, d1 = 0.f;
+            for (int jj = 0; jj < 8; ++jj) {
+                const int j = j0 + jj;
+                float v = -INFINITY;
+                if (j < nb) {
+                    const int position = kpos[j];
+                    const bool vis = position <= pos && (position < prefix_count || position >= start);
+                    if (vis) {
+                        float d0 = 0.f, d1 = 0.f;
 #pragma unroll
-                    for (int d = 0; d < HD; d += 4) {
-                        const float4 kv = *reinterpret_cast<const float4 *>(&ks_f[j][d]);
-                        d0 = fmaf(q[d], kv.x, d0);
-                        d1 = fmaf(q[d + 1], kv.y, d1);
-                        d0 = fmaf(q[d + 2], kv.z, d0);
-                        d1 = fmaf(q[d + 3], kv.w, d1);
+                        for (int d = 0; d < HD; d += 4) {
+                            const float4 kv = *reinterpret_cast<const float4 *>(&ks_f[j][d]);
+                            d0 = fmaf(q[d], kv.x, d0);
+                            d1 = fmaf(q[d + 1], kv.y, d1);
+                            d0 = fmaf(q[d + 2], kv.z, d0);
+                            d1 = fmaf(q[d + 3], kv.w, d1);
+                        }
+                        v = __fmul_rn(__fmul_rn(d0 + d1, kscale[j]), inv_sqrt);
                     }
-                    v = __fmul_rn(__fmul_rn(d0 + d1, kscale[j]), inv_sqrt);
                 }
+                sc[jj] = v;
+                mx = fmaxf(mx, v);
             }
-            sc[j] = v;
-            mx = fmaxf(mx, v);
-        }
-        if (mx == -INFINITY) continue;   // nothing of this block is visible to this row
-        const float mn = fmaxf(m, mx);
-        const float corr = m == -INFINITY ? 0.f : __expf(m - mn);
-        m = mn;
-        l *= corr;
+            if (mx == -INFINITY) continue;   // nothing of these keys is visible to this row
+            const float mn = fmaxf(m, mx);
+            const float corr = m == -INFINITY ? 0.f : __expf(m - mn);
+            m = mn;
+            l *= corr;
 #pragma unroll
-        for (int d = 0; d < HD; ++d) acc[d] *= corr;
+            for (int d = 0; d < HD; ++d) acc[d] *= corr;
 #pragma unroll
-        for (int j = 0; j < kPBK; ++j) {
-            if (sc[j] == -INFINITY) continue;
-            const float pr = __expf(sc[j] - mn);
-            l += pr;
-            const float w = pr * vscale[j];
+            for (int jj = 0; jj < 8; ++jj) {
+                if (sc[jj] == -INFINITY) continue;
+                const int j = j0 + jj;
+                const float pr = __expf(sc[jj] - mn);
+                l += pr;
+                const float w = pr * vscale[j];
 #pragma unroll
-            for (int d = 0; d < HD; d += 4) {
-                const float4 vv = *reinterpret_cast<const float4 *>(&vs_f[j][d]);
-                acc[d] = fmaf(w, vv.x, acc[d]);
-                acc[d + 1] = fmaf(w, vv.y, acc[d + 1]);
-                acc[d + 2] = fmaf(w, vv.z, acc[d + 2]);
-                acc[d + 3] = fmaf(w, vv.w, acc[d + 3]);
+                for (int d = 0; d < HD; d += 4) {
+                    const float4 vv = *reinterpret_cast<const float4 *>(&vs_f[j][d]);
+                    acc[d] = fmaf(w, vv.x, acc[d]);
+                    acc[d + 1] = fmaf(w, vv.y, acc[d + 1]);
+                    acc[d + 2] = fmaf(w, vv.z, acc[d + 2]);
+                    acc[d + 3] = fmaf(w, vv.w, acc[d + 3]);
+                }
             }
         }
     }
