@@ -240,55 +240,57 @@ def kernel_ms(lib, handles, x, yp, stream, sdot, n):
     return float(np.mean([a.elapsed_time(b) for a, b in zip(starts, ends)]))
 
 
+def _gemm_ms(lib, dev, stream, packed, norms, cb, m, n, k, bits, reps):
+    """Mean kernel time (ms) of one M x K x N product in the int8 (SDOT) mode and
+    in the FP32 mode: the quantised / split activations are prepared outside the
+    timed launches, the weights are decoded once before them."""
+    import torch
+    x = torch.randn(m, k, device=dev)
+    y = torch.empty(m, n, device=dev)
+    sp = stream.cuda_stream
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    out = []
+    for create, linear, prep, mult, destroy in (
+            (lib.needle2_sdot_create, lib.needle2_sdot_linear_device, lib.needle2_sdot_prepare_device,
+             lib.needle2_sdot_multiply_device, lib.needle2_sdot_destroy),
+            (lib.needle2_cq_create, lib.needle2_cq_linear_device, lib.needle2_cq_prepare_device,
+             lib.needle2_cq_multiply_device, lib.needle2_cq_destroy)):
+        h = create(packed.ctypes.data, norms.ctypes.data, n, k, bits, GROUP, cb.ctypes.data)
+        if not h:
+            raise RuntimeError(lib.needle2_b200_error().decode())
+        check(linear(h, x.data_ptr(), y.data_ptr(), m, sp), lib)   # decodes the weights once
+        check(prep(h, x.data_ptr(), m, sp), lib)
+        for _ in range(3):
+            check(mult(h, y.data_ptr(), m, sp), lib)
+        a.record(stream)
+        for _ in range(reps):
+            check(mult(h, y.data_ptr(), m, sp), lib)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        out.append(a.elapsed_time(b) / reps)
+        destroy(h)
+    return out
+
+
+def _bf16_peak():
+    try:
+        with open(ROOT / "MEASURED_PEAKS.json") as f:
+            return float(json.load(f)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
 def prefill_gemm(lib, dev, stream, reps=20):
     """Config 3's largest case on the int8 prefill GEMM: x[2048][4096] against a
     CQ4 8192 x 4096 matrix (group 128); the GEMM kernel alone (quantised input
     prepared outside the timed launches), against twice the measured bf16 dense
     rate (B200 issues int8 MMAs at twice the bf16 rate)."""
-    import torch
     from openneedle_b200.quantize import synthetic_matrix
     m, n, k = 2048, 8192, 4096
     packed, norms, cb = synthetic_matrix(n, k, 4, GROUP, seed=3)
-    h = lib.needle2_sdot_create(packed.ctypes.data, norms.ctypes.data, n, k, 4, GROUP, cb.ctypes.data)
-    if not h:
-        raise RuntimeError(lib.needle2_b200_error().decode())
-    x = torch.randn(m, k, device=dev)
-    y = torch.empty(m, n, device=dev)
-    sp = stream.cuda_stream
-    check(lib.needle2_sdot_linear_device(h, x.data_ptr(), y.data_ptr(), m, sp), lib)   # decodes the weights once
-    check(lib.needle2_sdot_prepare_device(h, x.data_ptr(), m, sp), lib)
-    for _ in range(3):
-        check(lib.needle2_sdot_multiply_device(h, y.data_ptr(), m, sp), lib)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for _ in range(reps):
-        check(lib.needle2_sdot_multiply_device(h, y.data_ptr(), m, sp), lib)
-    b.record(stream)
-    torch.cuda.synchronize(dev)
-    ms = a.elapsed_time(b) / reps
-    lib.needle2_sdot_destroy(h)
-    # the same product in the FP32 mode (bf16 hi/lo split, three MMAs per K step)
-    hf = lib.needle2_cq_create(packed.ctypes.data, norms.ctypes.data, n, k, 4, GROUP, cb.ctypes.data)
-    if not hf:
-        raise RuntimeError(lib.needle2_b200_error().decode())
-    check(lib.needle2_cq_linear_device(hf, x.data_ptr(), y.data_ptr(), m, sp), lib)   # makes the bf16 copy
-    check(lib.needle2_cq_prepare_device(hf, x.data_ptr(), m, sp), lib)
-    for _ in range(3):
-        check(lib.needle2_cq_multiply_device(hf, y.data_ptr(), m, sp), lib)
-    a.record(stream)
-    for _ in range(reps):
-        check(lib.needle2_cq_multiply_device(hf, y.data_ptr(), m, sp), lib)
-    b.record(stream)
-    torch.cuda.synchronize(dev)
-    fms = a.elapsed_time(b) / reps
-    lib.needle2_cq_destroy(hf)
+    ms, fms = _gemm_ms(lib, dev, stream, packed, norms, cb, m, n, k, 4, reps)
     tops = 2.0 * m * n * k / (ms * 1e-3) / 1e12
-    bf16 = None
-    try:
-        with open(ROOT / "MEASURED_PEAKS.json") as f:
-            bf16 = float(json.load(f)["bf16_tflops"])
-    except (OSError, KeyError, ValueError):
-        pass
+    bf16 = _bf16_peak()
     peak = 2 * bf16 if bf16 else 2 * 1590.0
     ftf = 2.0 * m * n * k / (fms * 1e-3) / 1e12
     fp32 = {"kernel": "cq_gemm_f32x3_kernel (tcgen05 kind::f16, bf16 hi/lo split, 3 MMAs per K step, 128x256 tiles)",
@@ -302,6 +304,34 @@ def prefill_gemm(lib, dev, stream, reps=20):
             "kernel_ms": ms, "achieved": tops, "unit": "TOP/s", "bound": "tensor", "peak": peak,
             "frac": tops / peak, "peak_source": "2 x measured bf16 dense" if bf16 else "2 x fallback bf16 dense",
             "fp32_mode": fp32}
+
+
+def prefill_gemm_sweep(lib, dev, stream, reps=10):
+    """Config 3's grid: M = 2048 against N in {2048, 8192, 11008} x K in
+    {512, 2048, 4096}, CQ4 and CQ2, both modes; kernel ms per shape.  The packed
+    codes and group norms are seeded random bytes / half values of the real
+    layout: the kernels' time does not depend on the values (parity is covered by
+    the tests), and quantising 18 matrices on the host would take minutes."""
+    from openneedle_b200.quantize import codebook
+    rng = np.random.default_rng(5)
+    m = 2048
+    bf16 = _bf16_peak() or 1590.0
+    rows = []
+    for bits in (4, 2):
+        cb = np.ascontiguousarray(codebook(bits, GROUP), dtype=np.float32)
+        for n in (2048, 8192, 11008):
+            for k in (512, 2048, 4096):
+                packed = rng.integers(0, 256, (n, k * bits // 8), dtype=np.uint8)
+                norms = rng.uniform(0.15, 0.3, (n, k // GROUP)).astype(np.float16)
+                ms, fms = _gemm_ms(lib, dev, stream, packed, norms, cb, m, n, k, bits, reps)
+                ops = 2.0 * m * n * k
+                rows.append({"bits": bits, "n": n, "k": k, "int8_ms": round(ms, 4),
+                             "int8_frac": round(ops / (ms * 1e-3) / 1e12 / (2 * bf16), 3),
+                             "fp32_ms": round(fms, 4),
+                             "fp32_frac": round(ops / (fms * 1e-3) / 1e12 / bf16, 3)})
+    return {"m": m, "group": GROUP, "reps": reps,
+            "frac_note": "int8 against 2 x measured bf16 dense, fp32 (FP32-equivalent flops) against measured "
+                         "bf16 dense", "shapes": rows}
 
 
 def attention_decode(dev, stream, lengths=(512, 2048, 4096), reps=20):
@@ -565,6 +595,8 @@ def run_native(args, rank, world, dist):
         lib.needle2_sdot_destroy(h)
     if not args.skip_gemm:
         result["prefill_gemm"] = prefill_gemm(lib, dev, stream)
+        if world == 1 and not args.skip_sweep:
+            result["prefill_gemm_sweep"] = prefill_gemm_sweep(lib, dev, stream)
     if not args.skip_attention:
         result["attention_decode"] = attention_decode(dev, stream)
     if world > 1 and not args.skip_sharded:
@@ -594,6 +626,7 @@ def main():
     ap.add_argument("--skip-fp32", action="store_true", help="omit the FP32-mode side measurement")
     ap.add_argument("--skip-e2e", action="store_true", help="omit the host-buffer end-to-end measurement")
     ap.add_argument("--skip-gemm", action="store_true", help="omit the prefill GEMM side measurement")
+    ap.add_argument("--skip-sweep", action="store_true", help="omit the config-3 prefill GEMM shape sweep")
     ap.add_argument("--skip-attention", action="store_true", help="omit the INT8 KV attention side measurement")
     ap.add_argument("--skip-sharded", action="store_true",
                     help="omit the N-sharded GEMM + all-gather side measurement (multi-GPU runs)")
