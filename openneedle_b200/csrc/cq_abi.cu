@@ -903,3 +903,13 @@ extern "C" int needle2_b200_set_int8_gemv(int kind) {
     nb200::set_int8_gemv_kernel(kind);
     return previous;
 }
+
+extern "C" int needle2_b200_set_f32_gemv(int kind) {
+    const int previous = nb200::f32_gemv_kernel();
+    if (kind < 0 || kind > 1) {
+        nb200::set_error("FP32 GEMV kernel kind must be 0 (automatic) or 1 (slot-per-lane kernel)");
+        return -1;
+    }
+    nb200::set_f32_gemv_kernel(kind);
+    return previous;
+}

@@ -737,7 +737,11 @@ bool launch_gemv(const GemvBatch &b, bool i8, cudaStream_t st) {
         set_error("GEMV launch outside the persistent kernel's envelope");
         return false;
     }
-    if (!i8) return dispatch<false>(b, st);
+    if (!i8) {
+        if (f32_gemv_kernel() == 0 && b.M <= gemv_rows_max_rows(b.bits, b.group, b.groups))
+            return launch_gemv_rows(b, st);
+        return dispatch<false>(b, st);
+    }
     bool tiled = true, frag = true;
     for (int j = 0; j < b.nmat; ++j) {
         tiled = tiled && b.mat[j].tiled && b.mat[j].normsT;

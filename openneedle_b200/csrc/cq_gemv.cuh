@@ -62,6 +62,14 @@ bool launch_gemv_mma(const GemvBatch &b, cudaStream_t st);
 // int8 GEMV on tcgen05 (cq_gemv_tc.cu).
 int gemv_tc_max_rows(int bits, int group, int groups);
 bool launch_gemv_tc(const GemvBatch &b, cudaStream_t st);
+// FP32-mode GEMV with one output row per lane (cq_gemv_rows.cu) for up to
+// gemv_rows_max_rows activation rows; launch_gemv routes FP32 batches there.
+int gemv_rows_max_rows(int bits, int group, int groups);
+bool launch_gemv_rows(const GemvBatch &b, cudaStream_t st);
+// Which FP32 GEMV kernel launch_gemv uses: 0 automatic (the row kernel where it
+// fits), 1 the slot-per-lane kernel of cq_gemv.cu.
+void set_f32_gemv_kernel(int kind);
+int f32_gemv_kernel();
 // int8 GEMV with weights as the mma.sync A operand (cq_gemv_frag.cu).  The
 // fragment-order copy: 16-row tiles; per tile and group one block of
 // 32 lanes x (gb / 2) bytes; lane (g, t) holds, for every 32-wide K step s,

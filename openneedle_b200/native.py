@@ -57,6 +57,8 @@ def _library() -> ct.CDLL:
         getattr(lib, name).restype = _i
     lib.needle2_b200_set_int8_gemv.argtypes = [_i]
     lib.needle2_b200_set_int8_gemv.restype = _i
+    lib.needle2_b200_set_f32_gemv.argtypes = [_i]
+    lib.needle2_b200_set_f32_gemv.restype = _i
     lib.needle2_cq_linear_many_checked.argtypes = [ct.POINTER(_p), _i, _p, ct.POINTER(_p), _i, _i]
     lib.needle2_cq_linear_many_checked.restype = _i
     lib.needle2_cq_linear_many_device.argtypes = [ct.POINTER(_p), _i, _p, ct.POINTER(_p), _i, _i, _p]
@@ -342,6 +344,16 @@ def argmax_device(logits, out=None, stream=None):
         out = torch.empty(rows, dtype=torch.int32, device=logits.device)
     _check(fn(logits.data_ptr(), rows, vocab, logits.stride(0), out.data_ptr(), _stream_ptr(stream)), "argmax")
     return out
+
+
+def set_f32_gemv(kind: int) -> int:
+    """Select the FP32-mode GEMV kernel process-wide (0 automatic: the
+    row-per-lane kernel for up to 4 rows; 1 the slot-per-lane kernel); returns
+    the previous setting."""
+    prev = _library().needle2_b200_set_f32_gemv(int(kind))
+    if prev < 0:
+        raise ValueError(last_error())
+    return prev
 
 
 def set_int8_gemv(kind: int) -> int:
