@@ -178,11 +178,13 @@ int needle2_cq_geometry(void *handle, int *geometry6);
 int needle2_b200_set_int8_gemv(int kind);
 
 /* Which kernel runs FP32-mode GEMVs of up to 8 activation rows, process-wide:
- * 0 automatic (the row-per-lane kernel for up to 4 rows where the staged
- * activations fit, the slot-per-lane kernel otherwise), 1 always the
- * slot-per-lane kernel.  Both compute CQ::linear's sums in FP32 (association
- * differs; results agree within FP32 rounding); the switch exists for tests
- * and measurements.  Returns the previous setting, or -1 for an unknown kind. */
+ * 0 automatic (one activation row: the product-table cluster kernel; up to 4
+ * rows: the row-per-lane kernel; where their shared-memory tables fit, the
+ * slot-per-lane kernel otherwise), 1 always the slot-per-lane kernel, 2 the
+ * row-per-lane kernel without the product table.  All compute CQ::linear's
+ * sums in FP32 (association differs; results agree within FP32 rounding); the
+ * switch exists for tests and measurements.  Returns the previous setting, or
+ * -1 for an unknown kind. */
 int needle2_b200_set_f32_gemv(int kind);
 
 /* ---- additive: batched INT8 KV cache with a shared prefix ---------------- */

@@ -112,6 +112,8 @@ struct Matrix {
     float *d_nsT = nullptr;         // int8 mode: group scales for the prefill GEMM
     uint16_t *d_whl = nullptr;      // FP32 mode: bf16 hi/lo weights for the prefill GEMM (made at first use)
     uint16_t *d_normsF = nullptr;   // int8 mode: fragment-order norms
+    uint8_t *d_blocked = nullptr;   // FP32 mode: row-block weights for the decode GEMV
+    uint16_t *d_normsB = nullptr;   // FP32 mode: row-block norms
     Scratch<float> x, y, rot, xs;
     Scratch<int8_t> q;
     Scratch<uint16_t> ahl;   // FP32 mode: bf16 hi/lo activations for the prefill GEMM
@@ -135,6 +137,8 @@ struct Matrix {
         if (d_nsT) cudaFree(d_nsT);
         if (d_whl) cudaFree(d_whl);
         if (d_normsF) cudaFree(d_normsF);
+        if (d_blocked) cudaFree(d_blocked);
+        if (d_normsB) cudaFree(d_normsB);
         if (stream) cudaStreamDestroy(stream);
     }
 };
@@ -273,6 +277,21 @@ Matrix *create_matrix(const uint8_t *packed, const uint16_t *norms, int out, int
         }
         w.frag = m->d_frag;
         w.normsF = m->d_normsF;
+    }
+    if (!sdot && (bits == 2 || bits == 4) && (group == 64 || group == 128 || group == 256) && w.rowbytes % 16 == 0) {
+        // row-block copy for the FP32 decode GEMV, repacked on the device
+        e = cudaMalloc(&m->d_blocked, nb200::blocked_bytes(out, w.groups, group, bits));
+        if (e == cudaSuccess) e = cudaMalloc(&m->d_normsB, sizeof(uint16_t) * nb200::blocked_norm_count(out, w.groups));
+        bool ok = e == cudaSuccess && nb200::build_blocked_layout(m->d_packed, m->d_norms, out, w.groups, group, bits,
+                                                                   w.rowbytes, m->d_blocked, m->d_normsB, m->stream);
+        if (ok) ok = cudaStreamSynchronize(m->stream) == cudaSuccess;
+        if (!ok) {
+            if (e != cudaSuccess) set_error(std::string("CQ device upload failed: ") + cudaGetErrorString(e));
+            delete m;
+            return nullptr;
+        }
+        w.blocked = m->d_blocked;
+        w.normsB = m->d_normsB;
     }
     return m;
 }
@@ -524,6 +543,8 @@ bool multiply_many(Matrix *const *ms, int count, float *const *ys, int batch, cu
                 b.mat[j].normsT = wj.normsT;
                 b.mat[j].frag = wj.frag;
                 b.mat[j].normsF = wj.normsF;
+                b.mat[j].blocked = wj.blocked;
+                b.mat[j].normsB = wj.normsB;
                 b.mat[j].out = wj.out;
                 b.mat[j].y = ys[i0 + j] + (size_t)r0 * wj.out;
             }
@@ -906,8 +927,9 @@ extern "C" int needle2_b200_set_int8_gemv(int kind) {
 
 extern "C" int needle2_b200_set_f32_gemv(int kind) {
     const int previous = nb200::f32_gemv_kernel();
-    if (kind < 0 || kind > 1) {
-        nb200::set_error("FP32 GEMV kernel kind must be 0 (automatic) or 1 (slot-per-lane kernel)");
+    if (kind < 0 || kind > 2) {
+        nb200::set_error("FP32 GEMV kernel kind must be 0 (automatic), 1 (slot-per-lane kernel) or 2 (row-per-lane "
+                         "kernel without the product table)");
         return -1;
     }
     nb200::set_f32_gemv_kernel(kind);

@@ -738,7 +738,9 @@ bool launch_gemv(const GemvBatch &b, bool i8, cudaStream_t st) {
         return false;
     }
     if (!i8) {
-        if (f32_gemv_kernel() == 0 && b.M <= gemv_rows_max_rows(b.bits, b.group, b.groups))
+        bool blocked = true;
+        for (int j = 0; j < b.nmat; ++j) blocked = blocked && b.mat[j].blocked && b.mat[j].normsB;
+        if (f32_gemv_kernel() != 1 && blocked && b.M <= gemv_rows_max_rows(b.bits, b.group, b.groups))
             return launch_gemv_rows(b, st);
         return dispatch<false>(b, st);
     }

@@ -17,6 +17,8 @@ struct GemvMatrix {
     const uint16_t *normsT;  // int8 mode: [tile][groups rounded up to 8][128] FP16 bits, or null
     const uint8_t *frag;     // int8 mode: fragment-order copy (build_frag_layout), or null
     const uint16_t *normsF;  // int8 mode: norms [16-row tile][group][row g: (g, g + 8)], or null
+    const uint8_t *blocked;  // FP32 mode: row-block copy (build_blocked_layout), or null
+    const uint16_t *normsB;  // FP32 mode: norms [32-row block][group][32 rows], or null
     float *y;                // [M][out]
     int out;
 };
@@ -63,11 +65,23 @@ bool launch_gemv_mma(const GemvBatch &b, cudaStream_t st);
 int gemv_tc_max_rows(int bits, int group, int groups);
 bool launch_gemv_tc(const GemvBatch &b, cudaStream_t st);
 // FP32-mode GEMV with one output row per lane (cq_gemv_rows.cu) for up to
-// gemv_rows_max_rows activation rows; launch_gemv routes FP32 batches there.
+// gemv_rows_max_rows activation rows; launch_gemv routes FP32 batches there
+// when every matrix carries the row-block copy: rows in blocks of 32; per
+// block and group, the group's packed bytes in units of U bytes (32 where a
+// group's bytes are a multiple of 32, else 16), unit c of all 32 rows stored
+// one after another, so one warp load reads one contiguous span of 32 * U
+// bytes; rows past the matrix are zero.  normsB holds per block and group the
+// 32 rows' norms.
+size_t blocked_bytes(int out, int groups, int group, int bits);
+size_t blocked_norm_count(int out, int groups);
+bool build_blocked_layout(const uint8_t *packed, const uint16_t *norms, int out, int groups, int group, int bits,
+                          int rowbytes, uint8_t *blocked, uint16_t *normsB, cudaStream_t st);
 int gemv_rows_max_rows(int bits, int group, int groups);
 bool launch_gemv_rows(const GemvBatch &b, cudaStream_t st);
-// Which FP32 GEMV kernel launch_gemv uses: 0 automatic (the row kernel where it
-// fits), 1 the slot-per-lane kernel of cq_gemv.cu.
+// Which FP32 GEMV kernel launch_gemv uses: 0 automatic (for one activation row
+// the product-table cluster kernel where its table fits, else the row kernel
+// where it fits), 1 the slot-per-lane kernel of cq_gemv.cu, 2 the row kernel
+// without the product table.
 void set_f32_gemv_kernel(int kind);
 int f32_gemv_kernel();
 // int8 GEMV with weights as the mma.sync A operand (cq_gemv_frag.cu).  The

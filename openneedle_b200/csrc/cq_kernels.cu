@@ -526,6 +526,8 @@ GemvBatch single_batch(const CQDevice &w) {
     b.mat[0].normsT = w.normsT;
     b.mat[0].frag = w.frag;
     b.mat[0].normsF = w.normsF;
+    b.mat[0].blocked = w.blocked;
+    b.mat[0].normsB = w.normsB;
     b.mat[0].out = w.out;
     b.bits = w.bits;
     b.group = w.group;

@@ -19,6 +19,8 @@ struct CQDevice {
     const uint16_t *normsT;   // SDOT: norms [tile][groups rounded up to 8][128 rows], or null
     const uint8_t *frag;      // SDOT: fragment-order copy for the warp-MMA kernel, or null
     const uint16_t *normsF;   // SDOT: norms in fragment order, or null
+    const uint8_t *blocked;   // FP32: row-block copy for the row GEMV kernels (see blocked_bytes), or null
+    const uint16_t *normsB;   // FP32: norms of the row-block copy, or null
     float lut[16];            // FP32 mode: value of each stored index
     uint32_t ctab[4];         // SDOT: int8 centroids, four per word
     uint32_t ntab[2], ptab[2];   // SDOT CQ4 sign split: |c| of entries 0-7, c of entries 8-15

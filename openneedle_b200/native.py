@@ -348,8 +348,9 @@ def argmax_device(logits, out=None, stream=None):
 
 def set_f32_gemv(kind: int) -> int:
     """Select the FP32-mode GEMV kernel process-wide (0 automatic: the
-    row-per-lane kernel for up to 4 rows; 1 the slot-per-lane kernel); returns
-    the previous setting."""
+    product-table cluster kernel for one row, the row-per-lane kernel for up to
+    4 rows; 1 the slot-per-lane kernel; 2 the row-per-lane kernel without the
+    product table); returns the previous setting."""
     prev = _library().needle2_b200_set_f32_gemv(int(kind))
     if prev < 0:
         raise ValueError(last_error())

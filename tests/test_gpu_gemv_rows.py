@@ -1,9 +1,10 @@
-"""GPU parity of the FP32-mode row-per-lane GEMV (decode batches of up to 4
-rows) against the oracle's CQ::linear, within the FP32 tolerance
-max|y - y_ref| / max|y_ref| <= 1e-4, and against the slot-per-lane kernel.
+"""GPU parity of the FP32-mode decode GEMVs against the oracle's CQ::linear,
+within the FP32 tolerance max|y - y_ref| / max|y_ref| <= 1e-4: the
+product-table cluster kernel (one activation row), the row-per-lane kernel
+(up to 4 rows) and the slot-per-lane kernel, also against one another.
 Shapes cover row counts that leave a partial 32-row block, group counts that
-split over 1, 2, 4 and 8 warps (including a count that is not a power of two),
-2- and 4-bit storage and group sizes 64, 128 and 256."""
+split over 1, 2, 4 and 8 warps or cluster CTAs (including a count that is not
+a power of two), 2- and 4-bit storage and group sizes 64, 128 and 256."""
 import numpy as np
 import pytest
 
@@ -35,15 +36,19 @@ def test_rows_kernel_against_oracle(native, oracle_lib, f32_kind, bits, group, d
     q = native.NativeCQ(packed, norms, shape, bits, group, cb)
     x = np.random.default_rng(dim + bits).normal(size=(4, dim)).astype(np.float32)
     for m in (1, 2, 3, 4):
-        y = q.linear(x[:m])
         ref = oracle_lib.cq_linear(packed, norms, shape, bits, group, cb, x[:m])
-        assert rel_err(y, ref) <= FP32_REL_TOL, (m, rel_err(y, ref))
-        # the slot-per-lane kernel computes the same sums in another order
-        native.set_f32_gemv(1)
-        y_slot = q.linear(x[:m])
-        native.set_f32_gemv(0)
-        assert rel_err(y_slot, ref) <= FP32_REL_TOL
-        assert rel_err(y, y_slot) <= FP32_REL_TOL
+        # automatic choice, slot-per-lane, row-per-lane without the table: the
+        # same sums in different orders
+        ys = []
+        for kind in (0, 1, 2):
+            native.set_f32_gemv(kind)
+            ys.append(q.linear(x[:m]))
+            native.set_f32_gemv(0)
+            assert rel_err(ys[-1], ref) <= FP32_REL_TOL, (m, kind, rel_err(ys[-1], ref))
+        assert rel_err(ys[0], ys[1]) <= FP32_REL_TOL
+        assert rel_err(ys[2], ys[1]) <= FP32_REL_TOL
+        # repeated calls give identical results (no atomics, fixed order)
+        np.testing.assert_array_equal(q.linear(x[:m]), ys[0])
     assert native.device_fault() == 0
 
 
