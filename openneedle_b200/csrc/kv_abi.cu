@@ -6,6 +6,7 @@
 // prefix" is simply continuing from position P.
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <new>
 #include <string>
 #include <vector>
@@ -103,8 +104,35 @@ int max_visible(const KVPool &kv, const int *positions, int count, int tokens) {
     return best;
 }
 
+// Session ids and positions of up to kIndexArgMax entries travel as a kernel
+// argument, which the launch copies from the host arrays as it is enqueued:
+// no staging copy of pageable memory (which a stream capture cannot record)
+// and no pinned buffer whose reuse would have to wait for the stream.
+constexpr int kIndexArgMax = 1024;
+struct IndexArgs {
+    int count;
+    int ids[kIndexArgMax];
+    int pos[kIndexArgMax];
+};
+
+__global__ void index_upload_kernel(const __grid_constant__ IndexArgs a, int *ids, int *pos) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.count; i += gridDim.x * blockDim.x) {
+        ids[i] = a.ids[i];
+        pos[i] = a.pos[i];
+    }
+}
+
 bool upload_index(KVPool &kv, const int *session_ids, const int *positions, int count, cudaStream_t st) {
     if (!kv.ids.reserve(count) || !kv.pos.reserve(count)) return false;
+    if (count <= kIndexArgMax) {
+        IndexArgs a;
+        a.count = count;
+        std::memcpy(a.ids, session_ids, sizeof(int) * count);
+        std::memcpy(a.pos, positions, sizeof(int) * count);
+        index_upload_kernel<<<1, 256, 0, st>>>(a, kv.ids.ptr, kv.pos.ptr);
+        NB_CUDA_TRY(cudaGetLastError());
+        return true;
+    }
     NB_CUDA_TRY(cudaMemcpyAsync(kv.ids.ptr, session_ids, sizeof(int) * count, cudaMemcpyHostToDevice, st));
     NB_CUDA_TRY(cudaMemcpyAsync(kv.pos.ptr, positions, sizeof(int) * count, cudaMemcpyHostToDevice, st));
     return true;
