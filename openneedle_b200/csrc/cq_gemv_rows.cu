@@ -360,10 +360,17 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
 }
 
 constexpr size_t kPtabMax = 96 * 1024;   // product-table bytes per CTA (two CTAs per SM)
+
+// CTAs per SM the table kernel is compiled for: as many as fit without
+// register spills for the group's register buffers (occupancy hides the
+// weight loads' latency; 4 CTAs = 64 registers a thread).
+__host__ __device__ constexpr int ptab_min_blocks(int bits, int group) {
+    return group * bits / 8 >= 128 ? 2 : (bits == 4 || group == 64 ? 4 : 3);
+}
 constexpr int kPtabBlocks = 4;           // row blocks a warp takes between two cluster barriers
 
 template <int BITS, int G, int D>
-__global__ void __launch_bounds__(kRowsThreads, 3) cq_gemv_ptab_kernel(const GemvBatch b, const int total_blocks) {
+__global__ void __launch_bounds__(kRowsThreads, ptab_min_blocks(BITS, G)) cq_gemv_ptab_kernel(const GemvBatch b, const int total_blocks) {
     constexpr int BYTES = G * BITS / 8;
     constexpr int CHUNKS = BYTES / 16;
     constexpr int BU = blocked_unit(BYTES);
