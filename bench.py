@@ -122,8 +122,29 @@ def cpu_threads() -> int:
         return os.cpu_count() or 1
 
 
+def ref_quantize():
+    """The reference's own CQ packer (needle2/quantize.py, as BASELINE config 1
+    prescribes), from the reference package: NEEDLE2_REFERENCE_SRC, default the
+    copy pip installed into baseline/_ref.  It only builds the synthetic inputs."""
+    root = Path(os.environ.get("NEEDLE2_REFERENCE_SRC", str(ROOT / "baseline" / "_ref")))
+    if not (root / "needle2" / "quantize.py").is_file():
+        raise SystemExit(f"reference package not found under {root} (needed to pack the synthetic weights); "
+                         "install it into baseline/_ref or set NEEDLE2_REFERENCE_SRC")
+    if str(root) not in sys.path:
+        sys.path.insert(0, str(root))
+    from needle2 import quantize
+    return quantize
+
+
+def synthetic_matrix(rows, cols, bits, group, seed):
+    """W ~ N(0, 0.02) from default_rng(seed), packed by the reference's quantizer."""
+    q = ref_quantize()
+    w = np.random.default_rng(seed).normal(0.0, 0.02, (rows, cols)).astype(np.float32)
+    packed, norms = q.quantize_matrix(w, bits, group)
+    return packed, norms, q.codebook(bits, group)
+
+
 def weights():
-    from openneedle_b200.quantize import synthetic_matrix
     return synthetic_matrix(N_OUT, K_IN, BITS, GROUP, seed=0)
 
 
@@ -285,7 +306,6 @@ def prefill_gemm(lib, dev, stream, reps=20):
     CQ4 8192 x 4096 matrix (group 128); the GEMM kernel alone (quantised input
     prepared outside the timed launches), against twice the measured bf16 dense
     rate (B200 issues int8 MMAs at twice the bf16 rate)."""
-    from openneedle_b200.quantize import synthetic_matrix
     m, n, k = 2048, 8192, 4096
     packed, norms, cb = synthetic_matrix(n, k, 4, GROUP, seed=3)
     ms, fms = _gemm_ms(lib, dev, stream, packed, norms, cb, m, n, k, 4, reps)
@@ -312,7 +332,7 @@ def prefill_gemm_sweep(lib, dev, stream, reps=10):
     codes and group norms are seeded random bytes / half values of the real
     layout: the kernels' time does not depend on the values (parity is covered by
     the tests), and quantising 18 matrices on the host would take minutes."""
-    from openneedle_b200.quantize import codebook
+    codebook = ref_quantize().codebook
     rng = np.random.default_rng(5)
     m = 2048
     bf16 = _bf16_peak() or 1590.0
@@ -434,12 +454,30 @@ def sharded_gemm(dev, stream, world, dist, packed, norms, cb, m=2048, reps=10):
     t = torch.tensor([fused, nccl, local], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     fused, nccl, local = t.tolist()
+    # correctness on every rank: the fused and the NCCL all-gather against the
+    # whole matrix on one GPU (same int8 GEMM per row, so bit for bit)
+    from openneedle_b200.native import DeviceMatrix
+    whole = DeviceMatrix(packed, norms, (N_OUT, K_IN), BITS, GROUP, cb)
+    with torch.cuda.stream(stream):
+        y_single = torch.empty(m, N_OUT, device=dev)
+        whole.sdot.linear_device(x, y_single, stream)
+        y_fused = sh.forward(x, stream).clone()
+        y_nccl = sh.forward_nccl(x, stream).clone()
+    torch.cuda.synchronize(dev)
+    flags = torch.tensor([float(torch.equal(y_fused, y_single)), float(torch.equal(y_nccl, y_single))],
+                         device=dev)
+    dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+    match_fused, match_nccl = (bool(v) for v in flags.tolist())
+    whole.close()
+    del y_single, y_fused, y_nccl
     sent = m * sh.ns * 4 * (world - 1)
     flops = 2.0 * m * N_OUT * K_IN
     res = {"config": f"{N_OUT}x{K_IN} CQ4 int8 mode, M={m}, {sh.ns} rows per GPU, outputs all-gathered to every GPU",
            "fused_ms": fused, "nccl_ms": nccl, "local_gemm_ms": local,
            "fused_top_s": flops / (fused * 1e-3) / 1e12, "nccl_top_s": flops / (nccl * 1e-3) / 1e12,
            "nvlink_bytes_sent_per_rank": sent, "fused_send_gbs_per_rank": sent / (fused * 1e-3) / 1e9,
+           "match": match_fused and match_nccl, "match_fused": match_fused, "match_nccl": match_nccl,
+           "match_against": "the whole matrix's int8 GEMM on one GPU, bitwise, on every rank",
            "timing": "max over ranks; each call = prepare + GEMM (+ exchange); fused includes the barrier all-reduce"}
     sh.close()
     return res
@@ -501,20 +539,6 @@ def run_native(args, rank, world, dist):
     n_kernel = max(5, min(args.steps, 40))
     fused_ms = kernel_ms(lib, handles, x, yp, stream, True, n_kernel)
     single_ms = kernel_ms(lib, handles[:1], x, yp, stream, True, n_kernel)
-    # the int8 GEMV kernels side by side (the automatic choice is the fragment-order one)
-    int8_kernels = {}
-    for kind, name in ((1, "diag_mma"), (2, "tcgen05"), (3, "frag_mma")):
-        prev = lib.needle2_b200_set_int8_gemv(kind)
-        # the tcgen05 kernel reads a tile-major copy that handles build only while it is selected
-        hs = [create(lib, packed, norms, cb, True) for _ in range(copies)] if kind == 2 else handles
-        kernel_ms(lib, hs, x, yp, stream, True, 3)
-        ms = kernel_ms(lib, hs, x, yp, stream, True, n_kernel)
-        if kind == 2:
-            for h in hs:
-                lib.needle2_sdot_destroy(h)
-        lib.needle2_b200_set_int8_gemv(prev)
-        int8_kernels[name] = {"kernel_ms": ms, "achieved_gbs": bytes_step / (ms * 1e-3) / 1e9}
-
     e2e = None
     if not args.skip_e2e:
         # the step's input and outputs in page-locked host memory (torch's pinned allocator)
@@ -599,7 +623,6 @@ def run_native(args, rank, world, dist):
         "timing": "K steps captured in one CUDA graph, replayed once between CUDA events on the launching stream",
         "clocks": clocks.summary(),
         "fp32_mode": fp32,
-        "int8_kernels": int8_kernels,
     }
     for h in handles:
         lib.needle2_sdot_destroy(h)

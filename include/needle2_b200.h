@@ -88,7 +88,11 @@ int needle2_sdot_linear_device(void *handle, const float *x, float *y, int batch
  * a device share it, so two calls whose kernels may overlap (different streams,
  * or different threads without ordering) race: serialise them.  The first call
  * on a device looks up the scratch address; make one call outside any stream
- * capture before capturing. */
+ * capture before capturing.  The address is looked up again whenever the
+ * device's context has changed (after cudaDeviceReset, for instance).  It
+ * always runs the int8 GEMV kernel, never the tensor-core GEMM that
+ * needle2_sdot_linear_device uses from 64 activation rows on, so
+ * prefill-sized batches are slower here than there (same results). */
 int needle2_sdot_linear_device_noalloc(void *handle, const float *x, float *y, int batch, void *stream);
 
 /* Several matrices against one activation batch: ys[i][batch][out_i].  Matrices
@@ -166,16 +170,6 @@ int needle2_b200_device_fault(void);
 
 /* Geometry of a handle: out, in, bits, group, padded, groups. */
 int needle2_cq_geometry(void *handle, int *geometry6);
-
-/* Which kernel runs int8 (SDOT) GEMVs of up to 16 activation rows, process-wide:
- * 0 automatic (fragment-order warp-MMA kernel where the matrix geometry allows
- * it, the diagonal warp-MMA kernel otherwise), 1 diagonal warp MMA, 2 tcgen05
- * tensor-core kernel, 3 fragment-order warp MMA.  All give bit-identical
- * results; the switch exists for tests and measurements.  The tcgen05 kernel
- * reads a tile-major weight copy that SDOT handles only build while kind 2 is
- * selected, so select it before creating the handles it should run on.
- * Returns the previous setting, or -1 for an unknown kind. */
-int needle2_b200_set_int8_gemv(int kind);
 
 /* Which kernel runs FP32-mode GEMVs of up to 8 activation rows, process-wide:
  * 0 automatic (one activation row: the product-table cluster kernel; up to 4

@@ -105,8 +105,6 @@ struct Matrix {
     uint8_t *d_packed = nullptr;
     uint16_t *d_norms = nullptr;
     uint16_t *d_norms8 = nullptr;   // padded copy when groups % 8 != 0 (int8 mode)
-    uint8_t *d_tiled = nullptr;     // int8 mode: tile-major weights for the tcgen05 kernel
-    uint16_t *d_normsT = nullptr;   // int8 mode: tile-major norms
     uint8_t *d_frag = nullptr;      // int8 mode: fragment-order weights for the warp-MMA kernel
     int8_t *d_w8 = nullptr;         // int8 mode: decoded weights for the prefill GEMM (made at first use)
     float *d_nsT = nullptr;         // int8 mode: group scales for the prefill GEMM
@@ -130,8 +128,6 @@ struct Matrix {
         if (d_packed) cudaFree(d_packed);
         if (d_norms) cudaFree(d_norms);
         if (d_norms8) cudaFree(d_norms8);
-        if (d_tiled) cudaFree(d_tiled);
-        if (d_normsT) cudaFree(d_normsT);
         if (d_frag) cudaFree(d_frag);
         if (d_w8) cudaFree(d_w8);
         if (d_nsT) cudaFree(d_nsT);
@@ -237,32 +233,6 @@ Matrix *create_matrix(const uint8_t *packed, const uint16_t *norms, int out, int
         w.norms8 = m->d_norms8;
     }
     if (sdot && (bits == 2 || bits == 4) && (group == 64 || group == 128 || group == 256)) {
-        if (nb200::int8_gemv_kernel() == 2) {
-            // tile-major copy for the tcgen05 kernel (zero rows pad the last tile); made
-            // only while that kernel is selected, since the default kernel does not read it
-            const int gb = group * bits / 8, g8 = (w.groups + 7) / 8 * 8;
-            const size_t tiles = ((size_t)out + 127) / 128;
-            std::vector<uint8_t> tp(tiles * g8 * 128 * (size_t)gb, 0);
-            std::vector<uint16_t> tn(tiles * g8 * 128, 0);
-            for (int r = 0; r < out; ++r)
-                for (int j = 0; j < w.groups; ++j) {
-                    const uint8_t *src = packed + (size_t)r * w.rowbytes + (size_t)j * gb;
-                    for (int b = 0; b < gb; b += 16) std::memcpy(&tp[nb200::tiled_offset(r, j, b, gb, g8)], src + b, 16);
-                    tn[((size_t)(r / 128) * g8 + j) * 128 + r % 128] = norms[(size_t)r * w.groups + j];
-                }
-            e = cudaMalloc(&m->d_tiled, tp.size());
-            if (e == cudaSuccess) e = cudaMalloc(&m->d_normsT, sizeof(uint16_t) * tn.size());
-            if (e == cudaSuccess) e = cudaMemcpy(m->d_tiled, tp.data(), tp.size(), cudaMemcpyHostToDevice);
-            if (e == cudaSuccess)
-                e = cudaMemcpy(m->d_normsT, tn.data(), sizeof(uint16_t) * tn.size(), cudaMemcpyHostToDevice);
-            if (e != cudaSuccess) {
-                set_error(std::string("CQ device upload failed: ") + cudaGetErrorString(e));
-                delete m;
-                return nullptr;
-            }
-            w.tiled = m->d_tiled;
-            w.normsT = m->d_normsT;
-        }
         // fragment-order copy, repacked on the device from the row-major upload
         const size_t fb = nb200::frag_bytes(out, w.groups, group, bits), fnc = nb200::frag_norm_count(out, w.groups);
         e = cudaMalloc(&m->d_frag, fb);
@@ -308,13 +278,21 @@ bool ensure_gemm_copy(Matrix *m, cudaStream_t st) {
         if (e == cudaSuccess) e = cudaMalloc(&m->d_nsT, sizeof(float) * gemm_ns_count(w.out, w.groups));
         if (e != cudaSuccess) {
             if (m->d_w8) cudaFree(m->d_w8);
+            if (m->d_nsT) cudaFree(m->d_nsT);
             m->d_w8 = nullptr;
+            m->d_nsT = nullptr;
             set_error(std::string("prefill weight allocation failed: ") + cudaGetErrorString(e));
             return false;
         }
         if (!gemm_prepare(w.packed, w.norms, w.out, w.groups, w.group, w.bits, w.rowbytes, w.padded, w.ctab,
-                          w.centroid_scale, m->d_w8, m->d_nsT, st))
+                          w.centroid_scale, m->d_w8, m->d_nsT, st)) {
+            // leave no half-made copy behind: the next call prepares again
+            cudaFree(m->d_w8);
+            cudaFree(m->d_nsT);
+            m->d_w8 = nullptr;
+            m->d_nsT = nullptr;
             return false;
+        }
     }
     return true;
 }
@@ -539,8 +517,6 @@ bool multiply_many(Matrix *const *ms, int count, float *const *ys, int batch, cu
                 b.mat[j].packed = wj.packed;
                 b.mat[j].norms = wj.norms;
                 b.mat[j].norms8 = wj.norms8;
-                b.mat[j].tiled = wj.tiled;
-                b.mat[j].normsT = wj.normsT;
                 b.mat[j].frag = wj.frag;
                 b.mat[j].normsF = wj.normsF;
                 b.mat[j].blocked = wj.blocked;
@@ -864,27 +840,60 @@ struct NoAllocScratch {
     float *xs = nullptr;
 };
 
-// Device addresses of the two arrays on `device`, looked up once per device.
+// Unique id of the calling thread's current CUDA context (cuCtxGetId, reached
+// through the runtime's driver entry points so the library links no libcuda),
+// or 0 when it cannot be read.  A device reset destroys the primary context
+// and the next call creates a new one with a new id, in which the library's
+// module -- and with it the scratch arrays -- is loaded again, possibly at
+// other addresses.
+unsigned long long current_context_id() {
+    using GetCurrent = int (*)(void **);
+    using GetId = int (*)(void *, unsigned long long *);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void *fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(fn);
+        fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(fn);
+    });
+    void *ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current && get_id && get_current(&ctx) == 0 && ctx && get_id(ctx, &id) == 0) return id;
+    return 0;
+}
+
+// Device addresses of the two arrays on `device` (the current device), looked
+// up once per device and context: a lookup is reused only while the context
+// it was made in is still the current one.
 bool noalloc_scratch(int device, NoAllocScratch &out) {
     static std::mutex mu;
     static NoAllocScratch cache[64];
-    static bool ready[64] = {};
+    static unsigned long long context[64] = {};
     if (device < 0 || device >= 64) {
         set_error("device ordinal outside the no-allocation scratch table");
         return false;
     }
+    const unsigned long long ctx = current_context_id();
     std::lock_guard<std::mutex> lock(mu);
-    if (!ready[device]) {
+    if (!ctx || context[device] != ctx) {
         void *q = nullptr, *xs = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&q, g_noalloc_q);
         if (e == cudaSuccess) e = cudaGetSymbolAddress(&xs, g_noalloc_xs);
         if (e != cudaSuccess || !q || !xs) {
+            context[device] = 0;
             set_error(std::string("no-allocation scratch lookup failed: ") + cudaGetErrorString(e));
             return false;
         }
         cache[device].q = static_cast<int8_t *>(q);
         cache[device].xs = static_cast<float *>(xs);
-        ready[device] = true;
+        context[device] = ctx;
     }
     out = cache[device];
     return true;
@@ -912,17 +921,6 @@ extern "C" int needle2_sdot_linear_device_noalloc(void *handle, const float *x, 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (!nb200::launch_quantize(w, x, batch, s.q, s.xs, st)) return -1;
     return nb200::launch_gemv_i8(w, s.q, s.xs, batch, y, w.out, nullptr, st) ? 0 : -1;
-}
-
-extern "C" int needle2_b200_set_int8_gemv(int kind) {
-    const int previous = nb200::int8_gemv_kernel();
-    if (kind < 0 || kind > 3) {
-        nb200::set_error("int8 GEMV kernel kind must be 0 (automatic), 1 (diagonal warp MMA), 2 (tcgen05) or "
-                         "3 (fragment-order warp MMA)");
-        return -1;
-    }
-    nb200::set_int8_gemv_kernel(kind);
-    return previous;
 }
 
 extern "C" int needle2_b200_set_f32_gemv(int kind) {

@@ -705,25 +705,8 @@ bool dispatch(const GemvBatch &b, cudaStream_t st) {
 
 }  // namespace
 
-namespace {
-int g_int8_gemv_kind = 0;
-}
-
-void set_int8_gemv_kernel(int kind) { g_int8_gemv_kind = kind; }
-int int8_gemv_kernel() { return g_int8_gemv_kind; }
-
 int gemv_max_rows(int bits, int group, int groups, bool i8) {
-    if (i8) {
-        switch (g_int8_gemv_kind) {
-            case 1: return gemv_mma_max_rows(bits, group, groups);
-            case 2: return gemv_tc_max_rows(bits, group, groups);
-            case 3: return gemv_frag_max_rows(bits, group, groups);
-            default: {
-                const int f = gemv_frag_max_rows(bits, group, groups);
-                return f > 0 ? f : gemv_mma_max_rows(bits, group, groups);
-            }
-        }
-    }
+    if (i8) return gemv_frag_max_rows(bits, group, groups);
     if ((bits != 2 && bits != 4) || (group != 64 && group != 128 && group != 256)) return 0;
     if (groups < 1 || groups > 32) return 0;
     for (int m : {8, 4, 2, 1})
@@ -744,20 +727,12 @@ bool launch_gemv(const GemvBatch &b, bool i8, cudaStream_t st) {
             return launch_gemv_rows(b, st);
         return dispatch<false>(b, st);
     }
-    bool tiled = true, frag = true;
-    for (int j = 0; j < b.nmat; ++j) {
-        tiled = tiled && b.mat[j].tiled && b.mat[j].normsT;
-        frag = frag && b.mat[j].frag && b.mat[j].normsF;
-    }
-    const int kind = g_int8_gemv_kind;
-    if ((kind == 0 || kind == 3) && frag && b.M <= gemv_frag_max_rows(b.bits, b.group, b.groups))
-        return launch_gemv_frag(b, st);
-    if (kind == 2 && tiled && b.M <= gemv_tc_max_rows(b.bits, b.group, b.groups)) return launch_gemv_tc(b, st);
-    if (kind == 2 || kind == 3) {
-        set_error("the selected int8 GEMV kernel cannot run this launch");
-        return false;
-    }
-    return launch_gemv_mma(b, st);
+    for (int j = 0; j < b.nmat; ++j)
+        if (!b.mat[j].frag || !b.mat[j].normsF) {
+            set_error("int8 GEMV needs the fragment-order copy of every matrix");
+            return false;
+        }
+    return launch_gemv_frag(b, st);
 }
 
 int read_and_clear_gemv_fault() {

@@ -13,8 +13,6 @@ struct GemvMatrix {
     const uint8_t *packed;   // [out][rowbytes]
     const uint16_t *norms;   // [out][groups] FP16 bits
     const uint16_t *norms8;  // [out][groups rounded up to 8] FP16 bits (int8 mode)
-    const uint8_t *tiled;    // int8 mode, tcgen05 layout (tiled_offset) or null
-    const uint16_t *normsT;  // int8 mode: [tile][groups rounded up to 8][128] FP16 bits, or null
     const uint8_t *frag;     // int8 mode: fragment-order copy (build_frag_layout), or null
     const uint16_t *normsF;  // int8 mode: norms [16-row tile][group][row g: (g, g + 8)], or null
     const uint8_t *blocked;  // FP32 mode: row-block copy (build_blocked_layout), or null
@@ -42,28 +40,9 @@ struct GemvBatch {
     float cs;                // SDOT: centroid scale
 };
 
-// Tile-major copy of a CQ matrix for the tcgen05 int8 GEMV: rows in tiles of
-// 128; within a tile, group by group, each row's packed bytes of the group
-// (gb = group * bits / 8) with its 16-byte chunks XOR-swizzled so that eight
-// consecutive rows reading the same chunk hit distinct shared-memory banks.
-// Byte b of row r (tile-local rl = r % 128), group j, lives at the returned offset.
-inline size_t tiled_offset(int r, int j, int b, int gb, int groups8) {
-    const int rl = r % 128, tile = r / 128;
-    const int chunks = gb / 16, rows_per_128 = gb < 128 ? 128 / gb : 1;
-    const int c = (b / 16) ^ ((rl / rows_per_128) & (chunks - 1));
-    return (((size_t)tile * groups8 + j) * 128 + rl) * gb + (size_t)c * 16 + b % 16;
-}
-
 // Activation rows one launch can take for this geometry (0: not supported).
 int gemv_max_rows(int bits, int group, int groups, bool i8);
 bool launch_gemv(const GemvBatch &b, bool i8, cudaStream_t st);
-// int8 (SDOT) GEMV with the products on the tensor cores (cq_gemv_mma.cu);
-// launch_gemv routes int8 batches here.
-int gemv_mma_max_rows(int bits, int group, int groups);
-bool launch_gemv_mma(const GemvBatch &b, cudaStream_t st);
-// int8 GEMV on tcgen05 (cq_gemv_tc.cu).
-int gemv_tc_max_rows(int bits, int group, int groups);
-bool launch_gemv_tc(const GemvBatch &b, cudaStream_t st);
 // FP32-mode GEMV with one output row per lane (cq_gemv_rows.cu) for up to
 // gemv_rows_max_rows activation rows; launch_gemv routes FP32 batches there
 // when every matrix carries the row-block copy: rows in blocks of 32; per
@@ -125,11 +104,6 @@ bool launch_gemm_f32x3(const uint16_t *a_hilo, int M, const uint16_t *w_hilo, in
 // Activation rows from which int8 products run as the tensor-core GEMM.
 constexpr int kGemmMinRows = 64;
 
-// Which int8 GEMV kernel launch_gemv uses: 0 automatic (fragment-order warp
-// MMA where the matrices carry that copy, else tcgen05, else the diagonal warp
-// MMA), 1 diagonal warp MMA, 2 tcgen05, 3 fragment-order warp MMA.
-void set_int8_gemv_kernel(int kind);
-int int8_gemv_kernel();
 // Fault flag of kernels with bounded waits (0 when none ran out); clears it.
 int read_and_clear_gemv_fault();
 

@@ -522,8 +522,6 @@ GemvBatch single_batch(const CQDevice &w) {
     b.mat[0].packed = w.packed;
     b.mat[0].norms = w.norms;
     b.mat[0].norms8 = w.norms8;
-    b.mat[0].tiled = w.tiled;
-    b.mat[0].normsT = w.normsT;
     b.mat[0].frag = w.frag;
     b.mat[0].normsF = w.normsF;
     b.mat[0].blocked = w.blocked;

@@ -15,8 +15,6 @@ struct CQDevice {
     const uint8_t *packed;    // [out][rowbytes] device
     const uint16_t *norms;    // [out][groups] FP16 bits, device
     const uint16_t *norms8;   // SDOT: norms with rows padded to a multiple of 8 groups (== norms when aligned)
-    const uint8_t *tiled;     // SDOT: packed weights tile-major for the tcgen05 kernel (see tiled_offset), or null
-    const uint16_t *normsT;   // SDOT: norms [tile][groups rounded up to 8][128 rows], or null
     const uint8_t *frag;      // SDOT: fragment-order copy for the warp-MMA kernel, or null
     const uint16_t *normsF;   // SDOT: norms in fragment order, or null
     const uint8_t *blocked;   // FP32: row-block copy for the row GEMV kernels (see blocked_bytes), or null

@@ -1,10 +1,11 @@
-"""ctypes access to libneedle2_b200.so, mirroring OpenNeedle's ``needle2/native.py``.
+"""ctypes access to libneedle2_b200.so for this package's own Python callers.
 
-``NativeCQ`` keeps the reference class's constructor, validation messages,
-``linear``/``linear_sdot``/``rows``/``dequantize`` methods and error types
-(needle2/native.py:165-279), so code written against the reference runs on
-the GPU unchanged.  The compute runs in CUDA kernels only: when the library or
-a GPU is missing, calls raise instead of falling back to any CPU path.
+The reference's Python (needle2/native.py: NativeCQ, NativeEngine) binds the
+same library unchanged through NEEDLE2_NATIVE_LIBRARY; this module adds what
+that layer has no call for: device-pointer forms, the SDOT debug exports,
+fused multi-matrix calls and the kernel switches.  The compute runs in CUDA
+kernels only: when the library or a GPU is missing, calls raise instead of
+falling back to any CPU path.
 """
 from __future__ import annotations
 
@@ -55,8 +56,6 @@ def _library() -> ct.CDLL:
     for name in ("needle2_cq_multiply_device", "needle2_sdot_multiply_device"):
         getattr(lib, name).argtypes = [_p, _p, _i, _p]
         getattr(lib, name).restype = _i
-    lib.needle2_b200_set_int8_gemv.argtypes = [_i]
-    lib.needle2_b200_set_int8_gemv.restype = _i
     lib.needle2_b200_set_f32_gemv.argtypes = [_i]
     lib.needle2_b200_set_f32_gemv.restype = _i
     lib.needle2_cq_linear_many_checked.argtypes = [ct.POINTER(_p), _i, _p, ct.POINTER(_p), _i, _i]
@@ -117,178 +116,159 @@ def _stream_ptr(stream) -> int | None:
     return int(getattr(stream, "cuda_stream", stream))
 
 
-class NativeCQ:
-    """A packed ``[out, in]`` matrix held in device memory.
+class Handle:
+    """One library handle of a CQ matrix: the FP32-mode matrix
+    (needle2_cq_create) or the int8 SDOT matrix (needle2_sdot_create).
 
-    The codebook must already include ``1/sqrt(group_size)`` as in a CACT header.
-    ``bits=5`` denotes signed ternary crumb storage with 3 centroids.
+    Host calls take numpy arrays whose last axis is the matrix's input width and
+    return float32 arrays whose last axis is its output width; the ``*_device``
+    calls take contiguous float32 CUDA tensors and enqueue on a stream.
     """
 
-    def __init__(self, packed, norms, shape, bits, group_size, codebook):
-        self.shape = tuple(int(v) for v in shape)
-        if len(self.shape) != 2 or min(self.shape) <= 0:
-            raise ValueError("NativeCQ requires a positive two-dimensional matrix shape")
-        self.bits, self.group_size = int(bits), int(group_size)
-        if self.bits not in (2, 3, 4, 5):
-            raise ValueError("CQ storage bits must be 2, 3, 4, or ternary marker 5")
-        if self.group_size < 8 or self.group_size & (self.group_size - 1):
-            raise ValueError("CQ group size must be a power of two >= 8")
-        out, dim = self.shape
-        limit = np.iinfo(np.int32).max
-        if max(out, dim, self.group_size) > limit or dim + self.group_size - 1 > limit:
-            raise ValueError("CQ dimensions exceed the native int32 interface")
-        padded = ((dim + self.group_size - 1) // self.group_size) * self.group_size
-        storage_bits = 2 if self.bits == 5 else self.bits
-        if padded * storage_bits > limit:
-            raise ValueError("CQ row bit count exceeds the native int32 interface")
-        self.padded = padded
-        self.packed = np.ascontiguousarray(packed, dtype=np.uint8).reshape(out, padded * storage_bits // 8)
-        self.norms = np.ascontiguousarray(norms, dtype=np.float16).reshape(out, padded // self.group_size)
-        self.codebook = np.ascontiguousarray(codebook, dtype=np.float32)
-        if self.codebook.shape != (3 if self.bits == 5 else 1 << self.bits,):
-            raise ValueError("Codebook has incorrect number of centroids")
-        if not np.isfinite(self.norms).all() or np.any(self.norms < 0):
-            raise ValueError("CQ norms must be finite and nonnegative")
-        if not np.isfinite(self.codebook).all() or not np.all(np.diff(self.codebook) > 0):
-            raise ValueError("CQ codebook must be finite and strictly sorted")
-        if self.bits == 5:
-            for shift in (0, 2, 4, 6):
-                if np.any(((self.packed >> shift) & 3) == 2):
-                    raise ValueError("Invalid ternary crumb code 2")
-        self._lib = _library()
-        self._handle = self._lib.needle2_cq_create(self.packed.ctypes.data, self.norms.ctypes.data, out, dim,
-                                                   self.bits, self.group_size, self.codebook.ctypes.data)
-        if not self._handle:
-            raise MemoryError(f"Could not construct native CQ matrix: {last_error()}")
+    def __init__(self, owner: "DeviceMatrix", sdot: bool):
+        self.owner, self.sdot = owner, bool(sdot)
+        lib = owner._lib
+        create = lib.needle2_sdot_create if sdot else lib.needle2_cq_create
+        out, inp = owner.shape
+        self.ptr = create(owner._packed.ctypes.data, owner._norms.ctypes.data, out, inp, owner.bits, owner.group,
+                          owner._codebook.ctypes.data)
+        if not self.ptr:
+            raise RuntimeError(f"{'needle2_sdot_create' if sdot else 'needle2_cq_create'}: {last_error()}")
 
-    @classmethod
-    def from_record(cls, record):
-        cb = record.codebook
-        if record.bits == 5 and cb is None:
-            cb = (np.array([-1.2240064, 0., 1.2240064], np.float64) / np.sqrt(record.group_size)).astype(np.float32)
-        return cls(record.packed, record.norms, record.shape, record.bits, record.group_size, cb)
+    def close(self) -> None:
+        if self.ptr:
+            lib = self.owner._lib
+            (lib.needle2_sdot_destroy if self.sdot else lib.needle2_cq_destroy)(self.ptr)
+            self.ptr = None
 
     def __del__(self):
-        if getattr(self, "_sdot_handle", None):
-            self._lib.needle2_sdot_destroy(self._sdot_handle)
-            self._sdot_handle = None
-        if getattr(self, "_handle", None):
-            self._lib.needle2_cq_destroy(self._handle)
-            self._handle = None
+        self.close()
 
-    @property
-    def groups(self) -> int:
-        return self.padded // self.group_size
-
-    def linear(self, x, threads: int = 1, *, lookup: int = 0):
+    def _rows(self, x):
         x = np.ascontiguousarray(x, dtype=np.float32)
-        if x.ndim < 1 or x.shape[-1] != self.shape[1]:
-            raise ValueError(f"Expected input last dimension {self.shape[1]}; got {x.shape}")
-        if not 1 <= int(threads) <= 256:
-            raise ValueError("threads must be between 1 and 256")
-        if (x.size // self.shape[1]) * self.shape[0] > np.iinfo(np.int32).max:
-            raise ValueError("CQ batch output count exceeds the native int32 interface")
-        y = np.empty(x.shape[:-1] + (self.shape[0],), dtype=np.float32)
-        if lookup not in (0, 1, 2, 3):
-            raise ValueError("lookup must be 0 (NEON), 1 (byte table), 2 (nibble table), or 3 (group byte table)")
-        batch = x.size // self.shape[1]
+        if x.ndim < 1 or x.shape[-1] != self.owner.shape[1]:
+            raise ValueError(f"input last dimension must be {self.owner.shape[1]}, got shape {x.shape}")
+        return x, x.size // self.owner.shape[1]
+
+    def __call__(self, x) -> np.ndarray:
+        """y = W x on the GPU from host memory (one synchronous call)."""
+        x, batch = self._rows(x)
+        y = np.empty(x.shape[:-1] + (self.owner.shape[0],), np.float32)
         if batch:
-            _check(self._lib.needle2_cq_linear_checked(self._handle, x.ctypes.data, y.ctypes.data, batch),
-                   "needle2_cq_linear")
+            fn = self.owner._lib.needle2_sdot_linear_checked if self.sdot else self.owner._lib.needle2_cq_linear_checked
+            _check(fn(self.ptr, x.ctypes.data, y.ctypes.data, batch), "linear")
         return y
 
-    def _sdot(self):
-        if self.bits not in (2, 4) or not 64 <= self.group_size <= 131072:
-            raise ValueError("SDOT requires CQ2/CQ4 and group size between 64 and 131072")
-        if not getattr(self, "_sdot_handle", None):
-            self._sdot_handle = self._lib.needle2_sdot_create(self.packed.ctypes.data, self.norms.ctypes.data,
-                                                              *self.shape, self.bits, self.group_size,
-                                                              self.codebook.ctypes.data)
-            if not self._sdot_handle:
-                raise RuntimeError(f"could not construct SDOT matrix: {last_error()}")
-        return self._sdot_handle
-
-    def _sdot_input(self, x, threads):
-        x = np.ascontiguousarray(x, dtype=np.float32)
-        if x.ndim < 1 or x.shape[-1] != self.shape[1] or not np.isfinite(x).all():
-            raise ValueError("SDOT input must have the expected last dimension and finite values")
-        if not 1 <= int(threads) <= 256:
-            raise ValueError("threads must be between 1 and 256")
-        if (x.size // self.shape[1]) * self.shape[0] > np.iinfo(np.int32).max:
-            raise ValueError("SDOT batch output count exceeds the native int32 interface")
-        return x
-
-    def linear_sdot(self, x, threads: int = 1):
-        """int8 GEMV: rotated inputs and centroids rounded to INT8, exact int32 per group."""
-        handle = self._sdot()
-        x = self._sdot_input(x, threads)
-        y = np.empty(x.shape[:-1] + (self.shape[0],), dtype=np.float32)
-        batch = x.size // self.shape[1]
-        if batch:
-            _check(self._lib.needle2_sdot_linear_checked(handle, x.ctypes.data, y.ctypes.data, batch),
-                   "needle2_sdot_linear")
-        return y
-
-    def sdot_debug(self, x):
-        """(y, int32 partials [rows, out, groups], q int8 [rows, padded], scales [rows, groups])."""
-        handle = self._sdot()
-        x = self._sdot_input(x, 1).reshape(-1, self.shape[1])
-        rows = x.shape[0]
-        y = np.empty((rows, self.shape[0]), np.float32)
-        d = np.empty((rows, self.shape[0], self.groups), np.int32)
-        q = np.empty((rows, self.padded), np.int8)
-        s = np.empty((rows, self.groups), np.float32)
+    def debug(self, x):
+        """int8 mode only: (y, int32 group dots [rows, out, groups], int8 activations
+        [rows, padded], activation scales [rows, groups])."""
+        if not self.sdot:
+            raise ValueError("debug exports exist for the int8 (SDOT) handle only")
+        x, rows = self._rows(x)
+        out, groups, padded = self.owner.shape[0], self.owner.groups, self.owner.padded
+        y = np.empty((rows, out), np.float32)
+        d = np.empty((rows, out, groups), np.int32)
+        q = np.empty((rows, padded), np.int8)
+        s = np.empty((rows, groups), np.float32)
         if rows:
-            _check(self._lib.needle2_sdot_debug(handle, x.ctypes.data, rows, y.ctypes.data, d.ctypes.data,
-                                                q.ctypes.data, s.ctypes.data), "needle2_sdot_debug")
+            _check(self.owner._lib.needle2_sdot_debug(self.ptr, x.ctypes.data, rows, y.ctypes.data, d.ctypes.data,
+                                                      q.ctypes.data, s.ctypes.data), "needle2_sdot_debug")
         return y, d, q, s
 
-    def linear_device(self, x, y, *, sdot: bool = False, stream=None) -> None:
-        """y[batch, out] = W x[batch, in] on device tensors (torch CUDA float32, contiguous)."""
-        handle = self._sdot() if sdot else self._handle
-        batch = x.numel() // self.shape[1]
-        if x.shape[-1] != self.shape[1] or y.shape[-1] != self.shape[0] or y.numel() != batch * self.shape[0]:
+    def linear_device(self, x, y, stream=None) -> None:
+        """y[batch, out] = W x[batch, in] for CUDA tensors."""
+        out, inp = self.owner.shape
+        batch = x.numel() // inp
+        if x.shape[-1] != inp or y.shape[-1] != out or y.numel() != batch * out:
             raise ValueError("linear_device: shape mismatch")
         if not (x.is_contiguous() and y.is_contiguous()) or x.dtype != y.dtype:
             raise ValueError("linear_device: contiguous float32 tensors required")
-        fn = self._lib.needle2_sdot_linear_device if sdot else self._lib.needle2_cq_linear_device
-        _check(fn(handle, x.data_ptr(), y.data_ptr(), batch, _stream_ptr(stream)), "linear_device")
+        lib = self.owner._lib
+        fn = lib.needle2_sdot_linear_device if self.sdot else lib.needle2_cq_linear_device
+        _check(fn(self.ptr, x.data_ptr(), y.data_ptr(), batch, _stream_ptr(stream)), "linear_device")
 
-    def prepare_device(self, x, *, sdot: bool = False, stream=None) -> None:
-        """Rotate (and for SDOT quantise) device activations into the handle's scratch."""
-        handle = self._sdot() if sdot else self._handle
-        fn = self._lib.needle2_sdot_prepare_device if sdot else self._lib.needle2_cq_prepare_device
-        _check(fn(handle, x.data_ptr(), x.numel() // self.shape[1], _stream_ptr(stream)), "prepare_device")
+    def prepare_device(self, x, stream=None) -> None:
+        """Rotate (int8 mode: rotate and quantise) x into the handle's scratch."""
+        lib = self.owner._lib
+        fn = lib.needle2_sdot_prepare_device if self.sdot else lib.needle2_cq_prepare_device
+        _check(fn(self.ptr, x.data_ptr(), x.numel() // self.owner.shape[1], _stream_ptr(stream)), "prepare_device")
 
-    def multiply_device(self, y, batch: int, *, sdot: bool = False, stream=None) -> None:
+    def multiply_device(self, y, batch: int, stream=None) -> None:
         """y[batch, out] from the last prepare_device."""
-        handle = self._sdot() if sdot else self._handle
-        fn = self._lib.needle2_sdot_multiply_device if sdot else self._lib.needle2_cq_multiply_device
-        _check(fn(handle, y.data_ptr(), int(batch), _stream_ptr(stream)), "multiply_device")
+        lib = self.owner._lib
+        fn = lib.needle2_sdot_multiply_device if self.sdot else lib.needle2_cq_multiply_device
+        _check(fn(self.ptr, y.data_ptr(), int(batch), _stream_ptr(stream)), "multiply_device")
 
-    def rows(self, ids):
+
+class DeviceMatrix:
+    """A packed CQ matrix ``[out, in]`` uploaded to the GPU.
+
+    ``fp32`` and ``sdot`` are its two library handles (FP32 dequant-accumulate
+    and int8 SDOT arithmetic), each created on first use from the host arrays
+    this object keeps.  ``codebook`` holds the stored centroids (bits 5:
+    the three ternary centroids).  Argument checks are the library's: a
+    create that fails raises with its message.  There is no CPU path.
+    """
+
+    def __init__(self, packed, norms, shape, bits: int, group: int, codebook):
+        self.shape = (int(shape[0]), int(shape[1]))
+        self.bits, self.group = int(bits), int(group)
+        self._packed = np.ascontiguousarray(packed, dtype=np.uint8)
+        self._norms = np.ascontiguousarray(norms, dtype=np.float16)
+        self._codebook = np.ascontiguousarray(codebook, dtype=np.float32)
+        self._lib = _library()
+        self._handles = {}
+
+    @property
+    def padded(self) -> int:
+        return -(-self.shape[1] // self.group) * self.group
+
+    @property
+    def groups(self) -> int:
+        return self.padded // self.group
+
+    def _handle(self, sdot: bool) -> Handle:
+        h = self._handles.get(sdot)
+        if h is None:
+            h = self._handles[sdot] = Handle(self, sdot)
+        return h
+
+    @property
+    def fp32(self) -> Handle:
+        return self._handle(False)
+
+    @property
+    def sdot(self) -> Handle:
+        return self._handle(True)
+
+    def rows(self, ids) -> np.ndarray:
+        """Dequantised rows ``[*ids.shape, in]`` (needle2_cq_rows)."""
         ids = np.asarray(ids)
         if ids.dtype.kind not in "iu":
-            raise TypeError("row indices must be integers")
-        ids_shape = ids.shape
-        ids = np.ascontiguousarray(ids, dtype=np.int64)
-        if np.any((ids < 0) | (ids >= self.shape[0])):
-            raise IndexError("CQ row index outside matrix")
-        result = np.empty(ids_shape + (self.shape[1],), dtype=np.float32)
-        if ids.size:
-            self._lib.needle2_cq_rows(self._handle, ids.ctypes.data, result.ctypes.data, ids.size)
+            raise TypeError("row ids must be integers")
+        flat = np.ascontiguousarray(ids, dtype=np.int64).reshape(-1)
+        if flat.size and (flat.min() < 0 or flat.max() >= self.shape[0]):
+            raise IndexError("row id outside the matrix")
+        y = np.empty(ids.shape + (self.shape[1],), np.float32)
+        if flat.size:
+            self._lib.needle2_cq_rows(self.fp32.ptr, flat.ctypes.data, y.ctypes.data, flat.size)
             _check_void("needle2_cq_rows")
-        return result
+        return y
 
-    def dequantize(self):
-        return self.rows(np.arange(self.shape[0], dtype=np.int64))
+    def dense(self) -> np.ndarray:
+        return self.rows(np.arange(self.shape[0]))
+
+    def close(self) -> None:
+        for h in self._handles.values():
+            h.close()
+        self._handles.clear()
 
 
 def linear_many(matrices, x, threads: int = 1, lookup: int = 0):
     """One activation row against several matrices (needle2/csrc/cq.cpp:360-366)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
     outs = [np.empty(m.shape[0], np.float32) for m in matrices]
-    handles = (_p * len(matrices))(*[m._handle for m in matrices])
+    handles = (_p * len(matrices))(*[m.fp32.ptr for m in matrices])
     ys = (_p * len(matrices))(*[o.ctypes.data for o in outs])
     lib = _library()
     lib.needle2_cq_linear_many(handles, len(matrices), x.ctypes.data, ys, int(threads), int(lookup))
@@ -302,7 +282,7 @@ def linear_many_batch(matrices, x, *, sdot: bool = False):
     x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, matrices[0].shape[1])
     batch = x.shape[0]
     outs = [np.empty((batch, m.shape[0]), np.float32) for m in matrices]
-    hs = [m._sdot() if sdot else m._handle for m in matrices]
+    hs = [(m.sdot if sdot else m.fp32).ptr for m in matrices]
     handles = (_p * len(hs))(*hs)
     ys = (_p * len(outs))(*[o.ctypes.data for o in outs])
     _check(_library().needle2_cq_linear_many_checked(handles, len(hs), x.ctypes.data, ys, batch, int(sdot)),
@@ -352,15 +332,6 @@ def set_f32_gemv(kind: int) -> int:
     4 rows; 1 the slot-per-lane kernel; 2 the row-per-lane kernel without the
     product table); returns the previous setting."""
     prev = _library().needle2_b200_set_f32_gemv(int(kind))
-    if prev < 0:
-        raise ValueError(last_error())
-    return prev
-
-
-def set_int8_gemv(kind: int) -> int:
-    """Select the int8 GEMV kernel process-wide (0 automatic, 1 diagonal warp
-    MMA, 2 tcgen05, 3 fragment-order warp MMA); returns the previous setting."""
-    prev = _library().needle2_b200_set_int8_gemv(int(kind))
     if prev < 0:
         raise ValueError(last_error())
     return prev

@@ -154,17 +154,38 @@ class ShardedSdot:
         _check(self._lib.needle2_sdot_prepare_device(self._h, x.data_ptr(), batch, _stream_ptr(stream)), "prepare")
         return batch
 
-    def barrier(self) -> None:
-        """Orders every rank's enqueued GEMM before anything enqueued after it."""
-        self._dist.all_reduce(self._flag, group=self.group)
+    def _torch_stream(self, stream):
+        """The torch stream that `stream` names (None: the current stream)."""
+        torch = self._torch
+        if stream is None:
+            return torch.cuda.current_stream(self.device)
+        if isinstance(stream, torch.cuda.Stream):
+            return stream
+        return torch.cuda.ExternalStream(int(stream), device=self.device)
+
+    def barrier(self, stream=None) -> None:
+        """Orders, on `stream`, everything every rank enqueued on its stream
+        before this call ahead of anything any rank enqueues after it (a
+        one-element all-reduce; its kernel cannot finish before every rank's
+        stream has reached it)."""
+        with self._torch.cuda.stream(self._torch_stream(stream)):
+            self._dist.all_reduce(self._flag, group=self.group)
 
     def forward(self, x, stream=None):
-        """y[batch][out] with the all-gather fused into the GEMM's epilogue (a view
-        of this rank's shared output buffer, valid until the next call)."""
+        """y[batch][out] with the all-gather fused into the GEMM's epilogue.
+
+        Returns a view of this rank's shared output buffer.  Every rank's next
+        forward() overwrites every rank's buffer, so the view is valid until the
+        next call on any rank; work that reads it must be enqueued on `stream`
+        (or be ordered before the next forward() on it).  A barrier before the
+        GEMM makes every rank's earlier reads of its buffer finish before any
+        rank's epilogue stores into it; a barrier after it makes every rank's
+        stores land before this rank's later work reads them."""
         batch = self._prepare(x, stream)
+        self.barrier(stream)
         _check(self._lib.needle2_sdot_multiply_gather_device(self._h, self._dsts, self.world, self.world * self.ns,
                                                              batch, _stream_ptr(stream)), "multiply_gather")
-        self.barrier()
+        self.barrier(stream)
         return self.full[:batch, : self.out]
 
     def forward_local(self, x, stream=None):
@@ -180,5 +201,6 @@ class ShardedSdot:
         """The same y[batch][out] through a local GEMM and NCCL's all-gather."""
         y = self.forward_local(x, stream)
         g = self._torch.empty(self.world, y.shape[0], self.ns, device=self.device)
-        self._dist.all_gather_into_tensor(g, y.contiguous(), group=self.group)
-        return assemble(g, self.out)
+        with self._torch.cuda.stream(self._torch_stream(stream)):
+            self._dist.all_gather_into_tensor(g, y.contiguous(), group=self.group)
+            return assemble(g, self.out)

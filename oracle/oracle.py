@@ -23,7 +23,23 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "_build" / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libneedle2_ref.so"
-REF_SRC = Path(os.environ.get("NEEDLE2_REFERENCE_SRC", "/root/reference/needle2/csrc"))
+# Root of the reference project (the directory that holds needle2/):
+# NEEDLE2_REFERENCE_SRC when set, else the copy that pip installed into
+# baseline/_ref (git-ignored, it travels with the working tree).  Its
+# needle2/csrc holds the C++ sources that `make ref` compiles, its needle2/ the
+# Python (quantizer, NativeCQ/NativeEngine) that tests drive.
+REF_ROOT = Path(os.environ.get("NEEDLE2_REFERENCE_SRC", str(HERE.parent / "baseline" / "_ref")))
+REF_SRC = REF_ROOT / "needle2" / "csrc"
+
+
+def reference_package():
+    """The reference's own Python package root on sys.path, or None when absent."""
+    import sys
+    if not (REF_ROOT / "needle2" / "__init__.py").is_file():
+        return None
+    if str(REF_ROOT) not in sys.path:
+        sys.path.insert(0, str(REF_ROOT))
+    return REF_ROOT
 
 _p = ct.c_void_p
 _i = ct.c_int

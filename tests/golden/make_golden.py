@@ -1,6 +1,7 @@
 """Generates the golden fixtures in this directory from the reference itself.
 
-Run in a checkout that has the OpenNeedle sources (default /root/reference):
+Run where the reference is available (NEEDLE2_REFERENCE_SRC, default the copy
+installed into baseline/_ref):
 
     make -C oracle ref && python tests/golden/make_golden.py
 
@@ -23,13 +24,13 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REFERENCE = Path(os.environ.get("NEEDLE2_REFERENCE", "/root/reference"))
 sys.path.insert(0, str(ROOT))
-sys.path.insert(0, str(REFERENCE))
-
-from needle2 import quantize as ref_quantize  # noqa: E402  (the reference's packer)
 
 from oracle import oracle as O  # noqa: E402
+
+if O.reference_package() is None:
+    raise SystemExit(f"reference package not found under {O.REF_ROOT}; set NEEDLE2_REFERENCE_SRC")
+from needle2 import quantize as ref_quantize  # noqa: E402  (the reference's packer)
 
 
 def sha(a: np.ndarray) -> str:

@@ -1,5 +1,5 @@
-"""The C ABI library loads and exports what include/*.h declares (CPU only),
-and the host-side validation mirrors the reference's (needle2/native.py:172-276)."""
+"""The C ABI library loads and exports what include/*.h declares, the
+reference's Python binds it, and its creates validate their arguments (CPU only)."""
 import ctypes as ct
 import os
 import re
@@ -55,41 +55,37 @@ def test_features_and_sdot_flag_without_gpu(lib_path):
 
 def test_reference_binding_accepts_library(lib_path, tmp_path):
     """OpenNeedle's own ctypes layer binds this library via NEEDLE2_NATIVE_LIBRARY."""
-    ref = Path("/root/reference")
-    if not (ref / "needle2" / "native.py").is_file():
-        pytest.skip("reference sources unavailable")
+    from oracle import oracle as O
+    if O.reference_package() is None:
+        pytest.skip(f"reference package unavailable under {O.REF_ROOT}")
     code = ("import needle2.native as n; lib = n._library(); "
             "print(n.features()); print(n.sdot_available())")
-    env = dict(os.environ, NEEDLE2_NATIVE_LIBRARY=str(lib_path), PYTHONPATH=str(ref))
+    env = dict(os.environ, NEEDLE2_NATIVE_LIBRARY=str(lib_path), PYTHONPATH=str(O.REF_ROOT))
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, cwd=tmp_path)
     assert out.returncode == 0, out.stderr
     assert "cuda-sm100a" in out.stdout and "True" in out.stdout
 
 
-def test_host_validation_mirrors_reference():
-    from openneedle_b200.native import NativeCQ
+def test_create_validates_arguments_before_touching_the_gpu(lib_path):
+    """The C ABI's create calls reject bad geometry with NULL and a message of
+    their own (the reference's creates have no error channel; its Python
+    checks first, needle2/native.py:172-208)."""
+    lib = ct.CDLL(str(lib_path))
+    lib.needle2_b200_error.restype = ct.c_char_p
+    for name in ("needle2_cq_create", "needle2_sdot_create"):
+        getattr(lib, name).argtypes = [ct.c_void_p, ct.c_void_p, ct.c_int, ct.c_int, ct.c_int, ct.c_int, ct.c_void_p]
+        getattr(lib, name).restype = ct.c_void_p
     packed, norms, shape, cb, _ = example(2)
-    with pytest.raises(ValueError, match="positive two-dimensional"):
-        NativeCQ(packed, norms, (0, 257), 2, 128, cb)
-    with pytest.raises(ValueError, match="storage bits"):
-        NativeCQ(packed, norms, shape, 6, 128, cb)
-    with pytest.raises(ValueError, match="power of two"):
-        NativeCQ(packed, norms, shape, 2, 96, cb)
-    for value in (-1.0, np.inf, np.nan):
-        bad = norms.copy()
-        bad[0, 0] = value
-        with pytest.raises(ValueError, match="norms must be finite and nonnegative"):
-            NativeCQ(packed, bad, shape, 2, 128, cb)
-    for codebook in ([np.nan, 0, 1, 2], [-2, -1, 0, np.inf], [2, 1, 0, -1], [0, 0, 1, 2]):
-        with pytest.raises(ValueError, match="codebook must be finite and strictly sorted"):
-            NativeCQ(packed, norms, shape, 2, 128, codebook)
-    with pytest.raises(ValueError, match="incorrect number of centroids"):
-        NativeCQ(packed, norms, shape, 2, 128, cb[:3])
-    tern, tn, ts, tcb, _ = example(5)
-    bad = tern.copy()
-    bad[0, 0] = 0b10
-    with pytest.raises(ValueError, match="ternary crumb code 2"):
-        NativeCQ(bad, tn, ts, 5, 128, tcb)
+    p, n, c = packed.ctypes.data, norms.ctypes.data, cb.ctypes.data
+    cases = [("needle2_cq_create", (p, n, 0, 257, 2, 128, c), "positive two-dimensional"),
+             ("needle2_cq_create", (p, n, 9, 257, 6, 128, c), "storage bits"),
+             ("needle2_cq_create", (p, n, 9, 257, 2, 96, c), "power of two"),
+             ("needle2_cq_create", (None, n, 9, 257, 2, 128, c), "null"),
+             ("needle2_sdot_create", (p, n, 9, 257, 3, 128, c), "SDOT requires CQ2/CQ4"),
+             ("needle2_sdot_create", (p, n, 9, 257, 2, 32, c), "SDOT requires CQ2/CQ4")]
+    for name, args, message in cases:
+        assert getattr(lib, name)(*args) is None
+        assert message in lib.needle2_b200_error().decode()
 
 
 def test_create_fails_loudly_without_gpu():
@@ -97,7 +93,10 @@ def test_create_fails_loudly_without_gpu():
     import torch
     if torch.cuda.is_available():
         pytest.skip("a GPU is present")
-    from openneedle_b200.native import NativeCQ
+    from openneedle_b200.native import DeviceMatrix
     packed, norms, shape, cb, _ = example(4)
-    with pytest.raises(MemoryError, match="Could not construct native CQ matrix"):
-        NativeCQ(packed, norms, shape, 4, 128, cb)
+    m = DeviceMatrix(packed, norms, shape, 4, 128, cb)
+    with pytest.raises(RuntimeError, match="needle2_cq_create"):
+        m.fp32(np.zeros(shape[1], np.float32))
+    with pytest.raises(RuntimeError, match="needle2_sdot_create"):
+        m.sdot(np.zeros(shape[1], np.float32))

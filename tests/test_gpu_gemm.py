@@ -18,12 +18,12 @@ def native():
 @pytest.mark.parametrize("bits", [2, 4])
 @pytest.mark.parametrize("n,k,m", [(300, 512, 64), (301, 512, 130), (1000, 1024, 257), (2048, 512, 2048)])
 def test_prefill_gemm_matches_oracle(native, oracle_lib, bits, n, k, m):
-    from openneedle_b200.quantize import synthetic_matrix
+    from util import synthetic_matrix
     packed, norms, cb = synthetic_matrix(n, k, bits, seed=700 + n + bits)
-    q = native.NativeCQ(packed, norms, (n, k), bits, 128, cb)
+    q = native.DeviceMatrix(packed, norms, (n, k), bits, 128, cb)
     x = np.random.default_rng(m + k).normal(size=(m, k)).astype(np.float32)
     x[3] = 0                                   # an all-zero row (scale 1)
-    y = q.linear_sdot(x)
+    y = q.sdot(x)
     ry, _, _, _ = oracle_lib.sdot_linear(packed, norms, (n, k), bits, 128, cb, x)
     np.testing.assert_array_equal(y, ry)
 
@@ -33,11 +33,11 @@ def test_prefill_gemm_matches_gemv_at_config3_width(native, bits):
     """Config-3 width (N = 8192, K = 4096): the GEMM and the GEMV path (the
     no-allocation entry always runs the GEMV) agree bit for bit."""
     import torch
-    from openneedle_b200.quantize import synthetic_matrix
+    from util import synthetic_matrix
     n, k, m = 8192, 4096, 512
     packed, norms, cb = synthetic_matrix(n, k, bits, seed=91 + bits)
-    q = native.NativeCQ(packed, norms, (n, k), bits, 128, cb)
-    h = q._sdot()
+    q = native.DeviceMatrix(packed, norms, (n, k), bits, 128, cb)
+    h = q.sdot.ptr
     lib = native._library()
     lib.needle2_sdot_linear_device_noalloc.argtypes = [ct.c_void_p] * 3 + [ct.c_int, ct.c_void_p]
     lib.needle2_sdot_linear_device_noalloc.restype = ct.c_int
@@ -60,15 +60,39 @@ def test_prefill_gemm_matches_gemv_at_config3_width(native, bits):
 def test_fp32_prefill_gemm_matches_oracle(native, oracle_lib, bits, n, k, m, group):
     """FP32 mode from 64 rows on runs the bf16 hi/lo tensor-core GEMM; it must stay
     within the FP32 tolerance of the reference's per-group FP32 sums."""
-    from openneedle_b200.quantize import synthetic_matrix
-    from util import FP32_REL_TOL, rel_err
+    from util import FP32_REL_TOL, rel_err, synthetic_matrix
     packed, norms, cb = synthetic_matrix(n, k, bits, group, seed=900 + n + bits)
-    q = native.NativeCQ(packed, norms, (n, k), bits, group, cb)
+    q = native.DeviceMatrix(packed, norms, (n, k), bits, group, cb)
     x = np.random.default_rng(m + k + 1).normal(size=(m, k)).astype(np.float32)
     x[5] = 0
-    y = q.linear(x)
+    y = q.fp32(x)
     ref = oracle_lib.cq_linear(packed, norms, (n, k), bits, group, cb, x)
     assert rel_err(y, ref) <= FP32_REL_TOL
     # rows are independent of the batch they run in: the GEMV's result for the
     # first 16 rows agrees within the same tolerance
-    assert rel_err(y[:16], q.linear(x[:16])) <= FP32_REL_TOL
+    assert rel_err(y[:16], q.fp32(x[:16])) <= FP32_REL_TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits", [2, 4])
+@pytest.mark.parametrize("n,k", [(8192, 2048), (8192, 4096), (11008, 2048), (11008, 4096)])
+def test_fp32_prefill_gemm_config3_sizes(native, oracle_lib, bits, n, k):
+    """Config 3's FP32-mode shapes (M = 2048 activation rows, K up to 4096, N up
+    to 11008): the bf16 hi/lo GEMM's error grows with K, so it is checked at the
+    full widths.  The oracle runs on a sample of 24 activation rows (all N
+    outputs of each), spread over the batch and its tiles, including an
+    all-zero row; the bar is max|y - y_ref| / max|y_ref| <= 1e-4 per tensor."""
+    from util import FP32_REL_TOL, rel_err, synthetic_matrix
+    m = 2048
+    packed, norms, cb = synthetic_matrix(n, k, bits, 128, seed=30 + n + k + bits)
+    q = native.DeviceMatrix(packed, norms, (n, k), bits, 128, cb)
+    x = np.random.default_rng(n + k).normal(size=(m, k)).astype(np.float32)
+    x[1000] = 0
+    y = q.fp32(x)
+    sample = np.array([0, 1, 127, 128, 255, 511, 640, 777, 1000, 1023, 1024, 1151, 1200, 1337, 1500, 1535,
+                       1536, 1663, 1800, 1919, 1920, 2000, 2046, 2047])
+    ref = oracle_lib.cq_linear(packed, norms, (n, k), bits, 128, cb, x[sample])
+    err = rel_err(y[sample], ref)
+    print(f"config-3 FP32 GEMM CQ{bits} N={n} K={k}: max rel err {err:.3e}")
+    assert err <= FP32_REL_TOL
+    assert not y[1000].any()

@@ -33,7 +33,7 @@ def f32_kind(native):
 @pytest.mark.parametrize("rows", [33, 100])
 def test_rows_kernel_against_oracle(native, oracle_lib, f32_kind, bits, group, dim, rows):
     packed, norms, shape, cb, dense = example(bits, rows=rows, dim=dim, group=group, seed=7 * dim + rows)
-    q = native.NativeCQ(packed, norms, shape, bits, group, cb)
+    q = native.DeviceMatrix(packed, norms, shape, bits, group, cb)
     x = np.random.default_rng(dim + bits).normal(size=(4, dim)).astype(np.float32)
     for m in (1, 2, 3, 4):
         ref = oracle_lib.cq_linear(packed, norms, shape, bits, group, cb, x[:m])
@@ -42,13 +42,13 @@ def test_rows_kernel_against_oracle(native, oracle_lib, f32_kind, bits, group, d
         ys = []
         for kind in (0, 1, 2):
             native.set_f32_gemv(kind)
-            ys.append(q.linear(x[:m]))
+            ys.append(q.fp32(x[:m]))
             native.set_f32_gemv(0)
             assert rel_err(ys[-1], ref) <= FP32_REL_TOL, (m, kind, rel_err(ys[-1], ref))
         assert rel_err(ys[0], ys[1]) <= FP32_REL_TOL
         assert rel_err(ys[2], ys[1]) <= FP32_REL_TOL
         # repeated calls give identical results (no atomics, fixed order)
-        np.testing.assert_array_equal(q.linear(x[:m]), ys[0])
+        np.testing.assert_array_equal(q.fp32(x[:m]), ys[0])
     assert native.device_fault() == 0
 
 
@@ -57,18 +57,18 @@ def test_rows_kernel_large_and_fused(native, oracle_lib, f32_kind, bits):
     """A K = 4096 matrix (32 groups, eight warps per row block) against the
     oracle, and a fused launch over matrices of different heights giving the
     single-matrix results exactly."""
-    from openneedle_b200.quantize import synthetic_matrix
+    from util import synthetic_matrix
     p, nrm, cb = synthetic_matrix(2080, 4096, bits, seed=21)
-    big = native.NativeCQ(p, nrm, (2080, 4096), bits, 128, cb)
+    big = native.DeviceMatrix(p, nrm, (2080, 4096), bits, 128, cb)
     x = np.random.default_rng(5).normal(size=(2, 4096)).astype(np.float32)
-    assert rel_err(big.linear(x[:1]), oracle_lib.cq_linear(p, nrm, (2080, 4096), bits, 128, cb, x[:1])) \
+    assert rel_err(big.fp32(x[:1]), oracle_lib.cq_linear(p, nrm, (2080, 4096), bits, 128, cb, x[:1])) \
         <= FP32_REL_TOL
     mats = [big]
     for i, n in enumerate((31, 32, 4097)):
         pi, ni, _ = synthetic_matrix(n, 4096, bits, seed=60 + i)
-        mats.append(native.NativeCQ(pi, ni, (n, 4096), bits, 128, cb))
+        mats.append(native.DeviceMatrix(pi, ni, (n, 4096), bits, 128, cb))
     for m in (1, 2):
         outs = native.linear_many_batch(mats, x[:m], sdot=False)
         for mat, o in zip(mats, outs):
-            np.testing.assert_array_equal(o, mat.linear(x[:m]))
+            np.testing.assert_array_equal(o, mat.fp32(x[:m]))
     assert native.device_fault() == 0

@@ -21,7 +21,7 @@ def lib():
 @pytest.mark.parametrize("batch", [1, 64])
 def test_pinned_and_pageable_outputs_agree(lib, sdot, batch):
     import torch
-    from openneedle_b200.quantize import synthetic_matrix
+    from util import synthetic_matrix
     mats = [synthetic_matrix(1000 + 8 * i, 512, 4, 128, seed=40 + i) for i in range(3)]
     create = lib.needle2_sdot_create if sdot else lib.needle2_cq_create
     destroy = lib.needle2_sdot_destroy if sdot else lib.needle2_cq_destroy

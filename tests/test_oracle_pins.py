@@ -11,7 +11,6 @@ import pytest
 
 from util import example, golden, sha
 
-from openneedle_b200 import quantize as Q
 
 
 @pytest.mark.parametrize("bits", [2, 4])
@@ -123,33 +122,6 @@ def test_oracle_sdot_matches_reference_random(oracle_lib, bits, group):
     ref = oracle_lib.ref_sdot(packed, norms, shape, bits, group, cb, x)
     for a, b in zip(mine, ref):
         np.testing.assert_array_equal(a, b)
-
-
-@needs_ref
-@pytest.mark.reference
-def test_packer_matches_reference_quantizer():
-    import sys
-    sys.path.insert(0, "/root/reference")
-    ref_q = pytest.importorskip("needle2.quantize")
-    w = np.random.default_rng(42).normal(size=(129, 300)).astype(np.float32)
-    for bits in (2, 3, 4):
-        for group in (64, 128):
-            p1, n1 = ref_q.quantize_matrix(w, bits, group)
-            p2, n2 = Q.quantize_matrix(w, bits, group)
-            np.testing.assert_array_equal(p1, p2)
-            np.testing.assert_array_equal(n1.view(np.uint16), n2.view(np.uint16))
-            np.testing.assert_array_equal(ref_q.codebook(bits, group), Q.codebook(bits, group))
-
-
-def test_packer_round_trip():
-    idx = np.random.default_rng(1).integers(0, 16, (7, 64))
-    for bits in (2, 3, 4):
-        i = idx % (1 << bits)
-        np.testing.assert_array_equal(Q.unpack_indices(Q.pack_indices(i, bits), bits, 64), i)
-    w = np.random.default_rng(2).normal(0, 0.02, (16, 256)).astype(np.float32)
-    p, n = Q.quantize_matrix(w, 4, 128)
-    d = Q.dequantize_matrix(p, n, w.shape, 4, 128)
-    assert np.corrcoef(d.ravel(), w.ravel())[0, 1] > 0.99
 
 
 def test_argmax_first_max_and_nans(oracle_lib):

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch.multiprocessing as mp
 
-from openneedle_b200.quantize import dequantize_matrix, synthetic_matrix
+from util import ref_quantize, synthetic_matrix
 from openneedle_b200.sharded import assemble, shard_layout, shard_matrix
 
 
@@ -31,7 +31,7 @@ def test_shard_padding_rows_are_zero():
     assert p.shape == (ns, packed.shape[1]) and n.shape == (ns, norms.shape[1])
     np.testing.assert_array_equal(p[: r1 - r0], packed[r0:r1])
     assert not p[r1 - r0:].any() and not n[r1 - r0:].astype(np.float32).any()
-    w = dequantize_matrix(p, n, (ns, 256), 4, 128, cb)
+    w = ref_quantize().dequantize_matrix(p, n, (ns, 256), 4, 128, cb)
     assert not w[r1 - r0:].any()   # zero norms give zero rows
 
 
@@ -50,11 +50,11 @@ def _rank(rank, world, port, out, k, q):
         x = np.random.default_rng(9).normal(size=(6, k)).astype(np.float64)
         p, n = shard_matrix(packed, norms, out, rank, world)
         ns = p.shape[0]
-        y = x @ dequantize_matrix(p, n, (ns, k), 4, 128, cb).astype(np.float64).T
+        y = x @ ref_quantize().dequantize_matrix(p, n, (ns, k), 4, 128, cb).astype(np.float64).T
         parts = [torch.empty(6, ns, dtype=torch.float64) for _ in range(world)]
         dist.all_gather(parts, torch.from_numpy(np.ascontiguousarray(y)))
         full = assemble(torch.stack(parts), out).numpy()
-        ref = x @ dequantize_matrix(packed, norms, (out, k), 4, 128, cb).astype(np.float64).T
+        ref = x @ ref_quantize().dequantize_matrix(packed, norms, (out, k), 4, 128, cb).astype(np.float64).T
         q.put((rank, full.shape == ref.shape and bool(np.allclose(full, ref, rtol=1e-12, atol=1e-12))))
     finally:
         dist.destroy_process_group()

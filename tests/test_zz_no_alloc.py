@@ -23,8 +23,8 @@ def lib():
 
 def _sdot_handle(native, bits):
     g = golden(f"cq{bits}_2048x512.npz")
-    q = native.NativeCQ(g["packed"], g["norms"], (2048, 512), bits, 128, g["codebook"])
-    return q, q._sdot(), g
+    q = native.DeviceMatrix(g["packed"], g["norms"], (2048, 512), bits, 128, g["codebook"])
+    return q, q.sdot.ptr, g
 
 
 @pytest.mark.parametrize("bits", [2, 4])
@@ -48,7 +48,7 @@ def test_noalloc_matches_device_entry_twice(lib, bits):
     got = torch.empty(4, 2048, device="cuda")
     assert lib.needle2_sdot_linear_device_noalloc(handle, x.data_ptr(), got.data_ptr(), 4, stream) == 0
     torch.cuda.synchronize()
-    np.testing.assert_array_equal(got.cpu().numpy(), q.linear_sdot(g["x"][:4]))
+    np.testing.assert_array_equal(got.cpu().numpy(), q.sdot(g["x"][:4]))
 
 
 def test_noalloc_rejects_oversized_batch(lib):

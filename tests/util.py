@@ -9,6 +9,26 @@ import numpy as np
 GOLDEN = Path(__file__).resolve().parent / "golden"
 
 
+def ref_quantize():
+    """The reference's own CQ packer (needle2/quantize.py), from the reference
+    package (NEEDLE2_REFERENCE_SRC, default the pip install in baseline/_ref)."""
+    from oracle import oracle as O
+    if O.reference_package() is None:
+        raise RuntimeError(f"reference package not found under {O.REF_ROOT}: install it into baseline/_ref "
+                           "or set NEEDLE2_REFERENCE_SRC")
+    from needle2 import quantize
+    return quantize
+
+
+def synthetic_matrix(rows: int, cols: int, bits: int, group: int = 128, seed: int = 0, std: float = 0.02):
+    """W ~ N(0, std) from default_rng(seed), packed by the reference's quantizer:
+    (packed, norms, codebook)."""
+    q = ref_quantize()
+    w = np.random.default_rng(seed).normal(0.0, std, (rows, cols)).astype(np.float32)
+    packed, norms = q.quantize_matrix(w, bits, group)
+    return packed, norms, q.codebook(bits, group)
+
+
 def golden(name: str) -> dict:
     with np.load(GOLDEN / name) as z:
         return {k: z[k] for k in z.files}
