@@ -229,6 +229,93 @@ int needle2_attention_prefill_device(void *kv, const int *session_ids, const int
  * int8, scales [capacity][kvheads], capacity = window ? window + prefix_len : max_seq. */
 int needle2_kv_export(void *kv, int session, int8_t *keys, int8_t *values, float *k_scales, float *v_scales);
 
+/* ---- reference-compatible engine ABI (whole Needle-2 forward on the GPU) -- */
+/*
+ * Layouts of needle2/csrc/engine.cpp:14-19 and :327-339 (bound from Python by
+ * needle2/native.py:282-304).  Tensors come in the canonical order of
+ * needle2/native.py:350-395: embedding; per layer norm_in, q_proj, k_proj,
+ * v_proj, q_norm, k_norm, gate_proj, out_proj, post_norm, attn_gate, pre_hada,
+ * d1, d2, d3; mhc_a_pre/post/res, mhc_b_pre/post/res, mhc_phi_pre/post/res;
+ * per engram site tables, key_proj, value_proj, taps; final_norm.  A matrix is
+ * either a CQ handle of this library (needle2_cq_create; `cq`) or host FP32
+ * data (`data`, rows x cols, copied to the device at create time); the mHC
+ * projections must be FP32 data, as the reference's NativeEngine passes them.
+ */
+typedef struct {
+    void *cq;
+    const float *data;
+    int rows, cols;
+} needle2_tensor_desc;
+
+typedef struct {
+    int vocab, dim, heads, kvheads, layers, head_dim, max_seq, hada, lanes, window;
+    int slots, subdim, tables, taps, dilation, num_orders, orders[4], num_sites, sites[4];
+    float rope_theta;
+} needle2_engine_config;
+
+typedef struct {
+    int num_states, initial_state, eos_id, stop_id, tool_start_id, tool_end_id;
+    const int *state_types, *fallback_next_states, *candidate_offsets, *candidate_tokens, *next_states;
+} needle2_dfa_state_desc;
+
+/* Replace needle2_engine_* of needle2/csrc/engine.cpp:1499-1548 with the same
+ * arguments, return values and error convention (NULL / -1 and the thread-local
+ * needle2_engine_error()).  One engine = one sequence, as in the reference;
+ * calls on one engine must be serialised.  `threads` is accepted and unused. */
+void *needle2_engine_create(const needle2_engine_config *config, const needle2_tensor_desc *tensors, int count,
+                            int threads, int activation_bits);
+void needle2_engine_destroy(void *engine);
+void needle2_engine_set_lookup(void *engine, int mode);
+int needle2_engine_set_sdot(void *engine);
+void needle2_engine_reset(void *engine, int prefix_len);
+int needle2_engine_cache_prefix(void *engine);
+int needle2_engine_reset_to_prefix(void *engine);
+int needle2_engine_step(void *engine, int token, float *logits, float *hidden);
+int needle2_engine_prefill(void *engine, const int *tokens, int num_tokens, int last_only, float *logits,
+                           float *hidden);
+int needle2_engine_step_candidates(void *engine, int token, const int *candidates, int num_candidates,
+                                   float *candidate_logits, float *hidden);
+int needle2_engine_project_candidates(void *engine, const int *candidates, int num_candidates,
+                                      float *candidate_logits);
+int needle2_engine_decode_loop(void *engine, int first_token, int max_new_tokens, const needle2_dfa_state_desc *dfa,
+                               int *output_tokens, int *out_generated_count);
+int needle2_engine_import(void *engine, int position, int prefix_len, const int *ids, const int *positions,
+                          int count, const float *k, const float *v);
+int needle2_engine_set_int8_kv(void *engine, int enable);
+size_t needle2_engine_kv_storage_bytes(void *engine);
+const char *needle2_engine_error(void);
+
+/* ---- additive: many sequences of one engine's model, in lockstep --------- */
+/*
+ * The reference serves one unpadded sequence per Engine (needle2/native.py:307-314).
+ * A batch holds `sessions` sequences that share the engine's weights (the
+ * engine must outlive it) and one pinned prefix; every call advances all of
+ * them by the same number of tokens, each through exactly the per-sequence
+ * arithmetic of the engine (teacher-forced logits equal the engine's within
+ * FP32 rounding).  The KV format (INT8 or FP32) and the matmul mode (FP32 or
+ * SDOT) are the engine's at batch creation.
+ */
+void *needle2_batch_create(void *engine, int sessions, int prefix_len);
+void needle2_batch_destroy(void *batch);
+size_t needle2_batch_kv_storage_bytes(void *batch);
+/* Run the shared prefix (prefix_len tokens) once; every session then continues
+ * from position prefix_len with the prefix's KV, token history and engram state. */
+int needle2_batch_set_prefix(void *batch, const int *tokens);
+/* tokens[sessions][n] appended to every session; logits of each session's last
+ * token into logits[sessions][vocab] and/or its greedy token into next[sessions]
+ * (either may be NULL).  Host pointers; synchronous. */
+int needle2_batch_prefill(void *batch, const int *tokens, int n, float *logits, int *next);
+/* One token per session (teacher forcing): logits[sessions][vocab] and/or greedy next[sessions]. */
+int needle2_batch_step(void *batch, const int *tokens, float *logits, int *next);
+/* `steps` greedy steps from first[sessions]: out[sessions][steps] = the tokens
+ * fed at each step (first, then each step's greedy choice); the sessions
+ * advance by `steps` positions.  Host pointers; synchronous. */
+int needle2_batch_decode_greedy(void *batch, const int *first, int steps, int *out);
+/* The same on device pointers, enqueued on `stream` without host synchronisation. */
+int needle2_batch_decode_greedy_device(void *batch, const int *first, int steps, int *out, void *stream);
+/* Current position of every session (host copy). */
+int needle2_batch_positions(void *batch, int *positions);
+
 #ifdef __cplusplus
 }
 #endif

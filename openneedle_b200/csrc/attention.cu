@@ -58,10 +58,16 @@ __global__ void kv_quantize_kernel(const float *__restrict__ k, const float *__r
         row = (size_t)kh * dest.rows + t;                      // [KV][rows] (prefix or staging)
     } else {
         const int e = t / dest.tokens_per_entry, tt = t % dest.tokens_per_entry;
-        if (tt < dest.min_t) return;
         const int s = dest.session[e], pos = dest.position[e] + tt;
-        const int slot = dest.window ? (pos - dest.prefix) % dest.window : pos - dest.prefix;
-        row = ((size_t)s * kvheads + kh) * dest.rows + slot;   // [S][KV][Cs]
+        if (tt < dest.min_t && pos >= dest.prefix) return;   // overwritten later in the chunk's window
+        if (pos < dest.prefix) {
+            // a pinned prefix position (the prefix itself being prefilled)
+            row = (size_t)kh * dest.prefix + pos;              // [KV][P]
+            ko = dest.pk; vo = dest.pv; ks = dest.pks; vs = dest.pvs;
+        } else {
+            const int slot = dest.window ? (pos - dest.prefix) % dest.window : pos - dest.prefix;
+            row = ((size_t)s * kvheads + kh) * dest.rows + slot;   // [S][KV][Cs]
+        }
     }
     for (int d = lane; d < hd; d += 32) {
         ko[row * hd + d] = (int8_t)clamp127(rint_even(__fmul_rn(kp[d], ik)));
@@ -73,6 +79,34 @@ __global__ void kv_quantize_kernel(const float *__restrict__ k, const float *__r
     }
 }
 
+// FP32 cache store: one warp per (token, KV head), rows as kv_quantize_kernel.
+__global__ void kv_store_f32_kernel(const float *__restrict__ k, const float *__restrict__ v, int tokens, int kvheads,
+                                    int hd, float *__restrict__ ko, float *__restrict__ vo, KVDest dest) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= tokens * kvheads) return;
+    const int t = warp / kvheads, kh = warp % kvheads;
+    const float *kp = k + ((size_t)t * kvheads + kh) * hd, *vp = v + ((size_t)t * kvheads + kh) * hd;
+    size_t row;
+    if (dest.mode == KVDest::kLinear) {
+        row = (size_t)kh * dest.rows + t;
+    } else {
+        const int e = t / dest.tokens_per_entry, tt = t % dest.tokens_per_entry;
+        const int s = dest.session[e], pos = dest.position[e] + tt;
+        if (tt < dest.min_t && pos >= dest.prefix) return;
+        if (pos < dest.prefix) {
+            row = (size_t)kh * dest.prefix + pos;
+            ko = dest.pkf; vo = dest.pvf;
+        } else {
+            const int slot = dest.window ? (pos - dest.prefix) % dest.window : pos - dest.prefix;
+            row = ((size_t)s * kvheads + kh) * dest.rows + slot;
+        }
+    }
+    for (int d = lane; d < hd; d += 32) {
+        ko[row * hd + d] = kp[d];
+        vo[row * hd + d] = vp[d];
+    }
+}
+
 // Exact int8 -> float for four packed bytes.
 __device__ __forceinline__ void i8x4_to_f32(uint32_t w, float &a, float &b, float &c, float &d) {
     a = (float)(int8_t)(w & 0xff);
@@ -81,40 +115,55 @@ __device__ __forceinline__ void i8x4_to_f32(uint32_t w, float &a, float &b, floa
     d = (float)(int8_t)(w >> 24);
 }
 
+template <typename T>
 struct Row {
-    const int8_t *k, *v;
+    const T *k, *v;
     float ks, vs;
 };
 
-// Visible index i of query (session s, position pos) -> K/V row.
-__device__ __forceinline__ Row visible_row(const AttnParams &p, int s, int pos, int kh, int i, int prefix_count,
-                                           int start, int entry, int chunk_start) {
+// Visible index i of query (session s, position pos) -> K/V row.  A prefill
+// chunk's own rows come from the staging area even where the chunk lies inside
+// the pinned prefix (the prefix itself being prefilled).
+template <typename T>
+__device__ __forceinline__ Row<T> visible_row(const AttnParams &p, int s, int pos, int kh, int i, int prefix_count,
+                                              int start, int entry, int chunk_start) {
     int position;
     if (i < prefix_count) {
         position = i;
     } else {
         position = start + (i - prefix_count);
     }
-    Row r;
-    if (position < p.prefix) {
-        const size_t row = (size_t)kh * p.prefix + position;
-        r.k = p.pk + row * p.hd;
-        r.v = p.pv + row * p.hd;
-        r.ks = p.pks[row];
-        r.vs = p.pvs[row];
-    } else if (p.stage_k && position >= chunk_start) {
-        const size_t row = (size_t)kh * p.stage_rows + (size_t)entry * p.tokens + (position - chunk_start);
-        r.k = p.stage_k + row * p.hd;
-        r.v = p.stage_v + row * p.hd;
-        r.ks = p.stage_ks[row];
-        r.vs = p.stage_vs[row];
+    Row<T> r;
+    size_t row;
+    int where;   // 0 staged chunk, 1 pinned prefix, 2 session slots
+    if (p.stage_k && position >= chunk_start) {
+        row = (size_t)kh * p.stage_rows + (size_t)entry * p.tokens + (position - chunk_start);
+        where = 0;
+    } else if (position < p.prefix) {
+        row = (size_t)kh * p.prefix + position;
+        where = 1;
     } else {
         const int slot = p.window ? (position - p.prefix) % p.window : position - p.prefix;
-        const size_t row = ((size_t)s * p.kvheads + kh) * p.cs + slot;
-        r.k = p.sk + row * p.hd;
-        r.v = p.sv + row * p.hd;
-        r.ks = p.sks[row];
-        r.vs = p.svs[row];
+        row = ((size_t)s * p.kvheads + kh) * p.cs + slot;
+        where = 2;
+    }
+    if constexpr (sizeof(T) == 1) {
+        const int8_t *kb = where == 0 ? p.stage_k : where == 1 ? p.pk : p.sk;
+        const int8_t *vb = where == 0 ? p.stage_v : where == 1 ? p.pv : p.sv;
+        const float *ksb = where == 0 ? p.stage_ks : where == 1 ? p.pks : p.sks;
+        const float *vsb = where == 0 ? p.stage_vs : where == 1 ? p.pvs : p.svs;
+        r.k = kb + row * p.hd;
+        r.v = vb + row * p.hd;
+        r.ks = ksb[row];
+        r.vs = vsb[row];
+    } else {
+        // FP32 cache: no scales (the reference's FP32 KV arithmetic, engine.cpp:918-929)
+        const float *kb = where == 0 ? p.stage_kf : where == 1 ? p.pkf : p.skf;
+        const float *vb = where == 0 ? p.stage_vf : where == 1 ? p.pvf : p.svf;
+        r.k = kb + row * p.hd;
+        r.v = vb + row * p.hd;
+        r.ks = 1.f;
+        r.vs = 1.f;
     }
     return r;
 }
@@ -122,14 +171,14 @@ __device__ __forceinline__ Row visible_row(const AttnParams &p, int s, int pos, 
 // One CTA = (query, KV head, split): the R = heads/kvheads query heads of the
 // group over a contiguous range of the visible slots.  Lane-per-slot scores,
 // online softmax per warp, lane-per-dimension value accumulation.
-template <int HD, bool EXACT>
+template <int HD, bool EXACT, typename T>
 __global__ void __launch_bounds__(128) attn_split_kernel(const AttnParams p) {
     constexpr int NW = 4;
     const int hd = EXACT ? HD : p.hd;
     constexpr int DPL = (HD + 31) / 32;   // dims per lane in the PV phase
-    __shared__ float qs[kMaxGroup * HD];
-    __shared__ float wm[NW][kMaxGroup], wl[NW][kMaxGroup];
-    __shared__ float wacc[NW][kMaxGroup][HD];
+    __shared__ float qs[kMaxQueryGroup * HD];
+    __shared__ float wm[NW][kMaxQueryGroup], wl[NW][kMaxQueryGroup];
+    __shared__ float wacc[NW][kMaxQueryGroup][HD];
 
     const int split = blockIdx.x, kh = blockIdx.y, query = blockIdx.z;
     const int entry = query / p.tokens, t = query % p.tokens;
@@ -152,9 +201,9 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const AttnParams p) {
     __syncthreads();
 
     const float inv_sqrt = p.inv_sqrt_hd;
-    float m[kMaxGroup], l[kMaxGroup], acc[kMaxGroup][DPL];
+    float m[kMaxQueryGroup], l[kMaxQueryGroup], acc[kMaxQueryGroup][DPL];
 #pragma unroll
-    for (int r = 0; r < kMaxGroup; ++r) {
+    for (int r = 0; r < kMaxQueryGroup; ++r) {
         m[r] = -INFINITY;
         l[r] = 0.f;
 #pragma unroll
@@ -164,23 +213,30 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const AttnParams p) {
     for (int base = i0 + warp * 32; base < i1; base += NW * 32) {
         const int i = base + lane;
         const bool valid = i < i1;
-        Row row{};
-        float sc[kMaxGroup];
+        Row<T> row{};
+        float sc[kMaxQueryGroup];
 #pragma unroll
-        for (int r = 0; r < kMaxGroup; ++r) sc[r] = -INFINITY;
+        for (int r = 0; r < kMaxQueryGroup; ++r) sc[r] = -INFINITY;
         if (valid) {
-            row = visible_row(p, s, pos, kh, i, prefix_count, start, entry, chunk_start);
-            float dot[kMaxGroup];
+            row = visible_row<T>(p, s, pos, kh, i, prefix_count, start, entry, chunk_start);
+            float dot[kMaxQueryGroup];
 #pragma unroll
-            for (int r = 0; r < kMaxGroup; ++r) dot[r] = 0.f;
-            if (hd % 4 == 0) {
+            for (int r = 0; r < kMaxQueryGroup; ++r) dot[r] = 0.f;
+            if constexpr (sizeof(T) == 4) {
+                for (int d = 0; d < hd; ++d) {
+                    const float kf = __ldg(reinterpret_cast<const float *>(row.k) + d);
+#pragma unroll
+                    for (int r = 0; r < kMaxQueryGroup; ++r)
+                        if (r < R) dot[r] = fmaf(qs[r * HD + d], kf, dot[r]);
+                }
+            } else if (hd % 4 == 0) {
                 const uint32_t *kw = reinterpret_cast<const uint32_t *>(row.k);
 #pragma unroll 4
                 for (int d4 = 0; d4 < hd / 4; ++d4) {
                     float a, b, c, e;
                     i8x4_to_f32(__ldg(kw + d4), a, b, c, e);
 #pragma unroll
-                    for (int r = 0; r < kMaxGroup; ++r) {
+                    for (int r = 0; r < kMaxQueryGroup; ++r) {
                         if (r < R) {
                             const float4 qv = *reinterpret_cast<const float4 *>(qs + r * HD + 4 * d4);
                             dot[r] = fmaf(qv.x, a, dot[r]);
@@ -194,17 +250,17 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const AttnParams p) {
                 for (int d = 0; d < hd; ++d) {
                     const float kf = (float)row.k[d];
 #pragma unroll
-                    for (int r = 0; r < kMaxGroup; ++r)
+                    for (int r = 0; r < kMaxQueryGroup; ++r)
                         if (r < R) dot[r] = fmaf(qs[r * HD + d], kf, dot[r]);
                 }
             }
 #pragma unroll
-            for (int r = 0; r < kMaxGroup; ++r) sc[r] = __fmul_rn(__fmul_rn(dot[r], row.ks), inv_sqrt);
+            for (int r = 0; r < kMaxQueryGroup; ++r) sc[r] = __fmul_rn(__fmul_rn(dot[r], row.ks), inv_sqrt);
         }
         // online softmax update per head
-        float pr[kMaxGroup];
+        float pr[kMaxQueryGroup];
 #pragma unroll
-        for (int r = 0; r < kMaxGroup; ++r) {
+        for (int r = 0; r < kMaxQueryGroup; ++r) {
             if (r >= R) { pr[r] = 0.f; continue; }
             float bm = sc[r];
 #pragma unroll
@@ -224,18 +280,18 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const AttnParams p) {
         // values: lane owns dims lane + 32*j
         const int nvalid = min(32, i1 - base);
         for (int jt = 0; jt < nvalid; ++jt) {
-            const int8_t *vrow = reinterpret_cast<const int8_t *>(
+            const T *vrow = reinterpret_cast<const T *>(
                 __shfl_sync(kFull, reinterpret_cast<unsigned long long>(row.v), jt));
-            float w[kMaxGroup];
+            float w[kMaxQueryGroup];
 #pragma unroll
-            for (int r = 0; r < kMaxGroup; ++r) w[r] = __shfl_sync(kFull, pr[r], jt);
+            for (int r = 0; r < kMaxQueryGroup; ++r) w[r] = __shfl_sync(kFull, pr[r], jt);
 #pragma unroll
             for (int j = 0; j < DPL; ++j) {
                 const int d = lane + 32 * j;
                 if (d < hd) {
                     const float vf = (float)__ldg(vrow + d);
 #pragma unroll
-                    for (int r = 0; r < kMaxGroup; ++r)
+                    for (int r = 0; r < kMaxQueryGroup; ++r)
                         if (r < R) acc[r][j] = fmaf(w[r], vf, acc[r][j]);
                 }
             }
@@ -243,7 +299,7 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const AttnParams p) {
     }
     // combine the warps of this CTA
 #pragma unroll
-    for (int r = 0; r < kMaxGroup; ++r) {
+    for (int r = 0; r < kMaxQueryGroup; ++r) {
         if (r >= R) continue;
         if (lane == 0) {
             wm[warp][r] = m[r];
@@ -351,14 +407,15 @@ __device__ __forceinline__ RowPtr visible_ptr(const AttnParams &p, int s, int kh
     const int position = i < prefix_count ? i : start + (i - prefix_count);
     size_t row;
     RowPtr r;
-    if (position < p.prefix) {
-        row = (size_t)kh * p.prefix + position;
-        r.k = p.pk; r.v = p.pv; r.ks = p.pks; r.vs = p.pvs;
-        r.run = i < prefix_count ? prefix_count - i : p.prefix - position;
-    } else if (p.stage_k && position >= chunk_start) {
+    if (p.stage_k && position >= chunk_start) {
         row = (size_t)kh * p.stage_rows + (size_t)entry * p.tokens + (position - chunk_start);
         r.k = p.stage_k; r.v = p.stage_v; r.ks = p.stage_ks; r.vs = p.stage_vs;
         r.run = chunk_start + p.tokens - position;
+    } else if (position < p.prefix) {
+        row = (size_t)kh * p.prefix + position;
+        r.k = p.pk; r.v = p.pv; r.ks = p.pks; r.vs = p.pvs;
+        r.run = i < prefix_count ? prefix_count - i : p.prefix - position;
+        if (p.stage_k) r.run = min(r.run, chunk_start - position);
     } else {
         const int slot = p.window ? (position - p.prefix) % p.window : position - p.prefix;
         row = ((size_t)s * p.kvheads + kh) * p.cs + slot;
@@ -631,12 +688,12 @@ __device__ __forceinline__ RowPtr position_ptr(const AttnParams &p, int s, int k
                                                int chunk_start) {
     size_t row;
     RowPtr r;
-    if (position < p.prefix) {
-        row = (size_t)kh * p.prefix + position;
-        r.k = p.pk; r.v = p.pv; r.ks = p.pks; r.vs = p.pvs;
-    } else if (p.stage_k && position >= chunk_start) {
+    if (p.stage_k && position >= chunk_start) {
         row = (size_t)kh * p.stage_rows + (size_t)entry * p.tokens + (position - chunk_start);
         r.k = p.stage_k; r.v = p.stage_v; r.ks = p.stage_ks; r.vs = p.stage_vs;
+    } else if (position < p.prefix) {
+        row = (size_t)kh * p.prefix + position;
+        r.k = p.pk; r.v = p.pv; r.ks = p.pks; r.vs = p.pvs;
     } else {
         const int slot = p.window ? (position - p.prefix) % p.window : position - p.prefix;
         row = ((size_t)s * p.kvheads + kh) * p.cs + slot;
@@ -847,6 +904,15 @@ bool launch_kv_quantize(const float *k, const float *v, int tokens, int kvheads,
     return true;
 }
 
+bool launch_kv_store_f32(const float *k, const float *v, int tokens, int kvheads, int hd, float *ko, float *vo,
+                         const KVDest &dest, cudaStream_t st) {
+    if (tokens <= 0) return true;
+    const long long warps = (long long)tokens * kvheads;
+    kv_store_f32_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(k, v, tokens, kvheads, hd, ko, vo, dest);
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+}
+
 int attention_splits(int max_len, int queries_x_kv, int sms) {
     // enough CTAs to cover the machine about twice, at least 128 slots each
     int splits = 1;
@@ -856,12 +922,33 @@ int attention_splits(int max_len, int queries_x_kv, int sms) {
 
 bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
     if (queries <= 0) return true;
-    if (p.heads % p.kvheads || p.heads / p.kvheads > kMaxGroup) {
+    if (p.heads % p.kvheads || p.heads / p.kvheads > kMaxQueryGroup) {
         set_error("attention supports up to 8 query heads per KV head");
         return false;
     }
     dim3 grid(p.splits, p.kvheads, queries);
     const int R = p.heads / p.kvheads;
+    if (p.f32) {
+        switch (p.hd) {
+            case 32: attn_split_kernel<32, true, float><<<grid, 128, 0, st>>>(p); break;
+            case 64: attn_split_kernel<64, true, float><<<grid, 128, 0, st>>>(p); break;
+            case 128: attn_split_kernel<128, true, float><<<grid, 128, 0, st>>>(p); break;
+            default:
+                if (p.hd <= 32) attn_split_kernel<32, false, float><<<grid, 128, 0, st>>>(p);
+                else if (p.hd <= 64) attn_split_kernel<64, false, float><<<grid, 128, 0, st>>>(p);
+                else if (p.hd <= 128) attn_split_kernel<128, false, float><<<grid, 128, 0, st>>>(p);
+                else {
+                    set_error("head_dim above 128 is not supported by the GPU build");
+                    return false;
+                }
+        }
+        NB_CUDA_TRY(cudaGetLastError());
+        if (p.splits > 1) {
+            attn_combine_kernel<<<queries * p.heads, 64, 0, st>>>(p, p.hd);
+            NB_CUDA_TRY(cudaGetLastError());
+        }
+        return true;
+    }
     // prefill chunks of 16+ tokens: query tiles share every K/V read
     if (p.tokens >= 16 && p.hd == 64 && R <= 4 && queries % p.tokens == 0) {
         if (!launch_prefill_tile<64>(p, queries / p.tokens, R, st)) return false;
@@ -873,13 +960,13 @@ bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
     if (p.hd == 64 && R <= 4) streamed = launch_stream<64>(p, grid, R, st);
     else if (p.hd == 128 && R <= 2) streamed = launch_stream<128>(p, grid, R, st);
     if (!streamed) switch (p.hd) {
-        case 32: attn_split_kernel<32, true><<<grid, 128, 0, st>>>(p); break;
-        case 64: attn_split_kernel<64, true><<<grid, 128, 0, st>>>(p); break;
-        case 128: attn_split_kernel<128, true><<<grid, 128, 0, st>>>(p); break;
+        case 32: attn_split_kernel<32, true, int8_t><<<grid, 128, 0, st>>>(p); break;
+        case 64: attn_split_kernel<64, true, int8_t><<<grid, 128, 0, st>>>(p); break;
+        case 128: attn_split_kernel<128, true, int8_t><<<grid, 128, 0, st>>>(p); break;
         default:
-            if (p.hd <= 32) attn_split_kernel<32, false><<<grid, 128, 0, st>>>(p);
-            else if (p.hd <= 64) attn_split_kernel<64, false><<<grid, 128, 0, st>>>(p);
-            else if (p.hd <= 128) attn_split_kernel<128, false><<<grid, 128, 0, st>>>(p);
+            if (p.hd <= 32) attn_split_kernel<32, false, int8_t><<<grid, 128, 0, st>>>(p);
+            else if (p.hd <= 64) attn_split_kernel<64, false, int8_t><<<grid, 128, 0, st>>>(p);
+            else if (p.hd <= 128) attn_split_kernel<128, false, int8_t><<<grid, 128, 0, st>>>(p);
             else {
                 set_error("head_dim above 128 is not supported by the GPU build");
                 return false;

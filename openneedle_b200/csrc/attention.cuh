@@ -1,25 +1,31 @@
-// INT8 KV-cache attention launchers (see attention.cu).
+// INT8 (and FP32) KV-cache attention launchers (see attention.cu).
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace nb200 {
 
-constexpr int kMaxGroup = 8;  // query heads per KV head
+constexpr int kMaxQueryGroup = 8;  // query heads per KV head
 
-// Where kv_quantize_kernel writes token t.
+// Where the store kernels write token t.
 struct KVDest {
     enum Mode { kLinear = 0, kRing = 1 } mode;
     int rows;              // kLinear: rows per KV head; kRing: slots per session and head (Cs)
-    int prefix, window;    // kRing: slot = window ? (pos-prefix) % window : pos-prefix
+    int prefix, window;    // kRing: positions < prefix go to the pinned prefix rows [KV][prefix];
+                           // others to slot window ? (pos-prefix) % window : pos-prefix
     int tokens_per_entry;  // kRing: token t belongs to entry t / tokens_per_entry ...
     int min_t;             // ... and is skipped when t % tokens_per_entry < min_t
     const int *session;    // kRing, device [entries]
     const int *position;   // kRing, device [entries]: position of the entry's first token
+    // kRing: the pinned prefix rows (int8 + scales, or FP32), for positions < prefix
+    int8_t *pk, *pv;
+    float *pks, *pvs;
+    float *pkf, *pvf;
 };
 
 struct AttnParams {
     int heads, kvheads, hd, prefix, window, cs, splits, tokens;
+    int f32;                          // 1: FP32 cache (the *f pointers), 0: INT8 cache
     float inv_sqrt_hd;
     const int8_t *pk, *pv;            // shared prefix [KV][P][HD]
     const float *pks, *pvs;           // [KV][P]
@@ -27,6 +33,7 @@ struct AttnParams {
     const float *sks, *svs;           // [S][KV][Cs]
     const int8_t *stage_k, *stage_v;  // prefill chunk [KV][stage_rows][HD] or null
     const float *stage_ks, *stage_vs;
+    const float *pkf, *pvf, *skf, *svf, *stage_kf, *stage_vf;   // FP32 cache, same layouts
     int stage_rows;
     const int *session, *position;    // per entry (device): session, position of its first query
     const float *q;                   // [queries][heads][HD], queries = entries * tokens
@@ -34,8 +41,12 @@ struct AttnParams {
     float *part_m, *part_l, *part_acc; // split partials (splits > 1)
 };
 
+// INT8: quantise (engine.cpp:1005-1021) and store k/v [tokens][kvheads*hd].
 bool launch_kv_quantize(const float *k, const float *v, int tokens, int kvheads, int hd, int8_t *ko, int8_t *vo,
                         float *ks, float *vs, const KVDest &dest, cudaStream_t st);
+// FP32: store k/v unchanged (engine.cpp:1002-1004) in the same row layout.
+bool launch_kv_store_f32(const float *k, const float *v, int tokens, int kvheads, int hd, float *ko, float *vo,
+                         const KVDest &dest, cudaStream_t st);
 int attention_splits(int max_len, int queries_x_kv, int sms);
 bool launch_attention(const AttnParams &p, int queries, cudaStream_t st);
 

@@ -13,6 +13,7 @@
 #include "../../include/needle2_b200.h"
 #include "common.cuh"
 #include "cq_gemv.cuh"
+#include "cq_handle.cuh"
 #include "cq_kernels.cuh"
 
 namespace nb200 {
@@ -409,6 +410,52 @@ bool run_linear_host(Matrix *m, const float *x, float *y, int batch, int32_t *pa
 }
 
 }  // namespace
+}  // namespace nb200
+
+namespace nb200 {
+
+const CQDevice *handle_matrix(void *handle) { return handle ? &static_cast<Matrix *>(handle)->w : nullptr; }
+bool handle_is_sdot(void *handle) { return handle && static_cast<Matrix *>(handle)->sdot; }
+int handle_device(void *handle) { return static_cast<Matrix *>(handle)->device; }
+
+bool handle_prepare(void *handle, const float *x, int batch, const float **rot, const int8_t **q, const float **xs,
+                    cudaStream_t st) {
+    auto *m = static_cast<Matrix *>(handle);
+    const CQDevice &w = m->w;
+    m->prepared = 0;
+    if (m->sdot) {
+        if (!m->q.reserve((size_t)batch * w.padded) || !m->xs.reserve((size_t)batch * w.groups)) return false;
+        if (!launch_quantize(w, x, batch, m->q.ptr, m->xs.ptr, st)) return false;
+        if (q) *q = m->q.ptr;
+        if (xs) *xs = m->xs.ptr;
+    } else {
+        if (!m->rot.reserve((size_t)batch * w.padded)) return false;
+        if (!launch_rotate(w, x, batch, m->rot.ptr, st)) return false;
+        if (rot) *rot = m->rot.ptr;
+    }
+    m->prepared = batch;
+    return true;
+}
+
+void *handle_make_sdot(void *cq) {
+    auto *m = static_cast<Matrix *>(cq);
+    const CQDevice &w = m->w;
+    if (m->sdot) { set_error("handle is already an int8 matrix"); return nullptr; }
+    if (cudaSetDevice(m->device) != cudaSuccess) { set_error("cudaSetDevice failed"); return nullptr; }
+    std::vector<uint8_t> packed((size_t)w.out * w.rowbytes);
+    std::vector<uint16_t> norms((size_t)w.out * w.groups);
+    if (cudaStreamSynchronize(m->stream) != cudaSuccess ||
+        cudaMemcpy(packed.data(), w.packed, packed.size(), cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(norms.data(), w.norms, 2 * norms.size(), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        set_error("reading back the CQ matrix failed");
+        return nullptr;
+    }
+    float cb[16] = {};
+    const int ncb = w.bits == 5 ? 3 : 1 << w.bits;
+    for (int i = 0; i < ncb; ++i) cb[i] = w.lut[i];
+    return create_matrix(packed.data(), norms.data(), w.out, w.in, w.bits, w.group, cb, true);
+}
+
 }  // namespace nb200
 
 using nb200::Matrix;

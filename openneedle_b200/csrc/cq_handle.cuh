@@ -1,0 +1,25 @@
+// Internal access to CQ handles (cq_abi.cu) for the engine: the device view of
+// a handle's matrix, its prepared activations, and an int8 twin of an FP32
+// handle.  Not part of the C ABI.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "cq_kernels.cuh"
+
+namespace nb200 {
+
+// Device view of handle's matrix (null when handle is null).
+const CQDevice *handle_matrix(void *handle);
+bool handle_is_sdot(void *handle);
+int handle_device(void *handle);
+// Rotate (FP32 handle) or rotate and quantise (int8 handle) x[batch][in] into
+// the handle's scratch and return it: rot [batch][padded] (FP32), or q
+// [batch][padded] (CQ2 in bit-plane order) and xs [batch][groups] (int8).
+bool handle_prepare(void *handle, const float *x, int batch, const float **rot, const int8_t **q, const float **xs,
+                    cudaStream_t st);
+// A new int8 (SDOT) handle over the same packed matrix as the FP32 handle
+// `cq` (its device copy read back once), or null with the error set.
+void *handle_make_sdot(void *cq);
+
+}  // namespace nb200

@@ -14,6 +14,7 @@
 #include "../../include/needle2_b200.h"
 #include "attention.cuh"
 #include "common.cuh"
+#include "kv_pool.cuh"
 
 namespace nb200 {
 namespace {
@@ -43,24 +44,31 @@ struct Buf {
     }
 };
 
+}  // namespace
+
 struct KVPool {
     int sessions, heads, kvheads, hd, max_seq, window, prefix, cs, device = 0, sms = 148;
+    bool fp32 = false;
     bool prefix_set = false;
     cudaStream_t stream = nullptr;
     Buf<int8_t> pk, pv, sk, sv, stk, stv;
     Buf<float> pks, pvs, sks, svs, stks, stvs, pm, pl, pacc, hq, hk, hv, hout;
+    Buf<float> pkf, pvf, skf, svf, stkf, stvf;   // FP32 cache
     Buf<int> ids, pos;
     ~KVPool() {
         cudaSetDevice(device);
         if (stream) cudaStreamSynchronize(stream);
         for (auto *b : {&pk, &pv, &sk, &sv, &stk, &stv}) b->release();
         for (auto *b : {&pks, &pvs, &sks, &svs, &stks, &stvs, &pm, &pl, &pacc, &hq, &hk, &hv, &hout}) b->release();
+        for (auto *b : {&pkf, &pvf, &skf, &svf, &stkf, &stvf}) b->release();
         ids.release();
         pos.release();
         if (stream) cudaStreamDestroy(stream);
     }
     int capacity() const { return window ? window + prefix : max_seq; }
 };
+
+namespace {
 
 // Host-side checks of one call's sessions and positions (tokens per entry).
 bool validate(const KVPool &kv, const int *session_ids, const int *positions, int count, int tokens,
@@ -88,20 +96,11 @@ AttnParams base_params(KVPool &kv) {
     p.heads = kv.heads; p.kvheads = kv.kvheads; p.hd = kv.hd; p.prefix = kv.prefix; p.window = kv.window;
     p.cs = kv.cs;
     p.inv_sqrt_hd = 1 / std::sqrt((float)kv.hd);   // the reference's 1/sqrt(float(HD))
+    p.f32 = kv.fp32 ? 1 : 0;
     p.pk = kv.pk.ptr; p.pv = kv.pv.ptr; p.pks = kv.pks.ptr; p.pvs = kv.pvs.ptr;
     p.sk = kv.sk.ptr; p.sv = kv.sv.ptr; p.sks = kv.sks.ptr; p.svs = kv.svs.ptr;
+    p.pkf = kv.pkf.ptr; p.pvf = kv.pvf.ptr; p.skf = kv.skf.ptr; p.svf = kv.svf.ptr;
     return p;
-}
-
-int max_visible(const KVPool &kv, const int *positions, int count, int tokens) {
-    int best = 1;
-    for (int i = 0; i < count; ++i) {
-        const int pos = positions[i] + tokens - 1;
-        const int pc = kv.window ? std::min(kv.prefix, pos + 1) : 0;
-        const int start = kv.window ? std::max(kv.prefix, pos - kv.window + 1) : 0;
-        best = std::max(best, pc + std::max(0, pos - start + 1));
-    }
-    return best;
 }
 
 // Session ids and positions of up to kIndexArgMax entries travel as a kernel
@@ -138,7 +137,7 @@ bool upload_index(KVPool &kv, const int *session_ids, const int *positions, int 
     return true;
 }
 
-bool store_ring(KVPool &kv, const float *k, const float *v, int count, int tokens, int min_t, cudaStream_t st) {
+KVDest ring_dest(KVPool &kv, const int *ids, const int *pos, int tokens, int min_t) {
     KVDest d{};
     d.mode = KVDest::kRing;
     d.rows = kv.cs;
@@ -146,28 +145,39 @@ bool store_ring(KVPool &kv, const float *k, const float *v, int count, int token
     d.window = kv.window;
     d.tokens_per_entry = tokens;
     d.min_t = min_t;
-    d.session = kv.ids.ptr;
-    d.position = kv.pos.ptr;
+    d.session = ids;
+    d.position = pos;
+    d.pk = kv.pk.ptr; d.pv = kv.pv.ptr; d.pks = kv.pks.ptr; d.pvs = kv.pvs.ptr;
+    d.pkf = kv.pkf.ptr; d.pvf = kv.pvf.ptr;
+    return d;
+}
+
+bool store_ring(KVPool &kv, const int *ids, const int *pos, const float *k, const float *v, int count, int tokens,
+                int min_t, cudaStream_t st) {
+    const KVDest d = ring_dest(kv, ids, pos, tokens, min_t);
+    if (kv.fp32)
+        return launch_kv_store_f32(k, v, count * tokens, kv.kvheads, kv.hd, kv.skf.ptr, kv.svf.ptr, d, st);
     return launch_kv_quantize(k, v, count * tokens, kv.kvheads, kv.hd, kv.sk.ptr, kv.sv.ptr, kv.sks.ptr, kv.svs.ptr, d,
                               st);
 }
 
 // Attention of `count` entries x `tokens` queries; staging holds the entries'
-// own new K/V when tokens > 1 (prefill).
-bool attend(KVPool &kv, const int *positions, int count, int tokens, const float *q, float *out, bool staged,
-            cudaStream_t st) {
+// own new K/V when `staged` (prefill).
+bool attend(KVPool &kv, const int *ids, const int *pos, int count, int tokens, int max_len, const float *q, float *out,
+            bool staged, cudaStream_t st) {
     AttnParams p = base_params(kv);
     p.tokens = tokens;
-    p.session = kv.ids.ptr;
-    p.position = kv.pos.ptr;
+    p.session = ids;
+    p.position = pos;
     p.q = q;
     p.out = out;
     if (staged) {
         p.stage_k = kv.stk.ptr; p.stage_v = kv.stv.ptr; p.stage_ks = kv.stks.ptr; p.stage_vs = kv.stvs.ptr;
+        p.stage_kf = kv.stkf.ptr; p.stage_vf = kv.stvf.ptr;
         p.stage_rows = count * tokens;
     }
     const int queries = count * tokens;
-    p.splits = attention_splits(max_visible(kv, positions, count, tokens), queries * kv.kvheads, kv.sms);
+    p.splits = attention_splits(max_len, queries * kv.kvheads, kv.sms);
     if (p.splits > 1) {
         const size_t rows = (size_t)queries * kv.heads * p.splits;
         if (!kv.pm.reserve(rows) || !kv.pl.reserve(rows) || !kv.pacc.reserve(rows * kv.hd)) return false;
@@ -176,19 +186,110 @@ bool attend(KVPool &kv, const int *positions, int count, int tokens, const float
     return launch_attention(p, queries, st);
 }
 
+// The chunk's own K/V in the staging layout [KV][rows][HD] (quantised for INT8).
 bool stage(KVPool &kv, const float *k, const float *v, int rows, cudaStream_t st) {
     const size_t n = (size_t)kv.kvheads * rows;
-    if (!kv.stk.reserve(n * kv.hd) || !kv.stv.reserve(n * kv.hd) || !kv.stks.reserve(n) || !kv.stvs.reserve(n))
-        return false;
     KVDest d{};
     d.mode = KVDest::kLinear;
     d.rows = rows;
+    if (kv.fp32) {
+        if (!kv.stkf.reserve(n * kv.hd) || !kv.stvf.reserve(n * kv.hd)) return false;
+        // the FP32 staging rows are still written by the ring store's kernel, in linear mode
+        return launch_kv_store_f32(k, v, rows, kv.kvheads, kv.hd, kv.stkf.ptr, kv.stvf.ptr, d, st);
+    }
+    if (!kv.stk.reserve(n * kv.hd) || !kv.stv.reserve(n * kv.hd) || !kv.stks.reserve(n) || !kv.stvs.reserve(n))
+        return false;
     return launch_kv_quantize(k, v, rows, kv.kvheads, kv.hd, kv.stk.ptr, kv.stv.ptr, kv.stks.ptr, kv.stvs.ptr, d, st);
 }
 
 KVPool *pool(void *h) { return static_cast<KVPool *>(h); }
 
 }  // namespace
+
+// ---- the pool calls shared by the C ABI below and the engine --------------
+
+KVPool *kv_pool_new(int sessions, int heads, int kvheads, int head_dim, int max_seq, int window, int prefix,
+                    bool fp32) {
+    if (sessions < 1 || heads < 1 || kvheads < 1 || head_dim < 1 || max_seq < 1 || window < 0 || prefix < 0) {
+        set_error("invalid KV geometry");
+        return nullptr;
+    }
+    if (heads % kvheads || heads / kvheads > kMaxQueryGroup) {
+        set_error("heads must be a multiple of kvheads with at most 8 query heads per KV head");
+        return nullptr;
+    }
+    if (head_dim > 128) { set_error("head_dim above 128 is not supported by the GPU build"); return nullptr; }
+    if (prefix > max_seq) { set_error("prefix_len must lie between 0 and max_seq"); return nullptr; }
+    auto *kv = new (std::nothrow) KVPool();
+    if (!kv) { set_error("out of host memory"); return nullptr; }
+    kv->sessions = sessions; kv->heads = heads; kv->kvheads = kvheads; kv->hd = head_dim; kv->max_seq = max_seq;
+    kv->window = window; kv->prefix = prefix; kv->fp32 = fp32;
+    kv->cs = window ? window : max_seq - prefix;
+    cudaGetDevice(&kv->device);
+    cudaDeviceGetAttribute(&kv->sms, cudaDevAttrMultiProcessorCount, kv->device);
+    const size_t prow = (size_t)kvheads * prefix, srow = (size_t)sessions * kvheads * kv->cs;
+    bool ok = cudaStreamCreateWithFlags(&kv->stream, cudaStreamNonBlocking) == cudaSuccess;
+    if (fp32) {
+        ok = ok && kv->pkf.reserve(prow * head_dim) && kv->pvf.reserve(prow * head_dim);
+        ok = ok && kv->skf.reserve(srow * head_dim) && kv->svf.reserve(srow * head_dim);
+    } else {
+        ok = ok && kv->pk.reserve(prow * head_dim) && kv->pv.reserve(prow * head_dim) && kv->pks.reserve(prow) &&
+             kv->pvs.reserve(prow);
+        ok = ok && kv->sk.reserve(srow * head_dim) && kv->sv.reserve(srow * head_dim) && kv->sks.reserve(srow) &&
+             kv->svs.reserve(srow);
+    }
+    if (!ok) {
+        if (last_error()[0] == 0) set_error("KV pool creation failed");
+        delete kv;
+        return nullptr;
+    }
+    return kv;
+}
+
+void kv_pool_delete(KVPool *kv) { delete kv; }
+
+size_t kv_pool_bytes(const KVPool *kv) {
+    if (!kv) return 0;
+    const size_t rows = (size_t)kv->kvheads * kv->prefix + (size_t)kv->sessions * kv->kvheads * kv->cs;
+    return kv->fp32 ? rows * 2 * sizeof(float) * kv->hd : rows * (2 * (size_t)kv->hd + 2 * sizeof(float));
+}
+
+int kv_pool_device(const KVPool *kv) { return kv->device; }
+
+int kv_max_visible(int prefix, int window, const int *positions, int count, int tokens) {
+    int best = 1;
+    for (int i = 0; i < count; ++i) {
+        const int pos = positions[i] + tokens - 1;
+        const int pc = window ? std::min(prefix, pos + 1) : 0;
+        const int start = window ? std::max(prefix, pos - window + 1) : 0;
+        best = std::max(best, pc + std::max(0, pos - start + 1));
+    }
+    return best;
+}
+
+bool kv_pool_run(KVPool *kv, KVOp op, const int *ids, const int *pos, int count, int tokens, int max_visible,
+                 const float *q, const float *k, const float *v, float *out, cudaStream_t st) {
+    if (count <= 0) return true;
+    switch (op) {
+        case kStore: return store_ring(*kv, ids, pos, k, v, count, tokens, 0, st);
+        case kQuery: return attend(*kv, ids, pos, count, tokens, max_visible, q, out, false, st);
+        case kDecode:
+            if (tokens != 1) { set_error("decode takes one token per entry"); return false; }
+            return store_ring(*kv, ids, pos, k, v, count, 1, 0, st) &&
+                   attend(*kv, ids, pos, count, 1, max_visible, q, out, false, st);
+        case kPrefill: {
+            if (!stage(*kv, k, v, count * tokens, st)) return false;
+            if (!attend(*kv, ids, pos, count, tokens, max_visible, q, out, true, st)) return false;
+            // write the slots after attending; with a window only the last `window`
+            // tokens of the chunk outside the pinned prefix survive (earlier ones
+            // would be overwritten anyway)
+            const int min_t = kv->window && tokens > kv->window ? tokens - kv->window : 0;
+            return store_ring(*kv, ids, pos, k, v, count, tokens, min_t, st);
+        }
+    }
+    return false;
+}
+
 }  // namespace nb200
 
 using nb200::KVPool;
@@ -197,45 +298,12 @@ extern "C" {
 
 void *needle2_kv_create(int sessions, int heads, int kvheads, int head_dim, int max_seq, int window, int prefix_len) {
     nb200::clear_error();
-    if (sessions < 1 || heads < 1 || kvheads < 1 || head_dim < 1 || max_seq < 1 || window < 0 || prefix_len < 0) {
-        nb200::set_error("invalid KV geometry");
-        return nullptr;
-    }
-    if (heads % kvheads || heads / kvheads > nb200::kMaxGroup) {
-        nb200::set_error("heads must be a multiple of kvheads with at most 8 query heads per KV head");
-        return nullptr;
-    }
-    if (head_dim > 128) { nb200::set_error("head_dim above 128 is not supported by the GPU build"); return nullptr; }
-    if (prefix_len > max_seq) { nb200::set_error("prefix_len must lie between 0 and max_seq"); return nullptr; }
-    auto *kv = new (std::nothrow) KVPool();
-    if (!kv) { nb200::set_error("out of host memory"); return nullptr; }
-    kv->sessions = sessions; kv->heads = heads; kv->kvheads = kvheads; kv->hd = head_dim; kv->max_seq = max_seq;
-    kv->window = window; kv->prefix = prefix_len;
-    kv->cs = window ? window : max_seq - prefix_len;
-    cudaGetDevice(&kv->device);
-    cudaDeviceGetAttribute(&kv->sms, cudaDevAttrMultiProcessorCount, kv->device);
-    const size_t prow = (size_t)kvheads * prefix_len, srow = (size_t)sessions * kvheads * kv->cs;
-    bool ok = cudaStreamCreateWithFlags(&kv->stream, cudaStreamNonBlocking) == cudaSuccess;
-    ok = ok && kv->pk.reserve(prow * head_dim) && kv->pv.reserve(prow * head_dim) && kv->pks.reserve(prow) &&
-         kv->pvs.reserve(prow);
-    ok = ok && kv->sk.reserve(srow * head_dim) && kv->sv.reserve(srow * head_dim) && kv->sks.reserve(srow) &&
-         kv->svs.reserve(srow);
-    if (!ok) {
-        if (nb200::last_error()[0] == 0) nb200::set_error("KV pool creation failed");
-        delete kv;
-        return nullptr;
-    }
-    return kv;
+    return nb200::kv_pool_new(sessions, heads, kvheads, head_dim, max_seq, window, prefix_len, false);
 }
 
-void needle2_kv_destroy(void *h) { delete nb200::pool(h); }
+void needle2_kv_destroy(void *h) { nb200::kv_pool_delete(nb200::pool(h)); }
 
-size_t needle2_kv_storage_bytes(void *h) {
-    KVPool *kv = nb200::pool(h);
-    if (!kv) return 0;
-    const size_t prow = (size_t)kv->kvheads * kv->prefix, srow = (size_t)kv->sessions * kv->kvheads * kv->cs;
-    return (prow + srow) * (2 * (size_t)kv->hd + 2 * sizeof(float));
-}
+size_t needle2_kv_storage_bytes(void *h) { return nb200::kv_pool_bytes(nb200::pool(h)); }
 
 int needle2_kv_set_prefix_device(void *h, const float *k, const float *v, void *stream) {
     nb200::clear_error();
@@ -282,9 +350,9 @@ static int decode_device(void *h, const int *session_ids, const int *positions, 
     if (cudaSetDevice(kv->device) != cudaSuccess) { nb200::set_error("cudaSetDevice failed"); return -1; }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (!nb200::upload_index(*kv, session_ids, positions, count, st)) return -1;
-    if (mode != 2 && !nb200::store_ring(*kv, k, v, count, 1, 0, st)) return -1;
-    if (mode != 0 && !nb200::attend(*kv, positions, count, 1, q, out, false, st)) return -1;
-    return 0;
+    const nb200::KVOp op = mode == 0 ? nb200::kStore : mode == 1 ? nb200::kDecode : nb200::kQuery;
+    const int len = nb200::kv_max_visible(kv->prefix, kv->window, positions, count, 1);
+    return nb200::kv_pool_run(kv, op, kv->ids.ptr, kv->pos.ptr, count, 1, len, q, k, v, out, st) ? 0 : -1;
 }
 
 int needle2_attention_decode_device(void *h, const int *session_ids, const int *positions, const float *q,
@@ -311,13 +379,10 @@ int needle2_attention_prefill_device(void *h, const int *session_ids, const int 
     if (cudaSetDevice(kv->device) != cudaSuccess) { nb200::set_error("cudaSetDevice failed"); return -1; }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (!nb200::upload_index(*kv, session_ids, start_positions, count, st)) return -1;
-    if (!nb200::stage(*kv, k, v, count * tokens, st)) return -1;
-    if (!nb200::attend(*kv, start_positions, count, tokens, q, out, true, st)) return -1;
-    // write the ring after attending; with a window only the last `window`
-    // tokens of the chunk survive (earlier ones would be overwritten anyway)
-    const int min_t = kv->window && tokens > kv->window ? tokens - kv->window : 0;
-    if (!nb200::store_ring(*kv, k, v, count, tokens, min_t, st)) return -1;
-    return 0;
+    const int len = nb200::kv_max_visible(kv->prefix, kv->window, start_positions, count, tokens);
+    return nb200::kv_pool_run(kv, nb200::kPrefill, kv->ids.ptr, kv->pos.ptr, count, tokens, len, q, k, v, out, st)
+               ? 0
+               : -1;
 }
 
 // Host-pointer forms: copy in, run on the pool's stream, copy out, synchronise.

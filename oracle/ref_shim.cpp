@@ -123,3 +123,23 @@ void ref_attention_i8(int heads, int kvheads, int head_dim, int max_seq, int win
 }
 
 }  // extern "C"
+
+extern "C" {
+
+// Engine::configure_sdot (needle2/csrc/engine.cpp:424-432) without its ARM64
+// DotProd gate: the portable SdotCQ branches compute the same integers on
+// x86, so the reference engine's SDOT arithmetic can serve as the oracle here.
+int ref_engine_force_sdot(void *p) {
+    auto *e = static_cast<Engine *>(p);
+    for (size_t i = 0; i < e->t.size(); ++i)
+        if (e->t[i].cq) {
+            auto *q = static_cast<CQ *>(e->t[i].cq);
+            if ((q->bits == 2 || q->bits == 4) && q->group >= 64 && q->group <= 131072)
+                e->sdot[i] = std::make_unique<SdotCQ>(q->packed, q->norms, q->out, q->in, q->bits, q->group,
+                                                      q->cb.data());
+        }
+    e->sdot_enabled = true;
+    return 0;
+}
+
+}  // extern "C"

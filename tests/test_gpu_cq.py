@@ -126,7 +126,7 @@ def test_device_entry_points_match_host(native):
     q.fp32.linear_device(x, y)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(y.cpu().numpy(), q.fp32(g["x"][:16]))
-    q.sdot.fp32.linear_device(x, y)
+    q.sdot.linear_device(x, y)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(y.cpu().numpy(), q.sdot(g["x"][:16]))
 
