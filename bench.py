@@ -1,27 +1,33 @@
-"""Benchmark of the CQ4 decode GEMV on B200 (one JSON line on rank 0).
+"""Benchmark of OpenNeedle's quantized hot path on B200 (one JSON line on rank 0).
 
-Workload (the HBM-roofline decode GEMV of the benchmark plan): R = 17 distinct
-CQ4 matrices of 14336 x 4096 (group 128, the config-5 GEMM shape), each packed
-from N(0, 0.02) weights (seed 0), against one 4096-wide N(0, 1) activation row
-(seed 1), in the SDOT int8 mode (per-group int8 activations, int8 centroids,
-exact int32 per group).  One step = prepare (rotate + quantise x once) and one
-fused GEMV launch over the R matrices sharing that input, as the reference's
-fused projections do (needle2/csrc/engine.cpp:560-606): 516 MB of weights,
-more than 4x the 126 MB L2, so every step streams its weights from HBM.
+Headline (the batched-decode half of the metric): the
+Needle-2 decoder (d 512, 12 layers, 8 query / 4 KV heads x 64, vocab 32768,
+engram sites at layers 2 and 9) as the reference's NeedleModel default init
+(seed 0) packed by the reference's quantizer in the release scheme (CQ4
+embedding and mHC, CQ2 projections and engram tables), FP32 matmul mode,
+INT8 KV.  1024 sessions with 256-token prompts (default_rng(0) tokens) are
+prefilled (untimed), then every step decodes one greedy token for every
+session.  Sessions are split evenly over the GPUs (one process per GPU,
+weights replicated, no collective), so the total work is fixed: "strong".
 
-value     algorithmic bytes of all steps on all ranks / max-over-ranks device time
-          (K steps captured in one CUDA graph, replayed once between CUDA events)
-roofline  the fused GEMV kernel alone: its algorithmic bytes / its mean CUDA-event
-          duration, against the measured HBM copy bandwidth (MEASURED_PEAKS.json)
-e2e       the same metric through the reference-facing host call
-          (host x -> device, prepare, fused GEMV, R outputs -> host, synchronised)
+value     sessions * K steps / max-over-ranks device time of K steps (one
+          needle2_batch_decode_greedy_device call between CUDA events)
+roofline  the decode step's dominant stage (KV store + attention over the
+          INT8 cache, 12 layers), from the engine's per-stage CUDA-event timers
+          in a profiled pass: its algorithmic bytes / its time, against the
+          measured HBM copy bandwidth (MEASURED_PEAKS.json)
+e2e       the same metric through needle2_batch_step from host buffers: each
+          step's tokens copied in and its greedy tokens read back
 cpu_baseline / --impl reference
-          the reference's own CPU SDOT path (oracle/_ref, compiled from its
-          sources; SdotCQ prepare + multiply, OpenMP rows) on this host's cores,
-          one matrix per sample (a bounded sample of the R-matrix step).
+          the reference's own engine (needle2/native.py NativeEngine on its CPU
+          library built from its sources, oracle/_ref, all host threads, INT8
+          KV): decode steps of one session after a 256-token prefill; it serves
+          one sequence per engine, so its tokens/s is per sequence served.
 
-Multi-GPU: each rank runs the same workload on its own GPU (replicas: the
-standalone GEMV does not shard), scaling "weak".
+Side lines: cq_gemv (the HBM-roofline decode GEMV of 17 fused 14336x4096 CQ4
+matrices, SDOT mode, with its own roofline and CPU baseline), the config-3
+prefill GEMMs, config-4 INT8 KV attention, and on 2+ GPUs the N-sharded
+14336x4096 GEMM with its all-gather.
 """
 from __future__ import annotations
 
@@ -212,7 +218,7 @@ def reference_gemv(packed, norms, cb, x, seconds=None, steps=None, warmup=2, hos
     return per_matrix * n / el / 1e9, el / n, n, used, kind
 
 
-def run_reference_arm(args, rank, world):
+def gemv_reference_arm(args, rank, world):
     if rank != 0:
         return None
     packed, norms, cb = weights()
@@ -483,15 +489,10 @@ def sharded_gemm(dev, stream, world, dist, packed, norms, cb, m=2048, reps=10):
     return res
 
 
-def run_native(args, rank, world, dist):
+def gemv_native(args, rank, world, dist):
     import torch
-    from openneedle_b200 import build as b
     from openneedle_b200.native import _library
 
-    if rank == 0:
-        b.build()
-    if dist is not None:
-        dist.barrier()
     lib = _library()
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
@@ -647,6 +648,259 @@ def run_native(args, rank, world, dist):
     return result
 
 
+# ------------------------------------------------------ config-5 decoder
+
+DEC_SESSIONS, DEC_PROMPT, DEC_VOCAB = 1024, 256, 32768
+DEC_CONFIG = dict(vocab_size=DEC_VOCAB, d_model=512, num_heads=8, num_kv_heads=4, num_layers=12, head_dim=64,
+                  max_seq_len=4096, kv_window=0, engram_layers=(2, 9))
+
+
+def decoder_archive(seed: int = 0):
+    """BASELINE config 5 as an in-memory archive: the reference's
+    NeedleModel(config) default init under torch.manual_seed(seed)
+    (needle2/model.py:266-287; N(0, 0.02) matrices), packed by the reference's
+    quantizer in its release scheme (CQ4 embedding and mHC projections, CQ2
+    attention/engram projections and engram tables, FP32 elsewhere) into its
+    TensorRecord objects."""
+    from types import SimpleNamespace
+
+    import torch
+    Q = ref_quantize()
+    from needle2 import archive as A
+    from needle2 import model as M
+    torch.manual_seed(seed)
+    model = M.NeedleModel(M.NeedleConfig(**DEC_CONFIG))
+    records = {}
+    for name, t in model.canonical_state_dict().items():
+        a = t.detach().numpy().astype(np.float32)
+        if a.ndim == 2 and (name == "embedding" or name.startswith("mhc_phi") or name.endswith(("_proj", ".tables"))):
+            bits = 4 if name == "embedding" or name.startswith("mhc_phi") else 2
+            p, n = Q.quantize_matrix(a, bits, 128)
+            records[name] = A.TensorRecord(name, A.CQ, a.shape, p.tobytes() + n.tobytes(), 128, bits,
+                                           Q.codebook(bits, 128))
+        else:
+            records[name] = A.TensorRecord(name, A.FP32, a.shape, a.tobytes())
+    meta = model.config.to_dict()
+    meta["hada_n"] = 1 << (meta["d_model"] - 1).bit_length()
+    return SimpleNamespace(metadata=meta, tensors=records)
+
+
+def decoder_prompts():
+    return np.random.default_rng(0).integers(3, DEC_VOCAB, (DEC_SESSIONS, DEC_PROMPT)).astype(np.int32)
+
+
+def decoder_config(world):
+    return {"workload": f"needle2_config5_decode_{DEC_SESSIONS}x{DEC_PROMPT}", "sessions": DEC_SESSIONS,
+            "prompt_tokens": DEC_PROMPT, "d_model": 512, "layers": 12, "heads": 8, "kv_heads": 4, "head_dim": 64,
+            "vocab": DEC_VOCAB, "engram_layers": [2, 9], "matmul": "fp32 (CQ dequant-accumulate)", "kv_cache": "int8",
+            "weights": "CQ4 embedding + mHC, CQ2 projections + engram tables (reference quantizer)",
+            "parallelism": f"sessions split over {world} GPU(s), weights replicated, no collective",
+            "l2": f"inputs larger than L2: each step reads ~{DEC_SESSIONS * 12 * 4 * 2 * 136 * DEC_PROMPT / 1e9:.1f} GB "
+                  "of INT8 KV"}
+
+
+def decode_bytes(sessions, position):
+    """Algorithmic HBM bytes of one decode step of `sessions` sequences whose
+    new token sits at `position`: the KV cache read (position + 1 slots of
+    K and V, int8 + one FP32 scale per KV head, 12 layers) and the new slot
+    written, the weights once (packed CQ + FP32 tensors), the lane state
+    (4 lanes x 512 FP32) read and written once per layer, the logits written
+    once and read once by the greedy choice."""
+    kv_slot = 4 * (2 * 64 + 2 * 4)
+    kv = sessions * 12 * kv_slot * (position + 1 + 1)
+    weights = 14_977_344 + 12 * (24 * 2048 * 4)    # packed CQ records + FP32 mHC projections
+    lanes = sessions * 12 * 2 * 4 * 512 * 4
+    logits = sessions * DEC_VOCAB * 4 * 2
+    attn_only = sessions * 12 * (kv_slot * (position + 2) + 2 * 8 * 64 * 4)
+    return kv + weights + lanes + logits, attn_only
+
+
+def reference_decode(archive, prompt, steps, warmup=2, seconds=None):
+    """The reference's own engine on the host: NativeEngine (needle2/native.py)
+    on its CPU library built from its sources (oracle/_ref), all host
+    threads, INT8 KV, FP32 matmuls.  Prefill one session's prompt (untimed),
+    then time single-token decode steps.  Returns (tokens/s, steps, threads)."""
+    from oracle import oracle as O
+    if not O.ref_available():
+        return None
+    os.environ["NEEDLE2_NATIVE_LIBRARY"] = str(O.REF_LIB)
+    os.environ.setdefault("OMP_WAIT_POLICY", "PASSIVE")
+    ref_quantize()
+    from needle2.native import NativeEngine
+    threads = min(cpu_threads(), 256)
+    e = NativeEngine(archive, threads=threads, kv_cache="int8")
+    logits = e.prefill(prompt, last_only=True)
+    tok = int(np.argmax(logits))
+    for _ in range(warmup):
+        tok = int(np.argmax(e.step(tok)))
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        tok = int(np.argmax(e.step(tok)))
+        n += 1
+        el = time.perf_counter() - t0
+        if n >= steps or (seconds is not None and el >= seconds):
+            break
+    return n / el, n, threads
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return None
+    archive = decoder_archive()
+    steps = max(1, min(args.steps, 64))
+    r = reference_decode(archive, decoder_prompts()[0], steps, warmup=args.warmup, seconds=120)
+    if r is None:
+        return {"impl": "reference", "unavailable": "the reference's CPU build (oracle/_ref) is missing"}
+    tps, n, threads = r
+    return {
+        "impl": "reference", "metric": "batched_decode_tokens_per_s", "value": tps, "unit": "tokens/s",
+        "n_gpus": world, "steps": n, "warmup": args.warmup, "ms_per_step": 1e3 / tps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": decoder_config(world),
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                         "sample": f"{n} decode steps of one session (the reference serves one sequence per engine) "
+                                   f"after its {DEC_PROMPT}-token prefill, NativeEngine on oracle/_ref with "
+                                   f"{threads} threads; x86 runs the reference's portable (non-NEON) branches"},
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def decoder_native(args, rank, world, dist, dev):
+    import torch
+    from openneedle_b200.engine import GpuModel
+
+    if DEC_SESSIONS % world:
+        raise SystemExit(f"{DEC_SESSIONS} sessions do not split over {world} GPUs")
+    S = DEC_SESSIONS // world
+    archive = decoder_archive()
+    model = GpuModel(archive, kv_cache="int8", matmul="fp32")
+    batch = model.batch(S)
+    prompts = decoder_prompts()[rank * S:(rank + 1) * S]
+    t0 = time.perf_counter()
+    _, first = batch.prefill(prompts, logits=False, greedy=True)
+    prefill_s = time.perf_counter() - t0
+    stream = torch.cuda.current_stream(dev)
+    cur = torch.from_numpy(first).to(dev)
+    warm = torch.empty(S, args.warmup, dtype=torch.int32, device=dev)
+    batch.decode_greedy_device(cur, args.warmup, warm, stream)
+    cur = warm[:, -1].contiguous()
+    out = torch.empty(S, args.steps, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    position0 = int(batch.positions()[0])
+    with ClockSampler(dev.index) as clocks:
+        start.record(stream)
+        batch.decode_greedy_device(cur, args.steps, out, stream)
+        end.record(stream)
+        torch.cuda.synchronize(dev)
+    elapsed_ms = start.elapsed_time(end)
+    cur = out[:, -1].contiguous()
+
+    # per-stage breakdown of a few more steps (profiled separately: events at
+    # every stage boundary)
+    batch.profile(True)
+    prof_steps = 4
+    prof_out = torch.empty(S, prof_steps, dtype=torch.int32, device=dev)
+    position_p = int(batch.positions()[0])
+    batch.decode_greedy_device(cur, prof_steps, prof_out, stream)
+    stages = {k: v / prof_steps for k, v in batch.profile_read().items()}
+    batch.profile(False)
+    cur_host = prof_out[:, -1].cpu().numpy()
+
+    # end to end through the public host-pointer call: tokens in, greedy tokens out, every step
+    n_e2e = 8
+    tok = cur_host
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        _, tok = batch.step(tok, logits=False, greedy=True)
+    e2e_s = (time.perf_counter() - t0) / n_e2e
+
+    t = torch.tensor([elapsed_ms, e2e_s, prefill_s], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, e2e_s, prefill_s = t.tolist()
+    ms_step = elapsed_ms / args.steps
+    tokens_per_s = DEC_SESSIONS * args.steps / (elapsed_ms * 1e-3)
+    mid = position0 + args.steps // 2
+    step_bytes_all, _ = decode_bytes(S, mid)
+    _, attn_bytes = decode_bytes(S, position_p + prof_steps // 2)
+    hbm, peak_kind = peaks()
+    attn_ms = stages["kv_store+attention"]
+    total_prof = sum(stages.values())
+    dominant = max(stages, key=stages.get)
+    attn_gbs = attn_bytes / (attn_ms * 1e-3) / 1e9
+    step_gbs = step_bytes_all / (ms_step * 1e-3) / 1e9
+    result = {
+        "metric": "batched_decode_tokens_per_s",
+        "value": tokens_per_s,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_step,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": decoder_config(world),
+        "roofline": {"bound": "hbm", "achieved": attn_gbs, "peak": hbm, "unit": "GB/s", "frac": attn_gbs / hbm,
+                     "peak_source": peak_kind,
+                     "kernel": "KV store + attention stage (kv_quantize_kernel, attn_stream_kernel, "
+                               "attn_combine_kernel; 12 layers per step)",
+                     "stage_ms_per_step": attn_ms, "algorithmic_bytes_per_step": attn_bytes,
+                     "traffic": profiled_traffic("attn_stream_decode_config5")},
+        "step_hbm": {"achieved_gbs": step_gbs, "frac": step_gbs / hbm, "algorithmic_bytes_per_step": step_bytes_all,
+                     "note": "all of a step's algorithmic bytes (decode_bytes) over the timed step"},
+        "stages_ms_per_step": stages,
+        "dominant_stage": dominant,
+        "profiled_step_ms": total_prof,
+        "e2e": {"value": DEC_SESSIONS / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4 * S,
+                "d2h_bytes_per_step": 4 * S, "ms_per_step": e2e_s * 1e3,
+                "call": "needle2_batch_step per step (this rank's sessions' tokens copied in from host memory, "
+                        "their greedy tokens read back; synchronised)"},
+        "prefill_s": prefill_s,
+        "positions": [position0, position0 + args.steps],
+        "sessions_per_gpu": S,
+        "gpu_launches": None,
+        "timing": "K decode steps in one needle2_batch_decode_greedy_device call between CUDA events on the "
+                  "launching stream; max over ranks",
+        "clocks": clocks.summary(),
+    }
+    batch.close()
+    model.close()
+    return result, archive
+
+
+def run_native(args, rank, world, dist):
+    import torch
+    from openneedle_b200 import build as b
+
+    if rank == 0:
+        b.build()
+    if dist is not None:
+        dist.barrier()
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    result, archive = decoder_native(args, rank, world, dist, dev)
+    if not args.skip_gemv:
+        result["cq_gemv"] = gemv_native(args, rank, world, dist)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = reference_decode(archive, decoder_prompts()[0], 64, seconds=args.cpu_seconds)
+        if r is not None:
+            tps, n, threads = r
+            result["cpu_baseline"] = {
+                "value": tps, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                "sample": f"{n} decode steps of one session after its {DEC_PROMPT}-token prefill (the reference "
+                          f"serves one sequence per engine), NativeEngine on oracle/_ref with {threads} threads, "
+                          f"~{args.cpu_seconds:.0f} s bound; x86 runs the reference's portable branches"}
+    return result
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -661,6 +915,7 @@ def main():
     ap.add_argument("--skip-gemm", action="store_true", help="omit the prefill GEMM side measurement")
     ap.add_argument("--skip-sweep", action="store_true", help="omit the config-3 prefill GEMM shape sweep")
     ap.add_argument("--skip-attention", action="store_true", help="omit the INT8 KV attention side measurement")
+    ap.add_argument("--skip-gemv", action="store_true", help="omit the fused CQ4 GEMV side line")
     ap.add_argument("--skip-sharded", action="store_true",
                     help="omit the N-sharded GEMM + all-gather side measurement (multi-GPU runs)")
     args = ap.parse_args()

@@ -315,6 +315,15 @@ int needle2_batch_decode_greedy(void *batch, const int *first, int steps, int *o
 int needle2_batch_decode_greedy_device(void *batch, const int *first, int steps, int *out, void *stream);
 /* Current position of every session (host copy). */
 int needle2_batch_positions(void *batch, int *positions);
+/* Stage timers (CUDA events at every stage boundary of each forward pass, on
+ * the pass's stream) while enabled; enabling or disabling clears the totals.
+ * profile_read returns the milliseconds per stage since the last read and
+ * clears them (synchronises): 0 engrams and embedding, 1 mHC routing (lane
+ * RMS, projections, gates), 2 Q/K/V/gate projections, 3 QK norm and RoPE,
+ * 4 KV store and attention, 5 gate and out projection, 6 Hadamard MLP and
+ * lane mixing, 7 final norm, LM head and greedy choice. */
+int needle2_batch_profile(void *batch, int enable);
+int needle2_batch_profile_read(void *batch, double *ms, int n);
 
 #ifdef __cplusplus
 }

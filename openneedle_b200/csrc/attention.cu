@@ -136,7 +136,8 @@ __device__ __forceinline__ Row<T> visible_row(const AttnParams &p, int s, int po
     Row<T> r;
     size_t row;
     int where;   // 0 staged chunk, 1 pinned prefix, 2 session slots
-    if (p.stage_k && position >= chunk_start) {
+    const bool staged = sizeof(T) == 1 ? p.stage_k != nullptr : p.stage_kf != nullptr;
+    if (staged && position >= chunk_start) {
         row = (size_t)kh * p.stage_rows + (size_t)entry * p.tokens + (position - chunk_start);
         where = 0;
     } else if (position < p.prefix) {

@@ -124,6 +124,9 @@ struct Scratch {
     DevBuf<int> rsess, rpos, tokens, argmax;
 };
 
+// Stages of a forward pass timed by the profiler (needle2_batch_profile).
+constexpr int kStages = 8;
+
 struct State {
     Model *m = nullptr;
     int S = 1, prefix = 0;
@@ -138,9 +141,18 @@ struct State {
     bool snapshot = false;
     int snap_position = 0, snap_capacity = 0;
     Scratch s;
+    // stage timers: an event at every stage boundary of each forward pass while enabled
+    struct Prof {
+        bool on = false;
+        std::vector<cudaEvent_t> events;
+        std::vector<int> tags;   // stage that starts at events[i] (-1: a pass ends)
+        size_t used = 0;
+        double ms[kStages] = {};
+    } prof;
     ~State() {
         if (m) cudaSetDevice(m->device);
         for (auto *p : kv) kv_pool_delete(p);
+        for (auto e : prof.events) cudaEventDestroy(e);
     }
     int capacity() const { return m->c.window ? m->c.window + prefix : m->c.max_seq; }
     size_t engring_stride() const { return (size_t)std::max(1, m->c.num_sites) * m->engring() * m->c.dim; }
@@ -384,6 +396,34 @@ struct Outputs {
     bool keep_z = false;           // final-normed last row kept for candidate projections
 };
 
+// Records a profiler event where `stage` begins (-1: the pass ends).
+void mark(State &st, int stage, cudaStream_t stream) {
+    auto &p = st.prof;
+    if (!p.on) return;
+    if (p.used == p.events.size()) {
+        cudaEvent_t e;
+        cuda_check(cudaEventCreate(&e), "profiler event");
+        p.events.push_back(e);
+        p.tags.push_back(-1);
+    }
+    cuda_check(cudaEventRecord(p.events[p.used], stream), "profiler event");
+    p.tags[p.used++] = stage;
+}
+
+// Folds the recorded events into per-stage totals (synchronises).
+void collect(State &st) {
+    auto &p = st.prof;
+    if (!p.used) return;
+    cuda_check(cudaEventSynchronize(p.events[p.used - 1]), "profiler");
+    for (size_t i = 0; i + 1 < p.used; ++i) {
+        if (p.tags[i] < 0) continue;
+        float ms = 0.f;
+        cuda_check(cudaEventElapsedTime(&ms, p.events[i], p.events[i + 1]), "profiler");
+        p.ms[p.tags[i]] += ms;
+    }
+    p.used = 0;
+}
+
 // Engram keys/values of R = E*T rows (engine.cpp:755-783) into s.ek / s.ev
 // ([site][R][D]), and the engram value rings updated with this call's raw
 // values.  Row positions must be in s.rpos; tokens of the call are tokens[E][T].
@@ -464,6 +504,8 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
     }
 
     // engrams (engine.cpp:755-783), all sites, before the history ring takes this call's tokens
+    if (st.prof.on && st.prof.used > 4096) collect(st);
+    mark(st, 0, stream);
     engram_stage(st, E, T, tokens, stream);
     check(eng::launch_history_store(st.hist.ptr, m.hist_cap(), tokens, T, nullptr, st.base.ptr, E, stream), "history");
 
@@ -478,6 +520,7 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
     const int mh = m.mh();
     for (int l = 0; l < c.layers; ++l) {
         const int ti = 1 + 14 * l;
+        mark(st, 1, stream);
         check(eng::launch_rms(s.x.ptr, N * D, R, N * D, nullptr, s.nx.ptr, N * D, stream), "lane rms");
         eng::DenseSeg segs[3] = {{m.t[mh + 6].dense, l * N, N, s.raw.ptr, ldraw},
                                  {m.t[mh + 7].dense, l * N, N, s.raw.ptr + N, ldraw},
@@ -499,13 +542,17 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         check(eng::launch_mhc_pre(ml, s.raw.ptr, ldraw, s.x.ptr, R, s.hpost.ptr, s.u.ptr, s.bx.ptr, s.z.ptr, stream),
               "mHC routing");
         aq(m, s.z.ptr, R, D, stream);
+        mark(st, 2, stream);
         projections(m, ti, s.z.ptr, R, s.q.ptr, s.k.ptr, s.v.ptr, s.gate.ptr, stream);
+        mark(st, 3, stream);
         check(eng::launch_qk_norm_rope(s.q.ptr, s.k.ptr, R, c.heads, c.kvheads, c.head_dim, m.t[ti + 4].dense,
                                        m.t[ti + 5].dense, s.rpos.ptr, m.rope_divisor, stream),
               "q/k norm and RoPE");
+        mark(st, 4, stream);
         check(kv_pool_run(st.kv[l], T == 1 ? kDecode : kPrefill, st.iota.ptr, st.base.ptr, E, T, max_visible, s.q.ptr,
                           s.k.ptr, s.v.ptr, s.att.ptr, stream),
               "attention");
+        mark(st, 5, stream);
         check(eng::launch_gate(s.att.ptr, s.gate.ptr, R, A, stream), "gate");
         aq(m, s.att.ptr, R, A, stream);
         linear(m, ti + 7, s.att.ptr, R, s.proj.ptr, stream);
@@ -513,6 +560,7 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         pl.layer = l; pl.lanes = N; pl.D = D; pl.hada = c.hada; pl.a_res = ml.a_res; pl.b_res = ml.b_res;
         pl.post_norm = m.t[ti + 8].dense; pl.attn_gate = m.t[ti + 9].dense; pl.pre_hada = m.t[ti + 10].dense;
         pl.d1 = m.t[ti + 11].dense; pl.d2 = m.t[ti + 12].dense; pl.d3 = m.t[ti + 13].dense;
+        mark(st, 6, stream);
         float *hid = o.hidden ? s.hidden.ptr + (size_t)l * D : nullptr;
         check(eng::launch_mhc_post(pl, s.proj.ptr, s.raw.ptr, ldraw, s.hpost.ptr, s.u.ptr, s.bx.ptr, s.x.ptr, R, hid,
                                    c.layers * D, stream),
@@ -520,6 +568,7 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
     }
 
     // final norm (engine.cpp:1039-1041) on every row or each entry's last token
+    mark(st, 7, stream);
     const bool every = o.all_logits;
     const int rows = every ? R : E;
     if (o.logits || o.keep_z) {
@@ -548,6 +597,7 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         if (o.argmax_dev) check(launch_argmax(lg, rows, V, V, o.argmax_dev, stream), "argmax");
     }
     check(eng::launch_advance(st.base.ptr, E, T, stream), "advance");
+    mark(st, -1, stream);
     for (int e = 0; e < E; ++e) st.pos[e] += T;
 }
 
@@ -1199,6 +1249,24 @@ int needle2_batch_decode_greedy(void *b, const int *first, int steps, int *out) 
 int needle2_batch_decode_greedy_device(void *b, const int *first, int steps, int *out, void *stream) {
     return nb200::guarded([&] {
         nb200::batch_decode_device(*nb200::as_batch(b), first, steps, out, static_cast<cudaStream_t>(stream));
+    });
+}
+
+int needle2_batch_profile(void *b, int enable) {
+    return nb200::guarded([&] {
+        nb200::State &st = *nb200::as_batch(b)->state;
+        nb200::collect(st);
+        st.prof.on = enable != 0;
+        for (double &v : st.prof.ms) v = 0.0;
+    });
+}
+
+int needle2_batch_profile_read(void *b, double *ms, int n) {
+    return nb200::guarded([&] {
+        nb200::State &st = *nb200::as_batch(b)->state;
+        nb200::collect(st);
+        for (int i = 0; i < n && i < nb200::kStages; ++i) ms[i] = st.prof.ms[i];
+        for (double &v : st.prof.ms) v = 0.0;
     });
 }
 

@@ -97,6 +97,10 @@ def _bind(lib):
     lib.needle2_batch_decode_greedy_device.restype = _i
     lib.needle2_batch_positions.argtypes = [_p, _p]
     lib.needle2_batch_positions.restype = _i
+    lib.needle2_batch_profile.argtypes = [_p, _i]
+    lib.needle2_batch_profile.restype = _i
+    lib.needle2_batch_profile_read.argtypes = [_p, _p, _i]
+    lib.needle2_batch_profile_read.restype = _i
     lib._engine_bound = True
     return lib
 
@@ -198,6 +202,19 @@ class GpuBatch:
 
     def kv_storage_bytes(self) -> int:
         return int(self._lib.needle2_batch_kv_storage_bytes(self._h))
+
+    STAGES = ("engrams+embedding", "mhc_routing", "qkvg_projections", "qk_norm_rope", "kv_store+attention",
+              "gate+out_projection", "hadamard_mlp+mixing", "final_norm+lm_head+greedy")
+
+    def profile(self, enable: bool = True) -> None:
+        """Per-stage CUDA-event timers of every forward pass (clears the totals)."""
+        self._check(self._lib.needle2_batch_profile(self._h, int(bool(enable))))
+
+    def profile_read(self) -> dict:
+        """Milliseconds per stage since the last read (synchronises, clears)."""
+        ms = np.zeros(len(self.STAGES), np.float64)
+        self._check(self._lib.needle2_batch_profile_read(self._h, ms.ctypes.data, ms.size))
+        return dict(zip(self.STAGES, ms.tolist()))
 
     def positions(self) -> np.ndarray:
         out = np.empty(self.sessions, np.int32)

@@ -140,24 +140,31 @@ def test_batch_matches_reference_per_sequence(env):
     np.testing.assert_array_equal(gpu["0_positions"], [5 + 9 + 4] * 3)
 
 
-def test_config5_geometry_matches_reference(env):
+@pytest.mark.parametrize("kv", ["fp32", "int8"])
+def test_config5_geometry_matches_reference(env, kv):
     """BASELINE config 5's decoder (d 512, 12 layers, 8/4 heads x 64, vocab
-    32768, CQ4 embedding, CQ2 projections and tables, INT8 KV): a 48-token
-    prompt and 6 teacher-forced steps, then greedy tokens.  Greedy agreement
-    is checked where the reference's top-2 margin exceeds the FP32 bar."""
+    32768, CQ4 embedding, CQ2 projections and tables): a 48-token prompt and 6
+    teacher-forced steps.  With the FP32 cache the logits stay within the
+    1e-4 bar.  With the INT8 cache, a K or V element whose scaled value lies
+    within FP32 rounding of a half-integer can round to the neighbouring int8
+    code here and not there (the quantiser is discontinuous); such isolated
+    one-code differences move the logits by up to a few 1e-4 of their
+    maximum, so that case is held to 1e-3, and greedy tokens must agree
+    wherever the reference's top-2 margin exceeds that bar."""
     from engine_models import config5
     d, ref_lib, lib = env
     path = _archive(env, "config5", config5(), 0)
     ids = _tokens(54, 32768, 77)
-    plan = [{"op": "engine", "kv": "int8"}, {"op": "prefill", "tokens": ids[:48], "last_only": True}]
+    plan = [{"op": "engine", "kv": kv}, {"op": "prefill", "tokens": ids[:48], "last_only": True}]
     plan += [{"op": "step", "token": t} for t in ids[48:]]
-    ref, gpu = _both(env, path, plan, "config5")
+    ref, gpu = _both(env, path, plan, f"config5_{kv}")
+    bar = TOL if kv == "fp32" else 1e-3
     worst = 0.0
     for key in [k for k in ref if k.endswith("_logits")]:
         e = rel(gpu[key], ref[key])
         worst = max(worst, e)
         margin = top2_margin(ref[key]) / np.max(np.abs(ref[key]))
         if int(np.argmax(gpu[key])) != int(np.argmax(ref[key])):
-            assert margin <= 2 * TOL, f"{key}: greedy differs with top-2 margin {margin:.3e}"
-        assert e <= TOL, f"{key}: rel err {e:.3e}"
-    print(f"config-5 decoder: max rel err {worst:.3e}")
+            assert margin <= bar, f"{key}: greedy differs with top-2 margin {margin:.3e}"
+        assert e <= bar, f"{key}: rel err {e:.3e}"
+    print(f"config-5 decoder kv={kv}: max rel err {worst:.3e}")
