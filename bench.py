@@ -798,6 +798,7 @@ def decoder_native(args, rank, world, dist, dev):
         end.record(stream)
         torch.cuda.synchronize(dev)
     elapsed_ms = start.elapsed_time(end)
+    batch_kernels = batch.step_kernels()
     cur = out[:, -1].contiguous()
 
     # per-stage breakdown of a few more steps (profiled separately: events at
@@ -866,7 +867,9 @@ def decoder_native(args, rank, world, dist, dev):
         "prefill_s": prefill_s,
         "positions": [position0, position0 + args.steps],
         "sessions_per_gpu": S,
-        "gpu_launches": None,
+        "gpu_launches": batch_kernels * args.steps,
+        "gpu_launches_note": "kernels of one captured decode step x K steps (the first step launches the same "
+                             "kernels one by one)",
         "timing": "K decode steps in one needle2_batch_decode_greedy_device call between CUDA events on the "
                   "launching stream; max over ranks",
         "clocks": clocks.summary(),

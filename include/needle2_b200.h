@@ -311,8 +311,14 @@ int needle2_batch_step(void *batch, const int *tokens, float *logits, int *next)
  * fed at each step (first, then each step's greedy choice); the sessions
  * advance by `steps` positions.  Host pointers; synchronous. */
 int needle2_batch_decode_greedy(void *batch, const int *first, int steps, int *out);
-/* The same on device pointers, enqueued on `stream` without host synchronisation. */
+/* The same on device pointers, enqueued on `stream` without host synchronisation.
+ * From the second step on, the steps replay a CUDA graph of one step (unless
+ * disabled with needle2_batch_set_graphs or while the profiler runs). */
 int needle2_batch_decode_greedy_device(void *batch, const int *first, int steps, int *out, void *stream);
+/* 1 (default): decode steps replay a captured CUDA graph; 0: launch by launch. */
+int needle2_batch_set_graphs(void *batch, int enable);
+/* Kernels in the last captured decode-step graph (0 before any capture). */
+int needle2_batch_step_kernels(void *batch);
 /* Current position of every session (host copy). */
 int needle2_batch_positions(void *batch, int *positions);
 /* Stage timers (CUDA events at every stage boundary of each forward pass, on

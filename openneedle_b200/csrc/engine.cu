@@ -149,8 +149,16 @@ struct State {
         size_t used = 0;
         double ms[kStages] = {};
     } prof;
+    // CUDA graph of one decode step (needle2_batch_decode_greedy_device)
+    cudaStream_t capture = nullptr;
+    cudaGraphExec_t step_graph = nullptr;
+    bool graphs = true;
+    int step_kernels = 0;   // kernel nodes of the last captured step
     ~State() {
         if (m) cudaSetDevice(m->device);
+        if (step_graph || capture) cudaDeviceSynchronize();
+        if (step_graph) cudaGraphExecDestroy(step_graph);
+        if (capture) cudaStreamDestroy(capture);
         for (auto *p : kv) kv_pool_delete(p);
         for (auto e : prof.events) cudaEventDestroy(e);
     }
@@ -394,6 +402,7 @@ struct Outputs {
     int *argmax_dev = nullptr;     // greedy token of each logits row
     bool hidden = false;           // per-layer lane means of the last row
     bool keep_z = false;           // final-normed last row kept for candidate projections
+    int max_visible = 0;           // bound on the visible set (0: from the current positions)
 };
 
 // Records a profiler event where `stage` begins (-1: the pass ends).
@@ -497,8 +506,8 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
     s.rsess.reserve(R);
     s.rpos.reserve(R);
     check(eng::launch_row_positions(st.base.ptr, E, T, s.rsess.ptr, s.rpos.ptr, stream), "positions");
-    int max_visible = 1;
-    {
+    int max_visible = o.max_visible;
+    if (max_visible <= 0) {
         std::vector<int> first(st.pos.begin(), st.pos.begin() + E);
         max_visible = kv_max_visible(st.prefix, c.window, first.data(), E, T);
     }
@@ -1032,25 +1041,103 @@ void batch_step(Batch &b, const int *tokens, float *logits, int *next) {
     sync(m, stream);
 }
 
+// out[s][counter] = nxt[s]; cur[s] = nxt[s] (the step's greedy tokens become the next inputs).
+__global__ void commit_tokens_kernel(const int *__restrict__ nxt, int *__restrict__ cur, int S,
+                                     int *__restrict__ out, int steps, const int *__restrict__ counter) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    const int c = *counter;
+    if (s < S) {
+        out[(size_t)s * steps + c] = nxt[s];
+        cur[s] = nxt[s];
+    }
+}
+
+// One greedy decode step of every sequence: forward on cur, greedy tokens
+// committed to out's column *counter and to cur.
+void decode_step(State &st, int *cur, int *nxt, int *out, int steps, int *counter, int max_visible,
+                 cudaStream_t stream) {
+    Outputs o;
+    o.logits = true;
+    o.argmax_dev = nxt;
+    o.max_visible = max_visible;
+    forward(st, st.S, 1, cur, o, nullptr, stream);
+    commit_tokens_kernel<<<(st.S + 255) / 256, 256, 0, stream>>>(nxt, cur, st.S, out, steps, counter);
+    cuda_check(cudaGetLastError(), "tokens");
+    check(eng::launch_advance(counter, 1, 1, stream), "step counter");
+}
+
 // `steps` greedy steps on device buffers: first[S] in, out[S][steps] the
-// generated tokens, enqueued on `stream`.
+// generated tokens, enqueued on `stream`.  The first step runs launch by
+// launch (it also sizes every buffer); the others replay a CUDA graph of one
+// step captured on a private stream, with the attention split chosen for the
+// longest context of the run (each kernel reads the true positions from the
+// device, so only the work division is fixed).
 void batch_decode_device(Batch &b, const int *first, int steps, int *out, cudaStream_t stream) {
     State &st = *b.state;
     const Model &m = *st.m;
     const int S = st.S;
     if (steps <= 0) return;
     for (int e = 0; e < S; ++e) check_room(st, e, steps);
-    st.s.argmax.reserve(2 * (size_t)S);
-    int *cur = st.s.argmax.ptr, *nxt = st.s.argmax.ptr + S;
-    cuda_check(cudaMemcpyAsync(cur, first, sizeof(int) * S, cudaMemcpyDeviceToDevice, stream), "tokens");
-    for (int i = 0; i < steps; ++i) {
-        Outputs o;
-        o.logits = true;
-        o.argmax_dev = nxt;
-        forward(st, S, 1, cur, o, nullptr, stream);
-        check(eng::launch_copy_tokens(nxt, S, out + i, steps, stream), "tokens");
-        std::swap(cur, nxt);
+    if (st.step_graph) {
+        cuda_check(cudaDeviceSynchronize(), "graph");
+        cudaGraphExecDestroy(st.step_graph);
+        st.step_graph = nullptr;
     }
+    st.s.argmax.reserve(2 * (size_t)S + 1);
+    int *cur = st.s.argmax.ptr, *nxt = st.s.argmax.ptr + S, *counter = st.s.argmax.ptr + 2 * S;
+    cuda_check(cudaMemcpyAsync(cur, first, sizeof(int) * S, cudaMemcpyDeviceToDevice, stream), "tokens");
+    cuda_check(cudaMemsetAsync(counter, 0, sizeof(int), stream), "step counter");
+    int max_visible = 1;
+    {
+        std::vector<int> last(st.pos.begin(), st.pos.end());
+        for (int &p : last) p += steps - 1;
+        max_visible = kv_max_visible(st.prefix, m.c.window, last.data(), S, 1);
+    }
+    const std::vector<int> start = st.pos;
+    decode_step(st, cur, nxt, out, steps, counter, max_visible, stream);
+    int done = 1;
+    if (steps > 2 && st.graphs && !st.prof.on) {
+        if (!st.capture) cuda_check(cudaStreamCreateWithFlags(&st.capture, cudaStreamNonBlocking), "capture stream");
+        cudaEvent_t ready;
+        cuda_check(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming), "event");
+        cuda_check(cudaEventRecord(ready, stream), "event");
+        cuda_check(cudaStreamWaitEvent(st.capture, ready, 0), "event");
+        cudaEventDestroy(ready);
+        cudaGraph_t graph = nullptr;
+        bool captured = false;
+        if (cudaStreamBeginCapture(st.capture, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            try {
+                decode_step(st, cur, nxt, out, steps, counter, max_visible, st.capture);
+            } catch (const std::exception &) {
+            }
+            captured = cudaStreamEndCapture(st.capture, &graph) == cudaSuccess && graph &&
+                       cudaGraphInstantiate(&st.step_graph, graph, 0) == cudaSuccess;
+            if (captured) {
+                // kernels of one step (the launch count a step replays)
+                size_t n = 0;
+                cudaGraphGetNodes(graph, nullptr, &n);
+                std::vector<cudaGraphNode_t> nodes(n);
+                cudaGraphGetNodes(graph, nodes.data(), &n);
+                st.step_kernels = 0;
+                for (auto nd : nodes) {
+                    cudaGraphNodeType t;
+                    if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++st.step_kernels;
+                }
+            }
+            if (graph) cudaGraphDestroy(graph);
+        }
+        cudaGetLastError();   // a refused capture leaves its error behind; the steps then run eagerly
+        st.pos = start;
+        for (int &p : st.pos) p += 1;
+        if (captured) {
+            for (; done < steps; ++done) cuda_check(cudaGraphLaunch(st.step_graph, stream), "graph launch");
+            for (int &p : st.pos) p += steps - 1;
+        } else if (st.step_graph) {
+            cudaGraphExecDestroy(st.step_graph);
+            st.step_graph = nullptr;
+        }
+    }
+    for (; done < steps; ++done) decode_step(st, cur, nxt, out, steps, counter, max_visible, stream);
 }
 
 template <typename F>
@@ -1268,6 +1355,16 @@ int needle2_batch_profile_read(void *b, double *ms, int n) {
         for (int i = 0; i < n && i < nb200::kStages; ++i) ms[i] = st.prof.ms[i];
         for (double &v : st.prof.ms) v = 0.0;
     });
+}
+
+int needle2_batch_step_kernels(void *b) {
+    int n = -1;
+    nb200::guarded([&] { n = nb200::as_batch(b)->state->step_kernels; });
+    return n;
+}
+
+int needle2_batch_set_graphs(void *b, int enable) {
+    return nb200::guarded([&] { nb200::as_batch(b)->state->graphs = enable != 0; });
 }
 
 int needle2_batch_positions(void *b, int *positions) {

@@ -97,6 +97,10 @@ def _bind(lib):
     lib.needle2_batch_decode_greedy_device.restype = _i
     lib.needle2_batch_positions.argtypes = [_p, _p]
     lib.needle2_batch_positions.restype = _i
+    lib.needle2_batch_step_kernels.argtypes = [_p]
+    lib.needle2_batch_step_kernels.restype = _i
+    lib.needle2_batch_set_graphs.argtypes = [_p, _i]
+    lib.needle2_batch_set_graphs.restype = _i
     lib.needle2_batch_profile.argtypes = [_p, _i]
     lib.needle2_batch_profile.restype = _i
     lib.needle2_batch_profile_read.argtypes = [_p, _p, _i]
@@ -205,6 +209,14 @@ class GpuBatch:
 
     STAGES = ("engrams+embedding", "mhc_routing", "qkvg_projections", "qk_norm_rope", "kv_store+attention",
               "gate+out_projection", "hadamard_mlp+mixing", "final_norm+lm_head+greedy")
+
+    def set_graphs(self, enable: bool = True) -> None:
+        """Replay decode steps as a captured CUDA graph (default) or launch them one by one."""
+        self._check(self._lib.needle2_batch_set_graphs(self._h, int(bool(enable))))
+
+    def step_kernels(self) -> int:
+        """Kernels of one decode step (from the last captured step graph)."""
+        return int(self._lib.needle2_batch_step_kernels(self._h))
 
     def profile(self, enable: bool = True) -> None:
         """Per-stage CUDA-event timers of every forward pass (clears the totals)."""

@@ -84,6 +84,7 @@ def main(archive_path: str, plan_path: str, out_path: str) -> int:
                              activation_bits=op.get("abits", 0))
             prefix = op.get("prefix", [])
             b = model.batch(op["sessions"], len(prefix))
+            b.set_graphs(op.get("graphs", True))
             if prefix:
                 b.set_prefix(prefix)
             logits, nxt = b.prefill(np.asarray(op["prompts"], np.int32))

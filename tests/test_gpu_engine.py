@@ -126,18 +126,24 @@ def test_batch_matches_reference_per_sequence(env):
     prefix = _tokens(5, 61, 30)
     prompts = [_tokens(9, 61, 31 + s) for s in range(3)]
     teacher = [_tokens(4, 61, 41 + s) for s in range(3)]
-    gpu = run_plan(path, [{"op": "batch", "sessions": 3, "prefix": prefix, "prompts": prompts, "teacher": teacher,
-                           "kv": "int8"}], lib, d, "batch_gpu")
+    op = {"op": "batch", "sessions": 3, "prefix": prefix, "prompts": prompts, "teacher": teacher, "kv": "int8",
+          "steps": 6}
+    gpu = run_plan(path, [op, dict(op, graphs=False)], lib, d, "batch_gpu")
     for s in range(3):
         plan = [{"op": "engine", "kv": "int8"}, {"op": "reset", "prefix": 5},
                 {"op": "prefill", "tokens": prefix + prompts[s], "last_only": True}]
         plan += [{"op": "step", "token": t} for t in teacher[s]]
+        plan += [{"op": "decode", "first": int(gpu["0_first"][s]), "max_new": 7}]
         ref = run_plan(path, plan, ref_lib, d, f"batch_ref{s}")
         assert rel(gpu["0_prefill_logits"][s], ref["2_logits"]) <= TOL
         assert int(gpu["0_first"][s]) == int(np.argmax(ref["2_logits"]))
         for j in range(4):
             assert rel(gpu["0_teacher_logits"][s, j], ref[f"{3 + j}_logits"]) <= TOL
-    np.testing.assert_array_equal(gpu["0_positions"], [5 + 9 + 4] * 3)
+        np.testing.assert_array_equal(gpu["0_tokens"][s], ref["7_tokens"][1:])   # greedy decode, graph replay
+    np.testing.assert_array_equal(gpu["0_positions"], [5 + 9 + 4 + 6] * 3)
+    # the captured-graph steps and the launch-by-launch steps agree bit for bit
+    np.testing.assert_array_equal(gpu["0_tokens"], gpu["1_tokens"])
+    np.testing.assert_array_equal(gpu["0_teacher_logits"], gpu["1_teacher_logits"])
 
 
 @pytest.mark.parametrize("kv", ["fp32", "int8"])
