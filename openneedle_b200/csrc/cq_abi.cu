@@ -329,22 +329,31 @@ bool sdot_multiply_to(Matrix *m, const int8_t *q, const float *xs, int batch, fl
 // FP32 mode, y[batch][out] from rotated activations: the tensor-core GEMM from
 // kGemmMinRows rows on (bf16 hi/lo weights made at the first such call; the
 // activations split here unless a_hilo already holds them), the GEMV otherwise.
+// FP32 mode: bf16 hi/lo weights for the prefill GEMM, made at the first use.
+bool ensure_f32_copy(Matrix *m, cudaStream_t st) {
+    const CQDevice &w = m->w;
+    if (m->d_whl) return true;
+    const cudaError_t e = cudaMalloc(&m->d_whl, sizeof(uint16_t) * gemm_f32_weight_elems(w.out, w.padded));
+    if (e != cudaSuccess) {
+        m->d_whl = nullptr;
+        set_error(std::string("prefill weight allocation failed: ") + cudaGetErrorString(e));
+        return false;
+    }
+    if (!gemm_f32_prepare(w.packed, w.norms, w.out, w.groups, w.group, w.storage_bits, w.rowbytes, w.padded, w.lut,
+                          m->d_whl, st)) {
+        cudaFree(m->d_whl);
+        m->d_whl = nullptr;
+        return false;
+    }
+    return true;
+}
+
 bool f32_multiply(Matrix *m, const float *rot, int batch, float *y, cudaStream_t st,
                   const uint16_t *a_hilo = nullptr) {
     const CQDevice &w = m->w;
     if (batch < kGemmMinRows || !gemm_f32_supported(w.storage_bits, w.padded))
         return launch_gemv_f32(w, rot, batch, y, w.out, st);
-    if (!m->d_whl) {
-        const cudaError_t e = cudaMalloc(&m->d_whl, sizeof(uint16_t) * gemm_f32_weight_elems(w.out, w.padded));
-        if (e != cudaSuccess) {
-            m->d_whl = nullptr;
-            set_error(std::string("prefill weight allocation failed: ") + cudaGetErrorString(e));
-            return false;
-        }
-        if (!gemm_f32_prepare(w.packed, w.norms, w.out, w.groups, w.group, w.storage_bits, w.rowbytes, w.padded,
-                              w.lut, m->d_whl, st))
-            return false;
-    }
+    if (!ensure_f32_copy(m, st)) return false;
     if (!a_hilo) {
         if (!m->ahl.reserve(2 * (size_t)batch * w.padded)) return false;
         if (!launch_split_bf16(rot, (long long)batch * w.padded, m->ahl.ptr, st)) return false;
@@ -545,12 +554,15 @@ bool multiply_many(Matrix *const *ms, int count, float *const *ys, int batch, cu
         return true;
     }
     if (!i8 && batch >= kGemmMinRows && gemm_f32_supported(w.storage_bits, w.padded)) {
-        // FP32 prefill-sized batches: the activations split once, one GEMM per matrix
+        // FP32 prefill-sized batches: the activations split once, every matrix in one GEMM launch
         if (!m0->ahl.reserve(2 * (size_t)batch * w.padded)) return false;
         if (!launch_split_bf16(m0->rot.ptr, (long long)batch * w.padded, m0->ahl.ptr, st)) return false;
-        for (int i = 0; i < count; ++i)
-            if (!f32_multiply(ms[i], m0->rot.ptr, batch, ys[i], st, m0->ahl.ptr)) return false;
-        return true;
+        std::vector<F32Out> outs(count);
+        for (int i = 0; i < count; ++i) {
+            if (!ensure_f32_copy(ms[i], st)) return false;
+            outs[i] = F32Out{ms[i]->d_whl, ms[i]->w.out, ys[i], ms[i]->w.out};
+        }
+        return launch_gemm_f32x3_multi(m0->ahl.ptr, batch, w.padded, outs.data(), count, st);
     }
     const int cap = gemv_max_rows(w.bits, w.group, w.groups, i8);
     for (int i0 = 0; i0 < count; i0 += kGemvMaxMats) {

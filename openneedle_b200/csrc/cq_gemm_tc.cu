@@ -479,32 +479,50 @@ bool make_map(CUtensorMap *map, const void *base, int rows, int cols, int box_ro
 // 128 x 256 tiles, K = 64 (one 128-byte row of bf16) per stage, two stages of
 // 96 KB; warp 0 issues the TMA loads, warp 1 the MMAs, warps 2-5 read the
 // accumulator (32 rows each) and store y.
-constexpr int kFBM = 128, kFBN = 256, kFBK = 64;
+constexpr int kFBM = 128, kFBK = 64;
 constexpr int kFStages = 2;
-constexpr int kFPartA = kFBM * kFBK * 2, kFPartB = kFBN * kFBK * 2;   // bytes of one bf16 part
-constexpr int kFStageBytes = 2 * kFPartA + 2 * kFPartB;               // 96 KB
-constexpr size_t kFSmem = (size_t)kFStages * kFStageBytes + 1024;
+constexpr int kFPartA = kFBM * kFBK * 2;   // bytes of one bf16 part of the activation tile
 constexpr int kFThreads = 6 * 32;
-
-struct GemmF32Args {
-    int M, N, ksteps, ldy;
-    float *y;
+template <int BN>
+struct FTile {
+    static constexpr int kPartB = BN * kFBK * 2;
+    static constexpr int kStageBytes = 2 * kFPartA + 2 * kPartB;
+    static constexpr size_t kSmem = (size_t)kFStages * kStageBytes + 1024;
 };
 
+// One output matrix of a launch: its bf16 hi/lo weight maps, y[M][ldy] and
+// the first of its tiles along grid y.
+struct F32Seg {
+    CUtensorMap bh, bl;
+    float *y;
+    int N, ldy, tile0;
+};
+constexpr int kF32MaxSegs = 4;
+struct GemmF32Args {
+    F32Seg seg[kF32MaxSegs];
+    int nseg, M, ksteps;
+};
+
+// grid: (M tiles, total N tiles of all segments); tile width BN (256 for
+// prefill-sized launches, 64 when that leaves too few CTAs for the machine).
+template <int BN>
 __global__ void __launch_bounds__(kFThreads, 1)
     cq_gemm_f32x3_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
-                         const __grid_constant__ CUtensorMap tbh, const __grid_constant__ CUtensorMap tbl,
                          const __grid_constant__ GemmF32Args a) {
+    constexpr int kPartB = FTile<BN>::kPartB, kStageBytes = FTile<BN>::kStageBytes;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ __align__(8) uint64_t full[kFStages], empty[kFStages], dfull;
     __shared__ uint32_t tmem_s;
     __shared__ volatile int abort_flag;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m0 = blockIdx.x * kFBM, n0 = blockIdx.y * kFBN;
+    int si = 0;
+    while (si + 1 < a.nseg && (int)blockIdx.y >= a.seg[si + 1].tile0) ++si;
+    const F32Seg &sg = a.seg[si];
+    const int m0 = blockIdx.x * kFBM, n0 = ((int)blockIdx.y - sg.tile0) * BN;
     const int S = a.ksteps;
 
-    if (warp == 1) tc::alloc(&tmem_s, 256);
+    if (warp == 1) tc::alloc(&tmem_s, BN);
     if (tid == 0) {
         abort_flag = 0;
         for (int s = 0; s < kFStages; ++s) {
@@ -525,25 +543,25 @@ __global__ void __launch_bounds__(kFThreads, 1)
             for (int k = 0; k < S && !abort_flag; ++k) {
                 const int s = k % kFStages;
                 if (k >= kFStages && !gwait(&empty[s], (uint32_t)((k / kFStages) - 1) & 1, &abort_flag)) break;
-                uint8_t *st = smem + (size_t)s * kFStageBytes;
-                mbar_arrive_expect_tx(&full[s], kFStageBytes);
+                uint8_t *st = smem + (size_t)s * kStageBytes;
+                mbar_arrive_expect_tx(&full[s], kStageBytes);
                 const int x = k * kFBK * 2;   // byte column of this K step
                 tma_load_2d(st, &tah, x, m0, &full[s]);
                 tma_load_2d(st + kFPartA, &tal, x, m0, &full[s]);
-                tma_load_2d(st + 2 * kFPartA, &tbh, x, n0, &full[s]);
-                tma_load_2d(st + 2 * kFPartA + kFPartB, &tbl, x, n0, &full[s]);
+                tma_load_2d(st + 2 * kFPartA, &sg.bh, x, n0, &full[s]);
+                tma_load_2d(st + 2 * kFPartA + kPartB, &sg.bl, x, n0, &full[s]);
             }
         }
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = tc::idesc_bf16(kFBM, kFBN);
+            const uint32_t idesc = tc::idesc_bf16(kFBM, BN);
             for (int k = 0; k < S && !abort_flag; ++k) {
                 const int s = k % kFStages;
                 if (!gwait(&full[s], (uint32_t)(k / kFStages) & 1, &abort_flag)) break;
                 tc::fence_after();
-                const uint32_t ah = smem_addr(smem + (size_t)s * kFStageBytes), al = ah + kFPartA;
-                const uint32_t bh = ah + 2 * kFPartA, bl = bh + kFPartB;
+                const uint32_t ah = smem_addr(smem + (size_t)s * kStageBytes), al = ah + kFPartA;
+                const uint32_t bh = ah + 2 * kFPartA, bl = bh + kPartB;
 #pragma unroll
                 for (int kk = 0; kk < kFBK / 16; ++kk) {   // 16 bf16 = 32 bytes per MMA
                     const uint32_t o = kk * 32;
@@ -563,9 +581,9 @@ __global__ void __launch_bounds__(kFThreads, 1)
         const bool ok = gwait(&dfull, 0, &abort_flag);
         tc::fence_after();
         if (ok) {
-            const bool vec = (a.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
-            float *yr = a.y + (size_t)min(row, a.M - 1) * a.ldy + n0;
-            for (int c = 0; c < kFBN / 32; ++c) {
+            const bool vec = (sg.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(sg.y) & 15) == 0;
+            float *yr = sg.y + (size_t)min(row, a.M - 1) * sg.ldy + n0;
+            for (int c = 0; c < BN / 32; ++c) {
                 uint32_t v[32];
                 tc::ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(32 * c), v);
                 tc::wait_ld();
@@ -573,14 +591,14 @@ __global__ void __launch_bounds__(kFThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 32; j += 4) {
                         const int col = 32 * c + j;
-                        if (vec && n0 + col + 3 < a.N) {
+                        if (vec && n0 + col + 3 < sg.N) {
                             *reinterpret_cast<float4 *>(yr + col) = make_float4(
                                 __uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
                                 __uint_as_float(v[j + 3]));
                         } else {
 #pragma unroll
                             for (int e = 0; e < 4; ++e)
-                                if (n0 + col + e < a.N) yr[col + e] = __uint_as_float(v[j + e]);
+                                if (n0 + col + e < sg.N) yr[col + e] = __uint_as_float(v[j + e]);
                         }
                     }
                 }
@@ -590,7 +608,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
-    if (warp == 1) tc::dealloc(tmem, 256);
+    if (warp == 1) tc::dealloc(tmem, BN);
 }
 
 struct Lut16 {
@@ -728,39 +746,86 @@ bool launch_split_bf16(const float *x, long long n, uint16_t *hilo, cudaStream_t
     return true;
 }
 
-bool launch_gemm_f32x3(const uint16_t *a_hilo, int M, const uint16_t *w_hilo, int N, int padded, float *y, int ldy,
-                       cudaStream_t st) {
-    if (M <= 0 || N <= 0) return true;
+bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F32Out *outs, int count,
+                             cudaStream_t st) {
+    if (M <= 0 || count <= 0) return true;
     if (padded % kFBK) {
         set_error("FP32 prefill GEMM requires the padded width to be a multiple of 64");
         return false;
     }
-    const size_t an = (size_t)M * padded, wn = (size_t)N * padded;
-    CUtensorMap tah, tal, tbh, tbl;
-    // bf16 rows seen as bytes: 2 * padded bytes per row, 128-byte (64-element) boxes
-    if (!make_map(&tah, a_hilo, M, 2 * padded, kFBM) || !make_map(&tal, a_hilo + an, M, 2 * padded, kFBM) ||
-        !make_map(&tbh, w_hilo, N, 2 * padded, kFBN) || !make_map(&tbl, w_hilo + wn, N, 2 * padded, kFBN))
-        return false;
-    GemmF32Args args{M, N, padded / kFBK, ldy, y};
-    static bool configured[64] = {};
-    int dev = 0;
+    if (count > kF32MaxSegs) {
+        for (int i = 0; i < count; i += kF32MaxSegs)
+            if (!launch_gemm_f32x3_multi(a_hilo, M, padded, outs + i, std::min(kF32MaxSegs, count - i), st)) return false;
+        return true;
+    }
+    int dev = 0, sms = 148;
     NB_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 0 || dev >= 64 || !configured[dev]) {
-        NB_CUDA_TRY(cudaFuncSetAttribute(cq_gemm_f32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFSmem));
-        if (dev >= 0 && dev < 64) configured[dev] = true;
+    static int sm_count[64] = {};
+    if (dev >= 0 && dev < 64) {
+        if (!sm_count[dev]) NB_CUDA_TRY(cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev));
+        sms = sm_count[dev];
+    }
+    const int mtiles = (M + kFBM - 1) / kFBM;
+    int wide = 0;
+    for (int i = 0; i < count; ++i) wide += (outs[i].N + 255) / 256;
+    // 256-wide tiles where they fill the machine, 64-wide ones (four times the CTAs) otherwise
+    const bool narrow = (long long)mtiles * wide < 2LL * sms;
+    const int BN = narrow ? 64 : 256;
+    const size_t an = (size_t)M * padded;
+    CUtensorMap tah, tal;
+    // bf16 rows seen as bytes: 2 * padded bytes per row, 128-byte (64-element) boxes
+    if (!make_map(&tah, a_hilo, M, 2 * padded, kFBM) || !make_map(&tal, a_hilo + an, M, 2 * padded, kFBM)) return false;
+    GemmF32Args args{};
+    args.nseg = count;
+    args.M = M;
+    args.ksteps = padded / kFBK;
+    int tiles = 0;
+    for (int i = 0; i < count; ++i) {
+        const F32Out &o = outs[i];
+        const size_t wn = (size_t)o.N * padded;
+        if (!make_map(&args.seg[i].bh, o.w_hilo, o.N, 2 * padded, BN) ||
+            !make_map(&args.seg[i].bl, o.w_hilo + wn, o.N, 2 * padded, BN))
+            return false;
+        args.seg[i].y = o.y;
+        args.seg[i].N = o.N;
+        args.seg[i].ldy = o.ldy;
+        args.seg[i].tile0 = tiles;
+        tiles += (o.N + BN - 1) / BN;
     }
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3((M + kFBM - 1) / kFBM, (N + kFBN - 1) / kFBN);
+    cfg.gridDim = dim3(mtiles, tiles);
     cfg.blockDim = dim3(kFThreads);
-    cfg.dynamicSmemBytes = kFSmem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, cq_gemm_f32x3_kernel, tah, tal, tbh, tbl, args));
+    static bool configured[2][64] = {};
+    if (narrow) {
+        if (dev < 0 || dev >= 64 || !configured[0][dev]) {
+            NB_CUDA_TRY(cudaFuncSetAttribute(cq_gemm_f32x3_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)FTile<64>::kSmem));
+            if (dev >= 0 && dev < 64) configured[0][dev] = true;
+        }
+        cfg.dynamicSmemBytes = FTile<64>::kSmem;
+        NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, cq_gemm_f32x3_kernel<64>, tah, tal, args));
+    } else {
+        if (dev < 0 || dev >= 64 || !configured[1][dev]) {
+            NB_CUDA_TRY(cudaFuncSetAttribute(cq_gemm_f32x3_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)FTile<256>::kSmem));
+            if (dev >= 0 && dev < 64) configured[1][dev] = true;
+        }
+        cfg.dynamicSmemBytes = FTile<256>::kSmem;
+        NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, cq_gemm_f32x3_kernel<256>, tah, tal, args));
+    }
     return true;
+}
+
+bool launch_gemm_f32x3(const uint16_t *a_hilo, int M, const uint16_t *w_hilo, int N, int padded, float *y, int ldy,
+                       cudaStream_t st) {
+    const F32Out o{w_hilo, N, y, ldy};
+    return launch_gemm_f32x3_multi(a_hilo, M, padded, &o, 1, st);
 }
 
 }  // namespace nb200

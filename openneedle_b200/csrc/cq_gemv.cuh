@@ -101,6 +101,16 @@ bool gemm_f32_prepare(const uint8_t *packed, const uint16_t *norms, int out, int
 bool launch_split_bf16(const float *x, long long n, uint16_t *hilo, cudaStream_t st);
 bool launch_gemm_f32x3(const uint16_t *a_hilo, int M, const uint16_t *w_hilo, int N, int padded, float *y, int ldy,
                        cudaStream_t st);
+// Several matrices against the same split activations in one launch (the
+// fused projections): y_i[M][ldy_i] = A . W_i^T.
+struct F32Out {
+    const uint16_t *w_hilo;
+    int N;
+    float *y;
+    int ldy;
+};
+bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F32Out *outs, int count,
+                             cudaStream_t st);
 // Activation rows from which int8 products run as the tensor-core GEMM.
 constexpr int kGemmMinRows = 64;
 

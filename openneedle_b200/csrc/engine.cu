@@ -85,7 +85,7 @@ struct Tensor {
 
 struct Model {
     needle2_engine_config c{};
-    int abits = 0, device = 0, lookup = -1;
+    int abits = 0, device = 0, lookup = -1, sms = 148;
     bool sdot = false;
     std::vector<Tensor> t;
     float *rope_divisor = nullptr;   // [head_dim / 2]
@@ -254,6 +254,7 @@ Model *build_model(const needle2_engine_config &c, const needle2_tensor_desc *td
     m->c = c;
     m->abits = abits;
     cuda_check(cudaGetDevice(&m->device), "cudaGetDevice");
+    cuda_check(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, m->device), "SM count");
     cuda_check(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking), "stream");
     m->t.resize(count);
     const int mh = 1 + 14 * c.layers;
@@ -530,11 +531,6 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
     for (int l = 0; l < c.layers; ++l) {
         const int ti = 1 + 14 * l;
         mark(st, 1, stream);
-        check(eng::launch_rms(s.x.ptr, N * D, R, N * D, nullptr, s.nx.ptr, N * D, stream), "lane rms");
-        eng::DenseSeg segs[3] = {{m.t[mh + 6].dense, l * N, N, s.raw.ptr, ldraw},
-                                 {m.t[mh + 7].dense, l * N, N, s.raw.ptr + N, ldraw},
-                                 {m.t[mh + 8].dense, l * N * N, N * N, s.raw.ptr + 2 * N, ldraw}};
-        check(eng::launch_dense_rows(segs, 3, s.nx.ptr, N * D, R, N * D, stream), "mHC projections");
         eng::MhcLayer ml{};
         ml.layer = l; ml.lanes = N; ml.D = D;
         ml.a_pre = m.t[mh].host[l]; ml.a_post = m.t[mh + 1].host[l]; ml.a_res = m.t[mh + 2].host[l];
@@ -548,8 +544,18 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
                 ml.ev = s.ev.ptr + (size_t)site * R * D;
                 ml.ld_site = D;
             }
-        check(eng::launch_mhc_pre(ml, s.raw.ptr, ldraw, s.x.ptr, R, s.hpost.ptr, s.u.ptr, s.bx.ptr, s.z.ptr, stream),
-              "mHC routing");
+        if (!eng::launch_mhc_route(ml, m.t[mh + 6].dense, m.t[mh + 7].dense, m.t[mh + 8].dense, s.x.ptr, R, s.raw.ptr,
+                                   ldraw, s.hpost.ptr, s.u.ptr, s.bx.ptr, s.z.ptr, m.sms, stream)) {
+            check(last_error()[0] == 0, "mHC routing");
+            check(eng::launch_rms(s.x.ptr, N * D, R, N * D, nullptr, s.nx.ptr, N * D, stream), "lane rms");
+            eng::DenseSeg segs[3] = {{m.t[mh + 6].dense, l * N, N, s.raw.ptr, ldraw},
+                                     {m.t[mh + 7].dense, l * N, N, s.raw.ptr + N, ldraw},
+                                     {m.t[mh + 8].dense, l * N * N, N * N, s.raw.ptr + 2 * N, ldraw}};
+            check(eng::launch_dense_rows(segs, 3, s.nx.ptr, N * D, R, N * D, stream), "mHC projections");
+            check(eng::launch_mhc_pre(ml, s.raw.ptr, ldraw, s.x.ptr, R, s.hpost.ptr, s.u.ptr, s.bx.ptr, s.z.ptr,
+                                      stream),
+                  "mHC routing");
+        }
         aq(m, s.z.ptr, R, D, stream);
         mark(st, 2, stream);
         projections(m, ti, s.z.ptr, R, s.q.ptr, s.k.ptr, s.v.ptr, s.gate.ptr, stream);

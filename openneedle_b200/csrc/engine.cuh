@@ -50,6 +50,13 @@ struct MhcLayer {
 bool launch_mhc_pre(const MhcLayer &L, const float *raw, int ldraw, const float *x, int R, float *hpost, float *u,
                     float *bx, float *z, cudaStream_t st);
 
+// The same as launch_rms + launch_dense_rows (the three projections) +
+// launch_mhc_pre in one kernel; false (nothing launched) where the geometry
+// does not fit it (lanes * D % 128 != 0), and the caller takes that path.
+bool launch_mhc_route(const MhcLayer &L, const float *phi_pre, const float *phi_post, const float *phi_res,
+                      const float *x, int R, float *raw, int ldraw, float *hpost, float *u, float *bx, float *z,
+                      int sms, cudaStream_t st);
+
 // q/k RMS with (1 + norm) per head, then rotary embedding at each row's
 // position (engine.cpp:994-1000); positions pos[r] (device), divisor[HD/2] =
 // rope_theta^(2j/HD).

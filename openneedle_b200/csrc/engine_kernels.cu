@@ -168,6 +168,109 @@ __global__ void __launch_bounds__(256) mhc_pre_kernel(const MhcLayer L, const fl
     }
 }
 
+// Fused mHC routing of SB rows per CTA (engine.cpp:980-992): the lanes' RMS
+// (nx, staged in shared memory), the 2N + N^2 FP32 projections of nx (each
+// CTA streams the layer's projection rows once for its SB rows), the gates,
+// u, the engram mixing and z = rms(bx) * (1 + norm_in).  Needs N * D % 128 == 0.
+template <int SB>
+__global__ void __launch_bounds__(256) mhc_route_kernel(const MhcLayer L, const float *__restrict__ phi_pre,
+                                                        const float *__restrict__ phi_post,
+                                                        const float *__restrict__ phi_res,
+                                                        const float *__restrict__ x, int R, float *__restrict__ raw,
+                                                        int ldraw, float *__restrict__ hpost, float *__restrict__ u,
+                                                        float *__restrict__ bx, float *__restrict__ z) {
+    extern __shared__ float smem[];
+    const int N = L.lanes, D = L.D, ND = N * D;
+    float *nx = smem;                              // [SB][ND]
+    __shared__ float raws[SB][3 * kMaxLanes + kMaxLanes * kMaxLanes];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int r0 = blockIdx.x * SB;
+    // 1. nx = rms(x) over the N lanes (engine.cpp:980)
+    for (int s = warp; s < SB; s += nw) {
+        const int r = r0 + s;
+        if (r >= R) continue;
+        const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)r * ND);
+        float ss = 0.f;
+        for (int k = lane; k < ND / 4; k += 32) {
+            const float4 v = xr[k];
+            ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+        }
+        const float inv = rms_inv(warp_sum(ss), ND);
+        float4 *dst = reinterpret_cast<float4 *>(nx + (size_t)s * ND);
+        for (int k = lane; k < ND / 4; k += 32) {
+            const float4 v = xr[k];
+            dst[k] = make_float4(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv), __fmul_rn(v.z, inv), __fmul_rn(v.w, inv));
+        }
+    }
+    __syncthreads();
+    // 2. raw[s][j] = phi_j . nx[s] for the layer's 2N + N^2 projection rows (engine.cpp:529-559)
+    const int rows = 2 * N + N * N;
+    for (int j = warp; j < rows; j += nw) {
+        const float *w = j < N ? phi_pre + (size_t)(L.layer * N + j) * ND
+                       : j < 2 * N ? phi_post + (size_t)(L.layer * N + j - N) * ND
+                                   : phi_res + (size_t)(L.layer * N * N + j - 2 * N) * ND;
+        float acc[SB];
+#pragma unroll
+        for (int s = 0; s < SB; ++s) acc[s] = 0.f;
+        for (int k = lane; k < ND / 4; k += 32) {
+            const float4 wv = __ldg(reinterpret_cast<const float4 *>(w) + k);
+#pragma unroll
+            for (int s = 0; s < SB; ++s) {
+                const float4 v = reinterpret_cast<const float4 *>(nx + (size_t)s * ND)[k];
+                acc[s] = fmaf(wv.x, v.x, fmaf(wv.y, v.y, fmaf(wv.z, v.z, fmaf(wv.w, v.w, acc[s]))));
+            }
+        }
+#pragma unroll
+        for (int s = 0; s < SB; ++s) {
+            const float t = warp_sum(acc[s]);
+            if (lane == 0) raws[s][j] = t;
+        }
+    }
+    __syncthreads();
+    // 3. per row: gates, u = sum_n hpre[n] x[n], engram mixing, z (engine.cpp:982-992)
+    for (int s = warp; s < SB; s += nw) {
+        const int r = r0 + s;
+        if (r >= R) continue;
+        for (int j = lane; j < rows; j += 32) raw[(size_t)r * ldraw + j] = raws[s][j];
+        float hpre = 0.f;
+        if (lane < N) {
+            const bool own = lane == L.layer % N;
+            hpre = sigm(__fadd_rn(__fadd_rn(__fmul_rn(L.a_pre, raws[s][lane]), L.b_pre[lane]), own ? 4.f : -4.f));
+            hpost[(size_t)r * N + lane] = __fmul_rn(
+                2.f, sigm(__fadd_rn(__fadd_rn(__fmul_rn(L.a_post, raws[s][N + lane]), L.b_post[lane]), own ? 0.f : -4.f)));
+        }
+        float *bxs = nx + (size_t)s * ND;          // this row's nx is no longer needed: bx lives there
+        const float *xr = x + (size_t)r * ND;
+        for (int d = lane; d < D; d += 32) {
+            float sum = 0.f;
+            for (int n = 0; n < N; ++n)
+                sum = __fadd_rn(sum, __fmul_rn(__shfl_sync(kFull, hpre, n), xr[(size_t)n * D + d]));
+            u[(size_t)r * D + d] = sum;
+            bxs[d] = sum;
+        }
+        if (L.ek) {
+            const float *ek = L.ek + (size_t)r * L.ld_site, *ev = L.ev + (size_t)r * L.ld_site;
+            float su = 0.f, se = 0.f;
+            for (int d = lane; d < D; d += 32) {
+                su = fmaf(bxs[d], bxs[d], su);
+                se = fmaf(ek[d], ek[d], se);
+            }
+            const float iu = rms_inv(warp_sum(su), D), ie = rms_inv(warp_sum(se), D);
+            float dot = 0.f;
+            for (int d = lane; d < D; d += 32) dot = fmaf(__fmul_rn(bxs[d], iu), __fmul_rn(ek[d], ie), dot);
+            const float alpha = sigm(__fdiv_rn(warp_sum(dot), sqrtf((float)D)));
+            for (int d = lane; d < D; d += 32) bxs[d] = __fadd_rn(bxs[d], __fmul_rn(alpha, ev[d]));
+        }
+        float sb = 0.f;
+        for (int d = lane; d < D; d += 32) sb = fmaf(bxs[d], bxs[d], sb);
+        const float ib = rms_inv(warp_sum(sb), D);
+        for (int d = lane; d < D; d += 32) {
+            bx[(size_t)r * D + d] = bxs[d];
+            z[(size_t)r * D + d] = __fmul_rn(__fmul_rn(bxs[d], ib), __fadd_rn(1.f, L.norm_in[d]));
+        }
+    }
+}
+
 // One warp per head: RMS with (1 + norm), then RoPE on the half-split pairs.
 __global__ void qk_norm_rope_kernel(float *__restrict__ q, float *__restrict__ k, int heads, int kvheads, int hd,
                                     const float *__restrict__ q_norm, const float *__restrict__ k_norm,
@@ -324,6 +427,170 @@ __global__ void __launch_bounds__(256) mhc_post_kernel(const PostLayer L, const 
             mean = __fadd_rn(mean, val);
         }
         for (int n = 0; n < N; ++n) xr[(size_t)n * D + d] = nv[n];
+        if (hidden) hidden[(size_t)r * ldh + d] = __fdiv_rn(mean, (float)N);
+    }
+}
+
+// ---- warp-per-row post-attention mixing (hada = 32 * E) ---------------------
+//
+// Lane l holds elements [l*E, (l+1)*E) of the row's D- and hada-vectors in
+// registers.  The Walsh-Hadamard stages h < E pair elements within a lane,
+// the stages h >= E pair lane l with lane l ^ (h / E) (same element slot):
+// every butterfly is the reference's a + b, a - b on the same pair
+// (needle2/csrc/cq.cpp:30-46), so the transform is bit-identical to it.
+
+template <int E>
+__device__ __forceinline__ void warp_fwht_regs(float (&v)[E], int lane, float scale) {
+#pragma unroll
+    for (int h = 1; h < E; h *= 2) {
+#pragma unroll
+        for (int i = 0; i < E; ++i)
+            if (!(i & h)) {
+                const float a = v[i], b = v[i + h];
+                v[i] = __fadd_rn(a, b);
+                v[i + h] = __fsub_rn(a, b);
+            }
+    }
+#pragma unroll
+    for (int m = 1; m < 32; m *= 2) {
+        const bool upper = lane & m;
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            const float o = __shfl_xor_sync(kFull, v[i], m);
+            v[i] = upper ? __fsub_rn(o, v[i]) : __fadd_rn(v[i], o);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], scale);
+}
+
+// Sinkhorn of engine.cpp:151-180 on an n x n matrix (n <= 8) held one element
+// per lane (lanes n*n .. 31 hold nothing useful); sums in the reference's
+// sequential order, broadcast by shuffles.
+__device__ float warp_sinkhorn(float a, int n, int lane) {
+    const int nn = n * n;
+    const bool mine = lane < nn;
+    const int i = lane / n, j = lane % n;
+    float mx = mine ? a : -INFINITY, mn = mine ? a : INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+        mn = fminf(mn, __shfl_xor_sync(kFull, mn, o));
+    }
+    if (!isfinite(mx) || __fsub_rn(mx, mn) > 60.f) {
+        for (int it = 0; it < 20; ++it) {
+            for (int pass = 0; pass < 2; ++pass) {   // rows, then columns
+                float m = -INFINITY;
+                for (int t = 0; t < n; ++t) {
+                    const int src = pass == 0 ? i * n + t : t * n + j;
+                    m = fmaxf(m, __shfl_sync(kFull, a, src & 31));
+                }
+                float sum = 0.f;
+                for (int t = 0; t < n; ++t) {
+                    const int src = pass == 0 ? i * n + t : t * n + j;
+                    sum = __fadd_rn(sum, expf(__fsub_rn(__shfl_sync(kFull, a, src & 31), m)));
+                }
+                a = __fsub_rn(a, __fadd_rn(m, logf(sum)));
+            }
+        }
+        return expf(a);
+    }
+    a = expf(__fsub_rn(a, mx));
+    for (int it = 0; it < 20; ++it) {
+        for (int pass = 0; pass < 2; ++pass) {
+            float sum = 0.f;
+            for (int t = 0; t < n; ++t) sum = __fadd_rn(sum, __shfl_sync(kFull, a, (pass == 0 ? i * n + t : t * n + j) & 31));
+            a = __fmul_rn(a, __fdiv_rn(1.f, sum));
+        }
+    }
+    return a;
+}
+
+template <int E, int N>
+__global__ void __launch_bounds__(128) mhc_post_warp_kernel(const PostLayer L, const float *__restrict__ proj,
+                                                            const float *__restrict__ raw, int ldraw,
+                                                            const float *__restrict__ hpost,
+                                                            const float *__restrict__ u, const float *__restrict__ bx,
+                                                            float *__restrict__ x, int R, float *__restrict__ hidden,
+                                                            int ldh) {
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= R) return;
+    const int D = L.D;
+    const int base = lane * E;
+    // engine.cpp:1025-1026: proj = rms(proj) * (1 + post_norm); bx += sigmoid(attn_gate) * proj
+    float pv[E], b[E];
+    float sp = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        const int d = base + i;
+        pv[i] = d < D ? proj[(size_t)r * D + d] : 0.f;
+        sp = fmaf(pv[i], pv[i], sp);
+    }
+    const float ip = rms_inv(warp_sum(sp), D);
+    const float ag = sigm(L.attn_gate[0]);
+    float sb = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        const int d = base + i;
+        if (d < D) {
+            const float t = __fmul_rn(__fmul_rn(pv[i], ip), __fadd_rn(1.f, L.post_norm[d]));
+            b[i] = __fadd_rn(bx[(size_t)r * D + d], __fmul_rn(ag, t));
+        } else {
+            b[i] = 0.f;
+        }
+        sb = fmaf(b[i], b[i], sb);
+    }
+    // engine.cpp:1027-1031: Hadamard MLP on rms(bx) * (1 + pre_hada)
+    const float ib = rms_inv(warp_sum(sb), D);
+    float mlp[E];
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        const int d = base + i;
+        mlp[i] = d < D ? __fmul_rn(__fmul_rn(__fmul_rn(b[i], ib), __fadd_rn(1.f, L.pre_hada[d])), L.d1[d]) : 0.f;
+    }
+    const float scale = __fdiv_rn(1.f, sqrtf((float)L.hada));
+    warp_fwht_regs<E>(mlp, lane, scale);
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        const float a = __fmul_rn(mlp[i], L.d2[base + i]);
+        mlp[i] = __fmul_rn(a, sigm(a));
+    }
+    warp_fwht_regs<E>(mlp, lane, scale);
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        const int d = base + i;
+        if (d < D) b[i] = __fsub_rn(__fadd_rn(b[i], __fmul_rn(L.d3[d], mlp[i])), u[(size_t)r * D + d]);
+    }
+    // engine.cpp:1033-1034: hres = sinkhorn(res * a_res + b_res)
+    constexpr int nn = N * N;
+    const float hr = lane < nn ? __fadd_rn(__fmul_rn(raw[(size_t)r * ldraw + 2 * N + lane], L.a_res), L.b_res[lane])
+                               : 0.f;
+    const float hres = warp_sinkhorn(hr, N, lane);
+    float hres_all[nn];
+    float hp[N];
+#pragma unroll
+    for (int t = 0; t < nn; ++t) hres_all[t] = __shfl_sync(kFull, hres, t);
+#pragma unroll
+    for (int n = 0; n < N; ++n) hp[n] = hpost[(size_t)r * N + n];
+    // engine.cpp:1035-1037: x[n] = hpost[n] * bx + sum_j hres[n][j] * x[j]; hidden = lane mean
+    float *xr = x + (size_t)r * N * D;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        const int d = base + i;
+        if (d >= D) continue;
+        float xs[N];
+#pragma unroll
+        for (int n = 0; n < N; ++n) xs[n] = xr[(size_t)n * D + d];
+        float mean = 0.f;
+#pragma unroll
+        for (int n = 0; n < N; ++n) {
+            float val = __fmul_rn(hp[n], b[i]);
+#pragma unroll
+            for (int j = 0; j < N; ++j) val = __fadd_rn(val, __fmul_rn(hres_all[n * N + j], xs[j]));
+            xr[(size_t)n * D + d] = val;
+            mean = __fadd_rn(mean, val);
+        }
         if (hidden) hidden[(size_t)r * ldh + d] = __fdiv_rn(mean, (float)N);
     }
 }
@@ -548,6 +815,40 @@ bool launch_mhc_pre(const MhcLayer &L, const float *raw, int ldraw, const float 
     return true;
 }
 
+bool launch_mhc_route(const MhcLayer &L, const float *phi_pre, const float *phi_post, const float *phi_res,
+                      const float *x, int R, float *raw, int ldraw, float *hpost, float *u, float *bx, float *z,
+                      int sms, cudaStream_t st) {
+    if (R <= 0) return true;
+    const int ND = L.lanes * L.D;
+    if (ND % 128 || L.lanes > kMaxLanes) return false;
+    // rows per CTA: as many as keep about one CTA per SM busy, at most 8
+    int sb = 8;
+    while (sb > 1 && (R + sb - 1) / sb < sms - sms / 8) sb /= 2;
+    const size_t smem = sizeof(float) * (size_t)sb * ND;
+    if (smem > 200 * 1024) return false;
+    const unsigned grid = (unsigned)((R + sb - 1) / sb);
+#define NB_ROUTE(SB)                                                                                               \
+    {                                                                                                              \
+        static bool configured = false;                                                                            \
+        if (!configured) {                                                                                         \
+            NB_CUDA_TRY(cudaFuncSetAttribute(mhc_route_kernel<SB>, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
+                                             200 * 1024));                                                         \
+            configured = true;                                                                                     \
+        }                                                                                                          \
+        mhc_route_kernel<SB><<<grid, 256, smem, st>>>(L, phi_pre, phi_post, phi_res, x, R, raw, ldraw, hpost, u,   \
+                                                      bx, z);                                                      \
+    }
+    switch (sb) {
+        case 8: NB_ROUTE(8) break;
+        case 4: NB_ROUTE(4) break;
+        case 2: NB_ROUTE(2) break;
+        default: NB_ROUTE(1) break;
+    }
+#undef NB_ROUTE
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+}
+
 bool launch_qk_norm_rope(float *q, float *k, int R, int heads, int kvheads, int hd, const float *q_norm,
                          const float *k_norm, const int *pos, const float *divisor, cudaStream_t st) {
     if (R <= 0) return true;
@@ -569,6 +870,31 @@ bool launch_gate(float *att, const float *gate, int R, int A, cudaStream_t st) {
 bool launch_mhc_post(const PostLayer &L, const float *proj, const float *raw, int ldraw, const float *hpost,
                      const float *u, float *bx, float *x, int R, float *hidden, int ldh, cudaStream_t st) {
     if (R <= 0) return true;
+    // warp per row where the Hadamard width is 32 * E and the lane count N are supported
+    const unsigned grid = (unsigned)((R + 3) / 4);
+#define NB_POST(E, N)                                                                                     \
+    mhc_post_warp_kernel<E, N><<<grid, 128, 0, st>>>(L, proj, raw, ldraw, hpost, u, bx, x, R, hidden, ldh); \
+    break;
+#define NB_POST_LANES(E)                    \
+    switch (L.lanes) {                      \
+        case 1: NB_POST(E, 1)               \
+        case 2: NB_POST(E, 2)               \
+        case 4: NB_POST(E, 4)               \
+        default: goto block_kernel;         \
+    }                                       \
+    break;
+    switch (L.hada) {
+        case 128: NB_POST_LANES(4)
+        case 256: NB_POST_LANES(8)
+        case 512: NB_POST_LANES(16)
+        case 1024: NB_POST_LANES(32)
+        default: goto block_kernel;
+    }
+#undef NB_POST_LANES
+#undef NB_POST
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+block_kernel:
     mhc_post_kernel<<<R, 256, sizeof(float) * (L.D + L.hada), st>>>(L, proj, raw, ldraw, hpost, u, bx, x, hidden,
                                                                      ldh);
     NB_CUDA_TRY(cudaGetLastError());
