@@ -32,6 +32,12 @@ namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
 
+// The engine's output gate, o * sigmoid(g) with sigmoid(g) = 1 / (1 + exp(-g))
+// (needle2/csrc/engine.cpp:36,123-129), applied as attention writes its output.
+__device__ __forceinline__ float gated(const AttnParams &p, size_t i, float o) {
+    return p.gate ? __fmul_rn(o, __fdiv_rn(1.f, __fadd_rn(1.f, expf(-p.gate[i])))) : o;
+}
+
 // One warp per (token, KV head): quantise head_dim values of k and v.
 __global__ void kv_quantize_kernel(const float *__restrict__ k, const float *__restrict__ v, int tokens, int kvheads,
                                    int hd, int8_t *__restrict__ ko, int8_t *__restrict__ vo, float *__restrict__ ks,
@@ -326,7 +332,8 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const AttnParams p) {
         }
         const int h = kh * R + r;
         if (p.splits == 1) {
-            p.out[((size_t)query * p.heads + h) * hd + d] = ll > 0.f ? aa / ll : 0.f;
+            const size_t oi = ((size_t)query * p.heads + h) * hd + d;
+            p.out[oi] = gated(p, oi, ll > 0.f ? aa / ll : 0.f);
         } else {
             const size_t prow = ((size_t)query * p.heads + h) * p.splits + split;
             p.part_acc[prow * hd + d] = aa;
@@ -443,22 +450,29 @@ struct StreamGeo {
     static constexpr int RING = NCH * CHUNK;        // bytes per warp
 };
 
-template <int HD, int R>
+// WPQ (warp per query): each warp takes one whole (query, KV head) pair (no
+// split, no cross-warp combine, no block barrier) and the CTA's four warps four
+// queries -- the short-context decode case, where per-CTA work is small.
+template <int HD, int R, bool WPQ>
 __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p) {
     using Geo = StreamGeo<HD>;
     constexpr int NW = Geo::NW, DL = Geo::DL, U = Geo::U, WL = DL / 4, CH = Geo::CH, NCH = Geo::NCH;
     constexpr bool QREG = R * DL <= 32;   // query slice in registers
+    static_assert(!WPQ || QREG, "warp-per-query needs the query slice in registers");
     __shared__ __align__(16) uint8_t ring_all[NW * Geo::RING];
-    __shared__ __align__(16) float qs[R * HD];
-    __shared__ float wm[NW][R], wl[NW][R];
-    __shared__ float wacc[NW][R][HD];
+    __shared__ __align__(16) float qs[WPQ ? 4 : R * HD];
+    __shared__ float wm[WPQ ? 1 : NW][R], wl[WPQ ? 1 : NW][R];
+    __shared__ float wacc[WPQ ? 1 : NW][R][WPQ ? 1 : HD];
 
-    const int split = blockIdx.x, kh = blockIdx.y, query = blockIdx.z;
+    const int warp = threadIdx.x >> 5;
+    const int split = WPQ ? 0 : blockIdx.x, kh = blockIdx.y;
+    const int query = WPQ ? blockIdx.z * NW + warp : blockIdx.z;
+    if (WPQ && query >= p.queries) return;
     const int entry = query / p.tokens, t = query % p.tokens;
     const int s = p.session[entry];
     const int chunk_start = p.position[entry];
     const int pos = chunk_start + t;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane >> 2, c = lane & 3;
+    const int lane = threadIdx.x & 31, j = lane >> 2, c = lane & 3;
     uint8_t *ring = ring_all + warp * Geo::RING;
 
     const int prefix_count = p.window ? min(p.prefix, pos + 1) : 0;
@@ -466,9 +480,9 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
     const int len = prefix_count + max(0, pos - start + 1);
     const int per = (len + p.splits - 1) / p.splits;
     const int i0 = split * per, i1 = min(len, i0 + per);
-    // this warp's share of the split, in whole steps of 8 slots
-    const int steps = (max(0, i1 - i0) + 7) / 8, wsteps = (steps + NW - 1) / NW;
-    const int w0 = i0 + warp * wsteps * 8, w1 = min(i1, w0 + wsteps * 8);
+    // this warp's share of the split, in whole steps of 8 slots (all of it with WPQ)
+    const int steps = (max(0, i1 - i0) + 7) / 8, wsteps = WPQ ? steps : (steps + NW - 1) / NW;
+    const int w0 = i0 + (WPQ ? 0 : warp) * wsteps * 8, w1 = min(i1, w0 + wsteps * 8);
     const int nchunks = w1 > w0 ? (w1 - w0 + 8 * CH - 1) / (8 * CH) : 0;
 
     // copies of chunk ch into its ring slot: lane (j, c) brings its own K and V
@@ -505,17 +519,20 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
         cp_async_commit();   // one group per chunk, empty ones included
     };
 
-    for (int idx = threadIdx.x; idx < R * HD; idx += blockDim.x)
-        qs[idx] = p.q[((size_t)query * p.heads + kh * R) * HD + idx];
+    if (!WPQ)
+        for (int idx = threadIdx.x; idx < R * HD; idx += blockDim.x)
+            qs[idx] = p.q[((size_t)query * p.heads + kh * R) * HD + idx];
 #pragma unroll
     for (int ch = 0; ch < NCH - 1; ++ch) issue(ch);
-    __syncthreads();
+    if (!WPQ) __syncthreads();
     float2 qr[QREG ? R : 1][QREG ? DL / 2 : 1];
     if (QREG) {
+        const float *qsrc = WPQ ? p.q + ((size_t)query * p.heads + kh * R) * HD : qs;
 #pragma unroll
         for (int r = 0; r < R; ++r)
 #pragma unroll
-            for (int e = 0; e < DL / 2; ++e) qr[r][e] = *reinterpret_cast<const float2 *>(qs + r * HD + c * DL + 2 * e);
+            for (int e = 0; e < DL / 2; ++e)
+                qr[r][e] = *reinterpret_cast<const float2 *>(qsrc + r * HD + c * DL + 2 * e);
     }
 
     const float inv_sqrt = p.inv_sqrt_hd;
@@ -640,6 +657,19 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
                 acc[r][e].y += __shfl_xor_sync(kFull, acc[r][e].y, o);
             }
         }
+        if (WPQ) {
+            // lanes 0-3 hold the whole sums for dimensions c * DL ..
+            if (j == 0) {
+                const float inv = l[r] > 0.f ? 1.f / l[r] : 0.f;
+                const size_t o0 = ((size_t)query * p.heads + kh * R + r) * HD + c * DL;
+#pragma unroll
+                for (int e = 0; e < DL / 2; ++e) {
+                    p.out[o0 + 2 * e] = gated(p, o0 + 2 * e, acc[r][e].x * inv);
+                    p.out[o0 + 2 * e + 1] = gated(p, o0 + 2 * e + 1, acc[r][e].y * inv);
+                }
+            }
+            continue;
+        }
         if (lane == 0) {
             wm[warp][r] = m[r];
             wl[warp][r] = l[r];
@@ -648,6 +678,7 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
 #pragma unroll
             for (int e = 0; e < DL / 2; ++e) *reinterpret_cast<float2 *>(&wacc[warp][r][c * DL + 2 * e]) = acc[r][e];
     }
+    if (WPQ) return;
     __syncthreads();
     for (int idx = threadIdx.x; idx < R * HD; idx += blockDim.x) {
         const int r = idx / HD, d = idx % HD;
@@ -662,7 +693,8 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
         }
         const int h = kh * R + r;
         if (p.splits == 1) {
-            p.out[((size_t)query * p.heads + h) * HD + d] = ll > 0.f ? aa / ll : 0.f;
+            const size_t oi = ((size_t)query * p.heads + h) * HD + d;
+            p.out[oi] = gated(p, oi, ll > 0.f ? aa / ll : 0.f);
         } else {
             const size_t prow = ((size_t)query * p.heads + h) * p.splits + split;
             p.part_acc[prow * HD + d] = aa;
@@ -839,12 +871,14 @@ __global__ void __launch_bounds__(128) attn_prefill_tile_kernel(const AttnParams
         }
     }
     if (active) {
-        float *op = p.out + ((size_t)(entry * p.tokens + t) * p.heads + h) * HD;
+        const size_t o0 = ((size_t)(entry * p.tokens + t) * p.heads + h) * HD;
+        float *op = p.out + o0;
         const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
         for (int d = 0; d < HD; d += 4)
             *reinterpret_cast<float4 *>(op + d) =
-                make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv, acc[d + 3] * inv);
+                make_float4(gated(p, o0 + d, acc[d] * inv), gated(p, o0 + d + 1, acc[d + 1] * inv),
+                            gated(p, o0 + d + 2, acc[d + 2] * inv), gated(p, o0 + d + 3, acc[d + 3] * inv));
     }
 }
 
@@ -860,14 +894,19 @@ bool launch_prefill_tile(const AttnParams &p, int entries, int R, cudaStream_t s
     }
 }
 
-template <int HD>
+template <int HD, bool WPQ>
 bool launch_stream(const AttnParams &p, dim3 grid, int R, cudaStream_t st) {
     switch (R) {
-        case 1: attn_stream_kernel<HD, 1><<<grid, 128, 0, st>>>(p); return true;
-        case 2: attn_stream_kernel<HD, 2><<<grid, 128, 0, st>>>(p); return true;
+        case 1: attn_stream_kernel<HD, 1, WPQ><<<grid, 128, 0, st>>>(p); return true;
+        case 2:
+            if constexpr (!WPQ || 2 * HD / 4 <= 32) {
+                attn_stream_kernel<HD, 2, WPQ><<<grid, 128, 0, st>>>(p);
+                return true;
+            }
+            return false;
         case 4:
-            if constexpr (HD <= 64) {
-                attn_stream_kernel<HD, 4><<<grid, 128, 0, st>>>(p);
+            if constexpr (HD <= 64 && !WPQ) {
+                attn_stream_kernel<HD, 4, false><<<grid, 128, 0, st>>>(p);
                 return true;
             }
             return false;
@@ -889,7 +928,7 @@ __global__ void attn_combine_kernel(const AttnParams p, int hd) {
             ll += pl[j] * f;
             aa += p.part_acc[((size_t)qh * p.splits + j) * hd + d] * f;
         }
-        p.out[(size_t)qh * hd + d] = ll > 0.f ? aa / ll : 0.f;
+        p.out[(size_t)qh * hd + d] = gated(p, (size_t)qh * hd + d, ll > 0.f ? aa / ll : 0.f);
     }
 }
 
@@ -957,9 +996,16 @@ bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
         return true;
     }
     bool streamed = false;
+    // one warp per query where the context needs no split and the query fits the registers
+    const bool wpq = p.splits == 1 && ((p.hd == 64 && R <= 2) || (p.hd == 128 && R <= 1));
+    AttnParams pw = p;
+    pw.queries = queries;
+    const dim3 wgrid(1, p.kvheads, (queries + 3) / 4);
+    if (wpq && p.hd == 64) streamed = launch_stream<64, true>(pw, wgrid, R, st);
+    else if (wpq && p.hd == 128) streamed = launch_stream<128, true>(pw, wgrid, R, st);
     // the streaming kernel where its per-lane state fits in registers
-    if (p.hd == 64 && R <= 4) streamed = launch_stream<64>(p, grid, R, st);
-    else if (p.hd == 128 && R <= 2) streamed = launch_stream<128>(p, grid, R, st);
+    else if (p.hd == 64 && R <= 4) streamed = launch_stream<64, false>(p, grid, R, st);
+    else if (p.hd == 128 && R <= 2) streamed = launch_stream<128, false>(p, grid, R, st);
     if (!streamed) switch (p.hd) {
         case 32: attn_split_kernel<32, true, int8_t><<<grid, 128, 0, st>>>(p); break;
         case 64: attn_split_kernel<64, true, int8_t><<<grid, 128, 0, st>>>(p); break;

@@ -25,6 +25,7 @@ struct KVDest {
 
 struct AttnParams {
     int heads, kvheads, hd, prefix, window, cs, splits, tokens;
+    int queries;                      // entries * tokens (set by launch_attention)
     int f32;                          // 1: FP32 cache (the *f pointers), 0: INT8 cache
     float inv_sqrt_hd;
     const int8_t *pk, *pv;            // shared prefix [KV][P][HD]
@@ -38,6 +39,7 @@ struct AttnParams {
     const int *session, *position;    // per entry (device): session, position of its first query
     const float *q;                   // [queries][heads][HD], queries = entries * tokens
     float *out;                       // [queries][heads][HD]
+    const float *gate;                // null, or [queries][heads][HD]: out is written as out * sigmoid(gate)
     float *part_m, *part_l, *part_acc; // split partials (splits > 1)
 };
 

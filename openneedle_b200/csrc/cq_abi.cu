@@ -366,6 +366,12 @@ bool run_linear_device(Matrix *m, const float *x, float *y, int batch, cudaStrea
     m->prepared = 0;
     if (batch <= 0) return true;
     const CQDevice &w = m->w;
+    if (!m->sdot && batch >= kGemmMinRows && gemm_f32_supported(w.storage_bits, w.padded) && w.group <= 1024) {
+        // prefill-sized FP32 batch: the rotation writes the GEMM's bf16 operands directly
+        if (!m->ahl.reserve(2 * (size_t)batch * w.padded)) return false;
+        if (!launch_rotate_hilo(w, x, batch, m->ahl.ptr, st)) return false;
+        return f32_multiply(m, nullptr, batch, y, st, m->ahl.ptr);
+    }
     if (!m->sdot) {
         if (!m->rot.reserve((size_t)batch * w.padded)) return false;
         if (!launch_rotate(w, x, batch, m->rot.ptr, st)) return false;
@@ -530,6 +536,18 @@ bool many_device(Matrix *const *ms, int count, const float *x, float *const *ys,
     Matrix *m0 = ms[0];
     const CQDevice &w = m0->w;
     const bool i8 = m0->sdot;
+    if (!i8 && batch >= kGemmMinRows && gemm_f32_supported(w.storage_bits, w.padded) && w.group <= 1024) {
+        // prefill-sized FP32 batch: rotate straight into the bf16 operands, one GEMM launch for every matrix
+        if (!m0->ahl.reserve(2 * (size_t)batch * w.padded)) return false;
+        if (!launch_rotate_hilo(w, x, batch, m0->ahl.ptr, st)) return false;
+        m0->prepared = 0;   // the FP32 activations themselves were not kept
+        std::vector<F32Out> outs(count);
+        for (int i = 0; i < count; ++i) {
+            if (!ensure_f32_copy(ms[i], st)) return false;
+            outs[i] = F32Out{ms[i]->d_whl, ms[i]->w.out, ys[i], ms[i]->w.out};
+        }
+        return launch_gemm_f32x3_multi(m0->ahl.ptr, batch, w.padded, outs.data(), count, st);
+    }
     if (i8) {
         if (!m0->q.reserve((size_t)batch * w.padded) || !m0->xs.reserve((size_t)batch * w.groups)) return false;
         if (!launch_quantize(w, x, batch, m0->q.ptr, m0->xs.ptr, st)) return false;

@@ -16,6 +16,8 @@
 #include "common.cuh"
 #include "cq_gemv.cuh"
 #include "sm100_async.cuh"
+#include <cuda_bf16.h>
+
 #include "cq_kernels.cuh"
 
 namespace nb200 {
@@ -103,11 +105,15 @@ __device__ __forceinline__ float sdot_scale(float absmax) {
     return sc;
 }
 
+// FP32 mode writes rot[M][padded], or (hilo not null) the bf16 operands of
+// the FP32-mode GEMM directly: hilo[i] = bf16(v), hilo[lo_off + i] =
+// bf16(v - hi), as split_bf16_kernel makes them from rot.
 template <int G, bool QUANT>
 __global__ void __launch_bounds__(256) rotate_warp_kernel(const float *__restrict__ x, int M, int in, int padded,
                                                           float scale, float *__restrict__ rot,
                                                           int8_t *__restrict__ q, float *__restrict__ xs,
-                                                          int cq2_planes) {
+                                                          int cq2_planes, uint16_t *__restrict__ hilo,
+                                                          long long lo_off) {
     using S = WarpShape<G>;
     pdl_launch_dependents();
     pdl_wait();   // x may be produced by the preceding kernel in the stream
@@ -129,7 +135,15 @@ __global__ void __launch_bounds__(256) rotate_warp_kernel(const float *__restric
         }
         warp_fwht<G>(v, lig, scale);
         if (!QUANT) {
-            if (valid) {
+            if (valid && hilo) {
+                const size_t o = (size_t)m * padded + (size_t)g * G + lig * S::E;
+#pragma unroll
+                for (int j = 0; j < S::E; ++j) {
+                    const __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
+                    hilo[o + j] = __bfloat16_as_ushort(h);
+                    hilo[lo_off + o + j] = __bfloat16_as_ushort(__float2bfloat16_rn(__fsub_rn(v[j], __bfloat162float(h))));
+                }
+            } else if (valid) {
                 float *dst = rot + (size_t)m * padded + (size_t)g * G + lig * S::E;
 #pragma unroll
                 for (int j = 0; j < S::E; ++j) dst[j] = v[j];
@@ -192,7 +206,7 @@ __global__ void __launch_bounds__(1024) rotate_block_kernel(const float *__restr
 
 template <bool QUANT>
 bool launch_rotate_impl(const CQDevice &w, const float *x, int M, float *rot, int8_t *q, float *xs,
-                        int cq2_planes, cudaStream_t st) {
+                        int cq2_planes, cudaStream_t st, uint16_t *hilo = nullptr) {
     const float scale = 1.0f / sqrtf((float)w.group);  // host: same expression as the reference
     const long long items = (long long)M * w.groups;
     if (items == 0) return true;
@@ -209,8 +223,13 @@ bool launch_rotate_impl(const CQDevice &w, const float *x, int M, float *rot, in
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        cudaLaunchKernelEx(&cfg, kernel, x, M, w.in, w.padded, scale, rot, q, xs, cq2_planes);
+        cudaLaunchKernelEx(&cfg, kernel, x, M, w.in, w.padded, scale, rot, q, xs, cq2_planes, hilo,
+                           (long long)M * w.padded);
     };
+    if (hilo && (w.group < 8 || w.group > 1024)) {
+        set_error("the direct bf16 split needs a group of 8 to 1024");
+        return false;
+    }
     switch (w.group) {
         case 8: warp_launch(rotate_warp_kernel<8, QUANT>, 4); break;
         case 16: warp_launch(rotate_warp_kernel<16, QUANT>, 2); break;
@@ -510,6 +529,10 @@ bool gemv_fast_path(const CQDevice &w) {
 
 bool launch_rotate(const CQDevice &w, const float *x, int M, float *rot, cudaStream_t s) {
     return launch_rotate_impl<false>(w, x, M, rot, nullptr, nullptr, 0, s);
+}
+
+bool launch_rotate_hilo(const CQDevice &w, const float *x, int M, uint16_t *hilo, cudaStream_t s) {
+    return launch_rotate_impl<false>(w, x, M, nullptr, nullptr, nullptr, 0, s, hilo);
 }
 
 bool launch_quantize(const CQDevice &w, const float *x, int M, int8_t *q, float *xs, cudaStream_t s) {

@@ -28,6 +28,9 @@ struct CQDevice {
 
 // Rotation of activations x[M][in] (zero padded): rot[M][padded] FP32.
 bool launch_rotate(const CQDevice &w, const float *x, int M, float *rot, cudaStream_t s);
+// The rotation straight into the FP32-mode GEMM's bf16 operands: hilo[M][padded]
+// = bf16(rot), then hilo[M*padded + ...] = bf16(rot - hi) (groups 8 to 1024).
+bool launch_rotate_hilo(const CQDevice &w, const float *x, int M, uint16_t *hilo, cudaStream_t s);
 // SDOT quantiser: q[M][padded] int8 (CQ2: bit-plane order of each 16-element
 // block) and xs[M][groups].
 bool launch_quantize(const CQDevice &w, const float *x, int M, int8_t *q, float *xs, cudaStream_t s);

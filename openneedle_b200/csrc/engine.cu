@@ -544,8 +544,10 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
                 ml.ev = s.ev.ptr + (size_t)site * R * D;
                 ml.ld_site = D;
             }
-        if (!eng::launch_mhc_route(ml, m.t[mh + 6].dense, m.t[mh + 7].dense, m.t[mh + 8].dense, s.x.ptr, R, s.raw.ptr,
-                                   ldraw, s.hpost.ptr, s.u.ptr, s.bx.ptr, s.z.ptr, m.sms, stream)) {
+        const bool routed = eng::launch_mhc_route(ml, m.t[mh + 6].dense, m.t[mh + 7].dense, m.t[mh + 8].dense, s.x.ptr,
+                                                  R, s.raw.ptr, ldraw, s.hpost.ptr, s.u.ptr, s.bx.ptr, s.z.ptr, m.sms,
+                                                  stream);
+        if (!routed) {
             check(last_error()[0] == 0, "mHC routing");
             check(eng::launch_rms(s.x.ptr, N * D, R, N * D, nullptr, s.nx.ptr, N * D, stream), "lane rms");
             eng::DenseSeg segs[3] = {{m.t[mh + 6].dense, l * N, N, s.raw.ptr, ldraw},
@@ -560,19 +562,28 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         mark(st, 2, stream);
         projections(m, ti, s.z.ptr, R, s.q.ptr, s.k.ptr, s.v.ptr, s.gate.ptr, stream);
         mark(st, 3, stream);
-        check(eng::launch_qk_norm_rope(s.q.ptr, s.k.ptr, R, c.heads, c.kvheads, c.head_dim, m.t[ti + 4].dense,
-                                       m.t[ti + 5].dense, s.rpos.ptr, m.rope_divisor, stream),
-              "q/k norm and RoPE");
+        if (T == 1) {
+            // decode: the new token's K/V stored as RoPE finishes, then attention alone
+            check(eng::launch_qk_rope_store(s.q.ptr, s.k.ptr, s.v.ptr, R, c.heads, c.kvheads, c.head_dim,
+                                            m.t[ti + 4].dense, m.t[ti + 5].dense, s.rpos.ptr, m.rope_divisor,
+                                            kv_pool_target(st.kv[l], st.iota.ptr, st.base.ptr), stream),
+                  "q/k norm, RoPE and KV store");
+        } else {
+            check(eng::launch_qk_norm_rope(s.q.ptr, s.k.ptr, R, c.heads, c.kvheads, c.head_dim, m.t[ti + 4].dense,
+                                           m.t[ti + 5].dense, s.rpos.ptr, m.rope_divisor, stream),
+                  "q/k norm and RoPE");
+        }
         mark(st, 4, stream);
-        check(kv_pool_run(st.kv[l], T == 1 ? kDecode : kPrefill, st.iota.ptr, st.base.ptr, E, T, max_visible, s.q.ptr,
-                          s.k.ptr, s.v.ptr, s.att.ptr, stream),
+        // attention with the output gate applied as it is written (engine.cpp:1022-1023)
+        check(kv_pool_run(st.kv[l], T == 1 ? kQuery : kPrefill, st.iota.ptr, st.base.ptr, E, T, max_visible, s.q.ptr,
+                          s.k.ptr, s.v.ptr, s.att.ptr, stream, s.gate.ptr),
               "attention");
         mark(st, 5, stream);
-        check(eng::launch_gate(s.att.ptr, s.gate.ptr, R, A, stream), "gate");
         aq(m, s.att.ptr, R, A, stream);
         linear(m, ti + 7, s.att.ptr, R, s.proj.ptr, stream);
         eng::PostLayer pl{};
         pl.layer = l; pl.lanes = N; pl.D = D; pl.hada = c.hada; pl.a_res = ml.a_res; pl.b_res = ml.b_res;
+        pl.hres_ready = routed ? 1 : 0;
         pl.post_norm = m.t[ti + 8].dense; pl.attn_gate = m.t[ti + 9].dense; pl.pre_hada = m.t[ti + 10].dense;
         pl.d1 = m.t[ti + 11].dense; pl.d2 = m.t[ti + 12].dense; pl.d3 = m.t[ti + 13].dense;
         mark(st, 6, stream);

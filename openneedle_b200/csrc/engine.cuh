@@ -51,8 +51,10 @@ bool launch_mhc_pre(const MhcLayer &L, const float *raw, int ldraw, const float 
                     float *bx, float *z, cudaStream_t st);
 
 // The same as launch_rms + launch_dense_rows (the three projections) +
-// launch_mhc_pre in one kernel; false (nothing launched) where the geometry
-// does not fit it (lanes * D % 128 != 0), and the caller takes that path.
+// launch_mhc_pre in one kernel, which also replaces raw's residual part by
+// the Sinkhorn-normalised mixing matrix (PostLayer::hres_ready); false
+// (nothing launched) where the geometry does not fit it (lanes * D % 128 !=
+// 0), and the caller takes that path.
 bool launch_mhc_route(const MhcLayer &L, const float *phi_pre, const float *phi_post, const float *phi_res,
                       const float *x, int R, float *raw, int ldraw, float *hpost, float *u, float *bx, float *z,
                       int sms, cudaStream_t st);
@@ -63,11 +65,21 @@ bool launch_mhc_route(const MhcLayer &L, const float *phi_pre, const float *phi_
 bool launch_qk_norm_rope(float *q, float *k, int R, int heads, int kvheads, int hd, const float *q_norm,
                          const float *k_norm, const int *pos, const float *divisor, cudaStream_t st);
 
+}  // namespace eng
+struct KVStoreTarget;
+namespace eng {
+// launch_qk_norm_rope, then the KV store of the row's token (one token per
+// row; the positions are the rows' positions) into target.
+bool launch_qk_rope_store(float *q, float *k, const float *v, int R, int heads, int kvheads, int hd,
+                          const float *q_norm, const float *k_norm, const int *pos, const float *divisor,
+                          const KVStoreTarget &target, cudaStream_t st);
+
 // att *= sigmoid(gate) (engine.cpp:1023).
 bool launch_gate(float *att, const float *gate, int R, int A, cudaStream_t st);
 
 struct PostLayer {
     int layer, lanes, D, hada;
+    int hres_ready;                // raw's residual part already holds sinkhorn(res * a_res + b_res)
     float a_res;
     const float *b_res;            // [lanes * lanes]
     const float *post_norm, *attn_gate, *pre_hada, *d1, *d2, *d3;

@@ -10,6 +10,7 @@
 
 #include "common.cuh"
 #include "engine.cuh"
+#include "kv_pool.cuh"
 
 namespace nb200 {
 namespace eng {
@@ -168,6 +169,8 @@ __global__ void __launch_bounds__(256) mhc_pre_kernel(const MhcLayer L, const fl
     }
 }
 
+__device__ float warp_sinkhorn(float a, int n, int lane);
+
 // Fused mHC routing of SB rows per CTA (engine.cpp:980-992): the lanes' RMS
 // (nx, staged in shared memory), the 2N + N^2 FP32 projections of nx (each
 // CTA streams the layer's projection rows once for its SB rows), the gates,
@@ -231,7 +234,14 @@ __global__ void __launch_bounds__(256) mhc_route_kernel(const MhcLayer L, const 
     for (int s = warp; s < SB; s += nw) {
         const int r = r0 + s;
         if (r >= R) continue;
-        for (int j = lane; j < rows; j += 32) raw[(size_t)r * ldraw + j] = raws[s][j];
+        for (int j = lane; j < 2 * N; j += 32) raw[(size_t)r * ldraw + j] = raws[s][j];
+        {
+            // engine.cpp:1033-1034: hres = sinkhorn(res * a_res + b_res), stored in place of res
+            const int nn = N * N;
+            const float hr = lane < nn ? __fadd_rn(__fmul_rn(raws[s][2 * N + lane], L.a_res), L.b_res[lane]) : 0.f;
+            const float hres = warp_sinkhorn(hr, N, lane);
+            if (lane < nn) raw[(size_t)r * ldraw + 2 * N + lane] = hres;
+        }
         float hpre = 0.f;
         if (lane < N) {
             const bool own = lane == L.layer % N;
@@ -297,6 +307,74 @@ __global__ void qk_norm_rope_kernel(float *__restrict__ q, float *__restrict__ k
             v[j + half] = __fadd_rn(__fmul_rn(c, co), __fmul_rn(a, si));
         }
         __syncwarp();
+    }
+}
+
+// qk_norm_rope_kernel followed, for one token per row, by the KV store of the
+// row's K (after RoPE) and V: INT8 by the reference's rule (engine.cpp:1005-1021,
+// scale max/127 or 1, values rint(x * (127 / max)) clamped to +-127, as
+// kv_quantize_kernel) or FP32 as is, into the row of target.dest.
+__global__ void qk_rope_store_kernel(float *__restrict__ q, float *__restrict__ k, const float *__restrict__ v,
+                                     int heads, int kvheads, int hd, const float *__restrict__ q_norm,
+                                     const float *__restrict__ k_norm, const int *__restrict__ pos,
+                                     const float *__restrict__ divisor, const KVStoreTarget t) {
+    extern __shared__ float buf[];   // [warps][hd]
+    const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const float fpos = (float)pos[r];
+    const KVDest &d = t.dest;
+    for (int h = warp; h < heads + 2 * kvheads; h += nw) {
+        const bool isv = h >= heads + kvheads;
+        const bool isq = h < heads;
+        const int kh = isq ? 0 : isv ? h - heads - kvheads : h - heads;
+        float *vp = isq ? q + ((size_t)r * heads + h) * hd
+                        : isv ? const_cast<float *>(v) + ((size_t)r * kvheads + kh) * hd : k + ((size_t)r * kvheads + kh) * hd;
+        if (!isv) {
+            const float *nrm = isq ? q_norm : k_norm;
+            float *b = buf + warp * hd;
+            float s = 0.f;
+            for (int i = lane; i < hd; i += 32) s = fmaf(vp[i], vp[i], s);
+            const float inv = rms_inv(warp_sum(s), hd);
+            for (int i = lane; i < hd; i += 32) b[i] = __fmul_rn(__fmul_rn(vp[i], inv), __fadd_rn(1.f, nrm[i]));
+            __syncwarp();
+            const int half = hd / 2;
+            for (int j = lane; j < half; j += 32) {
+                const float ang = __fdiv_rn(fpos, divisor[j]);
+                const float co = cosf(ang), si = sinf(ang);
+                const float a = b[j], c = b[j + half];
+                vp[j] = __fsub_rn(__fmul_rn(a, co), __fmul_rn(c, si));
+                vp[j + half] = __fadd_rn(__fmul_rn(c, co), __fmul_rn(a, si));
+            }
+            __syncwarp();
+            if (isq) continue;
+        }
+        // store this row's K (roped) or V head
+        const int s = d.session[r], p = d.position[r];
+        size_t row;
+        bool pinned = p < d.prefix;
+        if (pinned) {
+            row = (size_t)kh * d.prefix + p;
+        } else {
+            const int slot = d.window ? (p - d.prefix) % d.window : p - d.prefix;
+            row = ((size_t)s * kvheads + kh) * d.rows + slot;
+        }
+        if (t.fp32) {
+            float *dst = isv ? (pinned ? d.pvf : t.vf) : (pinned ? d.pkf : t.kf);
+            for (int i = lane; i < hd; i += 32) dst[row * hd + i] = vp[i];
+            continue;
+        }
+        float mx = 0.f;
+        for (int i = lane; i < hd; i += 32) mx = fmaxf(mx, fabsf(vp[i]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+        const float sc = mx > 0.f ? __fdiv_rn(mx, 127.f) : 1.f;
+        const float iv = mx > 0.f ? __fdiv_rn(127.f, mx) : 0.f;
+        int8_t *dst = isv ? (pinned ? d.pv : t.v8) : (pinned ? d.pk : t.k8);
+        float *sdst = isv ? (pinned ? d.pvs : t.vs) : (pinned ? d.pks : t.ks);
+        for (int i = lane; i < hd; i += 32) {
+            const int qv = __float2int_rn(__fmul_rn(vp[i], iv));
+            dst[row * hd + i] = (int8_t)(qv < -127 ? -127 : (qv > 127 ? 127 : qv));
+        }
+        if (lane == 0) sdst[row] = sc;
     }
 }
 
@@ -392,9 +470,10 @@ __global__ void __launch_bounds__(256) mhc_post_kernel(const PostLayer L, const 
         bxs[d] = __fadd_rn(bx[(size_t)r * D + d], __fmul_rn(ag, pv));
     }
     if (threadIdx.x < N * N) {
-        // engine.cpp:1033: hres = res * a_res + b_res
+        // engine.cpp:1033: hres = res * a_res + b_res (or the routing kernel's finished hres)
         const int ij = threadIdx.x;
-        hres[ij] = __fadd_rn(__fmul_rn(raw[(size_t)r * ldraw + 2 * N + ij], L.a_res), L.b_res[ij]);
+        const float rv = raw[(size_t)r * ldraw + 2 * N + ij];
+        hres[ij] = L.hres_ready ? rv : __fadd_rn(__fmul_rn(rv, L.a_res), L.b_res[ij]);
     }
     if (threadIdx.x < N) hp[threadIdx.x] = hpost[(size_t)r * N + threadIdx.x];
     __syncthreads();
@@ -410,7 +489,7 @@ __global__ void __launch_bounds__(256) mhc_post_kernel(const PostLayer L, const 
         mlp[d] = __fmul_rn(a, sigm(a));
     }
     block_fwht(mlp, H);
-    if (threadIdx.x == 0) sinkhorn(hres, N);
+    if (threadIdx.x == 0 && !L.hres_ready) sinkhorn(hres, N);
     for (int d = threadIdx.x; d < D; d += blockDim.x)
         bxs[d] = __fsub_rn(__fadd_rn(bxs[d], __fmul_rn(L.d3[d], mlp[d])), u[(size_t)r * D + d]);
     __syncthreads();
@@ -564,9 +643,14 @@ __global__ void __launch_bounds__(128) mhc_post_warp_kernel(const PostLayer L, c
     }
     // engine.cpp:1033-1034: hres = sinkhorn(res * a_res + b_res)
     constexpr int nn = N * N;
-    const float hr = lane < nn ? __fadd_rn(__fmul_rn(raw[(size_t)r * ldraw + 2 * N + lane], L.a_res), L.b_res[lane])
-                               : 0.f;
-    const float hres = warp_sinkhorn(hr, N, lane);
+    float hres;
+    if (L.hres_ready) {
+        hres = lane < nn ? raw[(size_t)r * ldraw + 2 * N + lane] : 0.f;   // made by the routing kernel
+    } else {
+        const float hr = lane < nn ? __fadd_rn(__fmul_rn(raw[(size_t)r * ldraw + 2 * N + lane], L.a_res), L.b_res[lane])
+                                   : 0.f;
+        hres = warp_sinkhorn(hr, N, lane);
+    }
     float hres_all[nn];
     float hp[N];
 #pragma unroll
@@ -855,6 +939,17 @@ bool launch_qk_norm_rope(float *q, float *k, int R, int heads, int kvheads, int 
     const int warps = std::min(heads + kvheads, 16);
     qk_norm_rope_kernel<<<R, 32 * warps, sizeof(float) * warps * hd, st>>>(q, k, heads, kvheads, hd, q_norm, k_norm,
                                                                          pos, divisor);
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+}
+
+bool launch_qk_rope_store(float *q, float *k, const float *v, int R, int heads, int kvheads, int hd,
+                          const float *q_norm, const float *k_norm, const int *pos, const float *divisor,
+                          const KVStoreTarget &t, cudaStream_t st) {
+    if (R <= 0) return true;
+    const int warps = std::min(heads + 2 * kvheads, 32);
+    qk_rope_store_kernel<<<R, 32 * warps, sizeof(float) * warps * hd, st>>>(q, k, v, heads, kvheads, hd, q_norm,
+                                                                           k_norm, pos, divisor, t);
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }

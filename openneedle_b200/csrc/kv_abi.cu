@@ -164,8 +164,9 @@ bool store_ring(KVPool &kv, const int *ids, const int *pos, const float *k, cons
 // Attention of `count` entries x `tokens` queries; staging holds the entries'
 // own new K/V when `staged` (prefill).
 bool attend(KVPool &kv, const int *ids, const int *pos, int count, int tokens, int max_len, const float *q, float *out,
-            bool staged, cudaStream_t st) {
+            bool staged, cudaStream_t st, const float *gate = nullptr) {
     AttnParams p = base_params(kv);
+    p.gate = gate;
     p.tokens = tokens;
     p.session = ids;
     p.position = pos;
@@ -256,6 +257,17 @@ size_t kv_pool_bytes(const KVPool *kv) {
 
 int kv_pool_device(const KVPool *kv) { return kv->device; }
 
+KVStoreTarget kv_pool_target(KVPool *kv, const int *ids, const int *pos) {
+    KVStoreTarget t{};
+    t.dest = ring_dest(*kv, ids, pos, 1, 0);
+    t.k8 = kv->sk.ptr; t.v8 = kv->sv.ptr; t.ks = kv->sks.ptr; t.vs = kv->svs.ptr;
+    t.kf = kv->skf.ptr; t.vf = kv->svf.ptr;
+    t.fp32 = kv->fp32 ? 1 : 0;
+    t.kvheads = kv->kvheads;
+    t.hd = kv->hd;
+    return t;
+}
+
 int kv_max_visible(int prefix, int window, const int *positions, int count, int tokens) {
     int best = 1;
     for (int i = 0; i < count; ++i) {
@@ -268,18 +280,18 @@ int kv_max_visible(int prefix, int window, const int *positions, int count, int 
 }
 
 bool kv_pool_run(KVPool *kv, KVOp op, const int *ids, const int *pos, int count, int tokens, int max_visible,
-                 const float *q, const float *k, const float *v, float *out, cudaStream_t st) {
+                 const float *q, const float *k, const float *v, float *out, cudaStream_t st, const float *gate) {
     if (count <= 0) return true;
     switch (op) {
         case kStore: return store_ring(*kv, ids, pos, k, v, count, tokens, 0, st);
-        case kQuery: return attend(*kv, ids, pos, count, tokens, max_visible, q, out, false, st);
+        case kQuery: return attend(*kv, ids, pos, count, tokens, max_visible, q, out, false, st, gate);
         case kDecode:
             if (tokens != 1) { set_error("decode takes one token per entry"); return false; }
             return store_ring(*kv, ids, pos, k, v, count, 1, 0, st) &&
-                   attend(*kv, ids, pos, count, 1, max_visible, q, out, false, st);
+                   attend(*kv, ids, pos, count, 1, max_visible, q, out, false, st, gate);
         case kPrefill: {
             if (!stage(*kv, k, v, count * tokens, st)) return false;
-            if (!attend(*kv, ids, pos, count, tokens, max_visible, q, out, true, st)) return false;
+            if (!attend(*kv, ids, pos, count, tokens, max_visible, q, out, true, st, gate)) return false;
             // write the slots after attending; with a window only the last `window`
             // tokens of the chunk outside the pinned prefix survive (earlier ones
             // would be overwritten anyway)

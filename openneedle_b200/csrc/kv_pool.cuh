@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "attention.cuh"
+
 namespace nb200 {
 
 struct KVPool;
@@ -35,7 +37,22 @@ int kv_max_visible(int prefix, int window, const int *pos_host, int count, int t
 //   kQuery:  attend only
 // max_visible bounds the entries' visible sets (kv_max_visible).
 enum KVOp { kStore = 0, kDecode = 1, kPrefill = 2, kQuery = 3 };
+// gate (optional, same layout as out): out is written as out * sigmoid(gate),
+// the engine's attention output gate (engine.cpp:1023).
 bool kv_pool_run(KVPool *kv, KVOp op, const int *ids, const int *pos, int count, int tokens, int max_visible,
-                 const float *q, const float *k, const float *v, float *out, cudaStream_t st);
+                 const float *q, const float *k, const float *v, float *out, cudaStream_t st,
+                 const float *gate = nullptr);
+
+// Where kStore puts one token per entry (ids/pos device arrays): the ring
+// destination with this pool's arrays, for kernels that store K/V themselves
+// (the engine's fused RoPE + store) before a kQuery call attends.
+struct KVStoreTarget {
+    KVDest dest;
+    int8_t *k8, *v8;       // INT8 cache rows [S][KV][Cs][HD] and their scales
+    float *ks, *vs;
+    float *kf, *vf;        // FP32 cache rows
+    int fp32, kvheads, hd;
+};
+KVStoreTarget kv_pool_target(KVPool *kv, const int *ids, const int *pos);
 
 }  // namespace nb200
