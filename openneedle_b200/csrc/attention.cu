@@ -658,9 +658,11 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
             }
         }
         if (WPQ) {
-            // lanes 0-3 hold the whole sums for dimensions c * DL ..
+            // lanes 0-3 hold the whole sums for dimensions c * DL ..; the softmax
+            // denominator was counted on the c == 0 lanes only, so lane 0 has it
+            const float lt = __shfl_sync(kFull, l[r], 0);
             if (j == 0) {
-                const float inv = l[r] > 0.f ? 1.f / l[r] : 0.f;
+                const float inv = lt > 0.f ? 1.f / lt : 0.f;
                 const size_t o0 = ((size_t)query * p.heads + kh * R + r) * HD + c * DL;
 #pragma unroll
                 for (int e = 0; e < DL / 2; ++e) {
