@@ -24,6 +24,7 @@
 
 #include "attention.cuh"
 #include "common.cuh"
+#include "pdl.cuh"
 #include "sm100_async.cuh"
 
 namespace nb200 {
@@ -42,6 +43,7 @@ __device__ __forceinline__ float gated(const AttnParams &p, size_t i, float o) {
 __global__ void kv_quantize_kernel(const float *__restrict__ k, const float *__restrict__ v, int tokens, int kvheads,
                                    int hd, int8_t *__restrict__ ko, int8_t *__restrict__ vo, float *__restrict__ ks,
                                    float *__restrict__ vs, KVDest dest) {
+    pdl_enter();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= tokens * kvheads) return;
     const int t = warp / kvheads, kh = warp % kvheads;
@@ -88,6 +90,7 @@ __global__ void kv_quantize_kernel(const float *__restrict__ k, const float *__r
 // FP32 cache store: one warp per (token, KV head), rows as kv_quantize_kernel.
 __global__ void kv_store_f32_kernel(const float *__restrict__ k, const float *__restrict__ v, int tokens, int kvheads,
                                     int hd, float *__restrict__ ko, float *__restrict__ vo, KVDest dest) {
+    pdl_enter();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= tokens * kvheads) return;
     const int t = warp / kvheads, kh = warp % kvheads;
@@ -180,6 +183,7 @@ __device__ __forceinline__ Row<T> visible_row(const AttnParams &p, int s, int po
 // online softmax per warp, lane-per-dimension value accumulation.
 template <int HD, bool EXACT, typename T>
 __global__ void __launch_bounds__(128) attn_split_kernel(const AttnParams p) {
+    pdl_enter();
     constexpr int NW = 4;
     const int hd = EXACT ? HD : p.hd;
     constexpr int DPL = (HD + 31) / 32;   // dims per lane in the PV phase
@@ -455,6 +459,7 @@ struct StreamGeo {
 // queries -- the short-context decode case, where per-CTA work is small.
 template <int HD, int R, bool WPQ>
 __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p) {
+    pdl_enter();
     using Geo = StreamGeo<HD>;
     constexpr int NW = Geo::NW, DL = Geo::DL, U = Geo::U, WL = DL / 4, CH = Geo::CH, NCH = Geo::NCH;
     constexpr bool QREG = R * DL <= 32;   // query slice in registers
@@ -744,6 +749,7 @@ __device__ __forceinline__ RowPtr position_ptr(const AttnParams &p, int s, int k
 
 template <int HD, int R>
 __global__ void __launch_bounds__(128) attn_prefill_tile_kernel(const AttnParams p) {
+    pdl_enter();
     constexpr int TQ = 128 / R;
     __shared__ __align__(16) float ks_f[kPBK][HD], vs_f[kPBK][HD];
     __shared__ float kscale[kPBK], vscale[kPBK];
@@ -889,9 +895,9 @@ bool launch_prefill_tile(const AttnParams &p, int entries, int R, cudaStream_t s
     const int tq = 128 / R;
     const dim3 grid((p.tokens + tq - 1) / tq, p.kvheads, entries);
     switch (R) {
-        case 1: attn_prefill_tile_kernel<HD, 1><<<grid, 128, 0, st>>>(p); return true;
-        case 2: attn_prefill_tile_kernel<HD, 2><<<grid, 128, 0, st>>>(p); return true;
-        case 4: attn_prefill_tile_kernel<HD, 4><<<grid, 128, 0, st>>>(p); return true;
+        case 1: NB_CUDA_TRY(launch_pdl(attn_prefill_tile_kernel<HD, 1>, grid, 128, 0, st, p)); return true;
+        case 2: NB_CUDA_TRY(launch_pdl(attn_prefill_tile_kernel<HD, 2>, grid, 128, 0, st, p)); return true;
+        case 4: NB_CUDA_TRY(launch_pdl(attn_prefill_tile_kernel<HD, 4>, grid, 128, 0, st, p)); return true;
         default: return false;
     }
 }
@@ -899,16 +905,16 @@ bool launch_prefill_tile(const AttnParams &p, int entries, int R, cudaStream_t s
 template <int HD, bool WPQ>
 bool launch_stream(const AttnParams &p, dim3 grid, int R, cudaStream_t st) {
     switch (R) {
-        case 1: attn_stream_kernel<HD, 1, WPQ><<<grid, 128, 0, st>>>(p); return true;
+        case 1: NB_CUDA_TRY(launch_pdl(attn_stream_kernel<HD, 1, WPQ>, grid, 128, 0, st, p)); return true;
         case 2:
             if constexpr (!WPQ || 2 * HD / 4 <= 32) {
-                attn_stream_kernel<HD, 2, WPQ><<<grid, 128, 0, st>>>(p);
+                NB_CUDA_TRY(launch_pdl(attn_stream_kernel<HD, 2, WPQ>, grid, 128, 0, st, p));
                 return true;
             }
             return false;
         case 4:
             if constexpr (HD <= 64 && !WPQ) {
-                attn_stream_kernel<HD, 4, false><<<grid, 128, 0, st>>>(p);
+                NB_CUDA_TRY(launch_pdl(attn_stream_kernel<HD, 4, false>, grid, 128, 0, st, p));
                 return true;
             }
             return false;
@@ -918,6 +924,7 @@ bool launch_stream(const AttnParams &p, dim3 grid, int R, cudaStream_t st) {
 
 // Merge the split partials of each (query, head).
 __global__ void attn_combine_kernel(const AttnParams p, int hd) {
+    pdl_enter();
     const int qh = blockIdx.x;   // query * heads + h
     const float *pm = p.part_m + (size_t)qh * p.splits, *pl = p.part_l + (size_t)qh * p.splits;
     float mm = -INFINITY;
@@ -940,8 +947,8 @@ bool launch_kv_quantize(const float *k, const float *v, int tokens, int kvheads,
                         float *ks, float *vs, const KVDest &dest, cudaStream_t st) {
     if (tokens <= 0) return true;
     const long long warps = (long long)tokens * kvheads;
-    kv_quantize_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(k, v, tokens, kvheads, hd, ko, vo, ks, vs,
-                                                                             dest);
+    NB_CUDA_TRY(launch_pdl(kv_quantize_kernel, (unsigned)((warps * 32 + 255) / 256), 256, 0, st, k, v, tokens, kvheads, hd, ko, vo, ks, vs,
+                                                                             dest));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -950,7 +957,7 @@ bool launch_kv_store_f32(const float *k, const float *v, int tokens, int kvheads
                          const KVDest &dest, cudaStream_t st) {
     if (tokens <= 0) return true;
     const long long warps = (long long)tokens * kvheads;
-    kv_store_f32_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(k, v, tokens, kvheads, hd, ko, vo, dest);
+    NB_CUDA_TRY(launch_pdl(kv_store_f32_kernel, (unsigned)((warps * 32 + 255) / 256), 256, 0, st, k, v, tokens, kvheads, hd, ko, vo, dest));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -972,13 +979,13 @@ bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
     const int R = p.heads / p.kvheads;
     if (p.f32) {
         switch (p.hd) {
-            case 32: attn_split_kernel<32, true, float><<<grid, 128, 0, st>>>(p); break;
-            case 64: attn_split_kernel<64, true, float><<<grid, 128, 0, st>>>(p); break;
-            case 128: attn_split_kernel<128, true, float><<<grid, 128, 0, st>>>(p); break;
+            case 32: NB_CUDA_TRY(launch_pdl(attn_split_kernel<32, true, float>, grid, 128, 0, st, p)); break;
+            case 64: NB_CUDA_TRY(launch_pdl(attn_split_kernel<64, true, float>, grid, 128, 0, st, p)); break;
+            case 128: NB_CUDA_TRY(launch_pdl(attn_split_kernel<128, true, float>, grid, 128, 0, st, p)); break;
             default:
-                if (p.hd <= 32) attn_split_kernel<32, false, float><<<grid, 128, 0, st>>>(p);
-                else if (p.hd <= 64) attn_split_kernel<64, false, float><<<grid, 128, 0, st>>>(p);
-                else if (p.hd <= 128) attn_split_kernel<128, false, float><<<grid, 128, 0, st>>>(p);
+                if (p.hd <= 32) NB_CUDA_TRY(launch_pdl(attn_split_kernel<32, false, float>, grid, 128, 0, st, p));
+                else if (p.hd <= 64) NB_CUDA_TRY(launch_pdl(attn_split_kernel<64, false, float>, grid, 128, 0, st, p));
+                else if (p.hd <= 128) NB_CUDA_TRY(launch_pdl(attn_split_kernel<128, false, float>, grid, 128, 0, st, p));
                 else {
                     set_error("head_dim above 128 is not supported by the GPU build");
                     return false;
@@ -986,7 +993,7 @@ bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
         }
         NB_CUDA_TRY(cudaGetLastError());
         if (p.splits > 1) {
-            attn_combine_kernel<<<queries * p.heads, 64, 0, st>>>(p, p.hd);
+            NB_CUDA_TRY(launch_pdl(attn_combine_kernel, queries * p.heads, 64, 0, st, p, p.hd));
             NB_CUDA_TRY(cudaGetLastError());
         }
         return true;
@@ -1009,13 +1016,13 @@ bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
     else if (p.hd == 64 && R <= 4) streamed = launch_stream<64, false>(p, grid, R, st);
     else if (p.hd == 128 && R <= 2) streamed = launch_stream<128, false>(p, grid, R, st);
     if (!streamed) switch (p.hd) {
-        case 32: attn_split_kernel<32, true, int8_t><<<grid, 128, 0, st>>>(p); break;
-        case 64: attn_split_kernel<64, true, int8_t><<<grid, 128, 0, st>>>(p); break;
-        case 128: attn_split_kernel<128, true, int8_t><<<grid, 128, 0, st>>>(p); break;
+        case 32: NB_CUDA_TRY(launch_pdl(attn_split_kernel<32, true, int8_t>, grid, 128, 0, st, p)); break;
+        case 64: NB_CUDA_TRY(launch_pdl(attn_split_kernel<64, true, int8_t>, grid, 128, 0, st, p)); break;
+        case 128: NB_CUDA_TRY(launch_pdl(attn_split_kernel<128, true, int8_t>, grid, 128, 0, st, p)); break;
         default:
-            if (p.hd <= 32) attn_split_kernel<32, false, int8_t><<<grid, 128, 0, st>>>(p);
-            else if (p.hd <= 64) attn_split_kernel<64, false, int8_t><<<grid, 128, 0, st>>>(p);
-            else if (p.hd <= 128) attn_split_kernel<128, false, int8_t><<<grid, 128, 0, st>>>(p);
+            if (p.hd <= 32) NB_CUDA_TRY(launch_pdl(attn_split_kernel<32, false, int8_t>, grid, 128, 0, st, p));
+            else if (p.hd <= 64) NB_CUDA_TRY(launch_pdl(attn_split_kernel<64, false, int8_t>, grid, 128, 0, st, p));
+            else if (p.hd <= 128) NB_CUDA_TRY(launch_pdl(attn_split_kernel<128, false, int8_t>, grid, 128, 0, st, p));
             else {
                 set_error("head_dim above 128 is not supported by the GPU build");
                 return false;
@@ -1023,7 +1030,7 @@ bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
     }
     NB_CUDA_TRY(cudaGetLastError());
     if (p.splits > 1) {
-        attn_combine_kernel<<<queries * p.heads, 64, 0, st>>>(p, p.hd);
+        NB_CUDA_TRY(launch_pdl(attn_combine_kernel, queries * p.heads, 64, 0, st, p, p.hd));
         NB_CUDA_TRY(cudaGetLastError());
     }
     return true;

@@ -14,6 +14,7 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "pdl.cuh"
 #include "cq_gemv.cuh"
 #include "sm100_async.cuh"
 #include <cuda_bf16.h>
@@ -794,6 +795,7 @@ namespace {
 // scale = a / maxq, maxq = 2^(bits-1) - 1 (needle2/csrc/engine.cpp:185-191;
 // IEEE divide and multiply, so the result is the reference's bit for bit).
 __global__ void activation_quant_kernel(float *__restrict__ x, int rows, int dim, int bits) {
+    pdl_enter();
     const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
     if (warp >= rows) return;
     float *xr = x + (size_t)warp * dim;
@@ -829,6 +831,7 @@ __device__ __forceinline__ void better(float &v, int &i, float ov, int oi) {
 // logits[0] is NaN.  Each thread scans its indices in increasing order, then
 // the candidates are reduced with the same order.
 __global__ void argmax_kernel(const float *__restrict__ x, int vocab, int ld, int *__restrict__ out) {
+    pdl_enter();
     __shared__ float sv[32];
     __shared__ int si[32];
     const float *row = x + (size_t)blockIdx.x * ld;
@@ -875,7 +878,7 @@ __global__ void argmax_kernel(const float *__restrict__ x, int vocab, int ld, in
 
 bool launch_argmax(const float *x, int rows, int vocab, int ld, int *out, cudaStream_t st) {
     if (rows <= 0) return true;
-    argmax_kernel<<<rows, 1024, 0, st>>>(x, vocab, ld, out);
+    NB_CUDA_TRY(launch_pdl(argmax_kernel, rows, 1024, 0, st, x, vocab, ld, out));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -883,7 +886,7 @@ bool launch_argmax(const float *x, int rows, int vocab, int ld, int *out, cudaSt
 bool launch_activation_quant(float *x, int rows, int dim, int bits, cudaStream_t st) {
     if (rows <= 0 || dim <= 0 || bits == 0) return true;
     const long long threads = (long long)rows * 32;
-    activation_quant_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(x, rows, dim, bits);
+    NB_CUDA_TRY(launch_pdl(activation_quant_kernel, (unsigned)((threads + 255) / 256), 256, 0, st, x, rows, dim, bits));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }

@@ -30,6 +30,7 @@
 #include "cq_kernels.cuh"
 #include "engine.cuh"
 #include "kv_pool.cuh"
+#include "pdl.cuh"
 
 namespace nb200 {
 namespace {
@@ -975,6 +976,7 @@ size_t state_kv_bytes(const State &st) {
 // Copies sequence 0's history and engram rings to every sequence and sets all
 // positions to sequence 0's.
 __global__ void broadcast_state_kernel(int *hist, int hist_n, float *eng, size_t eng_n, int *base, int S) {
+    pdl_enter();
     const int s = blockIdx.x + 1;
     if (s >= S) return;
     for (int i = threadIdx.x; i < hist_n; i += blockDim.x) hist[(size_t)s * hist_n + i] = hist[i];
@@ -996,8 +998,8 @@ void batch_set_prefix(Batch &b, const int *tokens) {
         forward(st, 1, T, st.s.tokens.ptr, Outputs{}, nullptr, stream);
     }
     if (st.S > 1) {
-        broadcast_state_kernel<<<st.S - 1, 256, 0, stream>>>(st.hist.ptr, m.hist_cap(), st.engring.ptr,
-                                                             st.engring_stride(), st.base.ptr, st.S);
+        cuda_check(launch_pdl(broadcast_state_kernel, st.S - 1, 256, 0, stream, st.hist.ptr, m.hist_cap(), st.engring.ptr,
+                                                             st.engring_stride(), st.base.ptr, st.S), "kernel launch");
         cuda_check(cudaGetLastError(), "prefix broadcast");
     }
     std::fill(st.pos.begin(), st.pos.end(), P);
@@ -1061,6 +1063,7 @@ void batch_step(Batch &b, const int *tokens, float *logits, int *next) {
 // out[s][counter] = nxt[s]; cur[s] = nxt[s] (the step's greedy tokens become the next inputs).
 __global__ void commit_tokens_kernel(const int *__restrict__ nxt, int *__restrict__ cur, int S,
                                      int *__restrict__ out, int steps, const int *__restrict__ counter) {
+    pdl_enter();
     const int s = blockIdx.x * blockDim.x + threadIdx.x;
     const int c = *counter;
     if (s < S) {
@@ -1078,7 +1081,7 @@ void decode_step(State &st, int *cur, int *nxt, int *out, int steps, int *counte
     o.argmax_dev = nxt;
     o.max_visible = max_visible;
     forward(st, st.S, 1, cur, o, nullptr, stream);
-    commit_tokens_kernel<<<(st.S + 255) / 256, 256, 0, stream>>>(nxt, cur, st.S, out, steps, counter);
+    cuda_check(launch_pdl(commit_tokens_kernel, (st.S + 255) / 256, 256, 0, stream, nxt, cur, st.S, out, steps, counter), "kernel launch");
     cuda_check(cudaGetLastError(), "tokens");
     check(eng::launch_advance(counter, 1, 1, stream), "step counter");
 }

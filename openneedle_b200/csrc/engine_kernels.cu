@@ -9,6 +9,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "pdl.cuh"
 #include "engine.cuh"
 #include "kv_pool.cuh"
 
@@ -59,6 +60,7 @@ __device__ __forceinline__ float sigm(float x) { return __fdiv_rn(1.f, __fadd_rn
 
 __global__ void embed_lanes_kernel(const float *__restrict__ rows, int lanes, int D, float scale,
                                    float *__restrict__ x) {
+    pdl_enter();
     const int r = blockIdx.x;
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         const float v = __fmul_rn(rows[(size_t)r * D + d], scale);
@@ -68,6 +70,7 @@ __global__ void embed_lanes_kernel(const float *__restrict__ rows, int lanes, in
 
 __global__ void gather_dense_kernel(const float *__restrict__ w, const int64_t *__restrict__ ids, int cols,
                                     float *__restrict__ out) {
+    pdl_enter();
     const int r = blockIdx.x;
     const float *src = w + (size_t)ids[r] * cols;
     for (int c = threadIdx.x; c < cols; c += blockDim.x) out[(size_t)r * cols + c] = src[c];
@@ -75,6 +78,7 @@ __global__ void gather_dense_kernel(const float *__restrict__ w, const int64_t *
 
 __global__ void rms_kernel(const float *__restrict__ x, int ldx, int n, const float *__restrict__ scale,
                            float *__restrict__ y, int ldy) {
+    pdl_enter();
     __shared__ float sh[33];
     const int r = blockIdx.x;
     const float *xr = x + (size_t)r * ldx;
@@ -95,6 +99,7 @@ struct DenseSegs {
 // One warp per matrix row, eight input rows per CTA.
 __global__ void __launch_bounds__(256) dense_rows_kernel(const DenseSegs segs, const float *__restrict__ in, int ldin,
                                                          int R, int cols) {
+    pdl_enter();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int j = blockIdx.x * 8 + warp;
     int si = 0;
@@ -123,6 +128,7 @@ __global__ void __launch_bounds__(256) mhc_pre_kernel(const MhcLayer L, const fl
                                                       const float *__restrict__ x, float *__restrict__ hpost,
                                                       float *__restrict__ u, float *__restrict__ bx,
                                                       float *__restrict__ z) {
+    pdl_enter();
     extern __shared__ float smem[];
     float *bxs = smem;                 // [D]
     __shared__ float hpre[kMaxLanes];
@@ -182,6 +188,7 @@ __global__ void __launch_bounds__(256) mhc_route_kernel(const MhcLayer L, const 
                                                         const float *__restrict__ x, int R, float *__restrict__ raw,
                                                         int ldraw, float *__restrict__ hpost, float *__restrict__ u,
                                                         float *__restrict__ bx, float *__restrict__ z) {
+    pdl_enter();
     extern __shared__ float smem[];
     const int N = L.lanes, D = L.D, ND = N * D;
     float *nx = smem;                              // [SB][ND]
@@ -285,6 +292,7 @@ __global__ void __launch_bounds__(256) mhc_route_kernel(const MhcLayer L, const 
 __global__ void qk_norm_rope_kernel(float *__restrict__ q, float *__restrict__ k, int heads, int kvheads, int hd,
                                     const float *__restrict__ q_norm, const float *__restrict__ k_norm,
                                     const int *__restrict__ pos, const float *__restrict__ divisor) {
+    pdl_enter();
     extern __shared__ float buf[];   // [warps][hd]
     const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const float fpos = (float)pos[r];
@@ -318,6 +326,7 @@ __global__ void qk_rope_store_kernel(float *__restrict__ q, float *__restrict__ 
                                      int heads, int kvheads, int hd, const float *__restrict__ q_norm,
                                      const float *__restrict__ k_norm, const int *__restrict__ pos,
                                      const float *__restrict__ divisor, const KVStoreTarget t) {
+    pdl_enter();
     extern __shared__ float buf[];   // [warps][hd]
     const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const float fpos = (float)pos[r];
@@ -379,6 +388,7 @@ __global__ void qk_rope_store_kernel(float *__restrict__ q, float *__restrict__ 
 }
 
 __global__ void gate_kernel(float *__restrict__ att, const float *__restrict__ gate, long long n) {
+    pdl_enter();
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         att[i] = __fmul_rn(att[i], sigm(gate[i]));
 }
@@ -452,6 +462,7 @@ __global__ void __launch_bounds__(256) mhc_post_kernel(const PostLayer L, const 
                                                        const float *__restrict__ hpost, const float *__restrict__ u,
                                                        const float *__restrict__ bx, float *__restrict__ x,
                                                        float *__restrict__ hidden, int ldh) {
+    pdl_enter();
     extern __shared__ float smem[];
     float *bxs = smem;             // [D]
     float *mlp = smem + L.D;       // [hada]
@@ -592,6 +603,7 @@ __global__ void __launch_bounds__(128) mhc_post_warp_kernel(const PostLayer L, c
                                                             const float *__restrict__ u, const float *__restrict__ bx,
                                                             float *__restrict__ x, int R, float *__restrict__ hidden,
                                                             int ldh) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= R) return;
@@ -681,6 +693,7 @@ __global__ void __launch_bounds__(128) mhc_post_warp_kernel(const PostLayer L, c
 
 __global__ void final_norm_kernel(const float *__restrict__ x, int lanes, int D, const float *__restrict__ fnorm,
                                   float *__restrict__ z) {
+    pdl_enter();
     extern __shared__ float zs[];
     __shared__ float sh[33];
     const int r = blockIdx.x;
@@ -705,6 +718,7 @@ __device__ __forceinline__ int engram_token(const EngramHash &h, int e, int p) {
 
 __global__ void engram_ids_kernel(const EngramHash h, const int *__restrict__ pos, int R, int64_t *__restrict__ ids,
                                   uint8_t *__restrict__ valid) {
+    pdl_enter();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (long long)R * h.tables) return;
     const int r = (int)(i / h.tables), t = (int)(i % h.tables);
@@ -723,12 +737,14 @@ __global__ void engram_ids_kernel(const EngramHash h, const int *__restrict__ po
 }
 
 __global__ void engram_mask_kernel(float *__restrict__ e, const uint8_t *__restrict__ valid, int subdim) {
+    pdl_enter();
     const long long rt = blockIdx.x;   // row * tables + table
     if (valid[rt]) return;
     for (int c = threadIdx.x; c < subdim; c += blockDim.x) e[rt * subdim + c] = 0.f;
 }
 
 __global__ void engram_conv_kernel(const EngramConv c, const int *__restrict__ pos, float *__restrict__ ev, int ldev) {
+    pdl_enter();
     const int r = blockIdx.x, e = r / c.T, p = pos[r], cs = c.chunk_start[e];
     for (int d = threadIdx.x; d < c.D; d += blockDim.x) {
         float sum = 0.f;
@@ -747,6 +763,7 @@ __global__ void engram_conv_kernel(const EngramConv c, const int *__restrict__ p
 __global__ void engram_ring_store_kernel(float *__restrict__ ring, size_t ld_ring_s, const float *__restrict__ raw,
                                          int ld_chunk, const int *__restrict__ chunk_start, int T, int keep,
                                          int engring, int D) {
+    pdl_enter();
     const int e = blockIdx.x, j = blockIdx.y;
     const int t = T - keep + j, position = chunk_start[e] + t;
     float *dst = ring + (size_t)e * ld_ring_s + (size_t)(position % engring) * D;
@@ -756,6 +773,7 @@ __global__ void engram_ring_store_kernel(float *__restrict__ ring, size_t ld_rin
 
 __global__ void history_store_kernel(int *__restrict__ ring, int cap, const int *__restrict__ tokens, int T,
                                      const int *__restrict__ chunk_start, int keep, int entries) {
+    pdl_enter();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= entries * keep) return;
     const int e = i / keep, t = T - keep + i % keep;
@@ -765,6 +783,7 @@ __global__ void history_store_kernel(int *__restrict__ ring, int cap, const int 
 
 __global__ void row_positions_kernel(const int *__restrict__ base, int entries, int T, int *__restrict__ sess,
                                      int *__restrict__ pos) {
+    pdl_enter();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= entries * T) return;
     if (sess) sess[r] = r / T;
@@ -772,16 +791,19 @@ __global__ void row_positions_kernel(const int *__restrict__ base, int entries, 
 }
 
 __global__ void advance_kernel(int *base, int n, int delta) {
+    pdl_enter();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) base[i] += delta;
 }
 
 __global__ void copy_tokens_kernel(const int *__restrict__ src, int n, int *__restrict__ dst, int ld) {
+    pdl_enter();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) dst[(size_t)i * ld] = src[i];
 }
 
 __global__ void widen_ids_kernel(const int *__restrict__ src, int64_t *__restrict__ dst, int n) {
+    pdl_enter();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) dst[i] = src[i];
 }
@@ -805,6 +827,7 @@ __global__ void candidates_f32_kernel(const uint8_t *__restrict__ packed, const 
                                       int rowbytes, int groups, int group, int storage_bits, const Lut lut,
                                       const float *__restrict__ rot, const int *__restrict__ cand, int n,
                                       float *__restrict__ out) {
+    pdl_enter();
     const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (i >= n) return;
     const int row = cand[i];
@@ -829,6 +852,7 @@ __global__ void candidates_i8_kernel(const uint8_t *__restrict__ packed, const u
                                      int rowbytes, int groups, int group, int bits, const Ctab ctab, float cs,
                                      const int8_t *__restrict__ q, const float *__restrict__ xs,
                                      const int *__restrict__ cand, int n, float *__restrict__ out) {
+    pdl_enter();
     const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (i >= n) return;
     int8_t cent[16];
@@ -856,21 +880,21 @@ inline unsigned blocks_for(long long n, int threads) { return (unsigned)((n + th
 
 bool launch_embed_lanes(const float *rows, int R, int lanes, int D, float scale, float *x, cudaStream_t st) {
     if (R <= 0) return true;
-    embed_lanes_kernel<<<R, 256, 0, st>>>(rows, lanes, D, scale, x);
+    NB_CUDA_TRY(launch_pdl(embed_lanes_kernel, R, 256, 0, st, rows, lanes, D, scale, x));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
 
 bool launch_gather_dense(const float *w, const int64_t *ids, int R, int cols, float *out, cudaStream_t st) {
     if (R <= 0) return true;
-    gather_dense_kernel<<<R, 256, 0, st>>>(w, ids, cols, out);
+    NB_CUDA_TRY(launch_pdl(gather_dense_kernel, R, 256, 0, st, w, ids, cols, out));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
 
 bool launch_rms(const float *x, int ldx, int R, int n, const float *scale, float *y, int ldy, cudaStream_t st) {
     if (R <= 0) return true;
-    rms_kernel<<<R, 256, 0, st>>>(x, ldx, n, scale, y, ldy);
+    NB_CUDA_TRY(launch_pdl(rms_kernel, R, 256, 0, st, x, ldx, n, scale, y, ldy));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -886,7 +910,7 @@ bool launch_dense_rows(const DenseSeg *segs, int nseg, const float *in, int ldin
     }
     s.n = nseg;
     const dim3 grid((rows + 7) / 8, (R + 7) / 8);
-    dense_rows_kernel<<<grid, 256, 0, st>>>(s, in, ldin, R, cols);
+    NB_CUDA_TRY(launch_pdl(dense_rows_kernel, grid, 256, 0, st, s, in, ldin, R, cols));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -894,7 +918,7 @@ bool launch_dense_rows(const DenseSeg *segs, int nseg, const float *in, int ldin
 bool launch_mhc_pre(const MhcLayer &L, const float *raw, int ldraw, const float *x, int R, float *hpost, float *u,
                     float *bx, float *z, cudaStream_t st) {
     if (R <= 0) return true;
-    mhc_pre_kernel<<<R, 256, sizeof(float) * L.D, st>>>(L, raw, ldraw, x, hpost, u, bx, z);
+    NB_CUDA_TRY(launch_pdl(mhc_pre_kernel, R, 256, sizeof(float) * L.D, st, L, raw, ldraw, x, hpost, u, bx, z));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -919,8 +943,8 @@ bool launch_mhc_route(const MhcLayer &L, const float *phi_pre, const float *phi_
                                              200 * 1024));                                                         \
             configured = true;                                                                                     \
         }                                                                                                          \
-        mhc_route_kernel<SB><<<grid, 256, smem, st>>>(L, phi_pre, phi_post, phi_res, x, R, raw, ldraw, hpost, u,   \
-                                                      bx, z);                                                      \
+        NB_CUDA_TRY(launch_pdl(mhc_route_kernel<SB>, grid, 256, smem, st, L, phi_pre, phi_post, phi_res, x, R, raw, ldraw, hpost, u,   \
+                                                      bx, z));                                                      \
     }
     switch (sb) {
         case 8: NB_ROUTE(8) break;
@@ -937,8 +961,8 @@ bool launch_qk_norm_rope(float *q, float *k, int R, int heads, int kvheads, int 
                          const float *k_norm, const int *pos, const float *divisor, cudaStream_t st) {
     if (R <= 0) return true;
     const int warps = std::min(heads + kvheads, 16);
-    qk_norm_rope_kernel<<<R, 32 * warps, sizeof(float) * warps * hd, st>>>(q, k, heads, kvheads, hd, q_norm, k_norm,
-                                                                         pos, divisor);
+    NB_CUDA_TRY(launch_pdl(qk_norm_rope_kernel, R, 32 * warps, sizeof(float) * warps * hd, st, q, k, heads, kvheads, hd, q_norm, k_norm,
+                                                                         pos, divisor));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -948,8 +972,8 @@ bool launch_qk_rope_store(float *q, float *k, const float *v, int R, int heads, 
                           const KVStoreTarget &t, cudaStream_t st) {
     if (R <= 0) return true;
     const int warps = std::min(heads + 2 * kvheads, 32);
-    qk_rope_store_kernel<<<R, 32 * warps, sizeof(float) * warps * hd, st>>>(q, k, v, heads, kvheads, hd, q_norm,
-                                                                           k_norm, pos, divisor, t);
+    NB_CUDA_TRY(launch_pdl(qk_rope_store_kernel, R, 32 * warps, sizeof(float) * warps * hd, st, q, k, v, heads, kvheads, hd, q_norm,
+                                                                           k_norm, pos, divisor, t));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -957,7 +981,7 @@ bool launch_qk_rope_store(float *q, float *k, const float *v, int R, int heads, 
 bool launch_gate(float *att, const float *gate, int R, int A, cudaStream_t st) {
     const long long n = (long long)R * A;
     if (n <= 0) return true;
-    gate_kernel<<<std::min<unsigned>(blocks_for(n, 256), 4096), 256, 0, st>>>(att, gate, n);
+    NB_CUDA_TRY(launch_pdl(gate_kernel, std::min<unsigned>(blocks_for(n, 256), 4096), 256, 0, st, att, gate, n));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -968,7 +992,7 @@ bool launch_mhc_post(const PostLayer &L, const float *proj, const float *raw, in
     // warp per row where the Hadamard width is 32 * E and the lane count N are supported
     const unsigned grid = (unsigned)((R + 3) / 4);
 #define NB_POST(E, N)                                                                                     \
-    mhc_post_warp_kernel<E, N><<<grid, 128, 0, st>>>(L, proj, raw, ldraw, hpost, u, bx, x, R, hidden, ldh); \
+    NB_CUDA_TRY(launch_pdl(mhc_post_warp_kernel<E, N>, grid, 128, 0, st, L, proj, raw, ldraw, hpost, u, bx, x, R, hidden, ldh)); \
     break;
 #define NB_POST_LANES(E)                    \
     switch (L.lanes) {                      \
@@ -990,15 +1014,15 @@ bool launch_mhc_post(const PostLayer &L, const float *proj, const float *raw, in
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 block_kernel:
-    mhc_post_kernel<<<R, 256, sizeof(float) * (L.D + L.hada), st>>>(L, proj, raw, ldraw, hpost, u, bx, x, hidden,
-                                                                     ldh);
+    NB_CUDA_TRY(launch_pdl(mhc_post_kernel, R, 256, sizeof(float) * (L.D + L.hada), st, L, proj, raw, ldraw, hpost, u, bx, x, hidden,
+                                                                     ldh));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
 
 bool launch_final_norm(const float *x, int R, int lanes, int D, const float *final_norm, float *z, cudaStream_t st) {
     if (R <= 0) return true;
-    final_norm_kernel<<<R, 256, sizeof(float) * D, st>>>(x, lanes, D, final_norm, z);
+    NB_CUDA_TRY(launch_pdl(final_norm_kernel, R, 256, sizeof(float) * D, st, x, lanes, D, final_norm, z));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -1008,7 +1032,7 @@ bool launch_engram_ids(const EngramHash &h, const int *sess, const int *pos, int
     (void)sess;
     const long long n = (long long)R * h.tables;
     if (n <= 0) return true;
-    engram_ids_kernel<<<blocks_for(n, 128), 128, 0, st>>>(h, pos, R, ids, valid);
+    NB_CUDA_TRY(launch_pdl(engram_ids_kernel, blocks_for(n, 128), 128, 0, st, h, pos, R, ids, valid));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -1016,7 +1040,7 @@ bool launch_engram_ids(const EngramHash &h, const int *sess, const int *pos, int
 bool launch_engram_mask(float *e, const uint8_t *valid, int R, int tables, int subdim, cudaStream_t st) {
     const long long n = (long long)R * tables;
     if (n <= 0) return true;
-    engram_mask_kernel<<<(unsigned)n, 128, 0, st>>>(e, valid, subdim);
+    NB_CUDA_TRY(launch_pdl(engram_mask_kernel, (unsigned)n, 128, 0, st, e, valid, subdim));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -1025,7 +1049,7 @@ bool launch_engram_conv(const EngramConv &c, const int *sess, const int *pos, in
                         cudaStream_t st) {
     (void)sess;
     if (R <= 0) return true;
-    engram_conv_kernel<<<R, 256, 0, st>>>(c, pos, ev, ldev);
+    NB_CUDA_TRY(launch_pdl(engram_conv_kernel, R, 256, 0, st, c, pos, ev, ldev));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -1036,8 +1060,8 @@ bool launch_engram_ring_store(float *ring, size_t ld_ring_s, const float *chunk_
     (void)sess_of_entry;
     const int keep = std::min(T, engring);
     if (S_count <= 0 || keep <= 0) return true;
-    engram_ring_store_kernel<<<dim3(S_count, keep), 256, 0, st>>>(ring, ld_ring_s, chunk_raw, ld_chunk, chunk_start, T,
-                                                                  keep, engring, D);
+    NB_CUDA_TRY(launch_pdl(engram_ring_store_kernel, dim3(S_count, keep), 256, 0, st, ring, ld_ring_s, chunk_raw, ld_chunk, chunk_start, T,
+                                                                  keep, engring, D));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -1047,8 +1071,8 @@ bool launch_history_store(int *ring, int cap, const int *tokens, int T, const in
     (void)sess;
     const int keep = std::min(T, cap);
     if (entries <= 0 || keep <= 0) return true;
-    history_store_kernel<<<blocks_for((long long)entries * keep, 128), 128, 0, st>>>(ring, cap, tokens, T, chunk_start,
-                                                                                    keep, entries);
+    NB_CUDA_TRY(launch_pdl(history_store_kernel, blocks_for((long long)entries * keep, 128), 128, 0, st, ring, cap, tokens, T, chunk_start,
+                                                                                    keep, entries));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -1059,8 +1083,8 @@ bool launch_candidates_f32(const uint8_t *packed, const uint16_t *norms, int row
     if (n <= 0) return true;
     Lut lut;
     for (int i = 0; i < 16; ++i) lut.v[i] = lut_in[i];
-    candidates_f32_kernel<<<blocks_for((long long)n * 32, 256), 256, 0, st>>>(packed, norms, rowbytes, groups, group,
-                                                                             storage_bits, lut, rot, cand, n, out);
+    NB_CUDA_TRY(launch_pdl(candidates_f32_kernel, blocks_for((long long)n * 32, 256), 256, 0, st, packed, norms, rowbytes, groups, group,
+                                                                             storage_bits, lut, rot, cand, n, out));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -1071,8 +1095,8 @@ bool launch_candidates_i8(const uint8_t *packed, const uint16_t *norms, int rowb
     if (n <= 0) return true;
     Ctab ctab;
     for (int i = 0; i < 4; ++i) ctab.w[i] = ctab_in[i];
-    candidates_i8_kernel<<<blocks_for((long long)n * 32, 256), 256, 0, st>>>(packed, norms, rowbytes, groups, group,
-                                                                            bits, ctab, cs, q, xs, cand, n, out);
+    NB_CUDA_TRY(launch_pdl(candidates_i8_kernel, blocks_for((long long)n * 32, 256), 256, 0, st, packed, norms, rowbytes, groups, group,
+                                                                            bits, ctab, cs, q, xs, cand, n, out));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
@@ -1080,28 +1104,28 @@ bool launch_candidates_i8(const uint8_t *packed, const uint16_t *norms, int rowb
 bool launch_row_positions(const int *base, int entries, int T, int *sess_out, int *pos_out, cudaStream_t st) {
     const long long n = (long long)entries * T;
     if (n <= 0) return true;
-    row_positions_kernel<<<blocks_for(n, 256), 256, 0, st>>>(base, entries, T, sess_out, pos_out);
+    NB_CUDA_TRY(launch_pdl(row_positions_kernel, blocks_for(n, 256), 256, 0, st, base, entries, T, sess_out, pos_out));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
 
 bool launch_advance(int *base, int n, int delta, cudaStream_t st) {
     if (n <= 0) return true;
-    advance_kernel<<<blocks_for(n, 256), 256, 0, st>>>(base, n, delta);
+    NB_CUDA_TRY(launch_pdl(advance_kernel, blocks_for(n, 256), 256, 0, st, base, n, delta));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
 
 bool launch_widen_ids(const int *src, int64_t *dst, int n, cudaStream_t st) {
     if (n <= 0) return true;
-    widen_ids_kernel<<<blocks_for(n, 256), 256, 0, st>>>(src, dst, n);
+    NB_CUDA_TRY(launch_pdl(widen_ids_kernel, blocks_for(n, 256), 256, 0, st, src, dst, n));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
 
 bool launch_copy_tokens(const int *src, int n, int *dst, int ld_dst, cudaStream_t st) {
     if (n <= 0) return true;
-    copy_tokens_kernel<<<blocks_for(n, 256), 256, 0, st>>>(src, n, dst, ld_dst);
+    NB_CUDA_TRY(launch_pdl(copy_tokens_kernel, blocks_for(n, 256), 256, 0, st, src, n, dst, ld_dst));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }
