@@ -325,9 +325,12 @@ int needle2_batch_positions(void *batch, int *positions);
  * the pass's stream) while enabled; enabling or disabling clears the totals.
  * profile_read returns the milliseconds per stage since the last read and
  * clears them (synchronises): 0 engrams and embedding, 1 mHC routing (lane
- * RMS, projections, gates), 2 Q/K/V/gate projections, 3 QK norm and RoPE,
- * 4 KV store and attention, 5 gate and out projection, 6 Hadamard MLP and
- * lane mixing, 7 final norm, LM head and greedy choice. */
+ * RMS, projections, gates) where it runs on its own (the first layer, or
+ * geometries without the fused layer boundary), 2 Q/K/V/gate projections,
+ * 3 QK norm and RoPE, 4 KV store and attention, 5 out projection, 6 Hadamard
+ * MLP and lane mixing, with the next layer's routing (or the final norm)
+ * where the layer boundary is one kernel, 7 final norm (where separate), LM
+ * head and greedy choice. */
 int needle2_batch_profile(void *batch, int enable);
 int needle2_batch_profile_read(void *batch, double *ms, int n);
 

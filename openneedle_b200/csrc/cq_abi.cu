@@ -663,6 +663,38 @@ bool many_host(Matrix *const *ms, int count, const float *x, float *const *ys, i
 }
 
 }  // namespace
+
+// (this block sits inside the file's extern "C" region; these are C++ functions)
+extern "C++" {
+bool handle_hilo_gemm(void *const *hs, int count, int batch, int *group, float *scale) {
+    if (count < 1 || batch < kGemmMinRows) return false;
+    std::vector<Matrix *> ms(count);
+    for (int i = 0; i < count; ++i) ms[i] = static_cast<Matrix *>(hs[i]);
+    if (!ms[0] || ms[0]->sdot || !fusable(ms.data(), count)) return false;
+    const CQDevice &w = ms[0]->w;
+    if (!gemm_f32_supported(w.storage_bits, w.padded) || w.group > 1024 || w.padded != w.in) return false;
+    if (group) *group = w.group;
+    if (scale) *scale = 1.0f / sqrtf((float)w.group);   // the rotation's scale (launch_rotate_impl)
+    return true;
+}
+
+bool handle_many_hilo(void *const *hs, int count, const uint16_t *a_hilo, float *const *ys, int batch,
+                      cudaStream_t st) {
+    if (!handle_hilo_gemm(hs, count, batch, nullptr, nullptr)) {
+        set_error("these matrices do not take pre-split bf16 activations");
+        return false;
+    }
+    std::vector<F32Out> outs(count);
+    for (int i = 0; i < count; ++i) {
+        auto *m = static_cast<Matrix *>(hs[i]);
+        m->prepared = 0;
+        if (!ensure_f32_copy(m, st)) return false;
+        outs[i] = F32Out{m->d_whl, m->w.out, ys[i], m->w.out};
+    }
+    return launch_gemm_f32x3_multi(a_hilo, batch, static_cast<Matrix *>(hs[0])->w.padded, outs.data(), count, st);
+}
+}  // extern "C++"
+
 }  // namespace nb200
 
 void needle2_cq_linear_many(void *const *handles, int count, const float *x, float *const *ys, int threads,

@@ -476,18 +476,22 @@ bool make_map(CUtensorMap *map, const void *base, int rows, int cols, int box_ro
 // hi = bf16(v) and lo = bf16(v - hi), and each K step issues three
 // kind::f16 MMAs, A_hi B_hi + A_lo B_hi + A_hi B_lo, into one f32 accumulator
 // (about 2^-16 relative error per product; bf16 keeps FP32's exponent range).
-// 128 x 256 tiles, K = 64 (one 128-byte row of bf16) per stage, two stages of
-// 96 KB; warp 0 issues the TMA loads, warp 1 the MMAs, warps 2-5 read the
-// accumulator (32 rows each) and store y.
+// 128 x 256 tiles with K = 64 (one 128-byte row of bf16) per stage, two
+// stages of 96 KB; or, for decode-sized launches, 128 x 64 tiles with two
+// stages of 48 KB (two CTAs per SM) or, where the grid fits one CTA per SM,
+// four, so that half of a K = 512 product is in flight at once.
+// Warp 0 issues the TMA loads (the weight tiles of the first stages before the
+// kernel waits for its predecessor, which produces only the activations),
+// warp 1 the MMAs, warps 2-5 read the accumulator (32 rows each) and store y.
 constexpr int kFBM = 128, kFBK = 64;
-constexpr int kFStages = 2;
 constexpr int kFPartA = kFBM * kFBK * 2;   // bytes of one bf16 part of the activation tile
 constexpr int kFThreads = 6 * 32;
-template <int BN>
+template <int BN, int ST>
 struct FTile {
+    static constexpr int kStages = ST;
     static constexpr int kPartB = BN * kFBK * 2;
     static constexpr int kStageBytes = 2 * kFPartA + 2 * kPartB;
-    static constexpr size_t kSmem = (size_t)kFStages * kStageBytes + 1024;
+    static constexpr size_t kSmem = (size_t)kStages * kStageBytes + 1024;
 };
 
 // One output matrix of a launch: its bf16 hi/lo weight maps, y[M][ldy] and
@@ -505,11 +509,12 @@ struct GemmF32Args {
 
 // grid: (M tiles, total N tiles of all segments); tile width BN (256 for
 // prefill-sized launches, 64 when that leaves too few CTAs for the machine).
-template <int BN>
+template <int BN, int ST>
 __global__ void __launch_bounds__(kFThreads, 1)
     cq_gemm_f32x3_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
                          const __grid_constant__ GemmF32Args a) {
-    constexpr int kPartB = FTile<BN>::kPartB, kStageBytes = FTile<BN>::kStageBytes;
+    constexpr int kPartB = FTile<BN, ST>::kPartB, kStageBytes = FTile<BN, ST>::kStageBytes;
+    constexpr int kFStages = ST;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ __align__(8) uint64_t full[kFStages], empty[kFStages], dfull;
@@ -539,17 +544,28 @@ __global__ void __launch_bounds__(kFThreads, 1)
 
     if (warp == 0) {
         if (lane == 0) {
+            // weights of the first stages: they do not depend on the preceding kernel
+            const int pre = S < kFStages ? S : kFStages;
+            for (int k = 0; k < pre; ++k) {
+                uint8_t *st = smem + (size_t)k * kStageBytes;
+                mbar_arrive_expect_tx(&full[k], kStageBytes);
+                const int x = k * kFBK * 2;
+                tma_load_2d(st + 2 * kFPartA, &sg.bh, x, n0, &full[k]);
+                tma_load_2d(st + 2 * kFPartA + kPartB, &sg.bl, x, n0, &full[k]);
+            }
             pdl_wait();
             for (int k = 0; k < S && !abort_flag; ++k) {
                 const int s = k % kFStages;
-                if (k >= kFStages && !gwait(&empty[s], (uint32_t)((k / kFStages) - 1) & 1, &abort_flag)) break;
                 uint8_t *st = smem + (size_t)s * kStageBytes;
-                mbar_arrive_expect_tx(&full[s], kStageBytes);
                 const int x = k * kFBK * 2;   // byte column of this K step
+                if (k >= kFStages) {
+                    if (!gwait(&empty[s], (uint32_t)((k / kFStages) - 1) & 1, &abort_flag)) break;
+                    mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    tma_load_2d(st + 2 * kFPartA, &sg.bh, x, n0, &full[s]);
+                    tma_load_2d(st + 2 * kFPartA + kPartB, &sg.bl, x, n0, &full[s]);
+                }
                 tma_load_2d(st, &tah, x, m0, &full[s]);
                 tma_load_2d(st + kFPartA, &tal, x, m0, &full[s]);
-                tma_load_2d(st + 2 * kFPartA, &sg.bh, x, n0, &full[s]);
-                tma_load_2d(st + 2 * kFPartA + kPartB, &sg.bl, x, n0, &full[s]);
             }
         }
         __syncwarp();
@@ -801,25 +817,20 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    static bool configured[2][64] = {};
-    if (narrow) {
-        if (dev < 0 || dev >= 64 || !configured[0][dev]) {
-            NB_CUDA_TRY(cudaFuncSetAttribute(cq_gemm_f32x3_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)FTile<64>::kSmem));
-            if (dev >= 0 && dev < 64) configured[0][dev] = true;
+    static bool configured[3][64] = {};
+    auto launch = [&](auto kernel, size_t smem, int which) -> bool {
+        if (dev < 0 || dev >= 64 || !configured[which][dev]) {
+            NB_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            if (dev >= 0 && dev < 64) configured[which][dev] = true;
         }
-        cfg.dynamicSmemBytes = FTile<64>::kSmem;
-        NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, cq_gemm_f32x3_kernel<64>, tah, tal, args));
-    } else {
-        if (dev < 0 || dev >= 64 || !configured[1][dev]) {
-            NB_CUDA_TRY(cudaFuncSetAttribute(cq_gemm_f32x3_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)FTile<256>::kSmem));
-            if (dev >= 0 && dev < 64) configured[1][dev] = true;
-        }
-        cfg.dynamicSmemBytes = FTile<256>::kSmem;
-        NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, cq_gemm_f32x3_kernel<256>, tah, tal, args));
-    }
-    return true;
+        cfg.dynamicSmemBytes = smem;
+        NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, tah, tal, args));
+        return true;
+    };
+    if (!narrow) return launch(cq_gemm_f32x3_kernel<256, 2>, FTile<256, 2>::kSmem, 0);
+    // one CTA per SM with the deep pipeline while the grid fits the machine
+    if ((long long)mtiles * tiles <= sms) return launch(cq_gemm_f32x3_kernel<64, 4>, FTile<64, 4>::kSmem, 1);
+    return launch(cq_gemm_f32x3_kernel<64, 2>, FTile<64, 2>::kSmem, 2);
 }
 
 bool launch_gemm_f32x3(const uint16_t *a_hilo, int M, const uint16_t *w_hilo, int N, int padded, float *y, int ldy,

@@ -18,6 +18,14 @@ int handle_device(void *handle);
 // [batch][padded] (CQ2 in bit-plane order) and xs [batch][groups] (int8).
 bool handle_prepare(void *handle, const float *x, int batch, const float **rot, const int8_t **q, const float **xs,
                     cudaStream_t st);
+// Whether y_i = W_i x for these FP32 handles and `batch` rows runs the
+// tensor-core GEMM on activations rotated and split into bf16 hi/lo (true:
+// *group and *scale are the rotation's group size and 1/sqrt(group)).
+bool handle_hilo_gemm(void *const *hs, int count, int batch, int *group, float *scale);
+// That GEMM on activations the caller rotated and split: a_hilo [batch][in]
+// bf16 hi, then [batch][in] lo (in = the matrices' padded width).
+bool handle_many_hilo(void *const *hs, int count, const uint16_t *a_hilo, float *const *ys, int batch,
+                      cudaStream_t st);
 // A new int8 (SDOT) handle over the same packed matrix as the FP32 handle
 // `cq` (its device copy read back once), or null with the error set.
 void *handle_make_sdot(void *cq);

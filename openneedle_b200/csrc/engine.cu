@@ -120,6 +120,7 @@ struct Model {
 // Scratch of one forward pass, grown to the largest row count seen.
 struct Scratch {
     DevBuf<float> x, nx, raw, hpost, u, bx, z, q, k, v, gate, att, proj, e, ek, ev, rawv, zf, logits, hidden;
+    DevBuf<uint16_t> zhl;   // z rotated and split into the QKVG GEMM's bf16 operands
     DevBuf<int64_t> ids;
     DevBuf<uint8_t> valid;
     DevBuf<int> rsess, rpos, tokens, argmax;
@@ -529,10 +530,16 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
 
     if (o.hidden) s.hidden.reserve((size_t)R * c.layers * D);
     const int mh = m.mh();
-    for (int l = 0; l < c.layers; ++l) {
-        const int ti = 1 + 14 * l;
-        mark(st, 1, stream);
+    // Layer boundaries run as one kernel (post-attention part of layer l, then
+    // the routing of layer l + 1 or the final norm) where the geometry allows.
+    const bool mix = eng::mhc_mix_supported(D, N, c.hada);
+    const bool every = o.all_logits;
+    const int rows = every ? R : E;
+    const bool want_z = o.logits || o.keep_z;
+    const bool mix_final = mix && want_z && (every || T == 1);
+    auto route_layer = [&](int l) {
         eng::MhcLayer ml{};
+        const int ti = 1 + 14 * l;
         ml.layer = l; ml.lanes = N; ml.D = D;
         ml.a_pre = m.t[mh].host[l]; ml.a_post = m.t[mh + 1].host[l]; ml.a_res = m.t[mh + 2].host[l];
         ml.b_pre = m.t[mh + 3].dense + (size_t)l * N;
@@ -545,23 +552,89 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
                 ml.ev = s.ev.ptr + (size_t)site * R * D;
                 ml.ld_site = D;
             }
-        const bool routed = eng::launch_mhc_route(ml, m.t[mh + 6].dense, m.t[mh + 7].dense, m.t[mh + 8].dense, s.x.ptr,
-                                                  R, s.raw.ptr, ldraw, s.hpost.ptr, s.u.ptr, s.bx.ptr, s.z.ptr, m.sms,
-                                                  stream);
+        return ml;
+    };
+    auto post_layer = [&](int l, int routed) {
+        const int ti = 1 + 14 * l;
+        eng::PostLayer pl{};
+        pl.layer = l; pl.lanes = N; pl.D = D; pl.hada = c.hada; pl.a_res = m.t[mh + 2].host[l];
+        pl.b_res = m.t[mh + 5].dense + (size_t)l * N * N;
+        pl.hres_ready = routed;
+        pl.post_norm = m.t[ti + 8].dense; pl.attn_gate = m.t[ti + 9].dense; pl.pre_hada = m.t[ti + 10].dense;
+        pl.d1 = m.t[ti + 11].dense; pl.d2 = m.t[ti + 12].dense; pl.d3 = m.t[ti + 13].dense;
+        return pl;
+    };
+    // the routed z of each layer is also written rotated and split into the
+    // QKVG GEMM's bf16 operands when that GEMM takes them
+    auto qkvg_handles = [&](int l, void **hs) {
+        const int ti = 1 + 14 * l;
+        const int ids[4] = {ti + 1, ti + 2, ti + 3, ti + 6};
+        for (int j = 0; j < 4; ++j) {
+            if (!m.t[ids[j]].cq) return false;
+            hs[j] = m.handle(ids[j]);
+        }
+        return true;
+    };
+    auto zhl_for = [&](int l, eng::MixArgs &a) {
+        void *hs[4];
+        int G = 0;
+        float sc = 0.f;
+        a.zhl = nullptr;
+        if (m.abits || !qkvg_handles(l, hs) || !handle_hilo_gemm(hs, 4, R, &G, &sc) || D % G) return false;
+        s.zhl.reserve(2 * (size_t)R * D);
+        a.zhl = s.zhl.ptr; a.lo_off = (long long)R * D; a.group = G; a.rot_scale = sc;
+        return true;
+    };
+    auto mix_args = [&]() {
+        eng::MixArgs a{};
+        a.D = D; a.lanes = N; a.hada = c.hada;
+        a.phi_pre = m.t[mh + 6].dense; a.phi_post = m.t[mh + 7].dense; a.phi_res = m.t[mh + 8].dense;
+        a.proj = s.proj.ptr; a.raw = s.raw.ptr; a.ldraw = ldraw; a.hpost = s.hpost.ptr; a.u = s.u.ptr;
+        a.bx = s.bx.ptr; a.x = s.x.ptr; a.z = s.z.ptr;
+        return a;
+    };
+    bool routed = false, zhl_ready = false, final_done = false;
+    for (int l = 0; l < c.layers; ++l) {
+        const int ti = 1 + 14 * l;
         if (!routed) {
-            check(last_error()[0] == 0, "mHC routing");
-            check(eng::launch_rms(s.x.ptr, N * D, R, N * D, nullptr, s.nx.ptr, N * D, stream), "lane rms");
-            eng::DenseSeg segs[3] = {{m.t[mh + 6].dense, l * N, N, s.raw.ptr, ldraw},
-                                     {m.t[mh + 7].dense, l * N, N, s.raw.ptr + N, ldraw},
-                                     {m.t[mh + 8].dense, l * N * N, N * N, s.raw.ptr + 2 * N, ldraw}};
-            check(eng::launch_dense_rows(segs, 3, s.nx.ptr, N * D, R, N * D, stream), "mHC projections");
-            check(eng::launch_mhc_pre(ml, s.raw.ptr, ldraw, s.x.ptr, R, s.hpost.ptr, s.u.ptr, s.bx.ptr, s.z.ptr,
-                                      stream),
-                  "mHC routing");
+            mark(st, 1, stream);
+            const eng::MhcLayer ml = route_layer(l);
+            bool done = false;
+            if (mix) {
+                eng::MixArgs a = mix_args();
+                a.has_route = 1; a.route = ml;
+                zhl_ready = zhl_for(l, a);
+                done = eng::launch_mhc_mix(a, R, m.sms, stream);
+                check(done || last_error()[0] == 0, "mHC routing");
+                zhl_ready = zhl_ready && done;
+            }
+            if (!done) {
+                zhl_ready = false;
+                done = eng::launch_mhc_route(ml, m.t[mh + 6].dense, m.t[mh + 7].dense, m.t[mh + 8].dense, s.x.ptr, R,
+                                             s.raw.ptr, ldraw, s.hpost.ptr, s.u.ptr, s.bx.ptr, s.z.ptr, m.sms, stream);
+                check(done || last_error()[0] == 0, "mHC routing");
+            }
+            if (!done) {
+                check(eng::launch_rms(s.x.ptr, N * D, R, N * D, nullptr, s.nx.ptr, N * D, stream), "lane rms");
+                eng::DenseSeg segs[3] = {{m.t[mh + 6].dense, l * N, N, s.raw.ptr, ldraw},
+                                         {m.t[mh + 7].dense, l * N, N, s.raw.ptr + N, ldraw},
+                                         {m.t[mh + 8].dense, l * N * N, N * N, s.raw.ptr + 2 * N, ldraw}};
+                check(eng::launch_dense_rows(segs, 3, s.nx.ptr, N * D, R, N * D, stream), "mHC projections");
+                check(eng::launch_mhc_pre(ml, s.raw.ptr, ldraw, s.x.ptr, R, s.hpost.ptr, s.u.ptr, s.bx.ptr, s.z.ptr,
+                                          stream),
+                      "mHC routing");
+            }
+            routed = done;   // raw's residual part holds the normalised mixing matrix
         }
         aq(m, s.z.ptr, R, D, stream);
         mark(st, 2, stream);
-        projections(m, ti, s.z.ptr, R, s.q.ptr, s.k.ptr, s.v.ptr, s.gate.ptr, stream);
+        void *hs[4];
+        if (zhl_ready && qkvg_handles(l, hs)) {
+            float *outs[4] = {s.q.ptr, s.k.ptr, s.v.ptr, s.gate.ptr};
+            check(handle_many_hilo(hs, 4, s.zhl.ptr, outs, R, stream), "QKVG projections");
+        } else {
+            projections(m, ti, s.z.ptr, R, s.q.ptr, s.k.ptr, s.v.ptr, s.gate.ptr, stream);
+        }
         mark(st, 3, stream);
         if (T == 1) {
             // decode: the new token's K/V stored as RoPE finishes, then attention alone
@@ -582,25 +655,42 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         mark(st, 5, stream);
         aq(m, s.att.ptr, R, A, stream);
         linear(m, ti + 7, s.att.ptr, R, s.proj.ptr, stream);
-        eng::PostLayer pl{};
-        pl.layer = l; pl.lanes = N; pl.D = D; pl.hada = c.hada; pl.a_res = ml.a_res; pl.b_res = ml.b_res;
-        pl.hres_ready = routed ? 1 : 0;
-        pl.post_norm = m.t[ti + 8].dense; pl.attn_gate = m.t[ti + 9].dense; pl.pre_hada = m.t[ti + 10].dense;
-        pl.d1 = m.t[ti + 11].dense; pl.d2 = m.t[ti + 12].dense; pl.d3 = m.t[ti + 13].dense;
         mark(st, 6, stream);
         float *hid = o.hidden ? s.hidden.ptr + (size_t)l * D : nullptr;
-        check(eng::launch_mhc_post(pl, s.proj.ptr, s.raw.ptr, ldraw, s.hpost.ptr, s.u.ptr, s.bx.ptr, s.x.ptr, R, hid,
-                                   c.layers * D, stream),
-              "mHC mixing");
+        const bool last = l + 1 == c.layers;
+        bool fused = false;
+        if (mix && routed) {
+            eng::MixArgs a = mix_args();
+            a.has_post = 1; a.post = post_layer(l, 1);
+            a.hidden = hid; a.ldh = c.layers * D;
+            if (!last) {
+                a.has_route = 1; a.route = route_layer(l + 1);
+                zhl_ready = zhl_for(l + 1, a);
+            } else if (mix_final) {
+                s.zf.reserve((size_t)R * D);
+                a.final_norm = 1; a.fnorm = m.t[m.final_norm()].dense; a.zf = s.zf.ptr;
+            }
+            fused = eng::launch_mhc_mix(a, R, m.sms, stream);
+            check(fused || last_error()[0] == 0, "mHC mixing");
+            if (fused) final_done = last && a.final_norm;
+            zhl_ready = zhl_ready && fused;
+        }
+        if (!fused) {
+            zhl_ready = false;
+            check(eng::launch_mhc_post(post_layer(l, routed ? 1 : 0), s.proj.ptr, s.raw.ptr, ldraw, s.hpost.ptr,
+                                       s.u.ptr, s.bx.ptr, s.x.ptr, R, hid, c.layers * D, stream),
+                  "mHC mixing");
+        }
+        routed = fused && !last;
     }
 
     // final norm (engine.cpp:1039-1041) on every row or each entry's last token
     mark(st, 7, stream);
-    const bool every = o.all_logits;
-    const int rows = every ? R : E;
-    if (o.logits || o.keep_z) {
+    if (want_z) {
         s.zf.reserve((size_t)rows * D);
-        if (every || T == 1) {
+        if (final_done) {
+            // made by the last layer's boundary kernel for every row (rows == R here)
+        } else if (every || T == 1) {
             check(eng::launch_final_norm(s.x.ptr, rows, N, D, m.t[m.final_norm()].dense, s.zf.ptr, stream), "final norm");
         } else {
             for (int e = 0; e < E; ++e)

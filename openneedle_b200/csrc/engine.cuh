@@ -90,6 +90,37 @@ struct PostLayer {
 bool launch_mhc_post(const PostLayer &L, const float *proj, const float *raw, int ldraw, const float *hpost,
                      const float *u, float *bx, float *x, int R, float *hidden, int ldh, cudaStream_t st);
 
+// One launch at a layer boundary: the post-attention part of layer post.layer
+// (has_post; launch_mhc_post), then the routing of layer route.layer
+// (has_route; launch_mhc_route, with the Sinkhorn-normalised residual matrix
+// written into raw) or the final norm (final_norm; launch_final_norm).  Each
+// CTA owns whole rows, so the lane state stays on chip between the halves.
+struct MixArgs {
+    int D, lanes, hada;
+    int has_post, has_route, final_norm;
+    PostLayer post;                 // has_post (hres_ready must be 1)
+    MhcLayer route;                 // has_route
+    const float *phi_pre, *phi_post, *phi_res;   // the routing projections of every layer
+    const float *proj;              // post: out-projection output [R][D]
+    float *raw;                     // post reads layer l's mixing matrix; route writes layer l + 1's values
+    int ldraw;
+    float *hpost, *u, *bx;          // post reads layer l's; route writes layer l + 1's
+    float *x;                       // [R][lanes][D] lane state, updated in place
+    float *z;                       // route: z [R][D]
+    float *hidden;                  // post: lane means [R][ldh] (optional)
+    int ldh;
+    const float *fnorm;             // final: final_norm weights
+    float *zf;                      // final: [R][D]
+    uint16_t *zhl;                  // route (optional): z rotated per group and split to bf16, hi [R][D] then lo
+    long long lo_off;               // at zhl + lo_off
+    int group;                      // rotation group (a power of two dividing D)
+    float rot_scale;                // 1 / sqrt(group)
+};
+// Whether launch_mhc_mix takes this geometry (4 lanes, Hadamard width 256 or
+// 512, D a multiple of 32 up to that width).
+bool mhc_mix_supported(int D, int lanes, int hada);
+bool launch_mhc_mix(const MixArgs &a, int R, int sms, cudaStream_t st);
+
 // z[r] = rms(mean over lanes of x[r]) * (1 + final_norm) (engine.cpp:1039-1040).
 bool launch_final_norm(const float *x, int R, int lanes, int D, const float *final_norm, float *z, cudaStream_t st);
 

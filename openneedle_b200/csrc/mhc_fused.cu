@@ -1,0 +1,599 @@
+// Layer-boundary kernel of the decode/prefill forward: the post-attention part
+// of layer l (attention-output norm and gate, Hadamard MLP, Sinkhorn lane
+// mixing; needle2/csrc/engine.cpp:1025-1037) followed by the mHC routing of
+// layer l + 1 (lane RMS, the 2N + N^2 projections, gates, u, engram mixing, z;
+// engine.cpp:980-992), or by the final norm after the last layer
+// (engine.cpp:1039-1040).  Each CTA owns SB whole rows, so the lane state
+// never leaves the CTA between the two halves, and every phase runs on all of
+// the CTA's threads: thread t of the 256 compute threads owns elements
+// [tP, tP + P) of each D-wide vector (P = Hadamard width / 256).  A ninth warp
+// runs the Sinkhorn normalisation of the new mixing matrices while the others
+// finish the row.  Elementwise formulas keep the reference's operation order
+// with explicit round-to-nearest operations (the x86 reference has no FMA
+// contraction); sums over a row run as trees, a different association within
+// FP32 rounding; the Walsh-Hadamard stages run in the reference's order
+// (h = 1, 2, 4, ...), so each butterfly matches it.
+#include <math.h>
+#include <stdint.h>
+
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "engine.cuh"
+#include "engine_math.cuh"
+#include "pdl.cuh"
+
+namespace nb200 {
+namespace eng {
+namespace {
+
+constexpr int kComputeThreads = 256;
+constexpr int kMixThreads = kComputeThreads + 32;   // + the Sinkhorn warp
+constexpr int kMaxProj = 3 * kMaxLanes + kMaxLanes * kMaxLanes;
+
+// Barrier of the 8 compute warps only (the Sinkhorn warp never joins it).
+__device__ __forceinline__ void bar_compute() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// Exchange area of the compute warps: two alternating halves, each large
+// enough for one D-wide vector per row.  Every exchange writes one half,
+// passes one barrier and reads it back, and consecutive exchanges alternate
+// halves, so a half is rewritten only after every thread has passed the
+// barrier that follows its last read.
+template <int SB, int P>
+struct Xchg {
+    float *base;
+    int par = 0;
+    __device__ float *next() {
+        float *b = base + par * (SB * kComputeThreads * P);
+        par ^= 1;
+        return b;
+    }
+};
+
+// Sums of M values over the 256 compute threads; every thread gets them.
+// Warp trees, then the 8 warp partials added in warp order.
+template <int M, int SB, int P>
+__device__ __forceinline__ void cta_sums(float (&v)[M], Xchg<SB, P> &x) {
+    static_assert(M * 8 <= SB * kComputeThreads * P, "exchange area too small");
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float *b = x.next();
+#pragma unroll
+    for (int m = 0; m < M; ++m) v[m] = warp_sum(v[m]);
+    if (lane == 0) {
+#pragma unroll
+        for (int m = 0; m < M; ++m) b[warp * M + m] = v[m];
+    }
+    bar_compute();
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) t += b[w * M + m];
+        v[m] = t;
+    }
+}
+
+// Normalised Walsh-Hadamard transform of every `len`-element block (len a
+// power of two, P <= len <= 256 P) of each row's vector, P elements per thread:
+// stages h < P in registers, h < 32 P across lanes, the rest across warps
+// through the exchange area; then every element times `scale`.
+template <int SB, int P>
+__device__ __forceinline__ void cta_fwht(float (&v)[SB][P], int len, float scale, Xchg<SB, P> &x) {
+    const int t = threadIdx.x, lane = t & 31;
+#pragma unroll
+    for (int h = 1; h < P; h *= 2) {
+        if (h >= len) break;
+#pragma unroll
+        for (int s = 0; s < SB; ++s)
+#pragma unroll
+            for (int i = 0; i < P; ++i)
+                if (!(i & h)) {
+                    const float a = v[s][i], b = v[s][i + h];
+                    v[s][i] = __fadd_rn(a, b);
+                    v[s][i + h] = __fsub_rn(a, b);
+                }
+    }
+#pragma unroll
+    for (int m = 1; m < 32; m *= 2) {
+        if (m * P >= len) break;
+        const bool upper = lane & m;
+#pragma unroll
+        for (int s = 0; s < SB; ++s)
+#pragma unroll
+            for (int i = 0; i < P; ++i) {
+                const float o = __shfl_xor_sync(kFull, v[s][i], m);
+                v[s][i] = upper ? __fsub_rn(o, v[s][i]) : __fadd_rn(v[s][i], o);
+            }
+    }
+    for (int m = 32; m * P < len; m *= 2) {
+        float *b = x.next();
+#pragma unroll
+        for (int s = 0; s < SB; ++s)
+#pragma unroll
+            for (int i = 0; i < P; ++i) b[(s * kComputeThreads + t) * P + i] = v[s][i];
+        bar_compute();
+        const bool upper = t & m;
+        const int pt = t ^ m;
+#pragma unroll
+        for (int s = 0; s < SB; ++s)
+#pragma unroll
+            for (int i = 0; i < P; ++i) {
+                const float o = b[(s * kComputeThreads + pt) * P + i];
+                v[s][i] = upper ? __fsub_rn(o, v[s][i]) : __fadd_rn(v[s][i], o);
+            }
+    }
+#pragma unroll
+    for (int s = 0; s < SB; ++s)
+#pragma unroll
+        for (int i = 0; i < P; ++i) v[s][i] = __fmul_rn(v[s][i], scale);
+}
+
+// Sinkhorn of engine.cpp:151-180 on one N x N matrix held whole in one
+// thread's registers (sums in the reference's sequential order).
+template <int N>
+__device__ void reg_sinkhorn(float (&a)[N * N]) {
+    float mx = a[0], mn = a[0];
+#pragma unroll
+    for (int i = 1; i < N * N; ++i) {
+        mx = fmaxf(mx, a[i]);
+        mn = fminf(mn, a[i]);
+    }
+    if (!isfinite(mx) || __fsub_rn(mx, mn) > 60.f) {
+        for (int it = 0; it < 20; ++it) {
+#pragma unroll
+            for (int i = 0; i < N; ++i) {
+                float m = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < N; ++j) m = fmaxf(m, a[i * N + j]);
+                float sum = 0.f;
+#pragma unroll
+                for (int j = 0; j < N; ++j) sum = __fadd_rn(sum, expf(__fsub_rn(a[i * N + j], m)));
+                const float lse = __fadd_rn(m, logf(sum));
+#pragma unroll
+                for (int j = 0; j < N; ++j) a[i * N + j] = __fsub_rn(a[i * N + j], lse);
+            }
+#pragma unroll
+            for (int j = 0; j < N; ++j) {
+                float m = -INFINITY;
+#pragma unroll
+                for (int i = 0; i < N; ++i) m = fmaxf(m, a[i * N + j]);
+                float sum = 0.f;
+#pragma unroll
+                for (int i = 0; i < N; ++i) sum = __fadd_rn(sum, expf(__fsub_rn(a[i * N + j], m)));
+                const float lse = __fadd_rn(m, logf(sum));
+#pragma unroll
+                for (int i = 0; i < N; ++i) a[i * N + j] = __fsub_rn(a[i * N + j], lse);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < N * N; ++i) a[i] = expf(a[i]);
+        return;
+    }
+#pragma unroll
+    for (int i = 0; i < N * N; ++i) a[i] = expf(__fsub_rn(a[i], mx));
+    for (int it = 0; it < 20; ++it) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            float sum = 0.f;
+#pragma unroll
+            for (int j = 0; j < N; ++j) sum = __fadd_rn(sum, a[i * N + j]);
+            const float inv = __fdiv_rn(1.f, sum);
+#pragma unroll
+            for (int j = 0; j < N; ++j) a[i * N + j] = __fmul_rn(a[i * N + j], inv);
+        }
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+            float sum = 0.f;
+#pragma unroll
+            for (int i = 0; i < N; ++i) sum = __fadd_rn(sum, a[i * N + j]);
+            const float inv = __fdiv_rn(1.f, sum);
+#pragma unroll
+            for (int i = 0; i < N; ++i) a[i * N + j] = __fmul_rn(a[i * N + j], inv);
+        }
+    }
+}
+
+// P contiguous floats at p (P = 1, 2 or 4; p aligned to P floats).
+template <int P>
+__device__ __forceinline__ void load_p(float (&v)[P], const float *p) {
+    if constexpr (P == 4) {
+        const float4 t = *reinterpret_cast<const float4 *>(p);
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else if constexpr (P == 2) {
+        const float2 t = *reinterpret_cast<const float2 *>(p);
+        v[0] = t.x; v[1] = t.y;
+    } else {
+        v[0] = *p;
+    }
+}
+template <int P>
+__device__ __forceinline__ void store_p(float *p, const float (&v)[P]) {
+    if constexpr (P == 4) {
+        *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    } else if constexpr (P == 2) {
+        *reinterpret_cast<float2 *>(p) = make_float2(v[0], v[1]);
+    } else {
+        *p = v[0];
+    }
+}
+
+template <int P, int N, int SB>
+__global__ void __launch_bounds__(kMixThreads, 2) mhc_mix_kernel(const MixArgs a, int R) {
+    pdl_enter();
+    constexpr int NN = N * N, NPROJ = 2 * N + N * N;
+    extern __shared__ float smem[];
+    __shared__ float raws[SB][kMaxProj];
+    __shared__ float hres_s[SB][NN], hp_s[SB][N];
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int D = a.D, ND = N * D;
+    const int r0 = blockIdx.x * SB;
+    float *nx = smem;   // [SB][ND]
+
+    if (warp == 8) {
+        // Sinkhorn warp: the routed layer's residual mixing matrices, once the
+        // projections are in raws (engine.cpp:1033-1034)
+        if (!a.has_route) return;
+        __syncthreads();
+        if (lane < SB && r0 + lane < R) {
+            const int s = lane, r = r0 + lane;
+            float m[NN];
+#pragma unroll
+            for (int k = 0; k < NN; ++k)
+                m[k] = __fadd_rn(__fmul_rn(raws[s][2 * N + k], a.route.a_res), a.route.b_res[k]);
+            reg_sinkhorn<N>(m);
+#pragma unroll
+            for (int k = 0; k < NN; ++k) a.raw[(size_t)r * a.ldraw + 2 * N + k] = m[k];
+        }
+        return;
+    }
+
+    Xchg<SB, P> xc{smem + SB * ND};
+    const int d0 = t * P;
+    const bool dv = d0 < D;
+    bool rv[SB];
+#pragma unroll
+    for (int s = 0; s < SB; ++s) rv[s] = r0 + s < R;
+
+    // the thread's elements of the lane state
+    float xv[SB][N][P];
+#pragma unroll
+    for (int s = 0; s < SB; ++s)
+#pragma unroll
+        for (int n = 0; n < N; ++n) {
+            if (rv[s] && dv) load_p<P>(xv[s][n], a.x + ((size_t)(r0 + s) * N + n) * D + d0);
+            else
+#pragma unroll
+                for (int i = 0; i < P; ++i) xv[s][n][i] = 0.f;
+        }
+
+    float zout[SB][P];   // route: z; final: the lane means
+    if (a.has_post) {
+        const PostLayer &L = a.post;
+        for (int k = t; k < SB * (NN + N); k += kComputeThreads) {
+            const int s = k / (NN + N), j = k % (NN + N), r = r0 + s;
+            float v = 0.f;
+            if (r < R) v = j < NN ? a.raw[(size_t)r * a.ldraw + 2 * N + j] : a.hpost[(size_t)r * N + (j - NN)];
+            if (j < NN) hres_s[s][j] = v;
+            else hp_s[s][j - NN] = v;
+        }
+        float pv[SB][P], bb[SB][P], uv[SB][P];
+#pragma unroll
+        for (int s = 0; s < SB; ++s) {
+            const size_t o = (size_t)(r0 + s) * D + d0;
+            if (rv[s] && dv) {
+                load_p<P>(pv[s], a.proj + o);
+                load_p<P>(bb[s], a.bx + o);
+                load_p<P>(uv[s], a.u + o);
+            } else {
+#pragma unroll
+                for (int i = 0; i < P; ++i) pv[s][i] = bb[s][i] = uv[s][i] = 0.f;
+            }
+        }
+        float pn[P], ph[P], w1[P], w2[P], w3[P];
+#pragma unroll
+        for (int i = 0; i < P; ++i) {
+            const int d = d0 + i;
+            pn[i] = dv ? L.post_norm[d] : 0.f;
+            ph[i] = dv ? L.pre_hada[d] : 0.f;
+            w1[i] = dv ? L.d1[d] : 0.f;
+            w2[i] = L.d2[d];
+            w3[i] = dv ? L.d3[d] : 0.f;
+        }
+        // engine.cpp:1025-1026: proj = rms(proj) * (1 + post_norm); bx += sigmoid(attn_gate) * proj
+        float sp[SB];
+#pragma unroll
+        for (int s = 0; s < SB; ++s) {
+            sp[s] = 0.f;
+#pragma unroll
+            for (int i = 0; i < P; ++i) sp[s] = fmaf(pv[s][i], pv[s][i], sp[s]);
+        }
+        cta_sums<SB>(sp, xc);   // also publishes hres_s / hp_s
+        const float ag = sigm(L.attn_gate[0]);
+        float sb[SB];
+#pragma unroll
+        for (int s = 0; s < SB; ++s) {
+            const float ip = rms_inv(sp[s], D);
+            sb[s] = 0.f;
+#pragma unroll
+            for (int i = 0; i < P; ++i) {
+                if (dv) {
+                    const float tt = __fmul_rn(__fmul_rn(pv[s][i], ip), __fadd_rn(1.f, pn[i]));
+                    bb[s][i] = __fadd_rn(bb[s][i], __fmul_rn(ag, tt));
+                }
+                sb[s] = fmaf(bb[s][i], bb[s][i], sb[s]);
+            }
+        }
+        cta_sums<SB>(sb, xc);
+        // engine.cpp:1027-1031: Hadamard MLP on rms(bx) * (1 + pre_hada)
+        float mlp[SB][P];
+#pragma unroll
+        for (int s = 0; s < SB; ++s) {
+            const float ib = rms_inv(sb[s], D);
+#pragma unroll
+            for (int i = 0; i < P; ++i)
+                mlp[s][i] = dv ? __fmul_rn(__fmul_rn(__fmul_rn(bb[s][i], ib), __fadd_rn(1.f, ph[i])), w1[i]) : 0.f;
+        }
+        const float hs = __fdiv_rn(1.f, sqrtf((float)L.hada));
+        cta_fwht<SB, P>(mlp, L.hada, hs, xc);
+#pragma unroll
+        for (int s = 0; s < SB; ++s)
+#pragma unroll
+            for (int i = 0; i < P; ++i) {
+                const float v = __fmul_rn(mlp[s][i], w2[i]);
+                mlp[s][i] = __fmul_rn(v, sigm(v));
+            }
+        cta_fwht<SB, P>(mlp, L.hada, hs, xc);
+        // engine.cpp:1033-1037: x[n] = hpost[n] * bx + sum_j hres[n][j] * x[j]; hidden = lane mean
+#pragma unroll
+        for (int s = 0; s < SB; ++s) {
+            const int r = r0 + s;
+#pragma unroll
+            for (int i = 0; i < P; ++i) {
+                const float b = dv ? __fsub_rn(__fadd_rn(bb[s][i], __fmul_rn(w3[i], mlp[s][i])), uv[s][i]) : 0.f;
+                float xs[N];
+#pragma unroll
+                for (int n = 0; n < N; ++n) xs[n] = xv[s][n][i];
+                float mean = 0.f;
+#pragma unroll
+                for (int n = 0; n < N; ++n) {
+                    float val = __fmul_rn(hp_s[s][n], b);
+#pragma unroll
+                    for (int j = 0; j < N; ++j) val = __fadd_rn(val, __fmul_rn(hres_s[s][n * N + j], xs[j]));
+                    xv[s][n][i] = dv ? val : 0.f;
+                    mean = __fadd_rn(mean, val);
+                }
+                zout[s][i] = __fdiv_rn(mean, (float)N);
+                if (a.hidden && rv[s] && dv) a.hidden[(size_t)r * a.ldh + d0 + i] = zout[s][i];
+            }
+            if (rv[s] && dv)
+#pragma unroll
+                for (int n = 0; n < N; ++n) store_p<P>(a.x + ((size_t)r * N + n) * D + d0, xv[s][n]);
+        }
+    }
+
+    if (a.final_norm) {
+        // engine.cpp:1039-1040: z = rms(lane mean) * (1 + final_norm)
+        float sq[SB];
+#pragma unroll
+        for (int s = 0; s < SB; ++s) {
+            sq[s] = 0.f;
+#pragma unroll
+            for (int i = 0; i < P; ++i) sq[s] = fmaf(zout[s][i], zout[s][i], sq[s]);
+        }
+        cta_sums<SB>(sq, xc);
+#pragma unroll
+        for (int s = 0; s < SB; ++s) {
+            const float inv = rms_inv(sq[s], D);
+            if (!(rv[s] && dv)) continue;
+            float o[P];
+#pragma unroll
+            for (int i = 0; i < P; ++i) o[i] = __fmul_rn(__fmul_rn(zout[s][i], inv), __fadd_rn(1.f, a.fnorm[d0 + i]));
+            store_p<P>(a.zf + (size_t)(r0 + s) * D + d0, o);
+        }
+    }
+
+    if (!a.has_route) return;
+    const MhcLayer &L = a.route;
+    // engram key/value rows and the input norm, loaded ahead of the reductions
+    float ekv[SB][P], evv[SB][P], ni[P];
+#pragma unroll
+    for (int i = 0; i < P; ++i) ni[i] = dv ? L.norm_in[d0 + i] : 0.f;
+#pragma unroll
+    for (int s = 0; s < SB; ++s) {
+        if (L.ek && rv[s] && dv) {
+            load_p<P>(ekv[s], L.ek + (size_t)(r0 + s) * L.ld_site + d0);
+            load_p<P>(evv[s], L.ev + (size_t)(r0 + s) * L.ld_site + d0);
+        } else {
+#pragma unroll
+            for (int i = 0; i < P; ++i) ekv[s][i] = evv[s][i] = 0.f;
+        }
+    }
+    // engine.cpp:980: nx = rms(x) over the N lanes, staged for the projections
+    float ss[SB];
+#pragma unroll
+    for (int s = 0; s < SB; ++s) {
+        ss[s] = 0.f;
+#pragma unroll
+        for (int n = 0; n < N; ++n)
+#pragma unroll
+            for (int i = 0; i < P; ++i) ss[s] = fmaf(xv[s][n][i], xv[s][n][i], ss[s]);
+    }
+    cta_sums<SB>(ss, xc);
+#pragma unroll
+    for (int s = 0; s < SB; ++s) {
+        const float inv = rms_inv(ss[s], ND);
+        if (!dv) continue;
+#pragma unroll
+        for (int n = 0; n < N; ++n) {
+            float o[P];
+#pragma unroll
+            for (int i = 0; i < P; ++i) o[i] = __fmul_rn(xv[s][n][i], inv);
+            store_p<P>(nx + (size_t)s * ND + n * D + d0, o);
+        }
+    }
+    bar_compute();
+    // engine.cpp:529-559: raw[s][j] = phi_j . nx[s], one warp per projection row
+    {
+        constexpr int CMAX = N * P * 2;   // float4 chunks per lane at D = 256 P
+        const int chunks = ND / 4;
+        for (int j = warp; j < NPROJ; j += 8) {
+            const float *w = j < N ? a.phi_pre + (size_t)(L.layer * N + j) * ND
+                           : j < 2 * N ? a.phi_post + (size_t)(L.layer * N + j - N) * ND
+                                       : a.phi_res + (size_t)(L.layer * N * N + j - 2 * N) * ND;
+            float4 wv[CMAX];
+#pragma unroll
+            for (int c = 0; c < CMAX; ++c) {
+                const int k = c * 32 + lane;
+                wv[c] = k < chunks ? __ldg(reinterpret_cast<const float4 *>(w) + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            float acc[SB];
+#pragma unroll
+            for (int s = 0; s < SB; ++s) {
+                acc[s] = 0.f;
+#pragma unroll
+                for (int c = 0; c < CMAX; ++c) {
+                    const int k = c * 32 + lane;
+                    if (k < chunks) {
+                        const float4 v = reinterpret_cast<const float4 *>(nx + (size_t)s * ND)[k];
+                        acc[s] = fmaf(wv[c].x, v.x, fmaf(wv[c].y, v.y, fmaf(wv[c].z, v.z, fmaf(wv[c].w, v.w, acc[s]))));
+                    }
+                }
+            }
+#pragma unroll
+            for (int s = 0; s < SB; ++s) {
+                const float tot = warp_sum(acc[s]);
+                if (lane == 0) raws[s][j] = tot;
+            }
+        }
+    }
+    __syncthreads();   // raws ready for every warp, the Sinkhorn warp included
+    // engine.cpp:982-986: gates; u = sum_n hpre[n] x[n]
+    float hpre[SB][N];
+#pragma unroll
+    for (int s = 0; s < SB; ++s)
+#pragma unroll
+        for (int n = 0; n < N; ++n) {
+            const bool own = n == L.layer % N;
+            hpre[s][n] = sigm(__fadd_rn(__fadd_rn(__fmul_rn(L.a_pre, raws[s][n]), L.b_pre[n]), own ? 4.f : -4.f));
+        }
+    if (t < SB * 2 * N) {
+        const int s = t / (2 * N), j = t % (2 * N), r = r0 + s;
+        if (r < R) {
+            a.raw[(size_t)r * a.ldraw + j] = raws[s][j];
+            if (j >= N) {
+                const int n = j - N;
+                const bool own = n == L.layer % N;
+                a.hpost[(size_t)r * N + n] = __fmul_rn(
+                    2.f, sigm(__fadd_rn(__fadd_rn(__fmul_rn(L.a_post, raws[s][j]), L.b_post[n]), own ? 0.f : -4.f)));
+            }
+        }
+    }
+    float bxv[SB][P];
+    float su[2 * SB];
+#pragma unroll
+    for (int s = 0; s < SB; ++s) {
+        su[2 * s] = su[2 * s + 1] = 0.f;
+#pragma unroll
+        for (int i = 0; i < P; ++i) {
+            float sum = 0.f;
+#pragma unroll
+            for (int n = 0; n < N; ++n) sum = __fadd_rn(sum, __fmul_rn(hpre[s][n], xv[s][n][i]));
+            bxv[s][i] = sum;
+            su[2 * s] = fmaf(sum, sum, su[2 * s]);
+            su[2 * s + 1] = fmaf(ekv[s][i], ekv[s][i], su[2 * s + 1]);
+        }
+        if (rv[s] && dv) store_p<P>(a.u + (size_t)(r0 + s) * D + d0, bxv[s]);
+    }
+    if (L.ek) {
+        // engine.cpp:987-990: bx += sigmoid(rms(bx) . rms(ek) / sqrt(D)) * ev
+        cta_sums<2 * SB>(su, xc);
+        float dot[SB];
+#pragma unroll
+        for (int s = 0; s < SB; ++s) {
+            const float iu = rms_inv(su[2 * s], D), ie = rms_inv(su[2 * s + 1], D);
+            dot[s] = 0.f;
+#pragma unroll
+            for (int i = 0; i < P; ++i) dot[s] = fmaf(__fmul_rn(bxv[s][i], iu), __fmul_rn(ekv[s][i], ie), dot[s]);
+        }
+        cta_sums<SB>(dot, xc);
+#pragma unroll
+        for (int s = 0; s < SB; ++s) {
+            const float alpha = sigm(__fdiv_rn(dot[s], sqrtf((float)D)));
+#pragma unroll
+            for (int i = 0; i < P; ++i) bxv[s][i] = __fadd_rn(bxv[s][i], __fmul_rn(alpha, evv[s][i]));
+        }
+    }
+    // engine.cpp:991-992: z = rms(bx) * (1 + norm_in)
+    float sz[SB];
+#pragma unroll
+    for (int s = 0; s < SB; ++s) {
+        sz[s] = 0.f;
+#pragma unroll
+        for (int i = 0; i < P; ++i) sz[s] = fmaf(bxv[s][i], bxv[s][i], sz[s]);
+    }
+    cta_sums<SB>(sz, xc);
+#pragma unroll
+    for (int s = 0; s < SB; ++s) {
+        const float ib = rms_inv(sz[s], D);
+#pragma unroll
+        for (int i = 0; i < P; ++i) zout[s][i] = dv ? __fmul_rn(__fmul_rn(bxv[s][i], ib), __fadd_rn(1.f, ni[i])) : 0.f;
+        if (rv[s] && dv) {
+            const size_t o = (size_t)(r0 + s) * D + d0;
+            store_p<P>(a.bx + o, bxv[s]);
+            store_p<P>(a.z + o, zout[s]);
+        }
+    }
+    if (a.zhl) {
+        // the projections' input rotation (CQ::transform, group-wise) and bf16 hi/lo split
+        cta_fwht<SB, P>(zout, a.group, a.rot_scale, xc);
+#pragma unroll
+        for (int s = 0; s < SB; ++s) {
+            if (!(rv[s] && dv)) continue;
+            const size_t o = (size_t)(r0 + s) * D + d0;
+#pragma unroll
+            for (int i = 0; i < P; ++i) {
+                const __nv_bfloat16 h = __float2bfloat16_rn(zout[s][i]);
+                a.zhl[o + i] = __bfloat16_as_ushort(h);
+                a.zhl[a.lo_off + o + i] = __bfloat16_as_ushort(__float2bfloat16_rn(__fsub_rn(zout[s][i], __bfloat162float(h))));
+            }
+        }
+    }
+}
+
+}  // namespace
+
+bool mhc_mix_supported(int D, int lanes, int hada) {
+    return lanes == 4 && (hada == 256 || hada == 512) && D <= hada && D % 32 == 0 && D > 0;
+}
+
+bool launch_mhc_mix(const MixArgs &a, int R, int sms, cudaStream_t st) {
+    if (R <= 0) return true;
+    if (!mhc_mix_supported(a.D, a.lanes, a.hada)) return false;
+    if (a.has_post && (a.post.hada != a.hada || !a.post.hres_ready)) return false;
+    if (a.zhl && (a.group < 2 || a.group > a.hada || a.D % a.group || (a.group & (a.group - 1)))) return false;
+    const int P = a.hada / 256, N = 4;
+    const int sb = R <= 2 * sms ? 1 : R <= 8 * sms ? 2 : 4;
+    const size_t smem = sizeof(float) * ((size_t)sb * N * a.D + 2 * (size_t)sb * kComputeThreads * P);
+    const unsigned grid = (unsigned)((R + sb - 1) / sb);
+#define NB_MIX(PP, SBB)                                                                                          \
+    {                                                                                                          \
+        auto kernel = mhc_mix_kernel<PP, 4, SBB>;                                                              \
+        static bool configured = false;                                                                        \
+        if (!configured) {                                                                                     \
+            NB_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024)); \
+            configured = true;                                                                                 \
+        }                                                                                                      \
+        NB_CUDA_TRY(launch_pdl(kernel, grid, kMixThreads, smem, st, a, R));                                     \
+    }
+    if (P == 1) {
+        if (sb == 1) NB_MIX(1, 1) else if (sb == 2) NB_MIX(1, 2) else NB_MIX(1, 4)
+    } else {
+        if (sb == 1) NB_MIX(2, 1) else if (sb == 2) NB_MIX(2, 2) else NB_MIX(2, 4)
+    }
+#undef NB_MIX
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+}
+
+}  // namespace eng
+}  // namespace nb200

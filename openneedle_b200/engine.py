@@ -208,7 +208,7 @@ class GpuBatch:
         return int(self._lib.needle2_batch_kv_storage_bytes(self._h))
 
     STAGES = ("engrams+embedding", "mhc_routing", "qkvg_projections", "qk_norm_rope", "kv_store+attention",
-              "gate+out_projection", "hadamard_mlp+mixing", "final_norm+lm_head+greedy")
+              "out_projection", "mlp+mixing+next_routing", "final_norm+lm_head+greedy")
 
     def set_graphs(self, enable: bool = True) -> None:
         """Replay decode steps as a captured CUDA graph (default) or launch them one by one."""
