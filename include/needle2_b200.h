@@ -285,6 +285,30 @@ int needle2_engine_set_int8_kv(void *engine, int enable);
 size_t needle2_engine_kv_storage_bytes(void *engine);
 const char *needle2_engine_error(void);
 
+/* Vocabulary size of the engine's model (additive; -1 for a null engine). */
+int needle2_engine_vocab(void *engine);
+
+/* ---- frontend: needle2/csrc/frontend.h:15-35 ------------------------------
+ * The tokenizer and grammar entry points forward to the reference's own
+ * native library (built from its sources), loaded from the path in
+ * NEEDLE2_FRONTEND_LIBRARY at the first call; without it they fail (NULL / -1)
+ * with needle2_frontend_error() saying so.  needle2_engine_decode_compiled is
+ * this library's: argmax of the prefill logits (first maximum, NaN refused),
+ * then needle2_engine_decode_loop with the grammar's automaton
+ * (frontend.cpp:1057-1079).  The grammar's vocabulary is not compared with the
+ * engine's (the automaton carries none); candidate tokens are range-checked by
+ * the decode loop. */
+const char *needle2_frontend_error(void);
+void *needle2_tokenizer_create(const unsigned char *blob, size_t size);
+void needle2_tokenizer_free(void *tokenizer);
+int needle2_tokenizer_encode(void *tokenizer, const char *text, size_t size, int dummy, int *output, int capacity);
+int needle2_tokenizer_decode(void *tokenizer, const int *tokens, int count, char *output, int capacity);
+void *needle2_grammar_compile(void *tokenizer, const char *tools_json, size_t size);
+void needle2_grammar_free(void *grammar);
+const needle2_dfa_state_desc *needle2_grammar_dfa(void *grammar);
+int needle2_engine_decode_compiled(void *engine, const float *logits, int vocab, int limit, void *grammar,
+                                   int *output, int *count);
+
 /* ---- additive: many sequences of one engine's model, in lockstep --------- */
 /*
  * The reference serves one unpadded sequence per Engine (needle2/native.py:307-314).

@@ -509,7 +509,7 @@ struct GemmF32Args {
 
 // grid: (M tiles, total N tiles of all segments); tile width BN (256 for
 // prefill-sized launches, 64 when that leaves too few CTAs for the machine).
-template <int BN, int ST>
+template <int BN, int ST, int ACC>
 __global__ void __launch_bounds__(kFThreads, 1)
     cq_gemm_f32x3_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
                          const __grid_constant__ GemmF32Args a) {
@@ -527,7 +527,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     const int m0 = blockIdx.x * kFBM, n0 = ((int)blockIdx.y - sg.tile0) * BN;
     const int S = a.ksteps;
 
-    if (warp == 1) tc::alloc(&tmem_s, BN);
+    if (warp == 1) tc::alloc(&tmem_s, BN * ACC);
     if (tid == 0) {
         abort_flag = 0;
         for (int s = 0; s < kFStages; ++s) {
@@ -581,9 +581,14 @@ __global__ void __launch_bounds__(kFThreads, 1)
 #pragma unroll
                 for (int kk = 0; kk < kFBK / 16; ++kk) {   // 16 bf16 = 32 bytes per MMA
                     const uint32_t o = kk * 32;
-                    tc::mma_bf16_ss(tmem, sw128_desc(ah + o), sw128_desc(bh + o), idesc, (k | kk) != 0);
-                    tc::mma_bf16_ss(tmem, sw128_desc(al + o), sw128_desc(bh + o), idesc, 1);
-                    tc::mma_bf16_ss(tmem, sw128_desc(ah + o), sw128_desc(bl + o), idesc, 1);
+                    // MMA i of the tile goes to accumulator i % ACC (independent chains)
+                    const int i0 = 3 * (k * (kFBK / 16) + kk);
+                    const uint32_t d0 = tmem + (uint32_t)((i0 % ACC) * BN);
+                    const uint32_t d1 = tmem + (uint32_t)(((i0 + 1) % ACC) * BN);
+                    const uint32_t d2 = tmem + (uint32_t)(((i0 + 2) % ACC) * BN);
+                    tc::mma_bf16_ss(d0, sw128_desc(ah + o), sw128_desc(bh + o), idesc, i0 >= ACC);
+                    tc::mma_bf16_ss(d1, sw128_desc(al + o), sw128_desc(bh + o), idesc, i0 + 1 >= ACC);
+                    tc::mma_bf16_ss(d2, sw128_desc(ah + o), sw128_desc(bl + o), idesc, i0 + 2 >= ACC);
                 }
                 tc::commit(&empty[s]);
             }
@@ -591,7 +596,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
         }
         __syncwarp();
     } else {
-        // warps 2-5: TMEM lanes 32 (warp % 4) .. +31 = tile rows
+        // warps 2-5: TMEM lanes 32 (warp % 4) .. +31 = tile rows; the ACC
+        // accumulators added in order
         const int q = warp & 3;
         const int row = m0 + 32 * q + lane;
         const bool ok = gwait(&dfull, 0, &abort_flag);
@@ -603,6 +609,14 @@ __global__ void __launch_bounds__(kFThreads, 1)
                 uint32_t v[32];
                 tc::ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(32 * c), v);
                 tc::wait_ld();
+#pragma unroll
+                for (int x = 1; x < ACC; ++x) {
+                    uint32_t w[32];
+                    tc::ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(x * BN + 32 * c), w);
+                    tc::wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w[j]));
+                }
                 if (row < a.M) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 4) {
@@ -617,6 +631,175 @@ __global__ void __launch_bounds__(kFThreads, 1)
                                 if (n0 + col + e < sg.N) yr[col + e] = __uint_as_float(v[j + e]);
                         }
                     }
+                }
+            }
+        }
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    if (warp == 1) tc::dealloc(tmem, BN * ACC);
+}
+
+// ---------------------------------------------------------------------------
+// The same product split along K over a cluster of `ks` CTAs (2 <= ks <= 8),
+// for decode-sized launches whose 128 x 256 tiles are too few to fill the
+// machine: rank r of the cluster accumulates K steps [r S, (r + 1) S) of the
+// tile in its own TMEM; then every CTA sends column slice c (256 / ks columns)
+// of its partial tile to rank c's shared memory (distributed shared memory
+// stores), and rank c adds the ks partials of its slice in rank order and
+// stores y.  The order of the additions is fixed, so results do not depend on
+// timing.
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
+}
+
+constexpr int kSplitBN = 256;
+constexpr bool kSplitK = false;   // measured slower than the unsplit 64-wide tiles
+constexpr int kDecodeAcc = 1;      // accumulators per 64-wide tile
+
+__global__ void __launch_bounds__(kFThreads, 1)
+    cq_gemm_f32x3_splitk_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
+                                const __grid_constant__ GemmF32Args a, int ks) {
+    constexpr int BN = kSplitBN, ST = 2;
+    constexpr int kPartB = FTile<BN, ST>::kPartB, kStageBytes = FTile<BN, ST>::kStageBytes;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t full[ST], empty[ST], dfull;
+    __shared__ uint32_t tmem_s;
+    __shared__ volatile int abort_flag;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int si = 0;
+    while (si + 1 < a.nseg && (int)blockIdx.y >= a.seg[si + 1].tile0) ++si;
+    const F32Seg &sg = a.seg[si];
+    const int m0 = blockIdx.x * kFBM, n0 = ((int)blockIdx.y - sg.tile0) * BN;
+    const int S = a.ksteps;                       // K steps of this CTA
+    const uint32_t rank = cluster_rank();
+    const int kbeg = (int)rank * S;
+
+    if (warp == 1) tc::alloc(&tmem_s, BN);
+    if (tid == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&dfull, 1);
+        fence_barrier_init();
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = tmem_s;
+
+    bool ok = true;
+    if (warp == 0) {
+        if (lane == 0) {
+            const int pre = S < ST ? S : ST;
+            for (int k = 0; k < pre; ++k) {
+                uint8_t *st = smem + (size_t)k * kStageBytes;
+                mbar_arrive_expect_tx(&full[k], kStageBytes);
+                const int x = (kbeg + k) * kFBK * 2;
+                tma_load_2d(st + 2 * kFPartA, &sg.bh, x, n0, &full[k]);
+                tma_load_2d(st + 2 * kFPartA + kPartB, &sg.bl, x, n0, &full[k]);
+            }
+            pdl_wait();
+            for (int k = 0; k < S && !abort_flag; ++k) {
+                const int s = k % ST;
+                uint8_t *st = smem + (size_t)s * kStageBytes;
+                const int x = (kbeg + k) * kFBK * 2;
+                if (k >= ST) {
+                    if (!gwait(&empty[s], (uint32_t)((k / ST) - 1) & 1, &abort_flag)) break;
+                    mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    tma_load_2d(st + 2 * kFPartA, &sg.bh, x, n0, &full[s]);
+                    tma_load_2d(st + 2 * kFPartA + kPartB, &sg.bl, x, n0, &full[s]);
+                }
+                tma_load_2d(st, &tah, x, m0, &full[s]);
+                tma_load_2d(st + kFPartA, &tal, x, m0, &full[s]);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = tc::idesc_bf16(kFBM, BN);
+            for (int k = 0; k < S && !abort_flag; ++k) {
+                const int s = k % ST;
+                if (!gwait(&full[s], (uint32_t)(k / ST) & 1, &abort_flag)) break;
+                tc::fence_after();
+                const uint32_t ah = smem_addr(smem + (size_t)s * kStageBytes), al = ah + kFPartA;
+                const uint32_t bh = ah + 2 * kFPartA, bl = bh + kPartB;
+#pragma unroll
+                for (int kk = 0; kk < kFBK / 16; ++kk) {
+                    const uint32_t o = kk * 32;
+                    tc::mma_bf16_ss(tmem, sw128_desc(ah + o), sw128_desc(bh + o), idesc, (k | kk) != 0);
+                    tc::mma_bf16_ss(tmem, sw128_desc(al + o), sw128_desc(bh + o), idesc, 1);
+                    tc::mma_bf16_ss(tmem, sw128_desc(ah + o), sw128_desc(bl + o), idesc, 1);
+                }
+                tc::commit(&empty[s]);
+            }
+            tc::commit(&dfull);
+        }
+        __syncwarp();
+    } else {
+        ok = gwait(&dfull, 0, &abort_flag);
+        tc::fence_after();
+    }
+    // (1) every CTA of the cluster has finished its MMAs: the stage buffers
+    // take the partial tiles now
+    cluster_sync_all();
+    const int slice = BN / ks, stride = slice + 4;   // +4 floats: conflict-free float4 rows
+    float *recv = reinterpret_cast<float *>(smem);    // [ks][128][stride]
+    const int q = warp & 3, trow = 32 * q + lane;
+    if (warp >= 2 && ok) {
+        for (int c = 0; c < BN / 32; ++c) {
+            uint32_t v[32];
+            tc::ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(32 * c), v);
+            tc::wait_ld();
+            const int owner = (32 * c) / slice, col0 = 32 * c - owner * slice;
+            const uint32_t dst = smem_addr(recv + ((size_t)rank * kFBM + trow) * stride + col0);
+            const uint32_t rdst = map_rank(dst, (uint32_t)owner);
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) st_cluster_v4(rdst + 4 * j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+        }
+    }
+    // (2) every partial slice has arrived
+    cluster_sync_all();
+    if (warp >= 2 && ok) {
+        const int row = m0 + trow;
+        if (row < a.M) {
+            const int c0 = n0 + (int)rank * slice;
+            float *yr = sg.y + (size_t)row * sg.ldy;
+            const bool vec = (sg.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(sg.y) & 15) == 0;
+            for (int j = 0; j < slice; j += 4) {
+                float4 acc = *reinterpret_cast<const float4 *>(recv + (size_t)trow * stride + j);
+                for (int src = 1; src < ks; ++src) {
+                    const float4 p = *reinterpret_cast<const float4 *>(recv + ((size_t)src * kFBM + trow) * stride + j);
+                    acc.x += p.x;
+                    acc.y += p.y;
+                    acc.z += p.z;
+                    acc.w += p.w;
+                }
+                const int col = c0 + j;
+                if (vec && col + 3 < sg.N) {
+                    *reinterpret_cast<float4 *>(yr + col) = acc;
+                } else {
+                    const float e[4] = {acc.x, acc.y, acc.z, acc.w};
+                    for (int t = 0; t < 4; ++t)
+                        if (col + t < sg.N) yr[col + t] = e[t];
                 }
             }
         }
@@ -784,8 +967,16 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
     const int mtiles = (M + kFBM - 1) / kFBM;
     int wide = 0;
     for (int i = 0; i < count; ++i) wide += (outs[i].N + 255) / 256;
-    // 256-wide tiles where they fill the machine, 64-wide ones (four times the CTAs) otherwise
-    const bool narrow = (long long)mtiles * wide < 2LL * sms;
+    // Too few 128 x 256 tiles for the machine: split K over a cluster of ks
+    // CTAs (at most 8, each with one or more K steps) while the grid still fits
+    // one wave; where K is too short for that, 64-wide tiles (four times the
+    // CTAs); 256-wide tiles otherwise.
+    const int steps = padded / kFBK;
+    int ks = 1;
+    if (kSplitK)
+        while (ks < 8 && steps % (2 * ks) == 0 && (long long)mtiles * wide * 2 * ks <= sms) ks *= 2;
+    const bool split = ks > 1;
+    const bool narrow = !split && (long long)mtiles * wide < 2LL * sms;
     const int BN = narrow ? 64 : 256;
     const size_t an = (size_t)M * padded;
     CUtensorMap tah, tal;
@@ -794,7 +985,7 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
     GemmF32Args args{};
     args.nseg = count;
     args.M = M;
-    args.ksteps = padded / kFBK;
+    args.ksteps = steps / ks;
     int tiles = 0;
     for (int i = 0; i < count; ++i) {
         const F32Out &o = outs[i];
@@ -809,15 +1000,30 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
         tiles += (o.N + BN - 1) / BN;
     }
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(mtiles, tiles);
+    cfg.gridDim = dim3(mtiles, tiles, ks);
     cfg.blockDim = dim3(kFThreads);
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = (unsigned)ks;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    static bool configured[3][64] = {};
+    cfg.numAttrs = split ? 2 : 1;
+    static bool configured[4][64] = {};
+    if (split) {
+        constexpr size_t smem = FTile<kSplitBN, 2>::kSmem;
+        if (dev < 0 || dev >= 64 || !configured[3][dev]) {
+            NB_CUDA_TRY(cudaFuncSetAttribute(cq_gemm_f32x3_splitk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem));
+            if (dev >= 0 && dev < 64) configured[3][dev] = true;
+        }
+        cfg.dynamicSmemBytes = smem;
+        NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, cq_gemm_f32x3_splitk_kernel, tah, tal, args, ks));
+        return true;
+    }
     auto launch = [&](auto kernel, size_t smem, int which) -> bool {
         if (dev < 0 || dev >= 64 || !configured[which][dev]) {
             NB_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -827,10 +1033,11 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
         NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, tah, tal, args));
         return true;
     };
-    if (!narrow) return launch(cq_gemm_f32x3_kernel<256, 2>, FTile<256, 2>::kSmem, 0);
+    if (!narrow) return launch(cq_gemm_f32x3_kernel<256, 2, 1>, FTile<256, 2>::kSmem, 0);
     // one CTA per SM with the deep pipeline while the grid fits the machine
-    if ((long long)mtiles * tiles <= sms) return launch(cq_gemm_f32x3_kernel<64, 4>, FTile<64, 4>::kSmem, 1);
-    return launch(cq_gemm_f32x3_kernel<64, 2>, FTile<64, 2>::kSmem, 2);
+    if ((long long)mtiles * tiles <= sms)
+        return launch(cq_gemm_f32x3_kernel<64, 4, kDecodeAcc>, FTile<64, 4>::kSmem, 1);
+    return launch(cq_gemm_f32x3_kernel<64, 2, kDecodeAcc>, FTile<64, 2>::kSmem, 2);
 }
 
 bool launch_gemm_f32x3(const uint16_t *a_hilo, int M, const uint16_t *w_hilo, int N, int padded, float *y, int ldy,

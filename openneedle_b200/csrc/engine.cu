@@ -1390,6 +1390,8 @@ size_t needle2_engine_kv_storage_bytes(void *p) {
 
 const char *needle2_engine_error(void) { return nb200::g_engine_error.c_str(); }
 
+int needle2_engine_vocab(void *p) { return p ? static_cast<Engine *>(p)->model->c.vocab : -1; }
+
 void *needle2_batch_create(void *engine, int sessions, int prefix_len) {
     Batch *out = nullptr;
     const int rc = nb200::guarded([&] {

@@ -14,6 +14,10 @@ A plan is a list of operations:
   {"op": "step_candidates", "token": t, "candidates": [...]}
   {"op": "cache_prefix"} / {"op": "reset_to_prefix"}
   {"op": "decode", "first": t, "max_new": n}
+  {"op": "decode_compiled", "prompt": [...], "max_new": n, "tools": [...] | null, "first": t | null}
+    (needle2/frontend.py decode_native through NativeEngine.decode_from_logits: the
+    prompt's prefill logits, or logits whose maximum is `first`; the grammar is
+    compiled from `tools` with the tokenizer of engine_models.tokenizer_blob)
   {"op": "kv_bytes"}
   {"op": "batch", "sessions": S, "prefix": [...], "prompts": [[...]...], "steps": n, "kv": ..., "matmul": ...}
     (GPU library only: this repository's batch extension through openneedle_b200.engine)
@@ -74,6 +78,19 @@ def main(archive_path: str, plan_path: str, out_path: str) -> int:
             engine.reset_to_prefix()
         elif kind == "decode":
             out[f"{i}_tokens"] = np.asarray(engine.decode(int(op["first"]), int(op["max_new"])), np.int32)
+        elif kind == "decode_compiled":
+            from needle2.frontend import CompiledGrammar, NativeTokenizer
+            from engine_models import tokenizer_blob
+            grammar = None
+            if op.get("tools") is not None:
+                tok = NativeTokenizer(tokenizer_blob())
+                grammar = CompiledGrammar(tok, json.dumps(op["tools"], separators=(",", ":")))
+            engine.reset()
+            logits = engine.prefill(np.asarray(op["prompt"]), last_only=True)
+            if op.get("first") is not None:
+                logits = np.full_like(logits, -1.0)
+                logits[int(op["first"])] = 1.0
+            out[f"{i}_tokens"] = np.asarray(engine.decode_from_logits(logits, int(op["max_new"]), grammar), np.int32)
         elif kind == "kv_bytes":
             out[f"{i}_kv_bytes"] = np.array([engine.kv_storage_bytes], np.int64)
         elif kind == "batch":

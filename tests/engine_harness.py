@@ -21,7 +21,7 @@ def run_plan(archive_path, plan, library, workdir, tag, timeout=1800):
     plan_path = workdir / f"{tag}_plan.json"
     out_path = workdir / f"{tag}_out.npz"
     plan_path.write_text(json.dumps(plan))
-    env = dict(os.environ, NEEDLE2_NATIVE_LIBRARY=str(library),
+    env = dict(os.environ, NEEDLE2_NATIVE_LIBRARY=str(library), NEEDLE2_FRONTEND_LIBRARY=str(O.REF_LIB),
                PYTHONPATH=os.pathsep.join([str(O.REF_ROOT), str(ROOT), str(HERE)]),
                OMP_NUM_THREADS=os.environ.get("OMP_NUM_THREADS", "8"))
     proc = subprocess.run([sys.executable, str(HERE / "engine_child.py"), str(archive_path), str(plan_path),

@@ -26,12 +26,33 @@ def _ref():
     return A, M, Q
 
 
-def tiny_config(window: int = 0) -> dict:
+def tiny_config(window: int = 0, vocab: int = 61) -> dict:
     """A few-layer model exercising GQA, two lanes, two engram sites with
     nonidentity taps, a sliding window when window > 0."""
-    return dict(vocab_size=61, d_model=32, num_heads=4, num_kv_heads=2, num_layers=3, head_dim=8, mhc_lanes=2,
+    return dict(vocab_size=vocab, d_model=32, num_heads=4, num_kv_heads=2, num_layers=3, head_dim=8, mhc_lanes=2,
                 engram_layers=(0, 2), engram_orders=(2, 3), engram_slots=19, engram_sub_dim=8, num_engram_tables=4,
                 engram_conv_taps=4, engram_conv_dilation=3, max_seq_len=96, kv_window=window)
+
+
+def tokenizer_blob() -> bytes:
+    """A small tokenizer in the .cact tokenizer record format (needle2/
+    tokenizer.py:13-27: header <IIIIIBBH = pieces, pad, eos, bos, unk,
+    add_dummy_prefix, byte_fallback, reserved; then per piece <fBH = score,
+    type, byte length, UTF-8 bytes): control tokens, the grammar's special
+    markers at the ids the grammar compiler looks for (<stop> 5,
+    <tool_call> 10, </tool_call> 11), a few text pieces and all 256 byte
+    pieces, 269 in all."""
+    import struct
+    normal, unknown, control, user, byte = 0, 1, 2, 3, 4
+    pieces = [("<pad>", control), ("</s>", control), ("<s>", control), ("<unk>", unknown), ("\u2581", normal),
+              ("<stop>", user), ("a", normal), ("b", normal), ("ab", normal), ("ba", normal),
+              ("<tool_call>", user), ("</tool_call>", user), ("</tools>", user)]
+    pieces += [(f"<0x{v:02X}>", byte) for v in range(256)]
+    out = bytearray(struct.pack("<IIIIIBBH", len(pieces), 0, 1, 2, 3, 1, 1, 0))
+    for text, kind in pieces:
+        raw = text.encode("utf-8")
+        out += struct.pack("<fBH", -float(len(raw)), kind, len(raw)) + raw
+    return bytes(out)
 
 
 def config5() -> dict:

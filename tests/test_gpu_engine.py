@@ -174,3 +174,26 @@ def test_config5_geometry_matches_reference(env, kv):
             assert margin <= bar, f"{key}: greedy differs with top-2 margin {margin:.3e}"
         assert e <= bar, f"{key}: rel err {e:.3e}"
     print(f"config-5 decoder kv={kv}: max rel err {worst:.3e}")
+
+
+def test_decode_compiled_matches_reference(env):
+    """needle2_engine_decode_compiled (frontend.cpp:1057-1079) through the
+    reference's needle2/frontend.py decode_native: unconstrained greedy decoding
+    from the prompt's own logits, and grammar-constrained decoding of a tool
+    call (logits whose maximum is <tool_call>, then the compiled tool schema's
+    token automaton: candidate projections, single-candidate steps and the
+    terminal state).  The tokenizer and grammar compiler are the reference's,
+    reached through this library's forwarding entry points."""
+    from engine_models import tiny_config
+    path = _archive(env, "tiny_v269", tiny_config(0, vocab=269), 31)
+    tools = [{"name": "fn", "parameters": {"type": "object",
+                                           "properties": {"a": {"type": "integer"}, "b": {"type": "boolean"}},
+                                           "required": ["a", "b"]}}]
+    prompt = _tokens(9, 269, 77)
+    plan = [{"op": "engine", "kv": "fp32"},
+            {"op": "decode_compiled", "prompt": prompt, "max_new": 12, "tools": None},
+            {"op": "decode_compiled", "prompt": prompt, "max_new": 40, "tools": tools, "first": 10},
+            {"op": "decode_compiled", "prompt": prompt[:4], "max_new": 40, "tools": tools, "first": 10}]
+    ref, gpu = _both(env, path, plan, "compiled")
+    _compare(ref, gpu, what="decode_compiled")
+    assert ref["2_tokens"][0] == 10 and len(ref["2_tokens"]) > 1

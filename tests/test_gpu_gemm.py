@@ -96,3 +96,37 @@ def test_fp32_prefill_gemm_config3_sizes(native, oracle_lib, bits, n, k):
     print(f"config-3 FP32 GEMM CQ{bits} N={n} K={k}: max rel err {err:.3e}")
     assert err <= FP32_REL_TOL
     assert not y[1000].any()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m", [64, 128, 200, 1024])
+def test_fp32_decode_gemm_fused_projections(native, oracle_lib, m):
+    """Decode-sized FP32 GEMMs (a few hundred rows, K = 512): config 5's fused
+    Q/K/V/gate projections (N = 512, 256, 256, 512, CQ2) and its out
+    projection.  These launches split K over a cluster of CTAs and add the
+    partial tiles in a fixed order; outputs stay within the FP32 tolerance of
+    the oracle on every matrix and are identical from call to call."""
+    from util import FP32_REL_TOL, rel_err, synthetic_matrix
+    from openneedle_b200.native import linear_many_batch
+    k = 512
+    shapes = [512, 256, 256, 512]
+    mats, raw = [], []
+    for i, n in enumerate(shapes):
+        packed, norms, cb = synthetic_matrix(n, k, 2, 128, seed=4000 + 17 * i + n)
+        mats.append(native.DeviceMatrix(packed, norms, (n, k), 2, 128, cb))
+        raw.append((packed, norms, cb, n))
+    x = np.random.default_rng(m).normal(size=(m, k)).astype(np.float32)
+    x[m // 2] = 0
+    ys = linear_many_batch(mats, x)
+    again = linear_many_batch(mats, x)
+    sample = np.unique(np.array([0, 1, 31, 63, m // 2, m - 2, m - 1]))
+    for (packed, norms, cb, n), y, y2 in zip(raw, ys, again):
+        ref = oracle_lib.cq_linear(packed, norms, (n, k), 2, 128, cb, x[sample])
+        assert rel_err(y[sample], ref) <= FP32_REL_TOL
+        np.testing.assert_array_equal(y, y2)
+        assert not y[m // 2].any()
+    # the out projection alone (one 512-wide matrix: a wider K split)
+    packed, norms, cb, n = raw[0]
+    y = mats[0].fp32(x)
+    ref = oracle_lib.cq_linear(packed, norms, (n, k), 2, 128, cb, x[sample])
+    assert rel_err(y[sample], ref) <= FP32_REL_TOL
