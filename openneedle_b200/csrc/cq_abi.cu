@@ -679,7 +679,8 @@ bool handle_hilo_gemm(void *const *hs, int count, int batch, int *group, float *
 }
 
 bool handle_many_hilo(void *const *hs, int count, const uint16_t *a_hilo, float *const *ys, int batch,
-                      cudaStream_t st) {
+                      cudaStream_t st, const QkvgEpilogue *epi, bool *epi_done) {
+    if (epi_done) *epi_done = false;
     if (!handle_hilo_gemm(hs, count, batch, nullptr, nullptr)) {
         set_error("these matrices do not take pre-split bf16 activations");
         return false;
@@ -691,7 +692,8 @@ bool handle_many_hilo(void *const *hs, int count, const uint16_t *a_hilo, float 
         if (!ensure_f32_copy(m, st)) return false;
         outs[i] = F32Out{m->d_whl, m->w.out, ys[i], m->w.out};
     }
-    return launch_gemm_f32x3_multi(a_hilo, batch, static_cast<Matrix *>(hs[0])->w.padded, outs.data(), count, st);
+    return launch_gemm_f32x3_multi(a_hilo, batch, static_cast<Matrix *>(hs[0])->w.padded, outs.data(), count, st,
+                                   epi, epi_done);
 }
 }  // extern "C++"
 

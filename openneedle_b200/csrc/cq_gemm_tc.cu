@@ -31,6 +31,7 @@
 
 #include "common.cuh"
 #include "cq_gemv.cuh"
+#include "qkvg_epilogue.cuh"
 #include "tcgen05.cuh"
 
 namespace nb200 {
@@ -505,11 +506,85 @@ constexpr int kF32MaxSegs = 4;
 struct GemmF32Args {
     F32Seg seg[kF32MaxSegs];
     int nseg, M, ksteps;
+    QkvgEpilogue epi;   // used by the EPI instantiations only
 };
+
+// Norm, rotary embedding and KV store of one 64-wide head held by one thread
+// (QkvgEpilogue): segment seg (0 q, 1 k, 2 v, 3 gate), head `head` of it,
+// output row `row`; y receives the (roped) head.
+__device__ __forceinline__ void qkvg_head(const QkvgEpilogue &E, int seg, int head, int row, float (&h)[64],
+                                          float *yr) {
+    if (seg <= 1) {
+        const float *nrm = seg == 0 ? E.q_norm : E.k_norm;
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) s = fmaf(h[i], h[i], s);
+        const float inv = __fdiv_rn(1.f, sqrtf(__fadd_rn(__fdiv_rn(s, 64.f), 1e-6f)));
+#pragma unroll
+        for (int i = 0; i < 64; ++i) h[i] = __fmul_rn(__fmul_rn(h[i], inv), __fadd_rn(1.f, nrm[i]));
+        const int p = E.pos[row];
+        const bool tab = p < E.table_len;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            float co, si;
+            if (tab) {
+                co = E.cos_t[(size_t)p * 32 + j];
+                si = E.sin_t[(size_t)p * 32 + j];
+            } else {
+                const float ang = __fdiv_rn((float)p, E.divisor[j]);
+                co = cosf(ang);
+                si = sinf(ang);
+            }
+            const float a = h[j], c = h[j + 32];
+            h[j] = __fsub_rn(__fmul_rn(a, co), __fmul_rn(c, si));
+            h[j + 32] = __fadd_rn(__fmul_rn(c, co), __fmul_rn(a, si));
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4 *>(yr + i) = make_float4(h[i], h[i + 1], h[i + 2], h[i + 3]);
+    if (seg != 1 && seg != 2) return;
+    const KVDest &d = E.kv.dest;
+    const int sess = d.session[row], p = d.position[row];
+    const bool pinned = p < d.prefix;
+    const size_t krow = pinned ? (size_t)head * d.prefix + p
+                               : ((size_t)sess * E.kvheads + head) * d.rows +
+                                     (d.window ? (p - d.prefix) % d.window : p - d.prefix);
+    const bool isv = seg == 2;
+    if (E.kv.fp32) {
+        float *dst = (isv ? (pinned ? d.pvf : E.kv.vf) : (pinned ? d.pkf : E.kv.kf)) + krow * 64;
+#pragma unroll
+        for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4 *>(dst + i) = make_float4(h[i], h[i + 1], h[i + 2], h[i + 3]);
+        return;
+    }
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) mx = fmaxf(mx, fabsf(h[i]));
+    const float sc = mx > 0.f ? __fdiv_rn(mx, 127.f) : 1.f;
+    const float iv = mx > 0.f ? __fdiv_rn(127.f, mx) : 0.f;
+    int8_t *dst = (isv ? (pinned ? d.pv : E.kv.v8) : (pinned ? d.pk : E.kv.k8)) + krow * 64;
+    float *sdst = isv ? (pinned ? d.pvs : E.kv.vs) : (pinned ? d.pks : E.kv.ks);
+#pragma unroll
+    for (int i = 0; i < 64; i += 16) {
+        uint32_t w[4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                int qv = __float2int_rn(__fmul_rn(h[i + 4 * b + e], iv));
+                qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
+                word |= (uint32_t)(uint8_t)(int8_t)qv << (8 * e);
+            }
+            w[b] = word;
+        }
+        *reinterpret_cast<uint4 *>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    sdst[krow] = sc;
+}
 
 // grid: (M tiles, total N tiles of all segments); tile width BN (256 for
 // prefill-sized launches, 64 when that leaves too few CTAs for the machine).
-template <int BN, int ST, int ACC>
+template <int BN, int ST, int ACC, bool EPI>
 __global__ void __launch_bounds__(kFThreads, 1)
     cq_gemm_f32x3_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
                          const __grid_constant__ GemmF32Args a) {
@@ -602,7 +677,30 @@ __global__ void __launch_bounds__(kFThreads, 1)
         const int row = m0 + 32 * q + lane;
         const bool ok = gwait(&dfull, 0, &abort_flag);
         tc::fence_after();
-        if (ok) {
+        if constexpr (EPI) {
+            static_assert(BN == 64, "the decode epilogue takes one 64-wide head per tile");
+            if (ok) {
+                float h[64];
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t v[32];
+                    tc::ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(32 * c), v);
+                    tc::wait_ld();
+#pragma unroll
+                    for (int x = 1; x < ACC; ++x) {
+                        uint32_t w[32];
+                        tc::ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(x * BN + 32 * c), w);
+                        tc::wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w[j]));
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) h[32 * c + j] = __uint_as_float(v[j]);
+                }
+                if (row < a.M) qkvg_head(a.epi, si, n0 / 64, row, h, sg.y + (size_t)row * sg.ldy + n0);
+            }
+        } else if (ok) {
             const bool vec = (sg.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(sg.y) & 15) == 0;
             float *yr = sg.y + (size_t)min(row, a.M - 1) * sg.ldy + n0;
             for (int c = 0; c < BN / 32; ++c) {
@@ -946,7 +1044,8 @@ bool launch_split_bf16(const float *x, long long n, uint16_t *hilo, cudaStream_t
 }
 
 bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F32Out *outs, int count,
-                             cudaStream_t st) {
+                             cudaStream_t st, const QkvgEpilogue *epi, bool *epi_done) {
+    if (epi_done) *epi_done = false;
     if (M <= 0 || count <= 0) return true;
     if (padded % kFBK) {
         set_error("FP32 prefill GEMM requires the padded width to be a multiple of 64");
@@ -1012,7 +1111,7 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
     attr[1].val.clusterDim.z = (unsigned)ks;
     cfg.attrs = attr;
     cfg.numAttrs = split ? 2 : 1;
-    static bool configured[4][64] = {};
+    static bool configured[6][64] = {};
     if (split) {
         constexpr size_t smem = FTile<kSplitBN, 2>::kSmem;
         if (dev < 0 || dev >= 64 || !configured[3][dev]) {
@@ -1033,11 +1132,19 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
         NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, tah, tal, args));
         return true;
     };
-    if (!narrow) return launch(cq_gemm_f32x3_kernel<256, 2, 1>, FTile<256, 2>::kSmem, 0);
+    if (!narrow) return launch(cq_gemm_f32x3_kernel<256, 2, 1, false>, FTile<256, 2>::kSmem, 0);
+    // the decode epilogue: four segments (q, k, v, gate) of whole 64-wide heads
+    const bool with_epi = epi && epi->active && count == 4 && epi->hd == 64;
+    if (with_epi) {
+        args.epi = *epi;
+        if (epi_done) *epi_done = true;
+    }
     // one CTA per SM with the deep pipeline while the grid fits the machine
     if ((long long)mtiles * tiles <= sms)
-        return launch(cq_gemm_f32x3_kernel<64, 4, kDecodeAcc>, FTile<64, 4>::kSmem, 1);
-    return launch(cq_gemm_f32x3_kernel<64, 2, kDecodeAcc>, FTile<64, 2>::kSmem, 2);
+        return with_epi ? launch(cq_gemm_f32x3_kernel<64, 4, kDecodeAcc, true>, FTile<64, 4>::kSmem, 4)
+                        : launch(cq_gemm_f32x3_kernel<64, 4, kDecodeAcc, false>, FTile<64, 4>::kSmem, 1);
+    return with_epi ? launch(cq_gemm_f32x3_kernel<64, 2, kDecodeAcc, true>, FTile<64, 2>::kSmem, 5)
+                    : launch(cq_gemm_f32x3_kernel<64, 2, kDecodeAcc, false>, FTile<64, 2>::kSmem, 2);
 }
 
 bool launch_gemm_f32x3(const uint16_t *a_hilo, int M, const uint16_t *w_hilo, int N, int padded, float *y, int ldy,

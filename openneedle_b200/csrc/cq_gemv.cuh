@@ -109,8 +109,12 @@ struct F32Out {
     float *y;
     int ldy;
 };
+struct QkvgEpilogue;
+// epi (optional, four segments q, k, v, gate): the decode-step epilogue of
+// qkvg_epilogue.cuh, applied when the launch runs 64-wide tiles of one head
+// each; *epi_done tells whether it ran (else the caller still has to do it).
 bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F32Out *outs, int count,
-                             cudaStream_t st);
+                             cudaStream_t st, const QkvgEpilogue *epi = nullptr, bool *epi_done = nullptr);
 // Activation rows from which int8 products run as the tensor-core GEMM.
 constexpr int kGemmMinRows = 64;
 

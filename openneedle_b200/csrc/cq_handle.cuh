@@ -9,6 +9,8 @@
 
 namespace nb200 {
 
+struct QkvgEpilogue;
+
 // Device view of handle's matrix (null when handle is null).
 const CQDevice *handle_matrix(void *handle);
 bool handle_is_sdot(void *handle);
@@ -24,8 +26,9 @@ bool handle_prepare(void *handle, const float *x, int batch, const float **rot, 
 bool handle_hilo_gemm(void *const *hs, int count, int batch, int *group, float *scale);
 // That GEMM on activations the caller rotated and split: a_hilo [batch][in]
 // bf16 hi, then [batch][in] lo (in = the matrices' padded width).
+// epi / epi_done: the decode epilogue of launch_gemm_f32x3_multi (optional).
 bool handle_many_hilo(void *const *hs, int count, const uint16_t *a_hilo, float *const *ys, int batch,
-                      cudaStream_t st);
+                      cudaStream_t st, const QkvgEpilogue *epi = nullptr, bool *epi_done = nullptr);
 // A new int8 (SDOT) handle over the same packed matrix as the FP32 handle
 // `cq` (its device copy read back once), or null with the error set.
 void *handle_make_sdot(void *cq);

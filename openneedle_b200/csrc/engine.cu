@@ -31,6 +31,7 @@
 #include "engine.cuh"
 #include "kv_pool.cuh"
 #include "pdl.cuh"
+#include "qkvg_epilogue.cuh"
 
 namespace nb200 {
 namespace {
@@ -90,6 +91,8 @@ struct Model {
     bool sdot = false;
     std::vector<Tensor> t;
     float *rope_divisor = nullptr;   // [head_dim / 2]
+    float *rope_cos = nullptr, *rope_sin = nullptr;   // [rope_len][head_dim / 2], position / divisor
+    int rope_len = 0;
     cudaStream_t stream = nullptr;
     int count() const { return (int)t.size(); }
     int mh() const { return 1 + 14 * c.layers; }
@@ -111,6 +114,8 @@ struct Model {
             if (x.dense) cudaFree(x.dense);
         }
         if (rope_divisor) cudaFree(rope_divisor);
+        if (rope_cos) cudaFree(rope_cos);
+        if (rope_sin) cudaFree(rope_sin);
         if (stream) cudaStreamDestroy(stream);
     }
     // The handle a matmul of tensor i runs on: the int8 twin in SDOT mode.
@@ -293,6 +298,16 @@ Model *build_model(const needle2_engine_config &c, const needle2_tensor_desc *td
     for (int j = 0; j < c.head_dim / 2; ++j) div[j] = std::pow(c.rope_theta, float(2 * j) / c.head_dim);
     cuda_check(cudaMalloc(&m->rope_divisor, sizeof(float) * std::max<size_t>(div.size(), 1)), "rope");
     cuda_check(cudaMemcpy(m->rope_divisor, div.data(), sizeof(float) * div.size(), cudaMemcpyHostToDevice), "rope");
+    // cos / sin of every position below max_seq_len (the decode GEMM epilogue reads them)
+    if (c.head_dim == 64 && c.max_seq > 0) {
+        m->rope_len = c.max_seq;
+        const size_t n = (size_t)m->rope_len * (c.head_dim / 2);
+        cuda_check(cudaMalloc(&m->rope_cos, sizeof(float) * n), "rope table");
+        cuda_check(cudaMalloc(&m->rope_sin, sizeof(float) * n), "rope table");
+        check(launch_rope_table(m->rope_divisor, c.head_dim / 2, m->rope_len, m->rope_cos, m->rope_sin, m->stream),
+              "rope table");
+        cuda_check(cudaStreamSynchronize(m->stream), "rope table");
+    }
     return m.release();
 }
 
@@ -629,14 +644,29 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         aq(m, s.z.ptr, R, D, stream);
         mark(st, 2, stream);
         void *hs[4];
+        bool roped = false;   // norm, RoPE and the KV store done by the projections' epilogue
         if (zhl_ready && qkvg_handles(l, hs)) {
             float *outs[4] = {s.q.ptr, s.k.ptr, s.v.ptr, s.gate.ptr};
-            check(handle_many_hilo(hs, 4, s.zhl.ptr, outs, R, stream), "QKVG projections");
+            QkvgEpilogue epi{};
+            // measured: the fused epilogue pays off from four 128-row tiles on (1024 rows: 0.07 ms a
+            // step saved); with fewer tiles its per-thread work outlasts the separate kernel
+            if (T == 1 && m.rope_cos && R >= 512) {
+                epi.active = 1;
+                epi.heads = c.heads; epi.kvheads = c.kvheads; epi.hd = c.head_dim;
+                epi.q_norm = m.t[ti + 4].dense; epi.k_norm = m.t[ti + 5].dense;
+                epi.cos_t = m.rope_cos; epi.sin_t = m.rope_sin; epi.table_len = m.rope_len;
+                epi.divisor = m.rope_divisor; epi.pos = s.rpos.ptr;
+                epi.kv = kv_pool_target(st.kv[l], st.iota.ptr, st.base.ptr);
+            }
+            check(handle_many_hilo(hs, 4, s.zhl.ptr, outs, R, stream, epi.active ? &epi : nullptr, &roped),
+                  "QKVG projections");
         } else {
             projections(m, ti, s.z.ptr, R, s.q.ptr, s.k.ptr, s.v.ptr, s.gate.ptr, stream);
         }
         mark(st, 3, stream);
-        if (T == 1) {
+        if (roped) {
+            // q/k normed and roped, the token's K/V stored: attention follows
+        } else if (T == 1) {
             // decode: the new token's K/V stored as RoPE finishes, then attention alone
             check(eng::launch_qk_rope_store(s.q.ptr, s.k.ptr, s.v.ptr, R, c.heads, c.kvheads, c.head_dim,
                                             m.t[ti + 4].dense, m.t[ti + 5].dense, s.rpos.ptr, m.rope_divisor,

@@ -13,6 +13,7 @@
 #include "engine.cuh"
 #include "engine_math.cuh"
 #include "kv_pool.cuh"
+#include "qkvg_epilogue.cuh"
 
 namespace nb200 {
 namespace eng {
@@ -1116,4 +1117,27 @@ bool launch_copy_tokens(const int *src, int n, int *dst, int ld_dst, cudaStream_
 }
 
 }  // namespace eng
+
+namespace {
+__global__ void rope_table_kernel(const float *__restrict__ divisor, int half, int positions, float *cos_t,
+                                  float *sin_t) {
+    const long long n = (long long)positions * half;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int p = (int)(i / half), j = (int)(i % half);
+        const float ang = __fdiv_rn((float)p, divisor[j]);
+        cos_t[i] = cosf(ang);
+        sin_t[i] = sinf(ang);
+    }
+}
+}  // namespace
+
+bool launch_rope_table(const float *divisor, int half, int positions, float *cos_t, float *sin_t, cudaStream_t st) {
+    const long long n = (long long)positions * half;
+    if (n <= 0) return true;
+    rope_table_kernel<<<(unsigned)std::min<long long>((n + 255) / 256, 4096), 256, 0, st>>>(divisor, half, positions,
+                                                                                          cos_t, sin_t);
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+}
+
 }  // namespace nb200

@@ -20,7 +20,8 @@ A plan is a list of operations:
     compiled from `tools` with the tokenizer of engine_models.tokenizer_blob)
   {"op": "kv_bytes"}
   {"op": "batch", "sessions": S, "prefix": [...], "prompts": [[...]...], "steps": n, "kv": ..., "matmul": ...}
-    (GPU library only: this repository's batch extension through openneedle_b200.engine)
+    (GPU library only: this repository's batch extension through openneedle_b200.engine;
+    "keep": [...] saves only those sessions' logits)
 Outputs are saved as "<index>_<name>".
 """
 from __future__ import annotations
@@ -104,14 +105,16 @@ def main(archive_path: str, plan_path: str, out_path: str) -> int:
             b.set_graphs(op.get("graphs", True))
             if prefix:
                 b.set_prefix(prefix)
+            keep = op.get("keep")
+            pick = (lambda a: a[keep]) if keep is not None else (lambda a: a)
             logits, nxt = b.prefill(np.asarray(op["prompts"], np.int32))
-            out[f"{i}_prefill_logits"] = logits
+            out[f"{i}_prefill_logits"] = pick(logits)
             out[f"{i}_first"] = nxt
             if op.get("teacher"):
                 steps = []
                 for tok in np.asarray(op["teacher"], np.int32).T:
                     lg, _ = b.step(tok, greedy=False)
-                    steps.append(lg)
+                    steps.append(pick(lg))
                 out[f"{i}_teacher_logits"] = np.stack(steps, 1)
             if op.get("steps"):
                 out[f"{i}_tokens"] = b.decode_greedy(nxt, op["steps"])

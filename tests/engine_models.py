@@ -55,11 +55,12 @@ def tokenizer_blob() -> bytes:
     return bytes(out)
 
 
-def config5() -> dict:
+def config5(max_seq_len: int = 4096) -> dict:
     """d 512, 12 layers, 8 heads x 64 (4 KV heads), vocab
-    32768, max_seq 4096, no window, engram sites at layers 2 and 9."""
+    32768, max_seq 4096 (smaller values shrink only the KV capacity), no
+    window, engram sites at layers 2 and 9."""
     return dict(vocab_size=32768, d_model=512, num_heads=8, num_kv_heads=4, num_layers=12, head_dim=64,
-                max_seq_len=4096, kv_window=0, engram_layers=(2, 9))
+                max_seq_len=max_seq_len, kv_window=0, engram_layers=(2, 9))
 
 
 def build_archive(cfg: dict, seed: int = 0, *, taps_noise: float = 0.1, embedding_bits: int = 4,
