@@ -608,7 +608,10 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         a.bx = s.bx.ptr; a.x = s.x.ptr; a.z = s.z.ptr;
         return a;
     };
-    bool routed = false, zhl_ready = false, final_done = false;
+    // routed: layer l's routing already ran (in the previous layer's boundary kernel);
+    // hres_norm: raw's residual part holds the Sinkhorn-normalised matrix (the
+    // routing kernel's output) rather than the raw projections
+    bool routed = false, hres_norm = false, zhl_ready = false, final_done = false;
     for (int l = 0; l < c.layers; ++l) {
         const int ti = 1 + 14 * l;
         if (!routed) {
@@ -622,12 +625,14 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
                 done = eng::launch_mhc_mix(a, R, m.sms, stream);
                 check(done || last_error()[0] == 0, "mHC routing");
                 zhl_ready = zhl_ready && done;
+                hres_norm = false;
             }
             if (!done) {
                 zhl_ready = false;
                 done = eng::launch_mhc_route(ml, m.t[mh + 6].dense, m.t[mh + 7].dense, m.t[mh + 8].dense, s.x.ptr, R,
                                              s.raw.ptr, ldraw, s.hpost.ptr, s.u.ptr, s.bx.ptr, s.z.ptr, m.sms, stream);
                 check(done || last_error()[0] == 0, "mHC routing");
+                hres_norm = done;
             }
             if (!done) {
                 check(eng::launch_rms(s.x.ptr, N * D, R, N * D, nullptr, s.nx.ptr, N * D, stream), "lane rms");
@@ -639,7 +644,7 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
                                           stream),
                       "mHC routing");
             }
-            routed = done;   // raw's residual part holds the normalised mixing matrix
+            routed = true;
         }
         aq(m, s.z.ptr, R, D, stream);
         mark(st, 2, stream);
@@ -689,9 +694,9 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         float *hid = o.hidden ? s.hidden.ptr + (size_t)l * D : nullptr;
         const bool last = l + 1 == c.layers;
         bool fused = false;
-        if (mix && routed) {
+        if (mix && !hres_norm) {
             eng::MixArgs a = mix_args();
-            a.has_post = 1; a.post = post_layer(l, 1);
+            a.has_post = 1; a.post = post_layer(l, 0);   // the boundary kernel normalises the mixing matrix
             a.hidden = hid; a.ldh = c.layers * D;
             if (!last) {
                 a.has_route = 1; a.route = route_layer(l + 1);
@@ -707,11 +712,12 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         }
         if (!fused) {
             zhl_ready = false;
-            check(eng::launch_mhc_post(post_layer(l, routed ? 1 : 0), s.proj.ptr, s.raw.ptr, ldraw, s.hpost.ptr,
+            check(eng::launch_mhc_post(post_layer(l, hres_norm ? 1 : 0), s.proj.ptr, s.raw.ptr, ldraw, s.hpost.ptr,
                                        s.u.ptr, s.bx.ptr, s.x.ptr, R, hid, c.layers * D, stream),
                   "mHC mixing");
         }
         routed = fused && !last;
+        hres_norm = false;
     }
 
     // final norm (engine.cpp:1039-1041) on every row or each entry's last token

@@ -115,6 +115,7 @@ struct MixArgs {
     long long lo_off;               // at zhl + lo_off
     int group;                      // rotation group (a power of two dividing D)
     float rot_scale;                // 1 / sqrt(group)
+    int phi_smem;                   // set by launch_mhc_mix: projections staged in shared memory
 };
 // Whether launch_mhc_mix takes this geometry (4 lanes, Hadamard width 256 or
 // 512, D a multiple of 32 up to that width).

@@ -22,6 +22,7 @@
 #include "engine.cuh"
 #include "engine_math.cuh"
 #include "pdl.cuh"
+#include "sm100_async.cuh"
 
 namespace nb200 {
 namespace eng {
@@ -33,6 +34,9 @@ constexpr int kMaxProj = 3 * kMaxLanes + kMaxLanes * kMaxLanes;
 
 // Barrier of the 8 compute warps only (the Sinkhorn warp never joins it).
 __device__ __forceinline__ void bar_compute() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// The one barrier of all nine warps: the Sinkhorn warp's matrices are in
+// shared memory.
+__device__ __forceinline__ void bar_mix() { asm volatile("bar.sync 2, 288;" ::: "memory"); }
 
 // Exchange area of the compute warps: two alternating halves, each large
 // enough for one D-wide vector per row.  Every exchange writes one half,
@@ -128,69 +132,56 @@ __device__ __forceinline__ void cta_fwht(float (&v)[SB][P], int len, float scale
         for (int i = 0; i < P; ++i) v[s][i] = __fmul_rn(v[s][i], scale);
 }
 
-// Sinkhorn of engine.cpp:151-180 on one N x N matrix held whole in one
-// thread's registers (sums in the reference's sequential order).
+// Sinkhorn of engine.cpp:151-180 on an N x N matrix held one element per lane
+// by the N * N lanes from `base` (lane base + i N + j holds element (i, j));
+// every row and column sum runs in the reference's sequential order over
+// values fetched by shuffles, and 1 / sum is the correctly rounded reciprocal,
+// the same value as the reference's division.  All 32 lanes take part.
 template <int N>
-__device__ void reg_sinkhorn(float (&a)[N * N]) {
-    float mx = a[0], mn = a[0];
+__device__ float lanes_sinkhorn(float a, int base, int lane) {
+    const int e = lane - base, i = e / N, j = e % N;
+    const bool mine = e >= 0 && e < N * N;
+    float mx = mine ? a : -INFINITY, mn = mine ? a : INFINITY;
 #pragma unroll
-    for (int i = 1; i < N * N; ++i) {
-        mx = fmaxf(mx, a[i]);
-        mn = fminf(mn, a[i]);
+    for (int t = 0; t < N * N; ++t) {
+        const float v = __shfl_sync(kFull, a, (base + t) & 31);
+        mx = fmaxf(mx, v);
+        mn = fminf(mn, v);
     }
     if (!isfinite(mx) || __fsub_rn(mx, mn) > 60.f) {
         for (int it = 0; it < 20; ++it) {
 #pragma unroll
-            for (int i = 0; i < N; ++i) {
+            for (int pass = 0; pass < 2; ++pass) {
+                float v[N];
+#pragma unroll
+                for (int t = 0; t < N; ++t)
+                    v[t] = __shfl_sync(kFull, a, (base + (pass == 0 ? i * N + t : t * N + j)) & 31);
                 float m = -INFINITY;
 #pragma unroll
-                for (int j = 0; j < N; ++j) m = fmaxf(m, a[i * N + j]);
+                for (int t = 0; t < N; ++t) m = fmaxf(m, v[t]);
                 float sum = 0.f;
 #pragma unroll
-                for (int j = 0; j < N; ++j) sum = __fadd_rn(sum, expf(__fsub_rn(a[i * N + j], m)));
-                const float lse = __fadd_rn(m, logf(sum));
-#pragma unroll
-                for (int j = 0; j < N; ++j) a[i * N + j] = __fsub_rn(a[i * N + j], lse);
-            }
-#pragma unroll
-            for (int j = 0; j < N; ++j) {
-                float m = -INFINITY;
-#pragma unroll
-                for (int i = 0; i < N; ++i) m = fmaxf(m, a[i * N + j]);
-                float sum = 0.f;
-#pragma unroll
-                for (int i = 0; i < N; ++i) sum = __fadd_rn(sum, expf(__fsub_rn(a[i * N + j], m)));
-                const float lse = __fadd_rn(m, logf(sum));
-#pragma unroll
-                for (int i = 0; i < N; ++i) a[i * N + j] = __fsub_rn(a[i * N + j], lse);
+                for (int t = 0; t < N; ++t) sum = __fadd_rn(sum, expf(__fsub_rn(v[t], m)));
+                a = __fsub_rn(a, __fadd_rn(m, logf(sum)));
             }
         }
-#pragma unroll
-        for (int i = 0; i < N * N; ++i) a[i] = expf(a[i]);
-        return;
+        return expf(a);
     }
-#pragma unroll
-    for (int i = 0; i < N * N; ++i) a[i] = expf(__fsub_rn(a[i], mx));
+    a = expf(__fsub_rn(a, mx));
     for (int it = 0; it < 20; ++it) {
 #pragma unroll
-        for (int i = 0; i < N; ++i) {
+        for (int pass = 0; pass < 2; ++pass) {
+            float v[N];
+#pragma unroll
+            for (int t = 0; t < N; ++t)
+                v[t] = __shfl_sync(kFull, a, (base + (pass == 0 ? i * N + t : t * N + j)) & 31);
             float sum = 0.f;
 #pragma unroll
-            for (int j = 0; j < N; ++j) sum = __fadd_rn(sum, a[i * N + j]);
-            const float inv = __fdiv_rn(1.f, sum);
-#pragma unroll
-            for (int j = 0; j < N; ++j) a[i * N + j] = __fmul_rn(a[i * N + j], inv);
-        }
-#pragma unroll
-        for (int j = 0; j < N; ++j) {
-            float sum = 0.f;
-#pragma unroll
-            for (int i = 0; i < N; ++i) sum = __fadd_rn(sum, a[i * N + j]);
-            const float inv = __fdiv_rn(1.f, sum);
-#pragma unroll
-            for (int i = 0; i < N; ++i) a[i * N + j] = __fmul_rn(a[i * N + j], inv);
+            for (int t = 0; t < N; ++t) sum = __fadd_rn(sum, v[t]);
+            a = __fmul_rn(a, __frcp_rn(sum));
         }
     }
+    return a;
 }
 
 // P contiguous floats at p (P = 1, 2 or 4; p aligned to P floats).
@@ -217,37 +208,53 @@ __device__ __forceinline__ void store_p(float *p, const float (&v)[P]) {
     }
 }
 
-template <int P, int N, int SB>
-__global__ void __launch_bounds__(kMixThreads, 2) mhc_mix_kernel(const MixArgs a, int R) {
-    pdl_enter();
+template <int P, int N, int SB, bool STAGED>
+__global__ void __launch_bounds__(kMixThreads, STAGED ? 1 : 2) mhc_mix_kernel(const MixArgs a, int R) {
     constexpr int NN = N * N, NPROJ = 2 * N + N * N;
-    extern __shared__ float smem[];
+    extern __shared__ __align__(16) float smem[];
     __shared__ float raws[SB][kMaxProj];
     __shared__ float hres_s[SB][NN], hp_s[SB][N];
+    __shared__ __align__(8) uint64_t phibar;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int D = a.D, ND = N * D;
     const int r0 = blockIdx.x * SB;
-    float *nx = smem;   // [SB][ND]
+    float *phis = smem + 2 * SB * kComputeThreads * P;   // [NPROJ][ND] when a.phi_smem
+    auto phi_row = [&](int layer, int j) -> const float * {
+        return j < N ? a.phi_pre + (size_t)(layer * N + j) * ND
+             : j < 2 * N ? a.phi_post + (size_t)(layer * N + j - N) * ND
+                         : a.phi_res + (size_t)(layer * N * N + j - 2 * N) * ND;
+    };
+    if (STAGED && a.phi_smem && a.has_route && t == 0) {
+        // the routed layer's projection rows do not depend on earlier kernels:
+        // bulk-copy them into shared memory before waiting for those kernels
+        mbar_init(&phibar, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(&phibar, (uint32_t)(NPROJ * ND * sizeof(float)));
+        for (int j = 0; j < NPROJ; ++j)
+            bulk_g2s(phis + (size_t)j * ND, phi_row(a.route.layer, j), (uint32_t)(ND * sizeof(float)), &phibar);
+    }
+    pdl_enter();
 
     if (warp == 8) {
-        // Sinkhorn warp: the routed layer's residual mixing matrices, once the
-        // projections are in raws (engine.cpp:1033-1034)
-        if (!a.has_route) return;
-        __syncthreads();
-        if (lane < SB && r0 + lane < R) {
-            const int s = lane, r = r0 + lane;
-            float m[NN];
-#pragma unroll
-            for (int k = 0; k < NN; ++k)
-                m[k] = __fadd_rn(__fmul_rn(raws[s][2 * N + k], a.route.a_res), a.route.b_res[k]);
-            reg_sinkhorn<N>(m);
-#pragma unroll
-            for (int k = 0; k < NN; ++k) a.raw[(size_t)r * a.ldraw + 2 * N + k] = m[k];
+        // Sinkhorn warp: layer l's residual mixing matrices from the raw
+        // projections the routing left in raw (engine.cpp:1033-1034), while the
+        // compute warps run the attention-output norm and the Hadamard MLP
+        if (!a.has_post) return;
+        constexpr int PER = 32 / NN;   // matrices per pass of the warp
+        for (int s0 = 0; s0 < SB; s0 += PER) {
+            const int s = s0 + lane / NN, k = lane % NN;
+            const bool live = s < SB && r0 + s < R;
+            const float hr = live ? __fadd_rn(__fmul_rn(a.raw[(size_t)(r0 + s) * a.ldraw + 2 * N + k], a.post.a_res),
+                                              a.post.b_res[k])
+                                  : 0.f;
+            const float h = lanes_sinkhorn<N>(hr, (lane / NN) * NN, lane);
+            if (s < SB && lane / NN < PER) hres_s[s][k] = h;
         }
+        bar_mix();
         return;
     }
 
-    Xchg<SB, P> xc{smem + SB * ND};
+    Xchg<SB, P> xc{smem};
     const int d0 = t * P;
     const bool dv = d0 < D;
     bool rv[SB];
@@ -269,12 +276,9 @@ __global__ void __launch_bounds__(kMixThreads, 2) mhc_mix_kernel(const MixArgs a
     float zout[SB][P];   // route: z; final: the lane means
     if (a.has_post) {
         const PostLayer &L = a.post;
-        for (int k = t; k < SB * (NN + N); k += kComputeThreads) {
-            const int s = k / (NN + N), j = k % (NN + N), r = r0 + s;
-            float v = 0.f;
-            if (r < R) v = j < NN ? a.raw[(size_t)r * a.ldraw + 2 * N + j] : a.hpost[(size_t)r * N + (j - NN)];
-            if (j < NN) hres_s[s][j] = v;
-            else hp_s[s][j - NN] = v;
+        if (t < SB * N) {
+            const int s = t / N, n = t % N;
+            hp_s[s][n] = r0 + s < R ? a.hpost[(size_t)(r0 + s) * N + n] : 0.f;
         }
         float pv[SB][P], bb[SB][P], uv[SB][P];
 #pragma unroll
@@ -307,7 +311,7 @@ __global__ void __launch_bounds__(kMixThreads, 2) mhc_mix_kernel(const MixArgs a
 #pragma unroll
             for (int i = 0; i < P; ++i) sp[s] = fmaf(pv[s][i], pv[s][i], sp[s]);
         }
-        cta_sums<SB>(sp, xc);   // also publishes hres_s / hp_s
+        cta_sums<SB>(sp, xc);   // also publishes hp_s
         const float ag = sigm(L.attn_gate[0]);
         float sb[SB];
 #pragma unroll
@@ -343,6 +347,7 @@ __global__ void __launch_bounds__(kMixThreads, 2) mhc_mix_kernel(const MixArgs a
                 mlp[s][i] = __fmul_rn(v, sigm(v));
             }
         cta_fwht<SB, P>(mlp, L.hada, hs, xc);
+        bar_mix();   // hres_s from the Sinkhorn warp
         // engine.cpp:1033-1037: x[n] = hpost[n] * bx + sum_j hres[n][j] * x[j]; hidden = lane mean
 #pragma unroll
         for (int s = 0; s < SB; ++s) {
@@ -392,6 +397,7 @@ __global__ void __launch_bounds__(kMixThreads, 2) mhc_mix_kernel(const MixArgs a
         }
     }
 
+
     if (!a.has_route) return;
     const MhcLayer &L = a.route;
     // engram key/value rows and the input norm, loaded ahead of the reductions
@@ -408,7 +414,7 @@ __global__ void __launch_bounds__(kMixThreads, 2) mhc_mix_kernel(const MixArgs a
             for (int i = 0; i < P; ++i) ekv[s][i] = evv[s][i] = 0.f;
         }
     }
-    // engine.cpp:980: nx = rms(x) over the N lanes, staged for the projections
+    // engine.cpp:980: nx = rms(x) over the N lanes
     float ss[SB];
 #pragma unroll
     for (int s = 0; s < SB; ++s) {
@@ -419,54 +425,98 @@ __global__ void __launch_bounds__(kMixThreads, 2) mhc_mix_kernel(const MixArgs a
             for (int i = 0; i < P; ++i) ss[s] = fmaf(xv[s][n][i], xv[s][n][i], ss[s]);
     }
     cta_sums<SB>(ss, xc);
+    float nxv[SB][N][P];
 #pragma unroll
     for (int s = 0; s < SB; ++s) {
         const float inv = rms_inv(ss[s], ND);
-        if (!dv) continue;
 #pragma unroll
-        for (int n = 0; n < N; ++n) {
-            float o[P];
+        for (int n = 0; n < N; ++n)
 #pragma unroll
-            for (int i = 0; i < P; ++i) o[i] = __fmul_rn(xv[s][n][i], inv);
-            store_p<P>(nx + (size_t)s * ND + n * D + d0, o);
-        }
+            for (int i = 0; i < P; ++i) nxv[s][n][i] = __fmul_rn(xv[s][n][i], inv);
     }
-    bar_compute();
-    // engine.cpp:529-559: raw[s][j] = phi_j . nx[s], one warp per projection row
-    {
+    // engine.cpp:529-559: raw[s][j] = phi_j . nx[s]; each thread its N x P
+    // elements of every projection row, then a tree over the CTA
+    if constexpr (STAGED) {
+        // each thread its N x P elements of every staged projection row, then a
+        // tree over the CTA
+        bool staged = a.phi_smem != 0;
+        if (staged && !mbar_wait(&phibar, 0)) staged = false;   // (bounded) fall back to global reads
+        float *b = xc.next();   // [8 warps][SB * NPROJ]
+        constexpr int JC = 8;   // projection rows per pass (bounds the partials' registers)
+#pragma unroll
+        for (int j0 = 0; j0 < NPROJ; j0 += JC) {
+            float part[SB][JC];
+#pragma unroll
+            for (int jj = 0; jj < JC; ++jj) {
+                const int j = j0 + jj;
+#pragma unroll
+                for (int s = 0; s < SB; ++s) part[s][jj] = 0.f;
+                if (j >= NPROJ || !dv) continue;
+                const float *w = staged ? phis + (size_t)j * ND : phi_row(L.layer, j);
+#pragma unroll
+                for (int n = 0; n < N; ++n) {
+                    float wv[P];
+                    load_p<P>(wv, w + n * D + d0);
+#pragma unroll
+                    for (int s = 0; s < SB; ++s)
+#pragma unroll
+                        for (int i = 0; i < P; ++i) part[s][jj] = fmaf(wv[i], nxv[s][n][i], part[s][jj]);
+                }
+            }
+#pragma unroll
+            for (int s = 0; s < SB; ++s)
+#pragma unroll
+                for (int jj = 0; jj < JC; ++jj) {
+                    if (j0 + jj >= NPROJ) continue;
+                    const float v = warp_sum(part[s][jj]);
+                    if (lane == 0) b[warp * SB * NPROJ + s * NPROJ + j0 + jj] = v;
+                }
+        }
+        bar_compute();
+        if (t < SB * NPROJ) {
+            float v = 0.f;
+#pragma unroll
+            for (int w8 = 0; w8 < 8; ++w8) v += b[w8 * SB * NPROJ + t];
+            raws[t / NPROJ][t % NPROJ] = v;
+        }
+        bar_compute();
+    } else {
+        // many CTAs per SM: nx through shared memory, one warp per projection
+        // row streaming it from global memory (16 float4 loads in flight a lane)
+        float *nx = phis;   // [SB][ND]
+#pragma unroll
+        for (int s = 0; s < SB; ++s)
+#pragma unroll
+            for (int n = 0; n < N; ++n)
+                if (dv) store_p<P>(nx + (size_t)s * ND + n * D + d0, nxv[s][n]);
+        bar_compute();
         constexpr int CMAX = N * P * 2;   // float4 chunks per lane at D = 256 P
         const int chunks = ND / 4;
         for (int j = warp; j < NPROJ; j += 8) {
-            const float *w = j < N ? a.phi_pre + (size_t)(L.layer * N + j) * ND
-                           : j < 2 * N ? a.phi_post + (size_t)(L.layer * N + j - N) * ND
-                                       : a.phi_res + (size_t)(L.layer * N * N + j - 2 * N) * ND;
+            const float *w = phi_row(L.layer, j);
             float4 wv[CMAX];
 #pragma unroll
             for (int c = 0; c < CMAX; ++c) {
                 const int k = c * 32 + lane;
                 wv[c] = k < chunks ? __ldg(reinterpret_cast<const float4 *>(w) + k) : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            float acc[SB];
 #pragma unroll
             for (int s = 0; s < SB; ++s) {
-                acc[s] = 0.f;
+                float acc = 0.f;
 #pragma unroll
                 for (int c = 0; c < CMAX; ++c) {
                     const int k = c * 32 + lane;
                     if (k < chunks) {
                         const float4 v = reinterpret_cast<const float4 *>(nx + (size_t)s * ND)[k];
-                        acc[s] = fmaf(wv[c].x, v.x, fmaf(wv[c].y, v.y, fmaf(wv[c].z, v.z, fmaf(wv[c].w, v.w, acc[s]))));
+                        acc = fmaf(wv[c].x, v.x, fmaf(wv[c].y, v.y, fmaf(wv[c].z, v.z, fmaf(wv[c].w, v.w, acc))));
                     }
                 }
-            }
-#pragma unroll
-            for (int s = 0; s < SB; ++s) {
-                const float tot = warp_sum(acc[s]);
-                if (lane == 0) raws[s][j] = tot;
+                acc = warp_sum(acc);
+                if (lane == 0) raws[s][j] = acc;
             }
         }
+        bar_compute();
     }
-    __syncthreads();   // raws ready for every warp, the Sinkhorn warp included
     // engine.cpp:982-986: gates; u = sum_n hpre[n] x[n]
     float hpre[SB][N];
 #pragma unroll
@@ -476,11 +526,13 @@ __global__ void __launch_bounds__(kMixThreads, 2) mhc_mix_kernel(const MixArgs a
             const bool own = n == L.layer % N;
             hpre[s][n] = sigm(__fadd_rn(__fadd_rn(__fmul_rn(L.a_pre, raws[s][n]), L.b_pre[n]), own ? 4.f : -4.f));
         }
-    if (t < SB * 2 * N) {
-        const int s = t / (2 * N), j = t % (2 * N), r = r0 + s;
+    if (t < SB * NPROJ) {
+        // the raw projections, the residual part included: the next layer
+        // boundary normalises it (its Sinkhorn warp)
+        const int s = t / NPROJ, j = t % NPROJ, r = r0 + s;
         if (r < R) {
             a.raw[(size_t)r * a.ldraw + j] = raws[s][j];
-            if (j >= N) {
+            if (j >= N && j < 2 * N) {
                 const int n = j - N;
                 const bool own = n == L.layer % N;
                 a.hpost[(size_t)r * N + n] = __fmul_rn(
@@ -569,26 +621,35 @@ bool mhc_mix_supported(int D, int lanes, int hada) {
 bool launch_mhc_mix(const MixArgs &a, int R, int sms, cudaStream_t st) {
     if (R <= 0) return true;
     if (!mhc_mix_supported(a.D, a.lanes, a.hada)) return false;
-    if (a.has_post && (a.post.hada != a.hada || !a.post.hres_ready)) return false;
+    if (a.has_post && (a.post.hada != a.hada || a.post.hres_ready)) return false;
     if (a.zhl && (a.group < 2 || a.group > a.hada || a.D % a.group || (a.group & (a.group - 1)))) return false;
     const int P = a.hada / 256, N = 4;
-    const int sb = R <= 2 * sms ? 1 : R <= 8 * sms ? 2 : 4;
-    const size_t smem = sizeof(float) * ((size_t)sb * N * a.D + 2 * (size_t)sb * kComputeThreads * P);
+    // Up to one row per SM: one CTA per SM with the routing projections (24
+    // rows of N * D floats) staged whole in shared memory.  More rows: two
+    // rows a CTA, two CTAs per SM, the projections streamed from global
+    // memory (measured faster there than fewer, longer CTAs).
+    const bool staged = R <= sms;
+    const int sb = staged ? 1 : 2;
     const unsigned grid = (unsigned)((R + sb - 1) / sb);
-#define NB_MIX(PP, SBB)                                                                                          \
+    MixArgs args = a;
+    const size_t phi_bytes = sizeof(float) * (size_t)(2 * N + N * N) * N * a.D;
+    size_t smem = sizeof(float) * 2 * (size_t)sb * kComputeThreads * P;
+    args.phi_smem = staged && a.has_route && smem + phi_bytes <= 220 * 1024 ? 1 : 0;
+    smem += args.phi_smem ? phi_bytes : sizeof(float) * (size_t)sb * N * a.D;   // (else nx of the rows)
+#define NB_MIX(PP, SBB, ST)                                                                                      \
     {                                                                                                          \
-        auto kernel = mhc_mix_kernel<PP, 4, SBB>;                                                              \
+        auto kernel = mhc_mix_kernel<PP, 4, SBB, ST>;                                                          \
         static bool configured = false;                                                                        \
         if (!configured) {                                                                                     \
-            NB_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024)); \
+            NB_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024)); \
             configured = true;                                                                                 \
         }                                                                                                      \
-        NB_CUDA_TRY(launch_pdl(kernel, grid, kMixThreads, smem, st, a, R));                                     \
+        NB_CUDA_TRY(launch_pdl(kernel, grid, kMixThreads, smem, st, args, R));                                  \
     }
     if (P == 1) {
-        if (sb == 1) NB_MIX(1, 1) else if (sb == 2) NB_MIX(1, 2) else NB_MIX(1, 4)
+        if (staged) NB_MIX(1, 1, true) else NB_MIX(1, 2, false)
     } else {
-        if (sb == 1) NB_MIX(2, 1) else if (sb == 2) NB_MIX(2, 2) else NB_MIX(2, 4)
+        if (staged) NB_MIX(2, 1, true) else NB_MIX(2, 2, false)
     }
 #undef NB_MIX
     NB_CUDA_TRY(cudaGetLastError());
