@@ -689,13 +689,14 @@ def decoder_prompts():
     return np.random.default_rng(0).integers(3, DEC_VOCAB, (DEC_SESSIONS, DEC_PROMPT)).astype(np.int32)
 
 
-def decoder_config(world):
-    return {"workload": f"needle2_config5_decode_{DEC_SESSIONS}x{DEC_PROMPT}", "sessions": DEC_SESSIONS,
+def decoder_config(world, per_gpu=None):
+    sessions = (per_gpu or DEC_SESSIONS // world) * world
+    return {"workload": f"needle2_config5_decode_{sessions}x{DEC_PROMPT}", "sessions": sessions,
             "prompt_tokens": DEC_PROMPT, "d_model": 512, "layers": 12, "heads": 8, "kv_heads": 4, "head_dim": 64,
             "vocab": DEC_VOCAB, "engram_layers": [2, 9], "matmul": "fp32 (CQ dequant-accumulate)", "kv_cache": "int8",
             "weights": "CQ4 embedding + mHC, CQ2 projections + engram tables (reference quantizer)",
             "parallelism": f"sessions split over {world} GPU(s), weights replicated, no collective",
-            "l2": f"inputs larger than L2: each step reads ~{DEC_SESSIONS * 12 * 4 * 2 * 136 * DEC_PROMPT / 1e9:.1f} GB "
+            "l2": f"inputs larger than L2: each step reads more than {sessions * 12 * 4 * 2 * 68 * DEC_PROMPT / 1e9:.1f} GB "
                   "of INT8 KV"}
 
 
@@ -772,11 +773,11 @@ def decoder_native(args, rank, world, dist, dev):
 
     if DEC_SESSIONS % world:
         raise SystemExit(f"{DEC_SESSIONS} sessions do not split over {world} GPUs")
-    S = DEC_SESSIONS // world
+    S = args.sessions_per_gpu or DEC_SESSIONS // world
     archive = decoder_archive()
     model = GpuModel(archive, kv_cache="int8", matmul="fp32")
     batch = model.batch(S)
-    prompts = decoder_prompts()[rank * S:(rank + 1) * S]
+    prompts = np.resize(decoder_prompts(), (S * world, DEC_PROMPT))[rank * S:(rank + 1) * S]
     t0 = time.perf_counter()
     _, first = batch.prefill(prompts, logits=False, greedy=True)
     prefill_s = time.perf_counter() - t0
@@ -793,10 +794,14 @@ def decoder_native(args, rank, world, dist, dev):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     position0 = int(batch.positions()[0])
     with ClockSampler(dev.index) as clocks:
+        if args.profile_range:
+            torch.cuda.profiler.start()
         start.record(stream)
         batch.decode_greedy_device(cur, args.steps, out, stream)
         end.record(stream)
         torch.cuda.synchronize(dev)
+        if args.profile_range:
+            torch.cuda.profiler.stop()
     elapsed_ms = start.elapsed_time(end)
     batch_kernels = batch.step_kernels()
     cur = out[:, -1].contiguous()
@@ -825,7 +830,7 @@ def decoder_native(args, rank, world, dist, dev):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     elapsed_ms, e2e_s, prefill_s = t.tolist()
     ms_step = elapsed_ms / args.steps
-    tokens_per_s = DEC_SESSIONS * args.steps / (elapsed_ms * 1e-3)
+    tokens_per_s = S * world * args.steps / (elapsed_ms * 1e-3)
     mid = position0 + args.steps // 2
     step_bytes_all, _ = decode_bytes(S, mid)
     _, attn_bytes = decode_bytes(S, position_p + prof_steps // 2)
@@ -848,7 +853,7 @@ def decoder_native(args, rank, world, dist, dev):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": decoder_config(world),
+        "config": decoder_config(world, S),
         "roofline": {"bound": "hbm", "achieved": attn_gbs, "peak": hbm, "unit": "GB/s", "frac": attn_gbs / hbm,
                      "peak_source": peak_kind,
                      "kernel": "KV store + attention stage (kv_quantize_kernel, attn_stream_kernel, "
@@ -860,7 +865,7 @@ def decoder_native(args, rank, world, dist, dev):
         "stages_ms_per_step": stages,
         "dominant_stage": dominant,
         "profiled_step_ms": total_prof,
-        "e2e": {"value": DEC_SESSIONS / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4 * S,
+        "e2e": {"value": S * world / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4 * S,
                 "d2h_bytes_per_step": 4 * S, "ms_per_step": e2e_s * 1e3,
                 "call": "needle2_batch_step per step (this rank's sessions' tokens copied in from host memory, "
                         "their greedy tokens read back; synchronised)"},
@@ -920,6 +925,11 @@ def main():
     ap.add_argument("--skip-sweep", action="store_true", help="omit the config-3 prefill GEMM shape sweep")
     ap.add_argument("--skip-attention", action="store_true", help="omit the INT8 KV attention side measurement")
     ap.add_argument("--skip-gemv", action="store_true", help="omit the fused CQ4 GEMV side line")
+    ap.add_argument("--sessions-per-gpu", type=int, default=0,
+                    help="decode sessions per GPU (default: config 5's 1024 split over the GPUs); other values "
+                         "measure one GPU's share of a larger run and name the workload accordingly")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="bracket the timed decode steps with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--skip-sharded", action="store_true",
                     help="omit the N-sharded GEMM + all-gather side measurement (multi-GPU runs)")
     args = ap.parse_args()
