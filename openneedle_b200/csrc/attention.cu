@@ -17,6 +17,7 @@
 // Device layout (head-major, so one (sequence, KV head) is one contiguous
 // stream):  prefix  k/v [KV][P][HD] int8, scales [KV][P];  per session
 // k/v [S][KV][Cs][HD], scales [S][KV][Cs], Cs = window ? window : max_seq - P.
+#include <cuda_bf16.h>
 #include <math.h>
 
 #include <algorithm>
@@ -464,7 +465,7 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
     constexpr int NW = Geo::NW, DL = Geo::DL, U = Geo::U, WL = DL / 4, CH = Geo::CH, NCH = Geo::NCH;
     constexpr bool QREG = R * DL <= 32;   // query slice in registers
     static_assert(!WPQ || QREG, "warp-per-query needs the query slice in registers");
-    __shared__ __align__(16) uint8_t ring_all[NW * Geo::RING];
+    extern __shared__ __align__(16) uint8_t ring_all[];   // [NW][Geo::RING], dynamic (stream_smem)
     __shared__ __align__(16) float qs[WPQ ? 4 : R * HD];
     __shared__ float wm[WPQ ? 1 : NW][R], wl[WPQ ? 1 : NW][R];
     __shared__ float wacc[WPQ ? 1 : NW][R][WPQ ? 1 : HD];
@@ -666,13 +667,15 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
             // lanes 0-3 hold the whole sums for dimensions c * DL ..; the softmax
             // denominator was counted on the c == 0 lanes only, so lane 0 has it
             const float lt = __shfl_sync(kFull, l[r], 0);
-            if (j == 0) {
-                const float inv = lt > 0.f ? 1.f / lt : 0.f;
-                const size_t o0 = ((size_t)query * p.heads + kh * R + r) * HD + c * DL;
+            const float inv = lt > 0.f ? 1.f / lt : 0.f;
+            const size_t o0 = ((size_t)query * p.heads + kh * R + r) * HD + c * DL;
 #pragma unroll
-                for (int e = 0; e < DL / 2; ++e) {
-                    p.out[o0 + 2 * e] = gated(p, o0 + 2 * e, acc[r][e].x * inv);
-                    p.out[o0 + 2 * e + 1] = gated(p, o0 + 2 * e + 1, acc[r][e].y * inv);
+            for (int e = 0; e < DL / 2; ++e) {
+                acc[r][e].x = gated(p, o0 + 2 * e, acc[r][e].x * inv);
+                acc[r][e].y = gated(p, o0 + 2 * e + 1, acc[r][e].y * inv);
+                if (j == 0) {
+                    p.out[o0 + 2 * e] = acc[r][e].x;
+                    p.out[o0 + 2 * e + 1] = acc[r][e].y;
                 }
             }
             continue;
@@ -685,7 +688,69 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
 #pragma unroll
             for (int e = 0; e < DL / 2; ++e) *reinterpret_cast<float2 *>(&wacc[warp][r][c * DL + 2 * e]) = acc[r][e];
     }
-    if (WPQ) return;
+    if constexpr (WPQ) {
+        if (p.hilo) {
+            // the out projection's input rotation (CQ::transform over the R * HD
+            // outputs of this KV head: element r * HD + c * DL + i) and bf16
+            // split, with the Walsh-Hadamard stages in order h = 1, 2, 4, ...:
+            // i bits in registers, c bits across lanes 0-3, r bits in registers
+            float v[R][DL];
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+#pragma unroll
+                for (int e = 0; e < DL / 2; ++e) {
+                    v[r][2 * e] = acc[r][e].x;
+                    v[r][2 * e + 1] = acc[r][e].y;
+                }
+#pragma unroll
+            for (int h = 1; h < DL; h *= 2)
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+#pragma unroll
+                    for (int i = 0; i < DL; ++i)
+                        if (!(i & h)) {
+                            const float a = v[r][i], b = v[r][i + h];
+                            v[r][i] = __fadd_rn(a, b);
+                            v[r][i + h] = __fsub_rn(a, b);
+                        }
+#pragma unroll
+            for (int m = 1; m < 4; m *= 2) {
+                const bool upper = c & m;
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+#pragma unroll
+                    for (int i = 0; i < DL; ++i) {
+                        const float o = __shfl_xor_sync(kFull, v[r][i], m);
+                        v[r][i] = upper ? __fsub_rn(o, v[r][i]) : __fadd_rn(v[r][i], o);
+                    }
+            }
+#pragma unroll
+            for (int h = 1; h < R; h *= 2)
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+                    if (!(r & h))
+#pragma unroll
+                        for (int i = 0; i < DL; ++i) {
+                            const float a = v[r][i], b = v[r + h][i];
+                            v[r][i] = __fadd_rn(a, b);
+                            v[r + h][i] = __fsub_rn(a, b);
+                        }
+            if (j == 0) {
+                const size_t row = (size_t)query * p.hilo_ld + (size_t)kh * R * HD + c * DL;
+#pragma unroll
+                for (int r = 0; r < R; ++r)
+#pragma unroll
+                    for (int i = 0; i < DL; ++i) {
+                        const float x = __fmul_rn(v[r][i], p.rot_scale);
+                        const __nv_bfloat16 hv = __float2bfloat16_rn(x);
+                        p.hilo[row + r * HD + i] = __bfloat16_as_ushort(hv);
+                        p.hilo[p.hilo_lo + row + r * HD + i] =
+                            __bfloat16_as_ushort(__float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hv))));
+                    }
+            }
+        }
+        return;
+    }
     __syncthreads();
     for (int idx = threadIdx.x; idx < R * HD; idx += blockDim.x) {
         const int r = idx / HD, d = idx % HD;
@@ -902,21 +967,28 @@ bool launch_prefill_tile(const AttnParams &p, int entries, int R, cudaStream_t s
     }
 }
 
+// Dynamic shared memory of attn_stream_kernel<HD, ...>: the warps' copy rings.
+template <int HD>
+constexpr size_t stream_smem() { return (size_t)StreamGeo<HD>::NW * StreamGeo<HD>::RING; }
+
+template <typename K>
+bool launch_ring_kernel(K kernel, size_t smem, dim3 grid, cudaStream_t st, const AttnParams &p) {
+    if (smem > 48 * 1024)   // (every launch: the kernels share K, so a per-type flag would not do)
+        NB_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    NB_CUDA_TRY(launch_pdl(kernel, grid, 128, smem, st, p));
+    return true;
+}
+
 template <int HD, bool WPQ>
 bool launch_stream(const AttnParams &p, dim3 grid, int R, cudaStream_t st) {
+    constexpr size_t smem = stream_smem<HD>();
     switch (R) {
-        case 1: NB_CUDA_TRY(launch_pdl(attn_stream_kernel<HD, 1, WPQ>, grid, 128, 0, st, p)); return true;
+        case 1: return launch_ring_kernel(attn_stream_kernel<HD, 1, WPQ>, smem, grid, st, p);
         case 2:
-            if constexpr (!WPQ || 2 * HD / 4 <= 32) {
-                NB_CUDA_TRY(launch_pdl(attn_stream_kernel<HD, 2, WPQ>, grid, 128, 0, st, p));
-                return true;
-            }
+            if constexpr (!WPQ || 2 * HD / 4 <= 32) return launch_ring_kernel(attn_stream_kernel<HD, 2, WPQ>, smem, grid, st, p);
             return false;
         case 4:
-            if constexpr (HD <= 64 && !WPQ) {
-                NB_CUDA_TRY(launch_pdl(attn_stream_kernel<HD, 4, false>, grid, 128, 0, st, p));
-                return true;
-            }
+            if constexpr (HD <= 64 && !WPQ) return launch_ring_kernel(attn_stream_kernel<HD, 4, false>, smem, grid, st, p);
             return false;
         default: return false;
     }
@@ -939,6 +1011,50 @@ __global__ void attn_combine_kernel(const AttnParams p, int hd) {
         }
         p.out[(size_t)qh * hd + d] = gated(p, (size_t)qh * hd + d, ll > 0.f ? aa / ll : 0.f);
     }
+}
+
+// The split combine for one (query, KV head) with the out projection's input
+// rotation: thread t = r * hd + d combines head kh * R + r, dimension d as
+// attn_combine_kernel does, then the R * hd outputs are rotated (stages
+// h < 32 across lanes, the rest through shared memory, in order) and split.
+__global__ void attn_combine_rot_kernel(const AttnParams p, int hd) {
+    pdl_enter();
+    extern __shared__ float xs[];   // [2][R * hd]
+    const int R = p.heads / p.kvheads, n = R * hd;
+    const int t = threadIdx.x;
+    const int query = blockIdx.x / p.kvheads, kh = blockIdx.x % p.kvheads;
+    const int r = t / hd, d = t % hd;
+    const int qh = query * p.heads + kh * R + r;
+    const float *pm = p.part_m + (size_t)qh * p.splits, *pl = p.part_l + (size_t)qh * p.splits;
+    float mm = -INFINITY;
+    for (int j = 0; j < p.splits; ++j) mm = fmaxf(mm, pm[j]);
+    float ll = 0.f, aa = 0.f;
+    for (int j = 0; j < p.splits; ++j) {
+        if (pm[j] == -INFINITY) continue;
+        const float f = expf(pm[j] - mm);
+        ll += pl[j] * f;
+        aa += p.part_acc[((size_t)qh * p.splits + j) * hd + d] * f;
+    }
+    float v = gated(p, (size_t)qh * hd + d, ll > 0.f ? aa / ll : 0.f);
+    p.out[(size_t)qh * hd + d] = v;
+    int h = 1;
+    for (; h < 32 && h < n; h *= 2) {
+        const float o = __shfl_xor_sync(kFull, v, h);
+        v = (t & h) ? __fsub_rn(o, v) : __fadd_rn(v, o);
+    }
+    int buf = 0;
+    for (; h < n; h *= 2) {
+        xs[buf * n + t] = v;
+        __syncthreads();
+        const float o = xs[buf * n + (t ^ h)];
+        v = (t & h) ? __fsub_rn(o, v) : __fadd_rn(v, o);
+        buf ^= 1;
+    }
+    const float x = __fmul_rn(v, p.rot_scale);
+    const size_t i = (size_t)query * p.hilo_ld + (size_t)kh * n + t;
+    const __nv_bfloat16 hv = __float2bfloat16_rn(x);
+    p.hilo[i] = __bfloat16_as_ushort(hv);
+    p.hilo[p.hilo_lo + i] = __bfloat16_as_ushort(__float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hv))));
 }
 
 }  // namespace
@@ -969,8 +1085,24 @@ int attention_splits(int max_len, int queries_x_kv, int sms) {
     return splits;
 }
 
-bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
+// The split combine, rotating for the out projection where p.hilo asks for it.
+bool launch_combine(const AttnParams &p, int queries, cudaStream_t st, bool *rot_done) {
+    const int n = p.heads / p.kvheads * p.hd;
+    if (p.hilo && n % 32 == 0 && n <= 1024) {
+        NB_CUDA_TRY(launch_pdl(attn_combine_rot_kernel, queries * p.kvheads, n, 2 * n * sizeof(float), st, p, p.hd));
+        if (rot_done) *rot_done = true;
+    } else {
+        NB_CUDA_TRY(launch_pdl(attn_combine_kernel, queries * p.heads, 64, 0, st, p, p.hd));
+    }
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+}
+
+bool launch_attention(const AttnParams &p_in, int queries, cudaStream_t st, bool *rot_done) {
+    if (rot_done) *rot_done = false;
     if (queries <= 0) return true;
+    AttnParams p = p_in;
+    if (p.tokens != 1) p.hilo = nullptr;   // decode only
     if (p.heads % p.kvheads || p.heads / p.kvheads > kMaxQueryGroup) {
         set_error("attention supports up to 8 query heads per KV head");
         return false;
@@ -992,10 +1124,7 @@ bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
                 }
         }
         NB_CUDA_TRY(cudaGetLastError());
-        if (p.splits > 1) {
-            NB_CUDA_TRY(launch_pdl(attn_combine_kernel, queries * p.heads, 64, 0, st, p, p.hd));
-            NB_CUDA_TRY(cudaGetLastError());
-        }
+        if (p.splits > 1) return launch_combine(p, queries, st, rot_done);
         return true;
     }
     // prefill chunks of 16+ tokens: query tiles share every K/V read
@@ -1009,8 +1138,14 @@ bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
     const bool wpq = p.splits == 1 && ((p.hd == 64 && R <= 2) || (p.hd == 128 && R <= 1));
     AttnParams pw = p;
     pw.queries = queries;
+    // the warp-per-query epilogue rotates one KV head's 2 x 64 outputs
+    if (!(wpq && p.hd == 64 && R == 2)) pw.hilo = nullptr;
+    p.hilo = p.splits > 1 ? p.hilo : nullptr;   // the stream kernels themselves never write it
     const dim3 wgrid(1, p.kvheads, (queries + 3) / 4);
-    if (wpq && p.hd == 64) streamed = launch_stream<64, true>(pw, wgrid, R, st);
+    if (wpq && p.hd == 64) {
+        streamed = launch_stream<64, true>(pw, wgrid, R, st);
+        if (streamed && pw.hilo && rot_done) *rot_done = true;
+    }
     else if (wpq && p.hd == 128) streamed = launch_stream<128, true>(pw, wgrid, R, st);
     // the streaming kernel where its per-lane state fits in registers
     else if (p.hd == 64 && R <= 4) streamed = launch_stream<64, false>(p, grid, R, st);
@@ -1029,10 +1164,7 @@ bool launch_attention(const AttnParams &p, int queries, cudaStream_t st) {
             }
     }
     NB_CUDA_TRY(cudaGetLastError());
-    if (p.splits > 1) {
-        NB_CUDA_TRY(launch_pdl(attn_combine_kernel, queries * p.heads, 64, 0, st, p, p.hd));
-        NB_CUDA_TRY(cudaGetLastError());
-    }
+    if (p.splits > 1) return launch_combine(p, queries, st, rot_done);
     return true;
 }
 

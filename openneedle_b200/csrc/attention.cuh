@@ -41,6 +41,22 @@ struct AttnParams {
     float *out;                       // [queries][heads][HD]
     const float *gate;                // null, or [queries][heads][HD]: out is written as out * sigmoid(gate)
     float *part_m, *part_l, *part_acc; // split partials (splits > 1)
+    // null, or the operands of the out projection's tensor-core GEMM: out of
+    // each query, rotated per group of heads / kvheads heads (one KV head's
+    // query heads, the CQ group of the out projection) and split into bf16
+    // hi [queries][hilo_ld] and lo (at hilo + hilo_lo)
+    uint16_t *hilo;
+    long long hilo_lo;
+    int hilo_ld;
+    float rot_scale;
+};
+
+// Request for AttnParams::hilo (see there); group must equal heads / kvheads * hd.
+struct AttnRot {
+    uint16_t *hilo;
+    long long lo_off;
+    int ld, group;
+    float scale;
 };
 
 // INT8: quantise (engine.cpp:1005-1021) and store k/v [tokens][kvheads*hd].
@@ -50,6 +66,8 @@ bool launch_kv_quantize(const float *k, const float *v, int tokens, int kvheads,
 bool launch_kv_store_f32(const float *k, const float *v, int tokens, int kvheads, int hd, float *ko, float *vo,
                          const KVDest &dest, cudaStream_t st);
 int attention_splits(int max_len, int queries_x_kv, int sms);
-bool launch_attention(const AttnParams &p, int queries, cudaStream_t st);
+// rot_done (optional): whether p.hilo was written (the decode forms write it;
+// the others leave it to the caller and launch as if it were null).
+bool launch_attention(const AttnParams &p, int queries, cudaStream_t st, bool *rot_done = nullptr);
 
 }  // namespace nb200

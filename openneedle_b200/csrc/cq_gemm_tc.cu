@@ -769,6 +769,7 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_
 constexpr int kSplitBN = 256;
 constexpr bool kSplitK = false;   // measured slower than the unsplit 64-wide tiles
 constexpr int kDecodeAcc = 1;      // accumulators per 64-wide tile
+constexpr bool kNarrow32 = false;   // 32-wide tiles for the smallest decode grids (measured slower)
 
 __global__ void __launch_bounds__(kFThreads, 1)
     cq_gemm_f32x3_splitk_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
@@ -1076,7 +1077,14 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
         while (ks < 8 && steps % (2 * ks) == 0 && (long long)mtiles * wide * 2 * ks <= sms) ks *= 2;
     const bool split = ks > 1;
     const bool narrow = !split && (long long)mtiles * wide < 2LL * sms;
-    const int BN = narrow ? 64 : 256;
+    // the decode epilogue: four segments (q, k, v, gate) of whole 64-wide heads
+    const bool with_epi = narrow && epi && epi->active && count == 4 && epi->hd == 64;
+    // 32-wide tiles (twice the CTAs again, each MMA half as wide) where even the
+    // 64-wide grid leaves most SMs idle
+    int tiles64 = 0;
+    for (int i = 0; i < count; ++i) tiles64 += (outs[i].N + 63) / 64;
+    const bool narrow32 = kNarrow32 && narrow && !with_epi && (long long)mtiles * tiles64 * 2 <= sms;
+    const int BN = narrow32 ? 32 : narrow ? 64 : 256;
     const size_t an = (size_t)M * padded;
     CUtensorMap tah, tal;
     // bf16 rows seen as bytes: 2 * padded bytes per row, 128-byte (64-element) boxes
@@ -1111,7 +1119,7 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
     attr[1].val.clusterDim.z = (unsigned)ks;
     cfg.attrs = attr;
     cfg.numAttrs = split ? 2 : 1;
-    static bool configured[6][64] = {};
+    static bool configured[7][64] = {};
     if (split) {
         constexpr size_t smem = FTile<kSplitBN, 2>::kSmem;
         if (dev < 0 || dev >= 64 || !configured[3][dev]) {
@@ -1133,8 +1141,7 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
         return true;
     };
     if (!narrow) return launch(cq_gemm_f32x3_kernel<256, 2, 1, false>, FTile<256, 2>::kSmem, 0);
-    // the decode epilogue: four segments (q, k, v, gate) of whole 64-wide heads
-    const bool with_epi = epi && epi->active && count == 4 && epi->hd == 64;
+    if (narrow32) return launch(cq_gemm_f32x3_kernel<32, 4, kDecodeAcc, false>, FTile<32, 4>::kSmem, 6);
     if (with_epi) {
         args.epi = *epi;
         if (epi_done) *epi_done = true;

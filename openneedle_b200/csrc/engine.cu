@@ -126,6 +126,7 @@ struct Model {
 struct Scratch {
     DevBuf<float> x, nx, raw, hpost, u, bx, z, q, k, v, gate, att, proj, e, ek, ev, rawv, zf, logits, hidden;
     DevBuf<uint16_t> zhl;   // z rotated and split into the QKVG GEMM's bf16 operands
+    DevBuf<uint16_t> ahl;   // the attention output rotated and split for the out projection
     DevBuf<int64_t> ids;
     DevBuf<uint8_t> valid;
     DevBuf<int> rsess, rpos, tokens, argmax;
@@ -675,7 +676,8 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
             // decode: the new token's K/V stored as RoPE finishes, then attention alone
             check(eng::launch_qk_rope_store(s.q.ptr, s.k.ptr, s.v.ptr, R, c.heads, c.kvheads, c.head_dim,
                                             m.t[ti + 4].dense, m.t[ti + 5].dense, s.rpos.ptr, m.rope_divisor,
-                                            kv_pool_target(st.kv[l], st.iota.ptr, st.base.ptr), stream),
+                                            kv_pool_target(st.kv[l], st.iota.ptr, st.base.ptr), stream, m.rope_cos,
+                                            m.rope_sin, m.rope_len),
                   "q/k norm, RoPE and KV store");
         } else {
             check(eng::launch_qk_norm_rope(s.q.ptr, s.k.ptr, R, c.heads, c.kvheads, c.head_dim, m.t[ti + 4].dense,
@@ -684,12 +686,32 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         }
         mark(st, 4, stream);
         // attention with the output gate applied as it is written (engine.cpp:1022-1023)
+        // at decode the attention kernels also write their output rotated and split
+        // into the out projection's GEMM operands, when that GEMM takes them
+        AttnRot rot{};
+        void *oh = nullptr;
+        bool want_rot = false, rotated = false;
+        if (T == 1 && !m.abits && m.t[ti + 7].cq) {
+            oh = m.handle(ti + 7);
+            int G = 0;
+            float sc = 0.f;
+            if (handle_hilo_gemm(&oh, 1, R, &G, &sc)) {
+                s.ahl.reserve(2 * (size_t)R * A);
+                rot = AttnRot{s.ahl.ptr, (long long)R * A, A, G, sc};
+                want_rot = true;
+            }
+        }
         check(kv_pool_run(st.kv[l], T == 1 ? kQuery : kPrefill, st.iota.ptr, st.base.ptr, E, T, max_visible, s.q.ptr,
-                          s.k.ptr, s.v.ptr, s.att.ptr, stream, s.gate.ptr),
+                          s.k.ptr, s.v.ptr, s.att.ptr, stream, s.gate.ptr, want_rot ? &rot : nullptr, &rotated),
               "attention");
         mark(st, 5, stream);
-        aq(m, s.att.ptr, R, A, stream);
-        linear(m, ti + 7, s.att.ptr, R, s.proj.ptr, stream);
+        if (rotated) {
+            float *ys[1] = {s.proj.ptr};
+            check(handle_many_hilo(&oh, 1, s.ahl.ptr, ys, R, stream), "out projection");
+        } else {
+            aq(m, s.att.ptr, R, A, stream);
+            linear(m, ti + 7, s.att.ptr, R, s.proj.ptr, stream);
+        }
         mark(st, 6, stream);
         float *hid = o.hidden ? s.hidden.ptr + (size_t)l * D : nullptr;
         const bool last = l + 1 == c.layers;

@@ -69,10 +69,13 @@ bool launch_qk_norm_rope(float *q, float *k, int R, int heads, int kvheads, int 
 struct KVStoreTarget;
 namespace eng {
 // launch_qk_norm_rope, then the KV store of the row's token (one token per
-// row; the positions are the rows' positions) into target.
+// row; the positions are the rows' positions) into target.  cos_t / sin_t
+// (optional, [table_len][hd / 2]): cosf / sinf of position / divisor, read
+// instead of evaluated for positions the table covers (the same values).
 bool launch_qk_rope_store(float *q, float *k, const float *v, int R, int heads, int kvheads, int hd,
                           const float *q_norm, const float *k_norm, const int *pos, const float *divisor,
-                          const KVStoreTarget &target, cudaStream_t st);
+                          const KVStoreTarget &target, cudaStream_t st, const float *cos_t = nullptr,
+                          const float *sin_t = nullptr, int table_len = 0);
 
 // att *= sigmoid(gate) (engine.cpp:1023).
 bool launch_gate(float *att, const float *gate, int R, int A, cudaStream_t st);

@@ -311,7 +311,8 @@ __global__ void qk_norm_rope_kernel(float *__restrict__ q, float *__restrict__ k
 __global__ void qk_rope_store_kernel(float *__restrict__ q, float *__restrict__ k, const float *__restrict__ v,
                                      int heads, int kvheads, int hd, const float *__restrict__ q_norm,
                                      const float *__restrict__ k_norm, const int *__restrict__ pos,
-                                     const float *__restrict__ divisor, const KVStoreTarget t) {
+                                     const float *__restrict__ divisor, const KVStoreTarget t,
+                                     const float *__restrict__ cos_t, const float *__restrict__ sin_t, int table_len) {
     pdl_enter();
     extern __shared__ float buf[];   // [warps][hd]
     const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -332,9 +333,17 @@ __global__ void qk_rope_store_kernel(float *__restrict__ q, float *__restrict__ 
             for (int i = lane; i < hd; i += 32) b[i] = __fmul_rn(__fmul_rn(vp[i], inv), __fadd_rn(1.f, nrm[i]));
             __syncwarp();
             const int half = hd / 2;
+            const bool tab = cos_t && pos[r] < table_len;   // the per-position table, where it covers
             for (int j = lane; j < half; j += 32) {
-                const float ang = __fdiv_rn(fpos, divisor[j]);
-                const float co = cosf(ang), si = sinf(ang);
+                float co, si;
+                if (tab) {
+                    co = cos_t[(size_t)pos[r] * half + j];
+                    si = sin_t[(size_t)pos[r] * half + j];
+                } else {
+                    const float ang = __fdiv_rn(fpos, divisor[j]);
+                    co = cosf(ang);
+                    si = sinf(ang);
+                }
                 const float a = b[j], c = b[j + half];
                 vp[j] = __fsub_rn(__fmul_rn(a, co), __fmul_rn(c, si));
                 vp[j + half] = __fadd_rn(__fmul_rn(c, co), __fmul_rn(a, si));
@@ -955,11 +964,12 @@ bool launch_qk_norm_rope(float *q, float *k, int R, int heads, int kvheads, int 
 
 bool launch_qk_rope_store(float *q, float *k, const float *v, int R, int heads, int kvheads, int hd,
                           const float *q_norm, const float *k_norm, const int *pos, const float *divisor,
-                          const KVStoreTarget &t, cudaStream_t st) {
+                          const KVStoreTarget &t, cudaStream_t st, const float *cos_t, const float *sin_t,
+                          int table_len) {
     if (R <= 0) return true;
     const int warps = std::min(heads + 2 * kvheads, 32);
     NB_CUDA_TRY(launch_pdl(qk_rope_store_kernel, R, 32 * warps, sizeof(float) * warps * hd, st, q, k, v, heads, kvheads, hd, q_norm,
-                                                                           k_norm, pos, divisor, t));
+                           k_norm, pos, divisor, t, cos_t, sin_t, table_len));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }

@@ -164,9 +164,16 @@ bool store_ring(KVPool &kv, const int *ids, const int *pos, const float *k, cons
 // Attention of `count` entries x `tokens` queries; staging holds the entries'
 // own new K/V when `staged` (prefill).
 bool attend(KVPool &kv, const int *ids, const int *pos, int count, int tokens, int max_len, const float *q, float *out,
-            bool staged, cudaStream_t st, const float *gate = nullptr) {
+            bool staged, cudaStream_t st, const float *gate = nullptr, const AttnRot *rot = nullptr,
+            bool *rot_done = nullptr) {
     AttnParams p = base_params(kv);
     p.gate = gate;
+    if (rot && rot->group == kv.heads / kv.kvheads * kv.hd) {
+        p.hilo = rot->hilo;
+        p.hilo_lo = rot->lo_off;
+        p.hilo_ld = rot->ld;
+        p.rot_scale = rot->scale;
+    }
     p.tokens = tokens;
     p.session = ids;
     p.position = pos;
@@ -184,7 +191,7 @@ bool attend(KVPool &kv, const int *ids, const int *pos, int count, int tokens, i
         if (!kv.pm.reserve(rows) || !kv.pl.reserve(rows) || !kv.pacc.reserve(rows * kv.hd)) return false;
         p.part_m = kv.pm.ptr; p.part_l = kv.pl.ptr; p.part_acc = kv.pacc.ptr;
     }
-    return launch_attention(p, queries, st);
+    return launch_attention(p, queries, st, rot_done);
 }
 
 // The chunk's own K/V in the staging layout [KV][rows][HD] (quantised for INT8).
@@ -280,11 +287,13 @@ int kv_max_visible(int prefix, int window, const int *positions, int count, int 
 }
 
 bool kv_pool_run(KVPool *kv, KVOp op, const int *ids, const int *pos, int count, int tokens, int max_visible,
-                 const float *q, const float *k, const float *v, float *out, cudaStream_t st, const float *gate) {
+                 const float *q, const float *k, const float *v, float *out, cudaStream_t st, const float *gate,
+                 const AttnRot *rot, bool *rot_done) {
+    if (rot_done) *rot_done = false;
     if (count <= 0) return true;
     switch (op) {
         case kStore: return store_ring(*kv, ids, pos, k, v, count, tokens, 0, st);
-        case kQuery: return attend(*kv, ids, pos, count, tokens, max_visible, q, out, false, st, gate);
+        case kQuery: return attend(*kv, ids, pos, count, tokens, max_visible, q, out, false, st, gate, rot, rot_done);
         case kDecode:
             if (tokens != 1) { set_error("decode takes one token per entry"); return false; }
             return store_ring(*kv, ids, pos, k, v, count, 1, 0, st) &&

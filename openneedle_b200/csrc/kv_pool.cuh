@@ -39,9 +39,11 @@ int kv_max_visible(int prefix, int window, const int *pos_host, int count, int t
 enum KVOp { kStore = 0, kDecode = 1, kPrefill = 2, kQuery = 3 };
 // gate (optional, same layout as out): out is written as out * sigmoid(gate),
 // the engine's attention output gate (engine.cpp:1023).
+// rot (optional, kQuery): also write out rotated and split for the out
+// projection's GEMM (AttnRot); *rot_done tells whether it was.
 bool kv_pool_run(KVPool *kv, KVOp op, const int *ids, const int *pos, int count, int tokens, int max_visible,
                  const float *q, const float *k, const float *v, float *out, cudaStream_t st,
-                 const float *gate = nullptr);
+                 const float *gate = nullptr, const AttnRot *rot = nullptr, bool *rot_done = nullptr);
 
 // Where kStore puts one token per entry (ids/pos device arrays): the ring
 // destination with this pool's arrays, for kernels that store K/V themselves
