@@ -856,9 +856,10 @@ def decoder_native(args, rank, world, dist, dev):
         "config": decoder_config(world, S),
         "roofline": {"bound": "hbm", "achieved": attn_gbs, "peak": hbm, "unit": "GB/s", "frac": attn_gbs / hbm,
                      "peak_source": peak_kind,
-                     "kernel": "KV store + attention stage (kv_quantize_kernel, attn_stream_kernel, "
-                               "attn_combine_kernel; 12 layers per step)",
+                     "kernel": "attention stage (attn_stream_kernel, one launch per layer, 12 per step; with "
+                               "fewer sessions also attn_combine_rot_kernel); achieved and traffic per launch",
                      "stage_ms_per_step": attn_ms, "algorithmic_bytes_per_step": attn_bytes,
+                     "algorithmic_bytes_per_launch": attn_bytes / 12,
                      "traffic": profiled_traffic("attn_stream_decode_config5")},
         "step_hbm": {"achieved_gbs": step_gbs, "frac": step_gbs / hbm, "algorithmic_bytes_per_step": step_bytes_all,
                      "note": "all of a step's algorithmic bytes (decode_bytes) over the timed step"},

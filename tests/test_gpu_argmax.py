@@ -14,7 +14,8 @@ def native():
     return native
 
 
-@pytest.mark.parametrize("rows,vocab,ld", [(1, 32768, 32768), (7, 1000, 1003), (64, 5, 5), (3, 1, 1)])
+@pytest.mark.parametrize("rows,vocab,ld", [(1, 32768, 32768), (7, 1000, 1003), (64, 5, 5), (3, 1, 1),
+                                         (8, 1000, 1000), (16, 32768, 32768), (5, 4, 8)])
 def test_argmax_matches_oracle(native, oracle_lib, rows, vocab, ld):
     import torch
     rng = np.random.default_rng(rows * 7 + vocab)
