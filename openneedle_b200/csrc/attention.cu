@@ -465,7 +465,8 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
     constexpr int NW = Geo::NW, DL = Geo::DL, U = Geo::U, WL = DL / 4, CH = Geo::CH, NCH = Geo::NCH;
     constexpr bool QREG = R * DL <= 32;   // query slice in registers
     static_assert(!WPQ || QREG, "warp-per-query needs the query slice in registers");
-    extern __shared__ __align__(16) uint8_t ring_all[];   // [NW][Geo::RING], dynamic (stream_smem)
+    extern __shared__ __align__(16) uint8_t ring_raw[];   // [NW][Geo::RING] from a 128-byte boundary (stream_smem)
+    uint8_t *ring_all = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(ring_raw) + 127) & ~uintptr_t(127));
     __shared__ __align__(16) float qs[WPQ ? 4 : R * HD];
     __shared__ float wm[WPQ ? 1 : NW][R], wl[WPQ ? 1 : NW][R];
     __shared__ float wacc[WPQ ? 1 : NW][R][WPQ ? 1 : HD];
@@ -969,7 +970,7 @@ bool launch_prefill_tile(const AttnParams &p, int entries, int R, cudaStream_t s
 
 // Dynamic shared memory of attn_stream_kernel<HD, ...>: the warps' copy rings.
 template <int HD>
-constexpr size_t stream_smem() { return (size_t)StreamGeo<HD>::NW * StreamGeo<HD>::RING; }
+constexpr size_t stream_smem() { return (size_t)StreamGeo<HD>::NW * StreamGeo<HD>::RING + 128; }
 
 template <typename K>
 bool launch_ring_kernel(K kernel, size_t smem, dim3 grid, cudaStream_t st, const AttnParams &p) {

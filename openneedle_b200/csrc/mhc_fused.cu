@@ -211,7 +211,8 @@ __device__ __forceinline__ void store_p(float *p, const float (&v)[P]) {
 template <int P, int N, int SB, bool STAGED>
 __global__ void __launch_bounds__(kMixThreads, STAGED ? 1 : 2) mhc_mix_kernel(const MixArgs a, int R) {
     constexpr int NN = N * N, NPROJ = 2 * N + N * N;
-    extern __shared__ __align__(16) float smem[];
+    extern __shared__ __align__(16) float smem_raw[];   // from a 128-byte boundary (launch_mhc_mix adds 128)
+    float *smem = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     __shared__ float raws[SB][kMaxProj];
     __shared__ float hres_s[SB][NN], hp_s[SB][N];
     __shared__ __align__(8) uint64_t phibar;
@@ -636,6 +637,7 @@ bool launch_mhc_mix(const MixArgs &a, int R, int sms, cudaStream_t st) {
     size_t smem = sizeof(float) * 2 * (size_t)sb * kComputeThreads * P;
     args.phi_smem = staged && a.has_route && smem + phi_bytes <= 220 * 1024 ? 1 : 0;
     smem += args.phi_smem ? phi_bytes : sizeof(float) * (size_t)sb * N * a.D;   // (else nx of the rows)
+    smem += 128;                                                                // base alignment
 #define NB_MIX(PP, SBB, ST)                                                                                      \
     {                                                                                                          \
         auto kernel = mhc_mix_kernel<PP, 4, SBB, ST>;                                                          \
