@@ -753,6 +753,56 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
         return;
     }
     __syncthreads();
+    if constexpr (R * HD % 32 == 0 && R * HD <= 32 * NW) {
+        if (p.splits == 1 && p.hilo) {
+            // one output a thread: merge the warps, gate and store it, then the
+            // out projection's input rotation (CQ::transform over the R * HD
+            // outputs of this KV head, stages h = 1, 2, 4, ...: shuffles below
+            // 32, shared memory above) and bf16 split, as attn_combine_rot_kernel
+            constexpr int n = R * HD;
+            __shared__ float xs[2][n];
+            const int t = threadIdx.x, r = t / HD, d = t % HD;
+            float v = 0.f;
+            if (t < n) {
+                float mm = -INFINITY;
+                for (int w = 0; w < NW; ++w) mm = fmaxf(mm, wm[w][r]);
+                float ll = 0.f, aa = 0.f;
+                for (int w = 0; w < NW; ++w) {
+                    if (wm[w][r] == -INFINITY) continue;
+                    const float f = __expf(wm[w][r] - mm);
+                    ll += wl[w][r] * f;
+                    aa += wacc[w][r][d] * f;
+                }
+                const size_t oi = ((size_t)query * p.heads + kh * R + r) * HD + d;
+                v = gated(p, oi, ll > 0.f ? aa / ll : 0.f);
+                p.out[oi] = v;
+#pragma unroll
+                for (int h = 1; h < 32 && h < n; h *= 2) {   // whole warps (n is a multiple of 32)
+                    const float o = __shfl_xor_sync(kFull, v, h);
+                    v = (t & h) ? __fsub_rn(o, v) : __fadd_rn(v, o);
+                }
+            }
+            int buf = 0;
+#pragma unroll
+            for (int h = 32; h < n; h *= 2) {
+                if (t < n) xs[buf][t] = v;
+                __syncthreads();
+                if (t < n) {
+                    const float o = xs[buf][t ^ h];
+                    v = (t & h) ? __fsub_rn(o, v) : __fadd_rn(v, o);
+                }
+                buf ^= 1;
+            }
+            if (t < n) {
+                const float x = __fmul_rn(v, p.rot_scale);
+                const size_t i = (size_t)query * p.hilo_ld + (size_t)kh * n + t;
+                const __nv_bfloat16 hv = __float2bfloat16_rn(x);
+                p.hilo[i] = __bfloat16_as_ushort(hv);
+                p.hilo[p.hilo_lo + i] = __bfloat16_as_ushort(__float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hv))));
+            }
+            return;
+        }
+    }
     for (int idx = threadIdx.x; idx < R * HD; idx += blockDim.x) {
         const int r = idx / HD, d = idx % HD;
         float mm = -INFINITY;
@@ -1079,10 +1129,18 @@ bool launch_kv_store_f32(const float *k, const float *v, int tokens, int kvheads
     return true;
 }
 
+// (query, KV head) pairs from which decode runs one warp per pair: 1024 CTAs
+// of four warps, several waves on 148 SMs.
+constexpr long long kWpqMinPairs = 2048;
+
 int attention_splits(int max_len, int queries_x_kv, int sms) {
-    // enough CTAs to cover the machine about twice, at least 128 slots each
+    // split the context only while the (query, KV head) pairs leave SMs idle
+    // (fewer than two CTAs an SM), down to 128 slots a split.  Measured at
+    // config 5's 128 and 256 sessions (512 / 1024 pairs, ~300 slots): the
+    // unsplit kernel, which also needs no combine launch, beats two splits
+    // (0.600 vs 0.686 ms a decode step at 128 sessions).
     int splits = 1;
-    while (splits < 32 && (long long)queries_x_kv * splits < 2LL * sms * 4 && max_len / (splits * 2) >= 128) splits *= 2;
+    while (splits < 32 && (long long)queries_x_kv * splits < 2LL * sms && max_len / (splits * 2) >= 128) splits *= 2;
     return splits;
 }
 
@@ -1135,13 +1193,19 @@ bool launch_attention(const AttnParams &p_in, int queries, cudaStream_t st, bool
         return true;
     }
     bool streamed = false;
-    // one warp per query where the context needs no split and the query fits the registers
-    const bool wpq = p.splits == 1 && ((p.hd == 64 && R <= 2) || (p.hd == 128 && R <= 1));
+    // one warp per query where the context needs no split, the query fits the
+    // registers and the queries alone fill the machine; with fewer, the CTA's
+    // warps share each query's slots
+    const bool wpq = p.splits == 1 && ((p.hd == 64 && R <= 2) || (p.hd == 128 && R <= 1)) &&
+                     (long long)queries * p.kvheads >= kWpqMinPairs;
     AttnParams pw = p;
     pw.queries = queries;
     // the warp-per-query epilogue rotates one KV head's 2 x 64 outputs
     if (!(wpq && p.hd == 64 && R == 2)) pw.hilo = nullptr;
-    p.hilo = p.splits > 1 ? p.hilo : nullptr;   // the stream kernels themselves never write it
+    // the unsplit multi-warp stream kernel rotates up to 128 outputs of a KV head
+    const int nkv = R * p.hd;
+    const bool stream_rot = p.hilo && p.splits == 1 && !wpq && nkv % 32 == 0 && nkv <= 128;
+    if (p.splits == 1 && !stream_rot) p.hilo = nullptr;
     const dim3 wgrid(1, p.kvheads, (queries + 3) / 4);
     if (wpq && p.hd == 64) {
         streamed = launch_stream<64, true>(pw, wgrid, R, st);
@@ -1151,6 +1215,8 @@ bool launch_attention(const AttnParams &p_in, int queries, cudaStream_t st, bool
     // the streaming kernel where its per-lane state fits in registers
     else if (p.hd == 64 && R <= 4) streamed = launch_stream<64, false>(p, grid, R, st);
     else if (p.hd == 128 && R <= 2) streamed = launch_stream<128, false>(p, grid, R, st);
+    if (streamed && stream_rot && rot_done) *rot_done = true;
+    if (!streamed) p.hilo = p.splits > 1 ? p.hilo : nullptr;
     if (!streamed) switch (p.hd) {
         case 32: NB_CUDA_TRY(launch_pdl(attn_split_kernel<32, true, int8_t>, grid, 128, 0, st, p)); break;
         case 64: NB_CUDA_TRY(launch_pdl(attn_split_kernel<64, true, int8_t>, grid, 128, 0, st, p)); break;

@@ -679,8 +679,9 @@ bool handle_hilo_gemm(void *const *hs, int count, int batch, int *group, float *
 }
 
 bool handle_many_hilo(void *const *hs, int count, const uint16_t *a_hilo, float *const *ys, int batch,
-                      cudaStream_t st, const QkvgEpilogue *epi, bool *epi_done) {
+                      cudaStream_t st, const QkvgEpilogue *epi, bool *epi_done, const KParts *kp) {
     if (epi_done) *epi_done = false;
+    if (kp && kp->parts) *kp->parts = 1;
     if (!handle_hilo_gemm(hs, count, batch, nullptr, nullptr)) {
         set_error("these matrices do not take pre-split bf16 activations");
         return false;
@@ -693,7 +694,7 @@ bool handle_many_hilo(void *const *hs, int count, const uint16_t *a_hilo, float 
         outs[i] = F32Out{m->d_whl, m->w.out, ys[i], m->w.out};
     }
     return launch_gemm_f32x3_multi(a_hilo, batch, static_cast<Matrix *>(hs[0])->w.padded, outs.data(), count, st,
-                                   epi, epi_done);
+                                   epi, epi_done, kp);
 }
 }  // extern "C++"
 

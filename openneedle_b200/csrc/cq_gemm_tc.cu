@@ -505,8 +505,9 @@ struct F32Seg {
 constexpr int kF32MaxSegs = 4;
 struct GemmF32Args {
     F32Seg seg[kF32MaxSegs];
-    int nseg, M, ksteps;
-    QkvgEpilogue epi;   // used by the EPI instantiations only
+    int nseg, M, ksteps;   // ksteps: K steps of one CTA (of one part along grid z)
+    long long pstride;     // floats between the partial outputs of consecutive parts
+    QkvgEpilogue epi;      // used by the EPI instantiations only
 };
 
 // Norm, rotary embedding and KV store of one 64-wide head held by one thread
@@ -582,8 +583,11 @@ __device__ __forceinline__ void qkvg_head(const QkvgEpilogue &E, int seg, int he
     sdst[krow] = sc;
 }
 
-// grid: (M tiles, total N tiles of all segments); tile width BN (256 for
-// prefill-sized launches, 64 when that leaves too few CTAs for the machine).
+// grid: (M tiles, total N tiles of all segments, K parts); tile width BN (256
+// for prefill-sized launches, 64 or 128 when that leaves too few CTAs for the
+// machine).  Part z of a K-split launch takes K steps [z ksteps, (z + 1)
+// ksteps) and writes its partial tile to y + z pstride; the consumer adds the
+// parts in order.
 template <int BN, int ST, int ACC, bool EPI>
 __global__ void __launch_bounds__(kFThreads, 1)
     cq_gemm_f32x3_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
@@ -600,7 +604,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
     while (si + 1 < a.nseg && (int)blockIdx.y >= a.seg[si + 1].tile0) ++si;
     const F32Seg &sg = a.seg[si];
     const int m0 = blockIdx.x * kFBM, n0 = ((int)blockIdx.y - sg.tile0) * BN;
-    const int S = a.ksteps;
+    const int S = a.ksteps, k0 = (int)blockIdx.z * S;
+    float *const yout = sg.y + (size_t)blockIdx.z * a.pstride;
 
     if (warp == 1) tc::alloc(&tmem_s, BN * ACC);
     if (tid == 0) {
@@ -624,7 +629,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
             for (int k = 0; k < pre; ++k) {
                 uint8_t *st = smem + (size_t)k * kStageBytes;
                 mbar_arrive_expect_tx(&full[k], kStageBytes);
-                const int x = k * kFBK * 2;
+                const int x = (k0 + k) * kFBK * 2;
                 tma_load_2d(st + 2 * kFPartA, &sg.bh, x, n0, &full[k]);
                 tma_load_2d(st + 2 * kFPartA + kPartB, &sg.bl, x, n0, &full[k]);
             }
@@ -632,7 +637,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
             for (int k = 0; k < S && !abort_flag; ++k) {
                 const int s = k % kFStages;
                 uint8_t *st = smem + (size_t)s * kStageBytes;
-                const int x = k * kFBK * 2;   // byte column of this K step
+                const int x = (k0 + k) * kFBK * 2;   // byte column of this K step
                 if (k >= kFStages) {
                     if (!gwait(&empty[s], (uint32_t)((k / kFStages) - 1) & 1, &abort_flag)) break;
                     mbar_arrive_expect_tx(&full[s], kStageBytes);
@@ -701,8 +706,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
                 if (row < a.M) qkvg_head(a.epi, si, n0 / 64, row, h, sg.y + (size_t)row * sg.ldy + n0);
             }
         } else if (ok) {
-            const bool vec = (sg.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(sg.y) & 15) == 0;
-            float *yr = sg.y + (size_t)min(row, a.M - 1) * sg.ldy + n0;
+            const bool vec = (sg.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(yout) & 15) == 0;
+            float *yr = yout + (size_t)min(row, a.M - 1) * sg.ldy + n0;
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t v[32];
                 tc::ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(32 * c), v);
@@ -739,175 +744,9 @@ __global__ void __launch_bounds__(kFThreads, 1)
     if (warp == 1) tc::dealloc(tmem, BN * ACC);
 }
 
-// ---------------------------------------------------------------------------
-// The same product split along K over a cluster of `ks` CTAs (2 <= ks <= 8),
-// for decode-sized launches whose 128 x 256 tiles are too few to fill the
-// machine: rank r of the cluster accumulates K steps [r S, (r + 1) S) of the
-// tile in its own TMEM; then every CTA sends column slice c (256 / ks columns)
-// of its partial tile to rank c's shared memory (distributed shared memory
-// stores), and rank c adds the ks partials of its slice in rank order and
-// stores y.  The order of the additions is fixed, so results do not depend on
-// timing.
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
-                 : "memory");
-}
-
-constexpr int kSplitBN = 256;
-constexpr bool kSplitK = false;   // measured slower than the unsplit 64-wide tiles
-constexpr int kDecodeAcc = 1;      // accumulators per 64-wide tile
-constexpr bool kNarrow32 = false;   // 32-wide tiles for the smallest decode grids (measured slower)
-
-__global__ void __launch_bounds__(kFThreads, 1)
-    cq_gemm_f32x3_splitk_kernel(const __grid_constant__ CUtensorMap tah, const __grid_constant__ CUtensorMap tal,
-                                const __grid_constant__ GemmF32Args a, int ks) {
-    constexpr int BN = kSplitBN, ST = 2;
-    constexpr int kPartB = FTile<BN, ST>::kPartB, kStageBytes = FTile<BN, ST>::kStageBytes;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t full[ST], empty[ST], dfull;
-    __shared__ uint32_t tmem_s;
-    __shared__ volatile int abort_flag;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    int si = 0;
-    while (si + 1 < a.nseg && (int)blockIdx.y >= a.seg[si + 1].tile0) ++si;
-    const F32Seg &sg = a.seg[si];
-    const int m0 = blockIdx.x * kFBM, n0 = ((int)blockIdx.y - sg.tile0) * BN;
-    const int S = a.ksteps;                       // K steps of this CTA
-    const uint32_t rank = cluster_rank();
-    const int kbeg = (int)rank * S;
-
-    if (warp == 1) tc::alloc(&tmem_s, BN);
-    if (tid == 0) {
-        abort_flag = 0;
-        for (int s = 0; s < ST; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
-        }
-        mbar_init(&dfull, 1);
-        fence_barrier_init();
-    }
-    tc::fence_before();
-    __syncthreads();
-    tc::fence_after();
-    const uint32_t tmem = tmem_s;
-
-    bool ok = true;
-    if (warp == 0) {
-        if (lane == 0) {
-            const int pre = S < ST ? S : ST;
-            for (int k = 0; k < pre; ++k) {
-                uint8_t *st = smem + (size_t)k * kStageBytes;
-                mbar_arrive_expect_tx(&full[k], kStageBytes);
-                const int x = (kbeg + k) * kFBK * 2;
-                tma_load_2d(st + 2 * kFPartA, &sg.bh, x, n0, &full[k]);
-                tma_load_2d(st + 2 * kFPartA + kPartB, &sg.bl, x, n0, &full[k]);
-            }
-            pdl_wait();
-            for (int k = 0; k < S && !abort_flag; ++k) {
-                const int s = k % ST;
-                uint8_t *st = smem + (size_t)s * kStageBytes;
-                const int x = (kbeg + k) * kFBK * 2;
-                if (k >= ST) {
-                    if (!gwait(&empty[s], (uint32_t)((k / ST) - 1) & 1, &abort_flag)) break;
-                    mbar_arrive_expect_tx(&full[s], kStageBytes);
-                    tma_load_2d(st + 2 * kFPartA, &sg.bh, x, n0, &full[s]);
-                    tma_load_2d(st + 2 * kFPartA + kPartB, &sg.bl, x, n0, &full[s]);
-                }
-                tma_load_2d(st, &tah, x, m0, &full[s]);
-                tma_load_2d(st + kFPartA, &tal, x, m0, &full[s]);
-            }
-        }
-        __syncwarp();
-    } else if (warp == 1) {
-        if (lane == 0) {
-            const uint32_t idesc = tc::idesc_bf16(kFBM, BN);
-            for (int k = 0; k < S && !abort_flag; ++k) {
-                const int s = k % ST;
-                if (!gwait(&full[s], (uint32_t)(k / ST) & 1, &abort_flag)) break;
-                tc::fence_after();
-                const uint32_t ah = smem_addr(smem + (size_t)s * kStageBytes), al = ah + kFPartA;
-                const uint32_t bh = ah + 2 * kFPartA, bl = bh + kPartB;
-#pragma unroll
-                for (int kk = 0; kk < kFBK / 16; ++kk) {
-                    const uint32_t o = kk * 32;
-                    tc::mma_bf16_ss(tmem, sw128_desc(ah + o), sw128_desc(bh + o), idesc, (k | kk) != 0);
-                    tc::mma_bf16_ss(tmem, sw128_desc(al + o), sw128_desc(bh + o), idesc, 1);
-                    tc::mma_bf16_ss(tmem, sw128_desc(ah + o), sw128_desc(bl + o), idesc, 1);
-                }
-                tc::commit(&empty[s]);
-            }
-            tc::commit(&dfull);
-        }
-        __syncwarp();
-    } else {
-        ok = gwait(&dfull, 0, &abort_flag);
-        tc::fence_after();
-    }
-    // (1) every CTA of the cluster has finished its MMAs: the stage buffers
-    // take the partial tiles now
-    cluster_sync_all();
-    const int slice = BN / ks, stride = slice + 4;   // +4 floats: conflict-free float4 rows
-    float *recv = reinterpret_cast<float *>(smem);    // [ks][128][stride]
-    const int q = warp & 3, trow = 32 * q + lane;
-    if (warp >= 2 && ok) {
-        for (int c = 0; c < BN / 32; ++c) {
-            uint32_t v[32];
-            tc::ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(32 * c), v);
-            tc::wait_ld();
-            const int owner = (32 * c) / slice, col0 = 32 * c - owner * slice;
-            const uint32_t dst = smem_addr(recv + ((size_t)rank * kFBM + trow) * stride + col0);
-            const uint32_t rdst = map_rank(dst, (uint32_t)owner);
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) st_cluster_v4(rdst + 4 * j, v[j], v[j + 1], v[j + 2], v[j + 3]);
-        }
-    }
-    // (2) every partial slice has arrived
-    cluster_sync_all();
-    if (warp >= 2 && ok) {
-        const int row = m0 + trow;
-        if (row < a.M) {
-            const int c0 = n0 + (int)rank * slice;
-            float *yr = sg.y + (size_t)row * sg.ldy;
-            const bool vec = (sg.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(sg.y) & 15) == 0;
-            for (int j = 0; j < slice; j += 4) {
-                float4 acc = *reinterpret_cast<const float4 *>(recv + (size_t)trow * stride + j);
-                for (int src = 1; src < ks; ++src) {
-                    const float4 p = *reinterpret_cast<const float4 *>(recv + ((size_t)src * kFBM + trow) * stride + j);
-                    acc.x += p.x;
-                    acc.y += p.y;
-                    acc.z += p.z;
-                    acc.w += p.w;
-                }
-                const int col = c0 + j;
-                if (vec && col + 3 < sg.N) {
-                    *reinterpret_cast<float4 *>(yr + col) = acc;
-                } else {
-                    const float e[4] = {acc.x, acc.y, acc.z, acc.w};
-                    for (int t = 0; t < 4; ++t)
-                        if (col + t < sg.N) yr[col + t] = e[t];
-                }
-            }
-        }
-    }
-    tc::fence_before();
-    __syncthreads();
-    tc::fence_after();
-    if (warp == 1) tc::dealloc(tmem, BN);
-}
+constexpr int kDecodeAcc = 1;     // accumulators per 64-wide tile
+constexpr bool kNarrow32 = false;  // 32-wide tiles for the smallest decode grids (measured slower)
+constexpr int kPartWidth = 64;     // tile width of K-split launches (measured: 64 < 128 < 256)
 
 struct Lut16 {
     float v[16];
@@ -1045,8 +884,9 @@ bool launch_split_bf16(const float *x, long long n, uint16_t *hilo, cudaStream_t
 }
 
 bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F32Out *outs, int count,
-                             cudaStream_t st, const QkvgEpilogue *epi, bool *epi_done) {
+                             cudaStream_t st, const QkvgEpilogue *epi, bool *epi_done, const KParts *kp) {
     if (epi_done) *epi_done = false;
+    if (kp && kp->parts) *kp->parts = 1;
     if (M <= 0 || count <= 0) return true;
     if (padded % kFBK) {
         set_error("FP32 prefill GEMM requires the padded width to be a multiple of 64");
@@ -1065,26 +905,33 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
         sms = sm_count[dev];
     }
     const int mtiles = (M + kFBM - 1) / kFBM;
-    int wide = 0;
-    for (int i = 0; i < count; ++i) wide += (outs[i].N + 255) / 256;
-    // Too few 128 x 256 tiles for the machine: split K over a cluster of ks
-    // CTAs (at most 8, each with one or more K steps) while the grid still fits
-    // one wave; where K is too short for that, 64-wide tiles (four times the
-    // CTAs); 256-wide tiles otherwise.
-    const int steps = padded / kFBK;
-    int ks = 1;
-    if (kSplitK)
-        while (ks < 8 && steps % (2 * ks) == 0 && (long long)mtiles * wide * 2 * ks <= sms) ks *= 2;
-    const bool split = ks > 1;
-    const bool narrow = !split && (long long)mtiles * wide < 2LL * sms;
+    auto tiles_of = [&](int bn) {
+        int t = 0;
+        for (int i = 0; i < count; ++i) t += (outs[i].N + bn - 1) / bn;
+        return t;
+    };
+    // 128 x 256 tiles where they fill the machine; 64-wide tiles (four times
+    // the CTAs) where they do not
+    const bool narrow = (long long)mtiles * tiles_of(256) < 2LL * sms;
     // the decode epilogue: four segments (q, k, v, gate) of whole 64-wide heads
     const bool with_epi = narrow && epi && epi->active && count == 4 && epi->hd == 64;
+    // K split into parts where the caller adds partial outputs: each CTA then
+    // issues a fraction of the tile's MMAs (a 128-row MMA costs about the
+    // same whatever its width up to 256, so one CTA's chain of MMAs bounds a
+    // decode-sized launch), as many parts as keep the grid within one CTA per SM
+    const int steps = padded / kFBK;
+    int parts = 1;
+    if (narrow && !with_epi && kp && kp->max_parts > 1 && kp->pstride > 0) {
+        const long long grid = (long long)mtiles * tiles_of(kPartWidth);
+        while (2 * parts <= kp->max_parts && 2 * parts <= kMaxKParts && steps % (2 * parts) == 0 &&
+               grid * 2 * parts <= sms)
+            parts *= 2;
+    }
     // 32-wide tiles (twice the CTAs again, each MMA half as wide) where even the
     // 64-wide grid leaves most SMs idle
-    int tiles64 = 0;
-    for (int i = 0; i < count; ++i) tiles64 += (outs[i].N + 63) / 64;
-    const bool narrow32 = kNarrow32 && narrow && !with_epi && (long long)mtiles * tiles64 * 2 <= sms;
-    const int BN = narrow32 ? 32 : narrow ? 64 : 256;
+    const bool narrow32 =
+        kNarrow32 && parts == 1 && narrow && !with_epi && (long long)mtiles * tiles_of(64) * 2 <= sms;
+    const int BN = parts > 1 ? kPartWidth : narrow32 ? 32 : narrow ? 64 : 256;
     const size_t an = (size_t)M * padded;
     CUtensorMap tah, tal;
     // bf16 rows seen as bytes: 2 * padded bytes per row, 128-byte (64-element) boxes
@@ -1092,7 +939,8 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
     GemmF32Args args{};
     args.nseg = count;
     args.M = M;
-    args.ksteps = steps / ks;
+    args.ksteps = steps / parts;
+    args.pstride = parts > 1 ? kp->pstride : 0;
     int tiles = 0;
     for (int i = 0; i < count; ++i) {
         const F32Out &o = outs[i];
@@ -1107,30 +955,15 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
         tiles += (o.N + BN - 1) / BN;
     }
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(mtiles, tiles, ks);
+    cfg.gridDim = dim3(mtiles, tiles, parts);
     cfg.blockDim = dim3(kFThreads);
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = 1;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = (unsigned)ks;
     cfg.attrs = attr;
-    cfg.numAttrs = split ? 2 : 1;
+    cfg.numAttrs = 1;
     static bool configured[7][64] = {};
-    if (split) {
-        constexpr size_t smem = FTile<kSplitBN, 2>::kSmem;
-        if (dev < 0 || dev >= 64 || !configured[3][dev]) {
-            NB_CUDA_TRY(cudaFuncSetAttribute(cq_gemm_f32x3_splitk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem));
-            if (dev >= 0 && dev < 64) configured[3][dev] = true;
-        }
-        cfg.dynamicSmemBytes = smem;
-        NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, cq_gemm_f32x3_splitk_kernel, tah, tal, args, ks));
-        return true;
-    }
     auto launch = [&](auto kernel, size_t smem, int which) -> bool {
         if (dev < 0 || dev >= 64 || !configured[which][dev]) {
             NB_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -1140,6 +973,10 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
         NB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, tah, tal, args));
         return true;
     };
+    if (parts > 1) {
+        if (kp->parts) *kp->parts = parts;
+        return launch(cq_gemm_f32x3_kernel<kPartWidth, 2, 1, false>, FTile<kPartWidth, 2>::kSmem, 3);
+    }
     if (!narrow) return launch(cq_gemm_f32x3_kernel<256, 2, 1, false>, FTile<256, 2>::kSmem, 0);
     if (narrow32) return launch(cq_gemm_f32x3_kernel<32, 4, kDecodeAcc, false>, FTile<32, 4>::kSmem, 6);
     if (with_epi) {

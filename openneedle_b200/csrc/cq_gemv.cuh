@@ -110,11 +110,24 @@ struct F32Out {
     int ldy;
 };
 struct QkvgEpilogue;
+// Partial outputs of a launch split along K (decode-sized launches whose few
+// output tiles would leave most SMs idle): the launch may split K into up to
+// max_parts parts (a power of two); part p of output i is written to
+// y_i + p * pstride (part 0 included) and *parts receives how many were
+// written, so that the consumer adds them in order.
+struct KParts {
+    int max_parts;
+    long long pstride;
+    int *parts;
+};
+constexpr int kMaxKParts = 8;   // most K parts of one launch
 // epi (optional, four segments q, k, v, gate): the decode-step epilogue of
 // qkvg_epilogue.cuh, applied when the launch runs 64-wide tiles of one head
 // each; *epi_done tells whether it ran (else the caller still has to do it).
+// kp (optional, not with epi): K-split partial outputs as above.
 bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F32Out *outs, int count,
-                             cudaStream_t st, const QkvgEpilogue *epi = nullptr, bool *epi_done = nullptr);
+                             cudaStream_t st, const QkvgEpilogue *epi = nullptr, bool *epi_done = nullptr,
+                             const KParts *kp = nullptr);
 // Activation rows from which int8 products run as the tensor-core GEMM.
 constexpr int kGemmMinRows = 64;
 

@@ -10,6 +10,7 @@
 namespace nb200 {
 
 struct QkvgEpilogue;
+struct KParts;
 
 // Device view of handle's matrix (null when handle is null).
 const CQDevice *handle_matrix(void *handle);
@@ -26,9 +27,12 @@ bool handle_prepare(void *handle, const float *x, int batch, const float **rot, 
 bool handle_hilo_gemm(void *const *hs, int count, int batch, int *group, float *scale);
 // That GEMM on activations the caller rotated and split: a_hilo [batch][in]
 // bf16 hi, then [batch][in] lo (in = the matrices' padded width).
-// epi / epi_done: the decode epilogue of launch_gemm_f32x3_multi (optional).
+// epi / epi_done: the decode epilogue of launch_gemm_f32x3_multi (optional);
+// kp: its K-split partial outputs (optional; ys[i] + p * kp->pstride, the
+// output's rows of width out_i).
 bool handle_many_hilo(void *const *hs, int count, const uint16_t *a_hilo, float *const *ys, int batch,
-                      cudaStream_t st, const QkvgEpilogue *epi = nullptr, bool *epi_done = nullptr);
+                      cudaStream_t st, const QkvgEpilogue *epi = nullptr, bool *epi_done = nullptr,
+                      const KParts *kp = nullptr);
 // A new int8 (SDOT) handle over the same packed matrix as the FP32 handle
 // `cq` (its device copy read back once), or null with the error set.
 void *handle_make_sdot(void *cq);

@@ -26,6 +26,7 @@
 
 #include "../../include/needle2_b200.h"
 #include "common.cuh"
+#include "cq_gemv.cuh"
 #include "cq_handle.cuh"
 #include "cq_kernels.cuh"
 #include "engine.cuh"
@@ -127,6 +128,7 @@ struct Scratch {
     DevBuf<float> x, nx, raw, hpost, u, bx, z, q, k, v, gate, att, proj, e, ek, ev, rawv, zf, logits, hidden;
     DevBuf<uint16_t> zhl;   // z rotated and split into the QKVG GEMM's bf16 operands
     DevBuf<uint16_t> ahl;   // the attention output rotated and split for the out projection
+    DevBuf<float> part;     // K-split partial outputs of the decode projections (q/k/v/gate, then out)
     DevBuf<int64_t> ids;
     DevBuf<uint8_t> valid;
     DevBuf<int> rsess, rpos, tokens, argmax;
@@ -651,6 +653,7 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         mark(st, 2, stream);
         void *hs[4];
         bool roped = false;   // norm, RoPE and the KV store done by the projections' epilogue
+        eng::QkvgParts qkvg_src{};   // the projections' outputs as K parts (q null: in q, k, v, gate)
         if (zhl_ready && qkvg_handles(l, hs)) {
             float *outs[4] = {s.q.ptr, s.k.ptr, s.v.ptr, s.gate.ptr};
             QkvgEpilogue epi{};
@@ -664,8 +667,25 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
                 epi.divisor = m.rope_divisor; epi.pos = s.rpos.ptr;
                 epi.kv = kv_pool_target(st.kv[l], st.iota.ptr, st.base.ptr);
             }
-            check(handle_many_hilo(hs, 4, s.zhl.ptr, outs, R, stream, epi.active ? &epi : nullptr, &roped),
+            // decode without the fused epilogue: the projections may split K into parts,
+            // written side by side into s.part, which the RoPE/KV-store kernel adds
+            const int qn = c.heads * c.head_dim, kn = c.kvheads * c.head_dim;
+            int qparts = 0;
+            KParts kp{};
+            if (T == 1 && !epi.active && handle_matrix(hs[0])->out == qn && handle_matrix(hs[1])->out == kn &&
+                handle_matrix(hs[2])->out == kn && handle_matrix(hs[3])->out == qn) {
+                const long long span = (long long)R * 2 * (qn + kn);
+                s.part.reserve((size_t)kMaxKParts * span);
+                float *b = s.part.ptr;
+                outs[0] = b; outs[1] = b + (size_t)R * qn; outs[2] = b + (size_t)R * (qn + kn);
+                outs[3] = b + (size_t)R * (qn + 2 * kn);
+                kp = KParts{kMaxKParts, span, &qparts};
+                qkvg_src = eng::QkvgParts{outs[0], outs[1], outs[2], outs[3], s.gate.ptr, 1, span};
+            }
+            check(handle_many_hilo(hs, 4, s.zhl.ptr, outs, R, stream, epi.active ? &epi : nullptr, &roped,
+                                   kp.max_parts ? &kp : nullptr),
                   "QKVG projections");
+            qkvg_src.parts = qparts;
         } else {
             projections(m, ti, s.z.ptr, R, s.q.ptr, s.k.ptr, s.v.ptr, s.gate.ptr, stream);
         }
@@ -677,7 +697,7 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
             check(eng::launch_qk_rope_store(s.q.ptr, s.k.ptr, s.v.ptr, R, c.heads, c.kvheads, c.head_dim,
                                             m.t[ti + 4].dense, m.t[ti + 5].dense, s.rpos.ptr, m.rope_divisor,
                                             kv_pool_target(st.kv[l], st.iota.ptr, st.base.ptr), stream, m.rope_cos,
-                                            m.rope_sin, m.rope_len),
+                                            m.rope_sin, m.rope_len, qkvg_src.q ? &qkvg_src : nullptr),
                   "q/k norm, RoPE and KV store");
         } else {
             check(eng::launch_qk_norm_rope(s.q.ptr, s.k.ptr, R, c.heads, c.kvheads, c.head_dim, m.t[ti + 4].dense,
@@ -705,9 +725,20 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
                           s.k.ptr, s.v.ptr, s.att.ptr, stream, s.gate.ptr, want_rot ? &rot : nullptr, &rotated),
               "attention");
         mark(st, 5, stream);
+        // the out projection's K parts, when the layer-boundary kernel adds them
+        const float *proj_src = s.proj.ptr;
+        int proj_parts = 1;
         if (rotated) {
             float *ys[1] = {s.proj.ptr};
-            check(handle_many_hilo(&oh, 1, s.ahl.ptr, ys, R, stream), "out projection");
+            KParts kp{};
+            if (mix && !hres_norm) {
+                s.part.reserve((size_t)kMaxKParts * R * D);
+                ys[0] = s.part.ptr;
+                kp = KParts{kMaxKParts, (long long)R * D, &proj_parts};
+            }
+            check(handle_many_hilo(&oh, 1, s.ahl.ptr, ys, R, stream, nullptr, nullptr, kp.max_parts ? &kp : nullptr),
+                  "out projection");
+            proj_src = ys[0];
         } else {
             aq(m, s.att.ptr, R, A, stream);
             linear(m, ti + 7, s.att.ptr, R, s.proj.ptr, stream);
@@ -719,6 +750,7 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         if (mix && !hres_norm) {
             eng::MixArgs a = mix_args();
             a.has_post = 1; a.post = post_layer(l, 0);   // the boundary kernel normalises the mixing matrix
+            a.proj = proj_src; a.proj_parts = proj_parts; a.proj_pstride = (long long)R * D;
             a.hidden = hid; a.ldh = c.layers * D;
             if (!last) {
                 a.has_route = 1; a.route = route_layer(l + 1);
@@ -734,6 +766,9 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         }
         if (!fused) {
             zhl_ready = false;
+            if (proj_src != s.proj.ptr)
+                check(eng::launch_sum_parts(proj_src, proj_parts, (long long)R * D, (long long)R * D, s.proj.ptr, stream),
+                      "out projection parts");
             check(eng::launch_mhc_post(post_layer(l, hres_norm ? 1 : 0), s.proj.ptr, s.raw.ptr, ldraw, s.hpost.ptr,
                                        s.u.ptr, s.bx.ptr, s.x.ptr, R, hid, c.layers * D, stream),
                   "mHC mixing");

@@ -72,10 +72,21 @@ namespace eng {
 // row; the positions are the rows' positions) into target.  cos_t / sin_t
 // (optional, [table_len][hd / 2]): cosf / sinf of position / divisor, read
 // instead of evaluated for positions the table covers (the same values).
-bool launch_qk_rope_store(float *q, float *k, const float *v, int R, int heads, int kvheads, int hd,
+// src (optional): q, k, v and gate as K-split partial outputs of the
+// projections (qkvg_part of each at src.* + p * pstride, p < parts), added in
+// order into q, k, v and src.gate before the norm.
+struct QkvgParts {
+    const float *q, *k, *v, *g;
+    float *gate;
+    int parts;
+    long long pstride;
+};
+bool launch_qk_rope_store(float *q, float *k, float *v, int R, int heads, int kvheads, int hd,
                           const float *q_norm, const float *k_norm, const int *pos, const float *divisor,
                           const KVStoreTarget &target, cudaStream_t st, const float *cos_t = nullptr,
-                          const float *sin_t = nullptr, int table_len = 0);
+                          const float *sin_t = nullptr, int table_len = 0, const QkvgParts *src = nullptr);
+// out[i] = sum over p < parts of part[i + p * pstride], in order (i < n).
+bool launch_sum_parts(const float *part, int parts, long long pstride, long long n, float *out, cudaStream_t st);
 
 // att *= sigmoid(gate) (engine.cpp:1023).
 bool launch_gate(float *att, const float *gate, int R, int A, cudaStream_t st);
@@ -105,6 +116,8 @@ struct MixArgs {
     MhcLayer route;                 // has_route
     const float *phi_pre, *phi_post, *phi_res;   // the routing projections of every layer
     const float *proj;              // post: out-projection output [R][D]
+    int proj_parts;                 // post: proj as K-split parts (proj + p * proj_pstride; 0 or 1: one)
+    long long proj_pstride;
     float *raw;                     // post reads layer l's mixing matrix; route writes layer l + 1's values
     int ldraw;
     float *hpost, *u, *bx;          // post reads layer l's; route writes layer l + 1's

@@ -308,22 +308,34 @@ __global__ void qk_norm_rope_kernel(float *__restrict__ q, float *__restrict__ k
 // row's K (after RoPE) and V: INT8 by the reference's rule (engine.cpp:1005-1021,
 // scale max/127 or 1, values rint(x * (127 / max)) clamped to +-127, as
 // kv_quantize_kernel) or FP32 as is, into the row of target.dest.
-__global__ void qk_rope_store_kernel(float *__restrict__ q, float *__restrict__ k, const float *__restrict__ v,
-                                     int heads, int kvheads, int hd, const float *__restrict__ q_norm,
+__global__ void qk_rope_store_kernel(float *__restrict__ q, float *__restrict__ k, float *__restrict__ v, int heads,
+                                     int kvheads, int hd, const float *__restrict__ q_norm,
                                      const float *__restrict__ k_norm, const int *__restrict__ pos,
                                      const float *__restrict__ divisor, const KVStoreTarget t,
-                                     const float *__restrict__ cos_t, const float *__restrict__ sin_t, int table_len) {
+                                     const float *__restrict__ cos_t, const float *__restrict__ sin_t, int table_len,
+                                     const QkvgParts src) {
     pdl_enter();
     extern __shared__ float buf[];   // [warps][hd]
     const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const float fpos = (float)pos[r];
     const KVDest &d = t.dest;
-    for (int h = warp; h < heads + 2 * kvheads; h += nw) {
+    const int units = heads + 2 * kvheads + (src.q ? heads : 0);   // q, k, v heads (and gate heads)
+    for (int h = warp; h < units; h += nw) {
+        if (h >= heads + 2 * kvheads) {   // a gate head: its parts added
+            const size_t o = ((size_t)r * heads + (h - heads - 2 * kvheads)) * hd;
+            for (int i = lane; i < hd; i += 32) src.gate[o + i] = part_sum(src.g + o + i, src.parts, src.pstride);
+            continue;
+        }
         const bool isv = h >= heads + kvheads;
         const bool isq = h < heads;
         const int kh = isq ? 0 : isv ? h - heads - kvheads : h - heads;
-        float *vp = isq ? q + ((size_t)r * heads + h) * hd
-                        : isv ? const_cast<float *>(v) + ((size_t)r * kvheads + kh) * hd : k + ((size_t)r * kvheads + kh) * hd;
+        const size_t off = isq ? ((size_t)r * heads + h) * hd : ((size_t)r * kvheads + kh) * hd;
+        float *vp = (isq ? q : isv ? v : k) + off;
+        if (src.q) {
+            const float *sp = (isq ? src.q : isv ? src.v : src.k) + off;
+            for (int i = lane; i < hd; i += 32) vp[i] = part_sum(sp + i, src.parts, src.pstride);
+            __syncwarp();
+        }
         if (!isv) {
             const float *nrm = isq ? q_norm : k_norm;
             float *b = buf + warp * hd;
@@ -962,14 +974,37 @@ bool launch_qk_norm_rope(float *q, float *k, int R, int heads, int kvheads, int 
     return true;
 }
 
-bool launch_qk_rope_store(float *q, float *k, const float *v, int R, int heads, int kvheads, int hd,
+bool launch_qk_rope_store(float *q, float *k, float *v, int R, int heads, int kvheads, int hd,
                           const float *q_norm, const float *k_norm, const int *pos, const float *divisor,
                           const KVStoreTarget &t, cudaStream_t st, const float *cos_t, const float *sin_t,
-                          int table_len) {
+                          int table_len, const QkvgParts *src) {
     if (R <= 0) return true;
-    const int warps = std::min(heads + 2 * kvheads, 32);
+    const QkvgParts parts = src ? *src : QkvgParts{};
+    if (parts.q && (parts.parts < 1 || parts.parts > kMaxKParts || !parts.k || !parts.v || !parts.g || !parts.gate)) {
+        set_error("q/k/v/gate parts: bad arguments");
+        return false;
+    }
+    const int warps = std::min(heads + 2 * kvheads + (parts.q ? heads : 0), 32);
     NB_CUDA_TRY(launch_pdl(qk_rope_store_kernel, R, 32 * warps, sizeof(float) * warps * hd, st, q, k, v, heads, kvheads, hd, q_norm,
-                           k_norm, pos, divisor, t, cos_t, sin_t, table_len));
+                           k_norm, pos, divisor, t, cos_t, sin_t, table_len, parts));
+    NB_CUDA_TRY(cudaGetLastError());
+    return true;
+}
+
+__global__ void sum_parts_kernel(const float *__restrict__ part, int parts, long long pstride, long long n,
+                                 float *__restrict__ out) {
+    pdl_enter();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        out[i] = part_sum(part + i, parts, pstride);
+}
+
+bool launch_sum_parts(const float *part, int parts, long long pstride, long long n, float *out, cudaStream_t st) {
+    if (n <= 0) return true;
+    if (parts < 1 || parts > kMaxKParts) {
+        set_error("sum of parts: bad part count");
+        return false;
+    }
+    NB_CUDA_TRY(launch_pdl(sum_parts_kernel, std::min<unsigned>(blocks_for(n, 256), 4096), 256, 0, st, part, parts, pstride, n, out));
     NB_CUDA_TRY(cudaGetLastError());
     return true;
 }

@@ -3,6 +3,8 @@
 #pragma once
 #include <math.h>
 
+#include "cq_gemv.cuh"
+
 namespace nb200 {
 namespace eng {
 
@@ -21,6 +23,19 @@ __device__ __forceinline__ float rms_inv(float sumsq, int n) {
 
 // The reference's sigmoid, 1 / (1 + exp(-x)) (engine.cpp:36).
 __device__ __forceinline__ float sigm(float x) { return __fdiv_rn(1.f, __fadd_rn(1.f, expf(-x))); }
+
+// Sum of the K-split parts p[0], p[stride], ... of one GEMM output
+// (1 <= parts <= kMaxKParts), added in part order.
+__device__ __forceinline__ float part_sum(const float *__restrict__ p, int parts, long long stride) {
+    float v[kMaxKParts];
+#pragma unroll
+    for (int i = 0; i < kMaxKParts; ++i) v[i] = i < parts ? p[i * stride] : 0.f;
+    float s = v[0];
+#pragma unroll
+    for (int i = 1; i < kMaxKParts; ++i)
+        if (i < parts) s += v[i];
+    return s;
+}
 
 }  // namespace eng
 }  // namespace nb200

@@ -287,6 +287,16 @@ __global__ void __launch_bounds__(kMixThreads, STAGED ? 1 : 2) mhc_mix_kernel(co
             const size_t o = (size_t)(r0 + s) * D + d0;
             if (rv[s] && dv) {
                 load_p<P>(pv[s], a.proj + o);
+                // the out projection's K-split parts, added in order
+                float pp[kMaxKParts - 1][P];
+#pragma unroll
+                for (int k = 1; k < kMaxKParts; ++k)
+                    if (k < a.proj_parts) load_p<P>(pp[k - 1], a.proj + k * a.proj_pstride + o);
+#pragma unroll
+                for (int k = 1; k < kMaxKParts; ++k)
+                    if (k < a.proj_parts)
+#pragma unroll
+                        for (int i = 0; i < P; ++i) pv[s][i] += pp[k - 1][i];
                 load_p<P>(bb[s], a.bx + o);
                 load_p<P>(uv[s], a.u + o);
             } else {

@@ -232,31 +232,40 @@ def test_config5_batch_decode_kernels_match_reference(env):
             np.testing.assert_array_equal(gpu["0_tokens"][s], ref["5_tokens"][1:])
 
 
-def test_config5_small_batch_long_context_matches_reference(env):
-    """Config 5's decoder batched over 96 sessions with 260-token prompts: the
-    per-GPU share of an 8-GPU run.  Decode steps here take the one-CTA-per-SM
-    layer boundary, the 32-wide projection tiles, attention split over the
-    context with the out projection's input rotation done while combining the
-    splits.  Two sessions against the reference engine run on each alone:
-    logits within 1e-4, greedy tokens equal where the top-2 margin exceeds it."""
+@pytest.mark.parametrize("kv,S,prompt_len", [("fp32", 96, 260), ("int8", 64, 260), ("int8", 96, 260),
+                                             ("int8", 96, 16)])
+def test_config5_small_batch_matches_reference(env, kv, S, prompt_len):
+    """Config 5's decoder batched over 64-96 sessions: the per-GPU share of an
+    8-GPU run.  Decode steps here take the one-CTA-per-SM layer boundary and
+    the K-split projections (their parts added by the RoPE / KV-store kernel
+    and by the layer boundary).  Attention writes the out projection's rotated
+    operands: at 64 sessions and 260-token prompts it splits the context and
+    rotates while combining the splits; at 96 sessions it runs unsplit and
+    rotates inside the attention kernel.  Two sessions against the reference
+    engine run on each alone: logits within 1e-4 (1e-3 with the INT8 cache,
+    whose quantiser is discontinuous: see test_config5_geometry_matches_reference),
+    greedy tokens equal where the top-2 margin exceeds that bar."""
     from engine_models import config5
     d, ref_lib, lib = env
     path = _archive(env, "config5_s512", config5(512), 0)
-    S, keep = 96, [0, 95]
+    keep = [0, S - 1]
     rng = np.random.default_rng(11)
-    prompts = rng.integers(3, 32768, (S, 260)).tolist()
+    prompts = rng.integers(3, 32768, (S, prompt_len)).tolist()
     teacher = rng.integers(3, 32768, (S, 2)).tolist()
-    op = {"op": "batch", "sessions": S, "prompts": prompts, "teacher": teacher, "kv": "fp32", "steps": 3,
+    op = {"op": "batch", "sessions": S, "prompts": prompts, "teacher": teacher, "kv": kv, "steps": 3,
           "keep": keep}
-    gpu = run_plan(path, [op], lib, d, "c5small_gpu")
+    gpu = run_plan(path, [op], lib, d, f"c5small_gpu_{kv}_{S}_{prompt_len}")
     for i, s in enumerate(keep):
-        plan = [{"op": "engine", "kv": "fp32"}, {"op": "prefill", "tokens": prompts[s], "last_only": True}]
+        plan = [{"op": "engine", "kv": kv}, {"op": "prefill", "tokens": prompts[s], "last_only": True}]
         plan += [{"op": "step", "token": t} for t in teacher[s]]
         plan += [{"op": "decode", "first": int(gpu["0_first"][s]), "max_new": 4}]
-        ref = run_plan(path, plan, ref_lib, d, f"c5small_ref{s}")
+        ref = run_plan(path, plan, ref_lib, d, f"c5small_ref_{kv}_{S}_{prompt_len}_{s}")
         pairs = [(gpu["0_prefill_logits"][i], ref["1_logits"])]
         pairs += [(gpu["0_teacher_logits"][i, j], ref[f"{2 + j}_logits"]) for j in range(2)]
-        for a, b in pairs:
-            assert rel(a, b) <= TOL, f"session {s}: rel err {rel(a, b):.3e}"
+        bar = TOL if kv == "fp32" else 1e-3
+        for n, (a, b) in enumerate(pairs):
+            assert rel(a, b) <= bar, f"session {s}, logits {n}: rel err {rel(a, b):.3e}"
         if int(gpu["0_first"][s]) == int(np.argmax(ref["1_logits"])):
             np.testing.assert_array_equal(gpu["0_tokens"][s], ref["4_tokens"][1:])
+        else:
+            assert top2_margin(ref["1_logits"]) / np.max(np.abs(ref["1_logits"])) <= bar
