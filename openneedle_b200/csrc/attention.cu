@@ -25,6 +25,7 @@
 
 #include "attention.cuh"
 #include "common.cuh"
+#include "engine_math.cuh"
 #include "pdl.cuh"
 #include "sm100_async.cuh"
 
@@ -37,6 +38,15 @@ constexpr unsigned kFull = 0xffffffffu;
 // The engine's output gate, o * sigmoid(g) with sigmoid(g) = 1 / (1 + exp(-g))
 // (needle2/csrc/engine.cpp:36,123-129), applied as attention writes its output.
 __device__ __forceinline__ float gated(const AttnParams &p, size_t i, float o) {
+    if (!p.gate) return o;
+    // the gate's K parts, added in order (AttnParams::gate_parts)
+    const float g = p.gate_parts > 1 ? eng::part_sum(p.gate + i, p.gate_parts, p.gate_pstride) : p.gate[i];
+    return __fmul_rn(o, __fdiv_rn(1.f, __fadd_rn(1.f, expf(-g))));
+}
+// The same for kernels that never take the gate as parts: no branch between
+// the gate loads of an unrolled epilogue (measured: with one, the warp-per-query
+// decode at 1024 sessions ran 35 % slower, its gate loads serialised).
+__device__ __forceinline__ float gated_one(const AttnParams &p, size_t i, float o) {
     return p.gate ? __fmul_rn(o, __fdiv_rn(1.f, __fadd_rn(1.f, expf(-p.gate[i])))) : o;
 }
 
@@ -338,7 +348,7 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const AttnParams p) {
         const int h = kh * R + r;
         if (p.splits == 1) {
             const size_t oi = ((size_t)query * p.heads + h) * hd + d;
-            p.out[oi] = gated(p, oi, ll > 0.f ? aa / ll : 0.f);
+            p.out[oi] = gated_one(p, oi, ll > 0.f ? aa / ll : 0.f);
         } else {
             const size_t prow = ((size_t)query * p.heads + h) * p.splits + split;
             p.part_acc[prow * hd + d] = aa;
@@ -443,6 +453,79 @@ __device__ __forceinline__ RowPtr visible_ptr(const AttnParams &p, int s, int kh
     return r;
 }
 
+// Decode prologue of a CTA of attn_stream_kernel when the new token's
+// projections arrive as K-split parts (AttnParams::qkv_*): the parts added in
+// order, the CTA's R query heads RMS-normed (1 + q_norm) and roped into qs,
+// and -- where `own` (the CTA's slots include the token's) -- the KV head's K
+// (normed, roped) and V quantised and stored in the token's cache row.  The
+// arithmetic is qk_rope_store_kernel's (engine.cpp:994-1021).  Lane holds
+// elements lane + 32 e; the rotary pairs (j, j + HD / 2) sit in one lane.
+template <int HD, int R, int NW>
+__device__ __forceinline__ void qkv_prologue(const AttnParams &p, int query, int kh, int pos, int s, bool own,
+                                             float *qs, int warp, int lane) {
+    constexpr int E = HD / 32, half = HD / 2;
+    const int units = R + (own ? 2 : 0);
+    for (int u = warp; u < units; u += NW) {
+        const bool isq = u < R, isv = u == R + 1;
+        const size_t off = isq ? ((size_t)query * p.heads + kh * R + u) * HD : ((size_t)query * p.kvheads + kh) * HD;
+        const float *src = (isq ? p.qkv_q : isv ? p.qkv_v : p.qkv_k) + off;
+        float h[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) h[e] = eng::part_sum(src + lane + 32 * e, p.qkv_parts, p.qkv_pstride);
+        if (!isv) {
+            const float *nrm = isq ? p.q_norm : p.k_norm;
+            float ss = 0.f;
+#pragma unroll
+            for (int e = 0; e < E; ++e) ss = fmaf(h[e], h[e], ss);
+            const float inv = eng::rms_inv(eng::warp_sum(ss), HD);
+#pragma unroll
+            for (int e = 0; e < E; ++e) h[e] = __fmul_rn(__fmul_rn(h[e], inv), __fadd_rn(1.f, nrm[lane + 32 * e]));
+            const bool tab = p.rope_cos && pos < p.rope_len;
+#pragma unroll
+            for (int e = 0; e < E / 2; ++e) {
+                const int j = lane + 32 * e;
+                float co, si;
+                if (tab) {
+                    co = p.rope_cos[(size_t)pos * half + j];
+                    si = p.rope_sin[(size_t)pos * half + j];
+                } else {
+                    const float ang = __fdiv_rn((float)pos, p.rope_div[j]);
+                    co = cosf(ang);
+                    si = sinf(ang);
+                }
+                const float a = h[e], c = h[e + E / 2];
+                h[e] = __fsub_rn(__fmul_rn(a, co), __fmul_rn(c, si));
+                h[e + E / 2] = __fadd_rn(__fmul_rn(c, co), __fmul_rn(a, si));
+            }
+        }
+        if (isq) {
+#pragma unroll
+            for (int e = 0; e < E; ++e) qs[u * HD + lane + 32 * e] = h[e];
+            continue;
+        }
+        const bool pinned = pos < p.prefix;
+        const size_t row = pinned ? (size_t)kh * p.prefix + pos
+                                  : ((size_t)s * p.kvheads + kh) * p.cs +
+                                        (p.window ? (pos - p.prefix) % p.window : pos - p.prefix);
+        float mx = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) mx = fmaxf(mx, fabsf(h[e]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+        const float sc = mx > 0.f ? __fdiv_rn(mx, 127.f) : 1.f;
+        const float iv = mx > 0.f ? __fdiv_rn(127.f, mx) : 0.f;
+        int8_t *dst = const_cast<int8_t *>(isv ? (pinned ? p.pv : p.sv) : (pinned ? p.pk : p.sk)) + row * HD;
+        float *sdst = const_cast<float *>(isv ? (pinned ? p.pvs : p.svs) : (pinned ? p.pks : p.sks));
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            int qv = __float2int_rn(__fmul_rn(h[e], iv));
+            qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
+            dst[lane + 32 * e] = (int8_t)qv;
+        }
+        if (lane == 0) sdst[row] = sc;
+    }
+}
+
 template <int HD>
 struct StreamGeo {
     static constexpr int NW = 4;                    // warps per CTA
@@ -526,12 +609,27 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
         cp_async_commit();   // one group per chunk, empty ones included
     };
 
-    if (!WPQ)
-        for (int idx = threadIdx.x; idx < R * HD; idx += blockDim.x)
-            qs[idx] = p.q[((size_t)query * p.heads + kh * R) * HD + idx];
+    // with the new token's projections as parts, this CTA may first store the
+    // token's K/V: a warp issues its first chunks ahead of that only where they
+    // end before the token's slot (the last visible one)
+    const bool fused = !WPQ && p.qkv_q;
+    const bool early = !fused || w1 < len || w0 + (NCH - 1) * CH * 8 <= len - 1;
+    if (early)
 #pragma unroll
-    for (int ch = 0; ch < NCH - 1; ++ch) issue(ch);
-    if (!WPQ) __syncthreads();
+        for (int ch = 0; ch < NCH - 1; ++ch) issue(ch);
+    if constexpr (!WPQ) {
+        if (fused) {
+            qkv_prologue<HD, R, NW>(p, query, kh, pos, s, i0 < len && i1 == len, qs, warp, lane);
+            __threadfence_block();   // the token's K/V rows before any warp's copies of them
+        } else {
+            for (int idx = threadIdx.x; idx < R * HD; idx += blockDim.x)
+                qs[idx] = p.q[((size_t)query * p.heads + kh * R) * HD + idx];
+        }
+        __syncthreads();
+    }
+    if (!early)
+#pragma unroll
+        for (int ch = 0; ch < NCH - 1; ++ch) issue(ch);
     float2 qr[QREG ? R : 1][QREG ? DL / 2 : 1];
     if (QREG) {
         const float *qsrc = WPQ ? p.q + ((size_t)query * p.heads + kh * R) * HD : qs;
@@ -672,8 +770,8 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
             const size_t o0 = ((size_t)query * p.heads + kh * R + r) * HD + c * DL;
 #pragma unroll
             for (int e = 0; e < DL / 2; ++e) {
-                acc[r][e].x = gated(p, o0 + 2 * e, acc[r][e].x * inv);
-                acc[r][e].y = gated(p, o0 + 2 * e + 1, acc[r][e].y * inv);
+                acc[r][e].x = gated_one(p, o0 + 2 * e, acc[r][e].x * inv);
+                acc[r][e].y = gated_one(p, o0 + 2 * e + 1, acc[r][e].y * inv);
                 if (j == 0) {
                     p.out[o0 + 2 * e] = acc[r][e].x;
                     p.out[o0 + 2 * e + 1] = acc[r][e].y;
@@ -1001,8 +1099,8 @@ __global__ void __launch_bounds__(128) attn_prefill_tile_kernel(const AttnParams
 #pragma unroll
         for (int d = 0; d < HD; d += 4)
             *reinterpret_cast<float4 *>(op + d) =
-                make_float4(gated(p, o0 + d, acc[d] * inv), gated(p, o0 + d + 1, acc[d + 1] * inv),
-                            gated(p, o0 + d + 2, acc[d + 2] * inv), gated(p, o0 + d + 3, acc[d + 3] * inv));
+                make_float4(gated_one(p, o0 + d, acc[d] * inv), gated_one(p, o0 + d + 1, acc[d + 1] * inv),
+                            gated_one(p, o0 + d + 2, acc[d + 2] * inv), gated_one(p, o0 + d + 3, acc[d + 3] * inv));
     }
 }
 
@@ -1157,6 +1255,21 @@ bool launch_combine(const AttnParams &p, int queries, cudaStream_t st, bool *rot
     return true;
 }
 
+namespace {
+// INT8 decode runs one warp per (query, KV head) pair (attn_stream_kernel<.., true>).
+bool decode_wpq(const AttnParams &p, int queries) {
+    const int R = p.heads / p.kvheads;
+    return p.splits == 1 && ((p.hd == 64 && R <= 2) || (p.hd == 128 && R <= 1)) &&
+           (long long)queries * p.kvheads >= kWpqMinPairs;
+}
+}  // namespace
+
+bool attention_fuses_qkv(const AttnParams &p, int queries) {
+    if (p.f32 || p.tokens != 1 || p.stage_k || p.heads % p.kvheads || decode_wpq(p, queries)) return false;
+    const int R = p.heads / p.kvheads;
+    return (p.hd == 64 && (R == 1 || R == 2 || R == 4)) || (p.hd == 128 && (R == 1 || R == 2));
+}
+
 bool launch_attention(const AttnParams &p_in, int queries, cudaStream_t st, bool *rot_done) {
     if (rot_done) *rot_done = false;
     if (queries <= 0) return true;
@@ -1164,6 +1277,10 @@ bool launch_attention(const AttnParams &p_in, int queries, cudaStream_t st, bool
     if (p.tokens != 1) p.hilo = nullptr;   // decode only
     if (p.heads % p.kvheads || p.heads / p.kvheads > kMaxQueryGroup) {
         set_error("attention supports up to 8 query heads per KV head");
+        return false;
+    }
+    if (p.qkv_q && !attention_fuses_qkv(p, queries)) {
+        set_error("attention: the new token's projections as parts need the unsplit-or-split INT8 decode kernel");
         return false;
     }
     dim3 grid(p.splits, p.kvheads, queries);
@@ -1192,12 +1309,15 @@ bool launch_attention(const AttnParams &p_in, int queries, cudaStream_t st, bool
         NB_CUDA_TRY(cudaGetLastError());
         return true;
     }
+    if (decode_wpq(p, queries) && p.gate_parts > 1) {
+        set_error("attention: the warp-per-query decode takes no gate parts");
+        return false;
+    }
     bool streamed = false;
     // one warp per query where the context needs no split, the query fits the
     // registers and the queries alone fill the machine; with fewer, the CTA's
     // warps share each query's slots
-    const bool wpq = p.splits == 1 && ((p.hd == 64 && R <= 2) || (p.hd == 128 && R <= 1)) &&
-                     (long long)queries * p.kvheads >= kWpqMinPairs;
+    const bool wpq = decode_wpq(p, queries);
     AttnParams pw = p;
     pw.queries = queries;
     // the warp-per-query epilogue rotates one KV head's 2 x 64 outputs

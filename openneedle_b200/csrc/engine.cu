@@ -690,8 +690,15 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
             projections(m, ti, s.z.ptr, R, s.q.ptr, s.k.ptr, s.v.ptr, s.gate.ptr, stream);
         }
         mark(st, 3, stream);
-        if (roped) {
-            // q/k normed and roped, the token's K/V stored: attention follows
+        // decode with the projections as parts and a kernel that takes them:
+        // attention itself norms and ropes q and stores the token's K/V
+        QkvParts qkv{};
+        const bool qkv_fused = !roped && T == 1 && qkvg_src.q && kv_pool_fuses_qkv(st.kv[l], E, max_visible);
+        if (qkv_fused)
+            qkv = QkvParts{qkvg_src.q, qkvg_src.k, qkvg_src.v, qkvg_src.g, qkvg_src.parts, qkvg_src.pstride,
+                           m.t[ti + 4].dense, m.t[ti + 5].dense, m.rope_cos, m.rope_sin, m.rope_divisor, m.rope_len};
+        if (roped || qkv_fused) {
+            // q/k normed and roped, the token's K/V stored (or attention does it): attention follows
         } else if (T == 1) {
             // decode: the new token's K/V stored as RoPE finishes, then attention alone
             check(eng::launch_qk_rope_store(s.q.ptr, s.k.ptr, s.v.ptr, R, c.heads, c.kvheads, c.head_dim,
@@ -722,7 +729,8 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
             }
         }
         check(kv_pool_run(st.kv[l], T == 1 ? kQuery : kPrefill, st.iota.ptr, st.base.ptr, E, T, max_visible, s.q.ptr,
-                          s.k.ptr, s.v.ptr, s.att.ptr, stream, s.gate.ptr, want_rot ? &rot : nullptr, &rotated),
+                          s.k.ptr, s.v.ptr, s.att.ptr, stream, s.gate.ptr, want_rot ? &rot : nullptr, &rotated,
+                          qkv_fused ? &qkv : nullptr),
               "attention");
         mark(st, 5, stream);
         // the out projection's K parts, when the layer-boundary kernel adds them

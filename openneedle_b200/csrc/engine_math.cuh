@@ -27,13 +27,10 @@ __device__ __forceinline__ float sigm(float x) { return __fdiv_rn(1.f, __fadd_rn
 // Sum of the K-split parts p[0], p[stride], ... of one GEMM output
 // (1 <= parts <= kMaxKParts), added in part order.
 __device__ __forceinline__ float part_sum(const float *__restrict__ p, int parts, long long stride) {
-    float v[kMaxKParts];
-#pragma unroll
-    for (int i = 0; i < kMaxKParts; ++i) v[i] = i < parts ? p[i * stride] : 0.f;
-    float s = v[0];
+    float s = p[0];
 #pragma unroll
     for (int i = 1; i < kMaxKParts; ++i)
-        if (i < parts) s += v[i];
+        if (i < parts) s += p[i * stride];
     return s;
 }
 

@@ -14,6 +14,7 @@
 #include "../../include/needle2_b200.h"
 #include "attention.cuh"
 #include "common.cuh"
+#include "cq_gemv.cuh"
 #include "kv_pool.cuh"
 
 namespace nb200 {
@@ -165,9 +166,21 @@ bool store_ring(KVPool &kv, const int *ids, const int *pos, const float *k, cons
 // own new K/V when `staged` (prefill).
 bool attend(KVPool &kv, const int *ids, const int *pos, int count, int tokens, int max_len, const float *q, float *out,
             bool staged, cudaStream_t st, const float *gate = nullptr, const AttnRot *rot = nullptr,
-            bool *rot_done = nullptr) {
+            bool *rot_done = nullptr, const QkvParts *qkv = nullptr) {
     AttnParams p = base_params(kv);
     p.gate = gate;
+    if (qkv) {
+        p.gate = qkv->gate;
+        p.gate_parts = qkv->parts;
+        p.gate_pstride = qkv->pstride;
+        p.qkv_q = qkv->q; p.qkv_k = qkv->k; p.qkv_v = qkv->v;
+        p.qkv_parts = qkv->parts;
+        p.qkv_pstride = qkv->pstride;
+        p.q_norm = qkv->q_norm; p.k_norm = qkv->k_norm;
+        p.rope_cos = qkv->rope_cos; p.rope_sin = qkv->rope_sin; p.rope_div = qkv->rope_div;
+        p.rope_len = qkv->rope_len;
+        q = nullptr;
+    }
     if (rot && rot->group == kv.heads / kv.kvheads * kv.hd) {
         p.hilo = rot->hilo;
         p.hilo_lo = rot->lo_off;
@@ -264,6 +277,14 @@ size_t kv_pool_bytes(const KVPool *kv) {
 
 int kv_pool_device(const KVPool *kv) { return kv->device; }
 
+bool kv_pool_fuses_qkv(KVPool *kv, int count, int max_visible) {
+    if (!kv || count <= 0) return false;
+    AttnParams p = base_params(*kv);
+    p.tokens = 1;
+    p.splits = attention_splits(max_visible, count * kv->kvheads, kv->sms);
+    return attention_fuses_qkv(p, count);
+}
+
 KVStoreTarget kv_pool_target(KVPool *kv, const int *ids, const int *pos) {
     KVStoreTarget t{};
     t.dest = ring_dest(*kv, ids, pos, 1, 0);
@@ -288,12 +309,18 @@ int kv_max_visible(int prefix, int window, const int *positions, int count, int 
 
 bool kv_pool_run(KVPool *kv, KVOp op, const int *ids, const int *pos, int count, int tokens, int max_visible,
                  const float *q, const float *k, const float *v, float *out, cudaStream_t st, const float *gate,
-                 const AttnRot *rot, bool *rot_done) {
+                 const AttnRot *rot, bool *rot_done, const QkvParts *qkv) {
     if (rot_done) *rot_done = false;
     if (count <= 0) return true;
+    if (qkv && (op != kQuery || tokens != 1 || qkv->parts < 1 || qkv->parts > kMaxKParts || !qkv->q || !qkv->k ||
+                !qkv->v || !qkv->q_norm || !qkv->k_norm || !qkv->rope_div)) {
+        set_error("KV pool: projections as parts need a one-token query with every operand");
+        return false;
+    }
     switch (op) {
         case kStore: return store_ring(*kv, ids, pos, k, v, count, tokens, 0, st);
-        case kQuery: return attend(*kv, ids, pos, count, tokens, max_visible, q, out, false, st, gate, rot, rot_done);
+        case kQuery:
+            return attend(*kv, ids, pos, count, tokens, max_visible, q, out, false, st, gate, rot, rot_done, qkv);
         case kDecode:
             if (tokens != 1) { set_error("decode takes one token per entry"); return false; }
             return store_ring(*kv, ids, pos, k, v, count, 1, 0, st) &&
