@@ -38,15 +38,6 @@ constexpr unsigned kFull = 0xffffffffu;
 // The engine's output gate, o * sigmoid(g) with sigmoid(g) = 1 / (1 + exp(-g))
 // (needle2/csrc/engine.cpp:36,123-129), applied as attention writes its output.
 __device__ __forceinline__ float gated(const AttnParams &p, size_t i, float o) {
-    if (!p.gate) return o;
-    // the gate's K parts, added in order (AttnParams::gate_parts)
-    const float g = p.gate_parts > 1 ? eng::part_sum(p.gate + i, p.gate_parts, p.gate_pstride) : p.gate[i];
-    return __fmul_rn(o, __fdiv_rn(1.f, __fadd_rn(1.f, expf(-g))));
-}
-// The same for kernels that never take the gate as parts: no branch between
-// the gate loads of an unrolled epilogue (measured: with one, the warp-per-query
-// decode at 1024 sessions ran 35 % slower, its gate loads serialised).
-__device__ __forceinline__ float gated_one(const AttnParams &p, size_t i, float o) {
     return p.gate ? __fmul_rn(o, __fdiv_rn(1.f, __fadd_rn(1.f, expf(-p.gate[i])))) : o;
 }
 
@@ -348,7 +339,7 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const AttnParams p) {
         const int h = kh * R + r;
         if (p.splits == 1) {
             const size_t oi = ((size_t)query * p.heads + h) * hd + d;
-            p.out[oi] = gated_one(p, oi, ll > 0.f ? aa / ll : 0.f);
+            p.out[oi] = gated(p, oi, ll > 0.f ? aa / ll : 0.f);
         } else {
             const size_t prow = ((size_t)query * p.heads + h) * p.splits + split;
             p.part_acc[prow * hd + d] = aa;
@@ -460,12 +451,24 @@ __device__ __forceinline__ RowPtr visible_ptr(const AttnParams &p, int s, int kh
 // (normed, roped) and V quantised and stored in the token's cache row.  The
 // arithmetic is qk_rope_store_kernel's (engine.cpp:994-1021).  Lane holds
 // elements lane + 32 e; the rotary pairs (j, j + HD / 2) sit in one lane.
-template <int HD, int R, int NW>
+template <int HD, int R, int NWARPS>
 __device__ __forceinline__ void qkv_prologue(const AttnParams &p, int query, int kh, int pos, int s, bool own,
                                              float *qs, int warp, int lane) {
     constexpr int E = HD / 32, half = HD / 2;
-    const int units = R + (own ? 2 : 0);
-    for (int u = warp; u < units; u += NW) {
+    // units: R query heads; where own, the KV head's K and V, then the gate of the R query heads
+    const int units = R + (own ? 2 + (p.qkv_g ? R : 0) : 0);
+#pragma unroll
+    for (int u0 = 0; u0 < 2 * R + 2; u0 += NWARPS) {
+        const int u = u0 + warp;
+        if (u >= units) break;
+        if (u >= R + 2) {   // a gate head: the parts' sum, read back by this query's epilogue
+            const size_t o = ((size_t)query * p.heads + kh * R + (u - R - 2)) * HD;
+#pragma unroll
+            for (int e = 0; e < E; ++e)
+                const_cast<float *>(p.gate)[o + lane + 32 * e] =
+                    eng::part_sum(p.qkv_g + o + lane + 32 * e, p.qkv_parts, p.qkv_pstride);
+            continue;
+        }
         const bool isq = u < R, isv = u == R + 1;
         const size_t off = isq ? ((size_t)query * p.heads + kh * R + u) * HD : ((size_t)query * p.kvheads + kh) * HD;
         const float *src = (isq ? p.qkv_q : isv ? p.qkv_v : p.qkv_k) + off;
@@ -526,6 +529,119 @@ __device__ __forceinline__ void qkv_prologue(const AttnParams &p, int query, int
     }
 }
 
+// The same for one warp that owns a whole query (the warp-per-query decode,
+// R <= 2): every unit at once -- all parts loaded together, the three norms'
+// sums and the two quantisers' maxima reduced side by side -- so that the
+// prologue costs about one load round trip rather than one per unit.
+template <int HD, int R>
+__device__ __forceinline__ void wpq_prologue(const AttnParams &p, int query, int kh, int pos, int s, float *qs,
+                                             int lane) {
+    constexpr int E = HD / 32, half = HD / 2;
+    const int P = p.qkv_parts;
+    const long long ps = p.qkv_pstride;
+    const size_t qo = ((size_t)query * p.heads + kh * R) * HD, ko = ((size_t)query * p.kvheads + kh) * HD;
+    float q[R][E], k[E], v[E], g[R][E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int d = lane + 32 * e;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            q[r][e] = eng::part_sum(p.qkv_q + qo + r * HD + d, P, ps);
+            g[r][e] = p.qkv_g ? eng::part_sum(p.qkv_g + qo + r * HD + d, P, ps) : 0.f;
+        }
+        k[e] = eng::part_sum(p.qkv_k + ko + d, P, ps);
+        v[e] = eng::part_sum(p.qkv_v + ko + d, P, ps);
+    }
+    // RMS norms (1 + w) of the query heads and of K
+    float ss[R + 1];
+#pragma unroll
+    for (int r = 0; r <= R; ++r) {
+        ss[r] = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const float x = r < R ? q[r][e] : k[e];
+            ss[r] = fmaf(x, x, ss[r]);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int r = 0; r <= R; ++r) ss[r] += __shfl_xor_sync(kFull, ss[r], o);
+#pragma unroll
+    for (int r = 0; r <= R; ++r) {
+        const float inv = eng::rms_inv(ss[r], HD);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const int d = lane + 32 * e;
+            if (r < R) q[r][e] = __fmul_rn(__fmul_rn(q[r][e], inv), __fadd_rn(1.f, p.q_norm[d]));
+            else k[e] = __fmul_rn(__fmul_rn(k[e], inv), __fadd_rn(1.f, p.k_norm[d]));
+        }
+    }
+    // rotary embedding at the token's position: pairs (j, j + HD / 2) in one lane
+    const bool tab = p.rope_cos && pos < p.rope_len;
+#pragma unroll
+    for (int e = 0; e < E / 2; ++e) {
+        const int j = lane + 32 * e;
+        float co, si;
+        if (tab) {
+            co = p.rope_cos[(size_t)pos * half + j];
+            si = p.rope_sin[(size_t)pos * half + j];
+        } else {
+            const float ang = __fdiv_rn((float)pos, p.rope_div[j]);
+            co = cosf(ang);
+            si = sinf(ang);
+        }
+#pragma unroll
+        for (int r = 0; r <= R; ++r) {
+            float &x0 = r < R ? q[r][e] : k[e];
+            float &x1 = r < R ? q[r][e + E / 2] : k[e + E / 2];
+            const float a = x0, c = x1;
+            x0 = __fsub_rn(__fmul_rn(a, co), __fmul_rn(c, si));
+            x1 = __fadd_rn(__fmul_rn(c, co), __fmul_rn(a, si));
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int e = 0; e < E; ++e) qs[r * HD + lane + 32 * e] = q[r][e];
+    if (p.qkv_g)
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int e = 0; e < E; ++e) const_cast<float *>(p.gate)[qo + r * HD + lane + 32 * e] = g[r][e];
+    // K and V of the token quantised into its cache row
+    float mk = 0.f, mv = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        mk = fmaxf(mk, fabsf(k[e]));
+        mv = fmaxf(mv, fabsf(v[e]));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mk = fmaxf(mk, __shfl_xor_sync(kFull, mk, o));
+        mv = fmaxf(mv, __shfl_xor_sync(kFull, mv, o));
+    }
+    const bool pinned = pos < p.prefix;
+    const size_t row = pinned ? (size_t)kh * p.prefix + pos
+                              : ((size_t)s * p.kvheads + kh) * p.cs +
+                                    (p.window ? (pos - p.prefix) % p.window : pos - p.prefix);
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const float mx = t ? mv : mk;
+        const float sc = mx > 0.f ? __fdiv_rn(mx, 127.f) : 1.f;
+        const float iv = mx > 0.f ? __fdiv_rn(127.f, mx) : 0.f;
+        int8_t *dst = const_cast<int8_t *>(t ? (pinned ? p.pv : p.sv) : (pinned ? p.pk : p.sk)) + row * HD;
+        float *sdst = const_cast<float *>(t ? (pinned ? p.pvs : p.svs) : (pinned ? p.pks : p.sks));
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            int qv = __float2int_rn(__fmul_rn(t ? v[e] : k[e], iv));
+            qv = qv < -127 ? -127 : (qv > 127 ? 127 : qv);
+            dst[lane + 32 * e] = (int8_t)qv;
+        }
+        if (lane == 0) sdst[row] = sc;
+    }
+}
+
 template <int HD>
 struct StreamGeo {
     static constexpr int NW = 4;                    // warps per CTA
@@ -541,7 +657,9 @@ struct StreamGeo {
 // WPQ (warp per query): each warp takes one whole (query, KV head) pair (no
 // split, no cross-warp combine, no block barrier) and the CTA's four warps four
 // queries -- the short-context decode case, where per-CTA work is small.
-template <int HD, int R, bool WPQ>
+// FQ: decode with the new token's projections as K parts (AttnParams::qkv_*;
+// a separate instantiation, so that the plain kernels keep their code).
+template <int HD, int R, bool WPQ, bool FQ>
 __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p) {
     pdl_enter();
     using Geo = StreamGeo<HD>;
@@ -612,12 +730,22 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
     // with the new token's projections as parts, this CTA may first store the
     // token's K/V: a warp issues its first chunks ahead of that only where they
     // end before the token's slot (the last visible one)
-    const bool fused = !WPQ && p.qkv_q;
+    constexpr bool fused = FQ;
     const bool early = !fused || w1 < len || w0 + (NCH - 1) * CH * 8 <= len - 1;
     if (early)
 #pragma unroll
         for (int ch = 0; ch < NCH - 1; ++ch) issue(ch);
-    if constexpr (!WPQ) {
+    // one warp per query: the warp's own prologue, its query heads staged in the
+    // ring slot that the first issued chunks leave free
+    float *const qw = reinterpret_cast<float *>(ring + (NCH - 1) * Geo::CHUNK);
+    if constexpr (WPQ) {
+        static_assert(R * HD * 4 <= Geo::CHUNK, "query heads fit a ring chunk");
+        if (fused) {
+            wpq_prologue<HD, R>(p, query, kh, pos, s, qw, lane);
+            __threadfence_block();   // the token's K/V rows and gate before this warp's reads of them
+            __syncwarp();
+        }
+    } else {
         if (fused) {
             qkv_prologue<HD, R, NW>(p, query, kh, pos, s, i0 < len && i1 == len, qs, warp, lane);
             __threadfence_block();   // the token's K/V rows before any warp's copies of them
@@ -632,12 +760,13 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
         for (int ch = 0; ch < NCH - 1; ++ch) issue(ch);
     float2 qr[QREG ? R : 1][QREG ? DL / 2 : 1];
     if (QREG) {
-        const float *qsrc = WPQ ? p.q + ((size_t)query * p.heads + kh * R) * HD : qs;
+        const float *qsrc = WPQ ? (fused ? qw : p.q + ((size_t)query * p.heads + kh * R) * HD) : qs;
 #pragma unroll
         for (int r = 0; r < R; ++r)
 #pragma unroll
             for (int e = 0; e < DL / 2; ++e)
                 qr[r][e] = *reinterpret_cast<const float2 *>(qsrc + r * HD + c * DL + 2 * e);
+        if (WPQ && fused) __syncwarp();   // every lane has read qw before the ring slot is refilled
     }
 
     const float inv_sqrt = p.inv_sqrt_hd;
@@ -770,8 +899,8 @@ __global__ void __launch_bounds__(128, 4) attn_stream_kernel(const AttnParams p)
             const size_t o0 = ((size_t)query * p.heads + kh * R + r) * HD + c * DL;
 #pragma unroll
             for (int e = 0; e < DL / 2; ++e) {
-                acc[r][e].x = gated_one(p, o0 + 2 * e, acc[r][e].x * inv);
-                acc[r][e].y = gated_one(p, o0 + 2 * e + 1, acc[r][e].y * inv);
+                acc[r][e].x = gated(p, o0 + 2 * e, acc[r][e].x * inv);
+                acc[r][e].y = gated(p, o0 + 2 * e + 1, acc[r][e].y * inv);
                 if (j == 0) {
                     p.out[o0 + 2 * e] = acc[r][e].x;
                     p.out[o0 + 2 * e + 1] = acc[r][e].y;
@@ -1099,8 +1228,8 @@ __global__ void __launch_bounds__(128) attn_prefill_tile_kernel(const AttnParams
 #pragma unroll
         for (int d = 0; d < HD; d += 4)
             *reinterpret_cast<float4 *>(op + d) =
-                make_float4(gated_one(p, o0 + d, acc[d] * inv), gated_one(p, o0 + d + 1, acc[d + 1] * inv),
-                            gated_one(p, o0 + d + 2, acc[d + 2] * inv), gated_one(p, o0 + d + 3, acc[d + 3] * inv));
+                make_float4(gated(p, o0 + d, acc[d] * inv), gated(p, o0 + d + 1, acc[d + 1] * inv),
+                            gated(p, o0 + d + 2, acc[d + 2] * inv), gated(p, o0 + d + 3, acc[d + 3] * inv));
     }
 }
 
@@ -1128,19 +1257,24 @@ bool launch_ring_kernel(K kernel, size_t smem, dim3 grid, cudaStream_t st, const
     return true;
 }
 
-template <int HD, bool WPQ>
-bool launch_stream(const AttnParams &p, dim3 grid, int R, cudaStream_t st) {
+template <int HD, bool WPQ, bool FQ>
+bool launch_stream_fq(const AttnParams &p, dim3 grid, int R, cudaStream_t st) {
     constexpr size_t smem = stream_smem<HD>();
     switch (R) {
-        case 1: return launch_ring_kernel(attn_stream_kernel<HD, 1, WPQ>, smem, grid, st, p);
+        case 1: return launch_ring_kernel(attn_stream_kernel<HD, 1, WPQ, FQ>, smem, grid, st, p);
         case 2:
-            if constexpr (!WPQ || 2 * HD / 4 <= 32) return launch_ring_kernel(attn_stream_kernel<HD, 2, WPQ>, smem, grid, st, p);
+            if constexpr (!WPQ || 2 * HD / 4 <= 32)
+                return launch_ring_kernel(attn_stream_kernel<HD, 2, WPQ, FQ>, smem, grid, st, p);
             return false;
         case 4:
-            if constexpr (HD <= 64 && !WPQ) return launch_ring_kernel(attn_stream_kernel<HD, 4, false>, smem, grid, st, p);
+            if constexpr (HD <= 64 && !WPQ) return launch_ring_kernel(attn_stream_kernel<HD, 4, false, FQ>, smem, grid, st, p);
             return false;
         default: return false;
     }
+}
+template <int HD, bool WPQ>
+bool launch_stream(const AttnParams &p, dim3 grid, int R, cudaStream_t st) {
+    return p.qkv_q ? launch_stream_fq<HD, WPQ, true>(p, grid, R, st) : launch_stream_fq<HD, WPQ, false>(p, grid, R, st);
 }
 
 // Merge the split partials of each (query, head).
@@ -1264,8 +1398,13 @@ bool decode_wpq(const AttnParams &p, int queries) {
 }
 }  // namespace
 
-bool attention_fuses_qkv(const AttnParams &p, int queries) {
-    if (p.f32 || p.tokens != 1 || p.stage_k || p.heads % p.kvheads || decode_wpq(p, queries)) return false;
+bool attention_fuses_qkv(const AttnParams &p, int queries, int sms) {
+    if (p.f32 || p.tokens != 1 || p.stage_k || p.heads % p.kvheads) return false;
+    // the warp-per-query form while its CTAs (four queries each, four CTAs an SM)
+    // fit one wave: measured at config 5, 512 sessions 1.152 vs 1.25 ms a step
+    // with the projections' epilogue instead; 1024 sessions (1.7 waves, the
+    // prologue paid twice) 2.128 vs 1.997 ms
+    if (decode_wpq(p, queries)) return (long long)p.kvheads * ((queries + 3) / 4) <= 4LL * sms;
     const int R = p.heads / p.kvheads;
     return (p.hd == 64 && (R == 1 || R == 2 || R == 4)) || (p.hd == 128 && (R == 1 || R == 2));
 }
@@ -1279,7 +1418,7 @@ bool launch_attention(const AttnParams &p_in, int queries, cudaStream_t st, bool
         set_error("attention supports up to 8 query heads per KV head");
         return false;
     }
-    if (p.qkv_q && !attention_fuses_qkv(p, queries)) {
+    if (p.qkv_q && !attention_fuses_qkv(p, queries, 1 << 20)) {
         set_error("attention: the new token's projections as parts need the unsplit-or-split INT8 decode kernel");
         return false;
     }
@@ -1308,10 +1447,6 @@ bool launch_attention(const AttnParams &p_in, int queries, cudaStream_t st, bool
         if (!launch_prefill_tile<64>(p, queries / p.tokens, R, st)) return false;
         NB_CUDA_TRY(cudaGetLastError());
         return true;
-    }
-    if (decode_wpq(p, queries) && p.gate_parts > 1) {
-        set_error("attention: the warp-per-query decode takes no gate parts");
-        return false;
     }
     bool streamed = false;
     // one warp per query where the context needs no split, the query fits the

@@ -49,14 +49,13 @@ struct AttnParams {
     long long hilo_lo;
     int hilo_ld;
     float rot_scale;
-    int gate_parts;                   // gate as K-split parts (gate + k * gate_pstride); 0 or 1: one
-    long long gate_pstride;
     // null, or decode (tokens == 1, INT8 cache, attention_fuses_qkv) with the
-    // new token's projections as K-split parts: q [queries][heads][HD] and k, v
-    // [queries][kvheads][HD] (part k at + k * qkv_pstride).  Each CTA adds,
-    // norms and ropes its query heads, and the CTA whose slots include the
-    // token's own stores the token's K and V before it reads its slots.
-    const float *qkv_q, *qkv_k, *qkv_v;
+    // new token's projections as K-split parts: q and gate [queries][heads][HD]
+    // and k, v [queries][kvheads][HD] (part k at + k * qkv_pstride).  Each CTA
+    // (or warp, one per query) adds, norms and ropes its query heads; the one
+    // whose slots include the token's own stores the token's K and V before it
+    // reads its slots, and writes its heads' gate sums to `gate` (then required).
+    const float *qkv_q, *qkv_k, *qkv_v, *qkv_g;
     int qkv_parts;
     long long qkv_pstride;
     const float *q_norm, *k_norm;     // [HD]: RMS-norm weights (applied as 1 + w)
@@ -89,9 +88,10 @@ bool launch_kv_quantize(const float *k, const float *v, int tokens, int kvheads,
 bool launch_kv_store_f32(const float *k, const float *v, int tokens, int kvheads, int hd, float *ko, float *vo,
                          const KVDest &dest, cudaStream_t st);
 int attention_splits(int max_len, int queries_x_kv, int sms);
-// Whether launch_attention(p, queries) runs the decode kernel that takes the
-// new token's projections as parts (AttnParams::qkv_*; p.splits set).
-bool attention_fuses_qkv(const AttnParams &p, int queries);
+// Whether launch_attention(p, queries) on `sms` SMs should take the new
+// token's projections as parts (AttnParams::qkv_*; p.splits set): its decode
+// kernel can, and measured faster than the projections' own epilogue.
+bool attention_fuses_qkv(const AttnParams &p, int queries, int sms);
 // rot_done (optional): whether p.hilo was written (the decode forms write it;
 // the others leave it to the caller and launch as if it were null).
 bool launch_attention(const AttnParams &p, int queries, cudaStream_t st, bool *rot_done = nullptr);

@@ -653,13 +653,17 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         mark(st, 2, stream);
         void *hs[4];
         bool roped = false;   // norm, RoPE and the KV store done by the projections' epilogue
+        // decode whose attention kernel can take the projections as parts (then it
+        // norms and ropes q and stores the token's K/V itself)
+        const bool attn_qkv = T == 1 && kv_pool_fuses_qkv(st.kv[l], E, max_visible);
         eng::QkvgParts qkvg_src{};   // the projections' outputs as K parts (q null: in q, k, v, gate)
         if (zhl_ready && qkvg_handles(l, hs)) {
             float *outs[4] = {s.q.ptr, s.k.ptr, s.v.ptr, s.gate.ptr};
             QkvgEpilogue epi{};
-            // measured: the fused epilogue pays off from four 128-row tiles on (1024 rows: 0.07 ms a
-            // step saved); with fewer tiles its per-thread work outlasts the separate kernel
-            if (T == 1 && m.rope_cos && R >= 512) {
+            // where attention cannot take the projections as parts; measured: the fused epilogue pays
+            // off from four 128-row tiles on (1024 rows: 0.07 ms a step saved against the separate
+            // kernel); with fewer tiles its per-thread work outlasts the separate kernel
+            if (T == 1 && m.rope_cos && R >= 512 && !attn_qkv) {
                 epi.active = 1;
                 epi.heads = c.heads; epi.kvheads = c.kvheads; epi.hd = c.head_dim;
                 epi.q_norm = m.t[ti + 4].dense; epi.k_norm = m.t[ti + 5].dense;
@@ -693,7 +697,7 @@ void forward(State &st, int E, int T, const int *tokens, const Outputs &o, float
         // decode with the projections as parts and a kernel that takes them:
         // attention itself norms and ropes q and stores the token's K/V
         QkvParts qkv{};
-        const bool qkv_fused = !roped && T == 1 && qkvg_src.q && kv_pool_fuses_qkv(st.kv[l], E, max_visible);
+        const bool qkv_fused = !roped && attn_qkv && qkvg_src.q;
         if (qkv_fused)
             qkv = QkvParts{qkvg_src.q, qkvg_src.k, qkvg_src.v, qkvg_src.g, qkvg_src.parts, qkvg_src.pstride,
                            m.t[ti + 4].dense, m.t[ti + 5].dense, m.rope_cos, m.rope_sin, m.rope_divisor, m.rope_len};

@@ -170,10 +170,7 @@ bool attend(KVPool &kv, const int *ids, const int *pos, int count, int tokens, i
     AttnParams p = base_params(kv);
     p.gate = gate;
     if (qkv) {
-        p.gate = qkv->gate;
-        p.gate_parts = qkv->parts;
-        p.gate_pstride = qkv->pstride;
-        p.qkv_q = qkv->q; p.qkv_k = qkv->k; p.qkv_v = qkv->v;
+        p.qkv_q = qkv->q; p.qkv_k = qkv->k; p.qkv_v = qkv->v; p.qkv_g = qkv->gate;
         p.qkv_parts = qkv->parts;
         p.qkv_pstride = qkv->pstride;
         p.q_norm = qkv->q_norm; p.k_norm = qkv->k_norm;
@@ -282,7 +279,7 @@ bool kv_pool_fuses_qkv(KVPool *kv, int count, int max_visible) {
     AttnParams p = base_params(*kv);
     p.tokens = 1;
     p.splits = attention_splits(max_visible, count * kv->kvheads, kv->sms);
-    return attention_fuses_qkv(p, count);
+    return attention_fuses_qkv(p, count, kv->sms);
 }
 
 KVStoreTarget kv_pool_target(KVPool *kv, const int *ids, const int *pos) {
@@ -313,7 +310,7 @@ bool kv_pool_run(KVPool *kv, KVOp op, const int *ids, const int *pos, int count,
     if (rot_done) *rot_done = false;
     if (count <= 0) return true;
     if (qkv && (op != kQuery || tokens != 1 || qkv->parts < 1 || qkv->parts > kMaxKParts || !qkv->q || !qkv->k ||
-                !qkv->v || !qkv->q_norm || !qkv->k_norm || !qkv->rope_div)) {
+                !qkv->v || !qkv->q_norm || !qkv->k_norm || !qkv->rope_div || (qkv->gate && !gate))) {
         set_error("KV pool: projections as parts need a one-token query with every operand");
         return false;
     }

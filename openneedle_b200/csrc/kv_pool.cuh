@@ -41,10 +41,10 @@ enum KVOp { kStore = 0, kDecode = 1, kPrefill = 2, kQuery = 3 };
 // the engine's attention output gate (engine.cpp:1023).
 // rot (optional, kQuery): also write out rotated and split for the out
 // projection's GEMM (AttnRot); *rot_done tells whether it was.
-// qkv (optional, kQuery with tokens = 1 where kv_pool_fuses_qkv): q, k, v and
-// gate are the new token's projections as K-split parts (QkvParts); the
-// attention kernel norms and ropes q and stores the token's K/V itself, and q,
-// k, v and gate above are ignored.
+// qkv (optional, kQuery with tokens = 1 where kv_pool_fuses_qkv): the new
+// token's projections as K-split parts (QkvParts); the attention kernel norms
+// and ropes q and stores the token's K/V itself (q, k and v above are
+// ignored), and writes the gate's sum to `gate` (required with qkv->gate).
 bool kv_pool_run(KVPool *kv, KVOp op, const int *ids, const int *pos, int count, int tokens, int max_visible,
                  const float *q, const float *k, const float *v, float *out, cudaStream_t st,
                  const float *gate = nullptr, const AttnRot *rot = nullptr, bool *rot_done = nullptr,
