@@ -517,9 +517,11 @@ __device__ __forceinline__ void qkvg_head(const QkvgEpilogue &E, int seg, int he
                                           float *yr) {
     if (seg <= 1) {
         const float *nrm = seg == 0 ? E.q_norm : E.k_norm;
-        float s = 0.f;
+        // four interleaved partial sums: a quarter of the dependent chain
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int i = 0; i < 64; ++i) s = fmaf(h[i], h[i], s);
+        for (int i = 0; i < 64; ++i) s4[i & 3] = fmaf(h[i], h[i], s4[i & 3]);
+        const float s = (s4[0] + s4[1]) + (s4[2] + s4[3]);
         const float inv = __fdiv_rn(1.f, sqrtf(__fadd_rn(__fdiv_rn(s, 64.f), 1e-6f)));
 #pragma unroll
         for (int i = 0; i < 64; ++i) h[i] = __fmul_rn(__fmul_rn(h[i], inv), __fadd_rn(1.f, nrm[i]));
@@ -557,9 +559,10 @@ __device__ __forceinline__ void qkvg_head(const QkvgEpilogue &E, int seg, int he
         for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4 *>(dst + i) = make_float4(h[i], h[i + 1], h[i + 2], h[i + 3]);
         return;
     }
-    float mx = 0.f;
+    float m4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int i = 0; i < 64; ++i) mx = fmaxf(mx, fabsf(h[i]));
+    for (int i = 0; i < 64; ++i) m4[i & 3] = fmaxf(m4[i & 3], fabsf(h[i]));
+    const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
     const float sc = mx > 0.f ? __fdiv_rn(mx, 127.f) : 1.f;
     const float iv = mx > 0.f ? __fdiv_rn(127.f, mx) : 0.f;
     int8_t *dst = (isv ? (pinned ? d.pv : E.kv.v8) : (pinned ? d.pk : E.kv.k8)) + krow * 64;

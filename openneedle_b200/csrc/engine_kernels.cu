@@ -942,13 +942,15 @@ bool launch_mhc_route(const MhcLayer &L, const float *phi_pre, const float *phi_
     const size_t smem = sizeof(float) * (size_t)sb * ND;
     if (smem > 200 * 1024) return false;
     const unsigned grid = (unsigned)((R + sb - 1) / sb);
+    int dev = 0;   // the shared-memory limit is a per-device attribute
+    NB_CUDA_TRY(cudaGetDevice(&dev));
 #define NB_ROUTE(SB)                                                                                               \
     {                                                                                                              \
-        static bool configured = false;                                                                            \
-        if (!configured) {                                                                                         \
+        static bool configured[64] = {};                                                                           \
+        if (dev < 0 || dev >= 64 || !configured[dev]) {                                                           \
             NB_CUDA_TRY(cudaFuncSetAttribute(mhc_route_kernel<SB>, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
                                              200 * 1024));                                                         \
-            configured = true;                                                                                     \
+            if (dev >= 0 && dev < 64) configured[dev] = true;                                                      \
         }                                                                                                          \
         NB_CUDA_TRY(launch_pdl(mhc_route_kernel<SB>, grid, 256, smem, st, L, phi_pre, phi_post, phi_res, x, R, raw, ldraw, hpost, u,   \
                                                       bx, z));                                                      \

@@ -648,13 +648,16 @@ bool launch_mhc_mix(const MixArgs &a, int R, int sms, cudaStream_t st) {
     args.phi_smem = staged && a.has_route && smem + phi_bytes <= 220 * 1024 ? 1 : 0;
     smem += args.phi_smem ? phi_bytes : sizeof(float) * (size_t)sb * N * a.D;   // (else nx of the rows)
     smem += 128;                                                                // base alignment
+    // the shared-memory limit is a per-device attribute of each instantiation
+    int dev = 0;
+    NB_CUDA_TRY(cudaGetDevice(&dev));
 #define NB_MIX(PP, SBB, ST)                                                                                      \
     {                                                                                                          \
         auto kernel = mhc_mix_kernel<PP, 4, SBB, ST>;                                                          \
-        static bool configured = false;                                                                        \
-        if (!configured) {                                                                                     \
+        static bool configured[64] = {};                                                                       \
+        if (dev < 0 || dev >= 64 || !configured[dev]) {                                                       \
             NB_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024)); \
-            configured = true;                                                                                 \
+            if (dev >= 0 && dev < 64) configured[dev] = true;                                                  \
         }                                                                                                      \
         NB_CUDA_TRY(launch_pdl(kernel, grid, kMixThreads, smem, st, args, R));                                  \
     }
