@@ -748,7 +748,6 @@ __global__ void __launch_bounds__(kFThreads, 1)
 }
 
 constexpr int kDecodeAcc = 1;     // accumulators per 64-wide tile
-constexpr bool kNarrow32 = false;  // 32-wide tiles for the smallest decode grids (measured slower)
 constexpr int kPartWidth = 64;     // tile width of K-split launches (measured: 64 < 128 < 256)
 
 struct Lut16 {
@@ -930,11 +929,7 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
                grid * 2 * parts <= sms)
             parts *= 2;
     }
-    // 32-wide tiles (twice the CTAs again, each MMA half as wide) where even the
-    // 64-wide grid leaves most SMs idle
-    const bool narrow32 =
-        kNarrow32 && parts == 1 && narrow && !with_epi && (long long)mtiles * tiles_of(64) * 2 <= sms;
-    const int BN = parts > 1 ? kPartWidth : narrow32 ? 32 : narrow ? 64 : 256;
+    const int BN = parts > 1 ? kPartWidth : narrow ? 64 : 256;
     const size_t an = (size_t)M * padded;
     CUtensorMap tah, tal;
     // bf16 rows seen as bytes: 2 * padded bytes per row, 128-byte (64-element) boxes
@@ -981,7 +976,6 @@ bool launch_gemm_f32x3_multi(const uint16_t *a_hilo, int M, int padded, const F3
         return launch(cq_gemm_f32x3_kernel<kPartWidth, 2, 1, false>, FTile<kPartWidth, 2>::kSmem, 3);
     }
     if (!narrow) return launch(cq_gemm_f32x3_kernel<256, 2, 1, false>, FTile<256, 2>::kSmem, 0);
-    if (narrow32) return launch(cq_gemm_f32x3_kernel<32, 4, kDecodeAcc, false>, FTile<32, 4>::kSmem, 6);
     if (with_epi) {
         args.epi = *epi;
         if (epi_done) *epi_done = true;
